@@ -1,0 +1,468 @@
+#!/usr/bin/env python
+"""Benchmark of the JLUST hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload laplacian|spmv1|spmm|sddmm|bsr|convert]
+
+Default workload (the configuration the headline metric is quoted on): CSR
+SpMV fp64 on the 5-point Laplacian of a 4096 x 4096 grid, x <- A x, one step
+per iteration, rows partitioned across the N ranks with a halo exchange
+(strong scaling: the matrix is the same for every N).  Inputs are larger than
+L2 (1.34 GB per iteration), so no flush is needed between iterations.
+
+Prints ONE JSON line on rank 0.  `value` is whole-job GFLOP/s (2 flops per
+stored entry) from CUDA events on the launch stream, max over ranks; `e2e` is
+the same metric through the public API with the step's input copied from
+pinned host memory and its result copied back inside the timed region;
+`roofline` relates the dominant kernel's algorithmic bytes per launch to the
+measured HBM copy bandwidth; `cpu_baseline` times the CPU restatement of the
+reference's path on this host's cores.  `--impl reference` times only that
+CPU path (rank 0; other ranks exit).
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import re
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+
+METRIC = "SpMV/SpMM GFLOP/s and effective HBM GB/s (% roofline) at 1/2/4/8 B200"
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=200)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--workload", default="laplacian",
+                   choices=["laplacian", "spmv1", "spmm", "sddmm", "bsr", "convert"])
+    p.add_argument("--exchange", choices=["halo", "allgather"], default="halo")
+    p.add_argument("--grid", type=int, default=4096, help="Laplacian grid width")
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-cpu", action="store_true")
+    return p.parse_args()
+
+
+def env_int(name, default):
+    try:
+        return int(os.environ.get(name, default))
+    except ValueError:
+        return default
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained"), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback"}
+
+
+def profile_traffic(name: str):
+    """dram bytes per launch recorded from an ncu capture in profiles/<name>.md."""
+    path = os.path.join(ROOT, "profiles", name + ".md")
+    if not os.path.exists(path):
+        return None
+    m = re.search(r"dram_bytes_per_launch:\s*([0-9.eE+]+)", open(path).read())
+    return float(m.group(1)) if m else None
+
+
+# --------------------------------------------------------------- clocks ----
+_REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+            0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x1: "gpu_idle",
+            0x2: "applications_clocks_setting", 0x10: "sync_boost", 0x100: "display_clock"}
+
+
+class ClockSampler:
+    """Samples SM clock, power and clock-event reasons through NVML from a
+    background thread while the timed region runs."""
+
+    def __init__(self, torch_device, period_s=0.005):
+        self.period = period_s
+        self.samples = []
+        self.reasons = set()
+        self.max_mhz = None
+        self.h = None
+        try:
+            import pynvml as N
+            import torch
+            N.nvmlInit()
+            pr = torch.cuda.get_device_properties(torch_device)
+            bus = f"{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0"
+            self.h = N.nvmlDeviceGetHandleByPciBusId_v2(bus)
+            self.N = N
+            self.max_mhz = N.nvmlDeviceGetMaxClockInfo(self.h, N.NVML_CLOCK_SM)
+        except Exception as e:  # NVML missing: report no clocks rather than fail
+            self.err = repr(e)
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        N = self.N
+        while not self._stop.is_set():
+            try:
+                self.samples.append(N.nvmlDeviceGetClockInfo(self.h, N.NVML_CLOCK_SM))
+                bits = N.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for b, name in _REASONS.items():
+                    if bits & b and name != "gpu_idle":
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.h is not None:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        if self._t is not None:
+            self._stop.set()
+            self._t.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                    "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ------------------------------------------------------------ distributed --
+class Ctx:
+    def __init__(self, args):
+        import torch
+        self.torch = torch
+        self.rank = env_int("RANK", 0)
+        self.world = env_int("WORLD_SIZE", 1)
+        self.local = env_int("LOCAL_RANK", 0)
+        self.args = args
+        self.dist = None
+        if args.impl == "ours":
+            torch.cuda.set_device(self.local)
+            self.device = torch.device("cuda", self.local)
+            if self.world > 1:
+                import torch.distributed as dist
+                dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                        device_id=self.device)
+                self.dist = dist
+
+    def barrier(self):
+        if self.dist is not None:
+            self.dist.barrier()
+        self.torch.cuda.synchronize(self.device)
+
+    def max_over_ranks(self, v: float) -> float:
+        if self.dist is None:
+            return v
+        t = self.torch.tensor([v], dtype=self.torch.float64, device=self.device)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum_over_ranks(self, v: float) -> float:
+        if self.dist is None:
+            return v
+        t = self.torch.tensor([v], dtype=self.torch.float64, device=self.device)
+        self.dist.all_reduce(t)
+        return float(t.item())
+
+    def close(self):
+        if self.dist is not None:
+            self.dist.barrier()
+            self.dist.destroy_process_group()
+
+
+def timed(ctx, fn, steps, stream):
+    """Runs fn() `steps` times between a barrier+sync and CUDA events on
+    `stream`; returns (max-over-ranks seconds, clock summary)."""
+    torch = ctx.torch
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    ctx.barrier()
+    with ClockSampler(ctx.device) as clk:
+        start.record(stream)
+        for _ in range(steps):
+            fn()
+        end.record(stream)
+        torch.cuda.synchronize(ctx.device)
+    secs = start.elapsed_time(end) / 1e3
+    ctx.barrier()
+    return ctx.max_over_ranks(secs), clk.summary()
+
+
+# ------------------------------------------------------------- workloads --
+class Laplacian:
+    """Config 2: x <- A x on the 5-point Laplacian of a g x g grid, fp64."""
+
+    kernel = "spmv_tiles"
+    dtype = "f64"
+
+    def __init__(self, ctx):
+        import ctypes as C
+
+        import torch
+
+        import jlust_b200 as J
+        from jlust_b200 import _lib, synth
+        from jlust_b200 import dist as D
+
+        self.ctx, self.J, self.C, self._lib = ctx, J, C, _lib
+        g = ctx.args.grid
+        self.g, self.n = g, g * g
+        r0, r1 = D.partition_rows(self.n, ctx.world, ctx.rank, align=g)
+        self.r0, self.r1, self.R = r0, r1, r1 - r0
+        rp, ci, val = synth.laplacian_rows(g, r0, r1)
+        lci = (ci.astype(np.int64) - (r0 - g)).astype(np.int32)
+        self.nnz_local = int(rp[-1])
+        self.nnz_total = 5 * self.n - 4 * g
+        dev = ctx.device
+        self.rowptr = torch.from_numpy(rp).to(dev)
+        self.colind = torch.from_numpy(lci).to(dev)
+        self.val = torch.from_numpy(val).to(dev)
+        self.A = J.csr_tensor(self.rowptr, self.colind, self.val, (self.R, self.R + 2 * g), origin=0)
+        self.x0 = np.random.default_rng(1).uniform(-1.0, 1.0, size=self.n)
+        interior = D.interior_rows(rp, lci, self.R, g) if ctx.world > 1 else (0, self.R)
+        self.halo = D.HaloSpMV(self.R, g, self._spmv_rows, dev, mode=ctx.args.exchange,
+                               interior=interior)
+        self.launches_per_step = sum(1 for a, b in ((0, interior[0]), interior, (interior[1], self.R))
+                                     if b > a) if ctx.world > 1 and ctx.args.exchange == "halo" else 1
+        self.reset()
+
+    def reset(self):
+        import torch
+        g, r0, r1 = self.g, self.r0, self.r1
+        buf = np.zeros(self.R + 2 * g)
+        lo, hi = max(r0 - g, 0), min(r1 + g, self.n)
+        buf[lo - (r0 - g):hi - (r0 - g)] = self.x0[lo:hi]
+        self.halo.cur = 0
+        self.halo.bufs[0].copy_(torch.from_numpy(buf))
+        self.halo.bufs[1].zero_()
+
+    def _spmv_rows(self, lo, hi, x, y):
+        """Rows [lo, hi) through the C ABI (row-range view of the local CSR)."""
+        C = self.C
+        st = C.c_void_p(self.ctx.torch.cuda.current_stream(self.ctx.device).cuda_stream)
+        self._lib.call("jlb_csr_spmv", st, self._lib.F64, 0, hi - lo, self.R + 2 * self.g,
+                       self.nnz_local, C.c_void_p(self.rowptr.data_ptr() + 4 * lo),
+                       C.c_void_p(self.colind.data_ptr()), C.c_void_p(self.val.data_ptr()),
+                       C.c_void_p(x.data_ptr()), C.c_void_p(y.data_ptr() + 8 * (self.g + lo)),
+                       1.0, 0.0)
+
+    def step(self):
+        self.halo.step()
+
+    # algorithmic work, whole job, per step (bench_suitesparse.jl:170-172 form)
+    def flops(self):
+        return 2.0 * self.nnz_total
+
+    def bytes(self):
+        return 12.0 * self.nnz_total + 4.0 * (self.n + 1) + 8.0 * (2 * self.n)
+
+    def config(self):
+        return {"workload": f"cfg2: CSR SpMV fp64, 2D 5-point Laplacian {self.g}x{self.g} "
+                            f"(n={self.n}, nnz={self.nnz_total}), x <- A x per step",
+                "n": self.n, "nnz": self.nnz_total, "partition": f"rows/{self.ctx.world}",
+                "exchange": "none" if self.ctx.world == 1 else self.ctx.args.exchange,
+                "l2": "inputs larger than L2 (1.34 GB per iteration), no flush"}
+
+    # end to end through the public API: x from pinned host memory, y back to it
+    def e2e_setup(self):
+        import torch
+        self.hx = [torch.from_numpy(self.x0[self.r0:self.r1].copy()).pin_memory(),
+                   torch.empty(self.R, dtype=torch.float64).pin_memory()]
+        self.hcur = 0
+        self.h2d = 8 * self.n
+        self.d2h = 8 * self.n
+
+    def e2e_step(self):
+        J, h, g, R = self.J, self.halo, self.g, self.R
+        x, y = h.bufs[h.cur], h.bufs[1 - h.cur]
+        x[g:g + R].copy_(self.hx[self.hcur], non_blocking=True)
+        if self.ctx.world > 1:
+            if h.mode == "allgather":
+                h._allgather(x)
+            else:
+                for r in h._exchange(x):
+                    r.wait()
+        J.execute(J.SpMVOp, self.A, x, y[g:g + R])
+        self.hx[1 - self.hcur].copy_(y[g:g + R], non_blocking=True)
+        h.cur = 1 - h.cur
+        self.hcur = 1 - self.hcur
+
+    # CPU restatement of the reference's path on this host's cores
+    def cpu_setup(self):
+        from jlust_b200 import synth
+        self.crp, self.cci, self.cval = synth.laplacian_2d(self.g)
+        self.cx = self.x0.copy()
+
+    def cpu_step(self):
+        from oracle import oracle as O
+        self.cx = O.spmv(self.crp, self.cci, self.cval, self.cx)
+
+    def cpu_sample(self):
+        return f"full iterations x <- A x of the {self.g}^2 Laplacian (fp64, oracle row order)"
+
+
+WORKLOADS = {"laplacian": Laplacian}
+
+
+# ------------------------------------------------------------------- arms --
+def cpu_time(step, flops_per_step, min_steps=2, max_steps=20, budget_s=20.0):
+    """Times `step` on the host: one untimed call, then up to max_steps calls
+    or budget_s seconds.  Returns (GFLOP/s, steps timed)."""
+    step()
+    t0 = time.perf_counter()
+    k = 0
+    while k < min_steps or (k < max_steps and time.perf_counter() - t0 < budget_s):
+        step()
+        k += 1
+    dt = time.perf_counter() - t0
+    return flops_per_step * k / dt / 1e9, k
+
+
+def run_ours(args):
+    ctx = Ctx(args)
+    torch = ctx.torch
+    import jlust_b200 as J
+    W = WORKLOADS[args.workload](ctx)
+    stream = torch.cuda.current_stream(ctx.device)
+    for _ in range(args.warmup):
+        W.step()
+    J.device_status()
+    W.reset()
+    secs, clocks = timed(ctx, W.step, args.steps, stream)
+    J.device_status()
+    K = args.steps
+    value = W.flops() * K / secs / 1e9
+    eff_gbs = W.bytes() * K / secs / 1e9
+    pk = peaks()
+    per_launch_s = secs / K
+    achieved = (W.bytes() / ctx.world) / per_launch_s / 1e9
+    traffic = profile_traffic(f"{W.kernel}_{args.workload}")
+    roof = {"bound": "hbm", "kernel": W.kernel, "achieved": round(achieved, 1),
+            "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
+            "traffic": traffic, "peak_source": pk["source"] + " (hbm_gbs, copy burst)",
+            "algorithmic_bytes_per_launch": W.bytes() / ctx.world}
+    if ctx.world > 1:
+        roof["note"] = "per-rank bytes over the whole step, halo exchange included"
+
+    e2e = None
+    if not args.no_e2e:
+        W.reset()
+        W.e2e_setup()
+        for _ in range(2):
+            W.e2e_step()
+        J.device_status()
+        e_secs, _ = timed(ctx, W.e2e_step, K, stream)
+        J.device_status()
+        e2e = {"value": round(W.flops() * K / e_secs / 1e9, 3), "unit": "GFLOP/s",
+               "h2d_bytes_per_step": W.h2d, "d2h_bytes_per_step": W.d2h,
+               "ms_per_step": round(e_secs * 1e3 / K, 4), "api": "jlust_b200.execute(SpMVOp, ...)"}
+
+    cpu = None
+    if ctx.rank == 0 and ctx.world == 1 and not args.no_cpu:
+        from oracle import oracle as O
+        W.cpu_setup()
+        v, k = cpu_time(W.cpu_step, W.flops())
+        cpu = {"value": round(v, 3), "unit": "GFLOP/s", "cores": O.max_threads(), "kind": "port",
+               "sample": f"{k} {W.cpu_sample()}"}
+
+    launches = int(ctx.sum_over_ranks(W.launches_per_step * K))
+    line = {"metric": METRIC, "value": round(value, 3), "unit": "GFLOP/s", "n_gpus": ctx.world,
+            "steps": K, "warmup": args.warmup, "ms_per_step": round(secs * 1e3 / K, 5),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": W.dtype, "data": "synthetic (numpy PCG64, seeds of the configs)",
+            "config": W.config(), "effective_gbs": round(eff_gbs, 1), "roofline": roof,
+            "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches, "clocks": clocks}
+    if ctx.rank == 0:
+        print(json.dumps(line), flush=True)
+    ctx.close()
+
+
+def run_reference(args):
+    """The reference's path on the host cores: the CPU restatement (the
+    reference is Julia; no Julia toolchain exists on this box)."""
+    if env_int("RANK", 0) != 0:
+        return
+    from jlust_b200 import synth
+    from oracle import oracle as O
+    if args.workload != "laplacian":
+        print(json.dumps({"impl": "reference", "unavailable":
+                          "reference arm implemented for the default workload only"}))
+        return
+    g = args.grid
+    n = g * g
+    rp, ci, val = synth.laplacian_2d(g)
+    nnz = int(rp[-1])
+    x = np.random.default_rng(1).uniform(-1.0, 1.0, size=n)
+    threads = O.max_threads()
+    state = {"x": x}
+
+    def step():
+        state["x"] = O.spmv(rp, ci, val, state["x"])
+
+    t0 = time.perf_counter()
+    step()
+    one = time.perf_counter() - t0
+    for _ in range(max(args.warmup - 1, 0)):
+        step()
+    # bounded sample: full iterations while K of them fit in ~3 minutes
+    K = args.steps
+    frac = min(1.0, 180.0 / max(one * K, 1e-9))
+    if frac < 1.0:
+        rows = max(g, int(n * frac) // g * g)
+        rp_s = rp[:rows + 1]
+
+        def step():  # noqa: F811 - row-subset sample
+            O.spmv(rp_s, ci, val, state["x"])
+        flops = 2.0 * int(rp_s[-1])
+        sample = f"rows [0, {rows}) of each iteration ({frac:.3f} of the matrix)"
+    else:
+        flops = 2.0 * nnz
+        sample = "full iterations x <- A x"
+    t0 = time.perf_counter()
+    for _ in range(K):
+        step()
+    dt = time.perf_counter() - t0
+    value = flops * K / dt / 1e9
+    line = {"metric": METRIC, "value": round(value, 3), "unit": "GFLOP/s", "n_gpus": args.gpus,
+            "steps": K, "warmup": args.warmup, "ms_per_step": round(dt * 1e3 / K, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64",
+            "data": "synthetic (numpy PCG64, seeds of the configs)", "impl": "reference",
+            "config": {"workload": f"cfg2: CSR SpMV fp64, 2D 5-point Laplacian {g}x{g} "
+                                   f"(n={n}, nnz={nnz}), x <- A x per step",
+                       "n": n, "nnz": nnz},
+            "cpu_baseline": {"value": round(value, 3), "unit": "GFLOP/s", "cores": threads,
+                             "kind": "port",
+                             "sample": f"{K} steps, {sample}; C restatement of JLUST's CPU "
+                                       "walker (oracle/oracle.c), OpenMP over rows"},
+            "e2e": {"value": round(value, 3), "unit": "GFLOP/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

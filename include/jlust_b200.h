@@ -1,0 +1,232 @@
+/*
+ * jlust_b200.h -- C ABI of libjlust_b200.so, the B200 (sm_100a) sparse-kernel
+ * backend for JLUST.
+ *
+ * The library is what a `B200Backend <: AbstractUSTBackend` Julia extension
+ * reaches with `ccall`: plain pointers, sizes and enums, no C++ or torch types.
+ * Every entry point returns an int status (JLB_OK == 0); a failing call also
+ * stores a message retrievable with jlb_last_error() on the calling thread.
+ * Nothing throws across the ABI.
+ *
+ * Ownership: all matrix / vector buffers are device memory owned by the caller
+ * (CuArray in Julia).  The library never frees or retains them beyond a call,
+ * except that a plan remembers the index buffers it was created from; the
+ * caller keeps those alive until jlb_*_plan_destroy.
+ *
+ * Streams: `stream` is a cudaStream_t passed as void* (NULL = legacy default
+ * stream).  Execute calls are asynchronous, never synchronise the host and
+ * never allocate device memory, so they can be captured into CUDA graphs.
+ * Plan creation and conversion count phases synchronise `stream`.
+ *
+ * Index origin: idx_base is 0 (ZeroBased) or 1 (OneBased), applied to every
+ * position and coordinate buffer, as JLUST's `_origin_off`
+ * (ext/KernelAbstractionsExt/ops/spmv.jl:380).
+ *
+ * Dense operands carry (order, leading dimension): order JLB_ROW_MAJOR puts
+ * element (i, j) at i*ld + j, JLB_COL_MAJOR at i + j*ld (Julia's native
+ * layout, ext/CUDAExt/ops/spmm.jl:1-4).
+ */
+#ifndef JLUST_B200_H
+#define JLUST_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define JLB_API __attribute__((visibility("default")))
+
+/* Status codes.  Codes 1-7 map one to one onto JLUST's exception types
+ * (src/errors.jl:1-9); the Julia glue rethrows them as those exceptions. */
+enum jlb_status_code {
+    JLB_OK = 0,
+    JLB_ERR_UNSUPPORTED_FORMAT = 1,     /* UnsupportedFormat      errors.jl:3 */
+    JLB_ERR_UNSUPPORTED_INDEX_TYPE = 2, /* UnsupportedIndexType   errors.jl:4 */
+    JLB_ERR_UNSUPPORTED_VALUE_TYPE = 3, /* UnsupportedValueType   errors.jl:5 */
+    JLB_ERR_INDEX_ORIGIN_MISMATCH = 4,  /* IndexOriginMismatch    errors.jl:6 */
+    JLB_ERR_DEVICE_MISMATCH = 5,        /* DeviceMismatch         errors.jl:7 */
+    JLB_ERR_INCOMPATIBLE_EXTENTS = 6,   /* IncompatibleExtents    errors.jl:8 */
+    JLB_ERR_NONCANONICAL_STORAGE = 7,   /* NonCanonicalStorage    errors.jl:9 */
+    JLB_ERR_INVALID_ARGUMENT = 8,       /* null pointer, bad enum, bad alignment */
+    JLB_ERR_CUDA = 9,                   /* a CUDA runtime / driver call failed */
+    JLB_ERR_DEVICE_TIMEOUT = 10,        /* a bounded device-side wait gave up */
+    JLB_ERR_WORKSPACE = 11              /* workspace smaller than the size query */
+};
+
+/* Value types (JLUST eltype): Float32, Float64, BFloat16. */
+enum jlb_dtype { JLB_F32 = 0, JLB_F64 = 1, JLB_BF16 = 2 };
+
+/* Dense layouts. */
+enum jlb_order { JLB_ROW_MAJOR = 0, JLB_COL_MAJOR = 1 };
+
+/* SDDMM modes. */
+enum jlb_sddmm_mode {
+    JLB_SDDMM_ADD = 0, /* out[p] = alpha*dot + beta*out[p]        (reference) */
+    JLB_SDDMM_MUL = 1  /* out[p] = (alpha*dot)*S[p] + beta*out[p] (sampled)   */
+};
+
+typedef struct jlb_spmv_plan_s *jlb_spmv_plan;
+typedef struct jlb_spmm_plan_s *jlb_spmm_plan;
+
+/* ---------------------------------------------------------------- runtime */
+
+/* Library version, major*10000 + minor*100 + patch. */
+JLB_API int jlb_version(void);
+
+/* Static description of a status code. */
+JLB_API const char *jlb_status_string(int status);
+
+/* Copies the calling thread's last error message into buf (always
+ * NUL-terminated when len > 0) and returns the last status. */
+JLB_API int jlb_last_error(char *buf, size_t len);
+
+/* Binds the calling thread to `device` and checks that it is an sm_100 part.
+ * Replaces nothing in the reference (CUDA.jl does this implicitly). */
+JLB_API int jlb_init(int device);
+
+/* Synchronises `stream`, then reads and clears the device error word that
+ * kernels set when a bounded wait gave up or a bounds check failed.  Returns
+ * JLB_OK, JLB_ERR_DEVICE_TIMEOUT or JLB_ERR_NONCANONICAL_STORAGE. */
+JLB_API int jlb_device_status(void *stream);
+
+/* ------------------------------------------------------- validation (CSR) */
+
+/* Checks the invariants JLUST's validate_storage (src/backends.jl:309-316)
+ * and the kernels rely on: rowptr[0] == idx_base, rowptr non-decreasing,
+ * rowptr[m] == nnz + idx_base, idx_base <= colind < n + idx_base and, when
+ * `require_sorted` is set, strictly increasing columns inside each row.
+ * Synchronises `stream`.  Returns JLB_ERR_NONCANONICAL_STORAGE on violation. */
+JLB_API int jlb_csr_validate(void *stream, int idx_base, int64_t m, int64_t n, int64_t nnz,
+                             const int32_t *rowptr, const int32_t *colind, int require_sorted);
+
+/* ------------------------------------------------------------------- SpMV */
+
+/* y = alpha * A * x + beta * y for an m x n CSR matrix A (dtype F32 or F64).
+ * beta == 0 never reads y.  Rows of up to 32 entries are summed in storage
+ * order with separately rounded products and sums, which reproduces JLUST's
+ * CPU walker bit for bit; longer rows use a fixed-order warp reduction.
+ * Replaces execute(::EmitterBackend, ::Op{:SpMV}) in
+ * ext/KernelAbstractionsExt/ops/spmv.jl:371-504 (walker kernels K1/K2) and
+ * the merge-based hook _csr_spmv_merge! in ext/CUDAExt/ops/spmv.jl:195-208. */
+JLB_API int jlb_csr_spmv(void *stream, int dtype, int idx_base, int64_t m, int64_t n,
+                         int64_t nnz, const int32_t *rowptr, const int32_t *colind,
+                         const void *val, const void *x, void *y, double alpha, double beta);
+
+/* Prepared SpMV: validates the structure once, records the row-length
+ * profile and picks the kernel variant.  Replaces prepare(backend, SpMVOp,
+ * u_A) (src/ops.jl:187-202; EmitterSpMVHandle, KA spmv.jl:518-531). */
+JLB_API int jlb_spmv_plan_create(jlb_spmv_plan *plan, void *stream, int dtype, int idx_base,
+                                 int64_t m, int64_t n, int64_t nnz, const int32_t *rowptr,
+                                 const int32_t *colind);
+/* execute(h, u_A, u_x, u_y; alpha, beta) (KA spmv.jl:533-544); `val` may be a
+ * new value buffer of the same structure (update_values!, src/ops.jl:204-211). */
+JLB_API int jlb_spmv_plan_execute(jlb_spmv_plan plan, void *stream, const void *val,
+                                  const void *x, void *y, double alpha, double beta);
+/* Row-length profile recorded by the plan: max and mean entries per row and
+ * the variant code used by execute (0 staged thread-per-row, 1 mixed). */
+JLB_API int jlb_spmv_plan_info(jlb_spmv_plan plan, int64_t *max_row, double *mean_row,
+                               int *variant);
+JLB_API int jlb_spmv_plan_destroy(jlb_spmv_plan plan);
+
+/* ------------------------------------------------------------------- SpMM */
+
+/* C = alpha * A * B + beta * C; A m x n CSR (F32 or F64), B n x k, C m x k,
+ * each with its own order and leading dimension.  beta == 0 never reads C.
+ * Per (row, column) the sum runs over the row's entries in storage order
+ * (bit-exact with JLUST's Tiled strategy, KA spmm.jl:272-292) for rows of up
+ * to 256 entries; longer rows are split into 16 segments combined in order.
+ * Replaces execute(::EmitterBackend, ::Op{:SpMM}) (KA spmm.jl:397-423) and
+ * the CUSPARSEBackend SpMM default (ext/CUDAExt/ops/spmm.jl:50-58). */
+JLB_API int jlb_csr_spmm(void *stream, int dtype, int idx_base, int64_t m, int64_t n,
+                         int64_t nnz, const int32_t *rowptr, const int32_t *colind,
+                         const void *val, int64_t k, const void *B, int64_t ldb, int b_order,
+                         void *C, int64_t ldc, int c_order, double alpha, double beta);
+
+/* ------------------------------------------------------------------ SDDMM */
+
+/* Sampled dense-dense product over the sparsity pattern of the m x n CSR
+ * matrix (rowptr, colind): for every stored position p = (i, j)
+ *   dot = sum_{kk < K} A(i, kk) * B(kk, j)
+ * with A m x K (order a_order, leading dim lda) and B the K x n operand
+ * (order b_order, leading dim ldb; a row-major n x K array is the K x n
+ * operand in JLB_COL_MAJOR with ldb = K).  mode JLB_SDDMM_ADD writes
+ * out[p] = alpha*dot + beta*out[p] (KA sddmm.jl:23-36); JLB_SDDMM_MUL writes
+ * out[p] = (alpha*dot)*S[p] + beta*out[p].  beta == 0 never reads out.
+ * Replaces execute(::EmitterBackend, ::Op{:SDDMM}) (KA sddmm.jl:49-65) and
+ * the CUSPARSEBackend SDDMM default (ext/CUDAExt/ops/sddmm.jl:53-62). */
+JLB_API int jlb_sddmm(void *stream, int dtype, int idx_base, int64_t m, int64_t n, int64_t nnz,
+                      const int32_t *rowptr, const int32_t *colind, int64_t K, const void *A,
+                      int64_t lda, int a_order, const void *B, int64_t ldb, int b_order,
+                      const void *S, void *out, int mode, double alpha, double beta);
+
+/* --------------------------------------------------------------- BSR SpMM */
+
+/* C = alpha * A * B + beta * C for a BSRRight((bs, bs)) matrix A with mb
+ * block rows, nb block columns and nnzb stored row-major bs x bs blocks of
+ * bf16 values; B is (nb*bs) x N bf16 row-major (leading dim ldb), C is
+ * (mb*bs) x N fp32 row-major (leading dim ldc); fp32 accumulation.
+ * bs == 64 with N a multiple of 128 (N <= 512), ldb a multiple of 8 and
+ * 16-byte aligned B and values runs on tcgen05 tensor cores (TMA-fed shared
+ * memory tiles, accumulators in TMEM); other shapes run a SIMT kernel.
+ * Replaces execute(BlockSpMMOp, ...) (src/block_sparse.jl:284-302; fused CPU
+ * loop :177-188) for BSR-structured block matrices, which the reference
+ * cannot run on the GPU (no BSR path in ext/CUDAExt/CUDAExt.jl:253-290). */
+JLB_API int jlb_bsr_spmm(void *stream, int idx_base, int64_t mb, int64_t nb, int64_t nnzb,
+                         int bs, const int32_t *browptr, const int32_t *bcolind,
+                         const void *bval, int64_t N, const void *B, int64_t ldb, float *C,
+                         int64_t ldc, double alpha, double beta);
+
+/* ------------------------------------------------ conversion and scans */
+
+/* Exclusive scan of n int32 counts into n+1 positions, out[0] = idx_base
+ * (the composer's position buffer, src/convert.jl:154-168).  `workspace`
+ * holds at least jlb_scan_workspace_size(n) bytes of device memory.  `out`
+ * may alias `counts` shifted by one (in-place scan of a row pointer whose
+ * entries 1..n hold counts).  Overflow of int32 sets the device error word. */
+JLB_API size_t jlb_scan_workspace_size(int64_t n);
+JLB_API int jlb_exclusive_scan_i32(void *stream, int64_t n, const int32_t *counts, int32_t *out,
+                                   int idx_base, void *workspace, size_t workspace_bytes);
+
+/* CSR -> BSRRight((b1, b2)) on the GPU, bit-exact with JLUST's convert_format
+ * (src/convert.jl:302-388) using the block-row level extent ceil(m/b1):
+ * explicit zeros dropped, block columns ascending, b1 x b2 row-major tiles
+ * zero-filled where no entry lands, output origin = input origin.
+ * Phase 1 (count) fills browptr (ceil(m/b1)+1 entries) and returns nnzb in
+ * *nnzb (synchronises `stream`); the caller allocates bcolind (nnzb) and bval
+ * (nnzb*b1*b2 values of dtype); phase 2 (fill) writes them.  `workspace`
+ * holds jlb_to_bsr_workspace_size(...) bytes for both phases.
+ * Replaces convert_format(u, Formats.BSRRight((b1,b2))) for CSR sources and
+ * cuSPARSE csr2bsr (supports_convert, ext/CUDAExt/CUDAExt.jl:330-339). */
+JLB_API size_t jlb_csr_to_bsr_workspace_size(int64_t m, int64_t n, int64_t nnz, int b1, int b2);
+JLB_API int jlb_csr_to_bsr_count(void *stream, int dtype, int idx_base, int64_t m, int64_t n,
+                                 int64_t nnz, const int32_t *rowptr, const int32_t *colind,
+                                 const void *val, int b1, int b2, int32_t *browptr,
+                                 int64_t *nnzb, void *workspace, size_t workspace_bytes);
+JLB_API int jlb_csr_to_bsr_fill(void *stream, int dtype, int idx_base, int64_t m, int64_t n,
+                                int64_t nnz, const int32_t *rowptr, const int32_t *colind,
+                                const void *val, int b1, int b2, const int32_t *browptr,
+                                int64_t nnzb, int32_t *bcolind, void *bval, void *workspace,
+                                size_t workspace_bytes);
+
+/* COO -> BSRRight((b1, b2)); entries in any order, duplicates allowed: the
+ * nonzero entry with the lowest storage index wins a cell, as the composer's
+ * stable sort keeps the first value of a run (src/convert.jl:222,231-238). */
+JLB_API size_t jlb_coo_to_bsr_workspace_size(int64_t m, int64_t n, int64_t nnz, int b1, int b2,
+                                             int64_t nnzb);
+JLB_API int jlb_coo_to_bsr_count(void *stream, int dtype, int idx_base, int64_t m, int64_t n,
+                                 int64_t nnz, const int32_t *rows, const int32_t *cols,
+                                 const void *val, int b1, int b2, int32_t *browptr,
+                                 int64_t *nnzb, void *workspace, size_t workspace_bytes);
+JLB_API int jlb_coo_to_bsr_fill(void *stream, int dtype, int idx_base, int64_t m, int64_t n,
+                                int64_t nnz, const int32_t *rows, const int32_t *cols,
+                                const void *val, int b1, int b2, const int32_t *browptr,
+                                int64_t nnzb, int32_t *bcolind, void *bval, void *workspace,
+                                size_t workspace_bytes);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* JLUST_B200_H */

@@ -1,0 +1,107 @@
+// common.cuh -- helpers shared by the translation units of libjlust_b200.so.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+#include <stdarg.h>
+
+#include "../../include/jlust_b200.h"
+
+namespace jlb {
+
+// ---------------------------------------------------------------- host errors
+// Records `status` and a formatted message as the calling thread's last error
+// (implemented in api.cu) and returns `status`, so call sites can write
+// `return fail(JLB_ERR_..., "...")`.
+int fail(int status, const char *fmt, ...) __attribute__((format(printf, 2, 3)));
+int ok();  // clears the thread's last error, returns JLB_OK
+
+// Checks a CUDA runtime result; on failure records JLB_ERR_CUDA with the
+// CUDA error string and the call site.
+int cuda_check(cudaError_t e, const char *what);
+
+#define JLB_CUDA(call)                                              \
+    do {                                                            \
+        cudaError_t _e = (call);                                    \
+        if (_e != cudaSuccess) return ::jlb::cuda_check(_e, #call); \
+    } while (0)
+
+#define JLB_LAUNCH_CHECK(what)                                       \
+    do {                                                             \
+        cudaError_t _e = cudaGetLastError();                         \
+        if (_e != cudaSuccess) return ::jlb::cuda_check(_e, what);   \
+    } while (0)
+
+inline cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline size_t dtype_size(int dtype) {
+    return dtype == JLB_F64 ? 8 : dtype == JLB_F32 ? 4 : dtype == JLB_BF16 ? 2 : 0;
+}
+
+inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ------------------------------------------------------------ device errors
+// Kernels report a bounded wait that gave up, or a bounds check that failed,
+// by OR-ing a bit into a per-translation-unit device word.  The host reads and
+// clears every unit's word in jlb_device_status().
+enum DevErr : int {
+    DEV_ERR_TIMEOUT = 1,      // an mbarrier / flag wait exceeded its limit
+    DEV_ERR_BOUNDS = 2,       // an index outside the declared extents
+    DEV_ERR_OVERFLOW = 4,     // an int32 position buffer overflowed
+};
+
+// Per-unit accessors, defined once per .cu file by JLB_DEFINE_DEV_ERROR.
+int take_dev_error_spmv();
+int take_dev_error_spmm();
+int take_dev_error_sddmm();
+int take_dev_error_bsr();
+int take_dev_error_convert();
+
+#define JLB_DEFINE_DEV_ERROR(unit)                                           \
+    static __device__ int g_dev_error;                                       \
+    __device__ __forceinline__ void dev_error(int bit) {                     \
+        atomicOr(&g_dev_error, bit);                                         \
+    }                                                                        \
+    int take_dev_error_##unit() {                                            \
+        int v = 0;                                                           \
+        if (cudaMemcpyFromSymbol(&v, g_dev_error, sizeof(int)) != cudaSuccess) \
+            return -1;                                                       \
+        if (v) {                                                             \
+            int z = 0;                                                       \
+            if (cudaMemcpyToSymbol(g_dev_error, &z, sizeof(int)) != cudaSuccess) \
+                return -1;                                                   \
+        }                                                                    \
+        return v;                                                            \
+    }
+
+// ------------------------------------------------------ exact arithmetic ops
+// Separately rounded multiply and add.  nvcc contracts a*b + c into an FMA
+// unless told otherwise; these intrinsics are never contracted, which keeps
+// the kernels bit-identical to the reference's uncontracted sums.
+__device__ __forceinline__ double mul_rn(double a, double b) { return __dmul_rn(a, b); }
+__device__ __forceinline__ double add_rn(double a, double b) { return __dadd_rn(a, b); }
+__device__ __forceinline__ float mul_rn(float a, float b) { return __fmul_rn(a, b); }
+__device__ __forceinline__ float add_rn(float a, float b) { return __fadd_rn(a, b); }
+
+template <typename T>
+__device__ __forceinline__ T ldg(const T *p) { return __ldg(p); }
+
+__device__ __forceinline__ float bf16_bits_to_f32(uint16_t h) {
+    return __uint_as_float(((uint32_t)h) << 16);
+}
+
+// Warp sum with a fixed xor-butterfly order (deterministic for a given
+// assignment of values to lanes).
+template <typename T>
+__device__ __forceinline__ T warp_sum(T v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = add_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+constexpr int kWarp = 32;
+
+__host__ __device__ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+}  // namespace jlb

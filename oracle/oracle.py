@@ -1,0 +1,290 @@
+"""numpy front end of the C restatement in oracle.c.
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, by __graft_entry__.smoke() and by
+bench.py's CPU-baseline leg, always as the checker or as the timed CPU
+baseline, never by the product package.  See oracle.c for the reference
+semantics (file:line in the JLUST project) that each routine follows.
+
+Dense operands are numpy 2-D arrays in either C order (row-major) or Fortran
+order (column-major); their layout is passed to C as (order, leading dim).
+bf16 arrays are numpy uint16 arrays holding the bf16 bit patterns.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_SO = os.path.join(_HERE, "_build", "liboracle.so")
+
+F32, F64, BF16 = 0, 1, 2
+
+_lib = None
+
+
+def build() -> str:
+    """Compile oracle.c with oracle/Makefile (idempotent) and return the .so path."""
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return _SO
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_SO) or os.path.getmtime(_SO) < os.path.getmtime(
+                os.path.join(_HERE, "oracle.c")):
+            build()
+        _lib = C.CDLL(_SO)
+        _declare(_lib)
+    return _lib
+
+
+_p = C.c_void_p
+_i64 = C.c_int64
+_i = C.c_int
+_d = C.c_double
+
+
+def _declare(L):
+    L.or_max_threads.restype = _i
+    L.or_set_threads.argtypes = [_i]
+    for n in ("or_csr_spmv_f64", "or_csr_spmv_f32"):
+        getattr(L, n).argtypes = [_i64, _p, _p, _p, _p, _p, _d, _d, _i]
+    L.or_csr_spmv_ref64.argtypes = [_i, _i64, _p, _p, _p, _p, _p, _p, _p, _d, _d, _i]
+    for n in ("or_csr_spmm_f32", "or_csr_spmm_f64"):
+        getattr(L, n).argtypes = [_i64, _i64, _p, _p, _p, _p, _i64, _i, _p, _i64, _i, _d, _d, _i]
+    L.or_csr_spmm_ref64_f32.argtypes = [_i64, _i64, _p, _p, _p, _p, _i64, _i, _p, _i64, _i,
+                                        _p, _p, _d, _d, _i]
+    for n in ("or_sddmm_f32", "or_sddmm_f64"):
+        getattr(L, n).argtypes = [_i64, _i64, _p, _p, _p, _i64, _i, _p, _i64, _i, _p, _p,
+                                  _i, _d, _d, _i]
+    L.or_sddmm_ref64_f32.argtypes = [_i64, _i64, _p, _p, _p, _i64, _i, _p, _i64, _i, _p, _p,
+                                     _p, _p, _i, _d, _d, _i]
+    L.or_bsr_spmm_bf16.argtypes = [_i64, _i64, _i, _i, _p, _p, _p, _p, _i64, _p, _i64,
+                                   _d, _d, _i]
+    L.or_bsr_spmm_ref64_bf16.argtypes = [_i64, _i64, _i, _i, _p, _p, _p, _p, _i64, _p, _i64,
+                                         _p, _p, _d, _d, _i]
+    L.or_exclusive_scan_i32.argtypes = [_i64, _p, _p, _i]
+    L.or_exclusive_scan_i32.restype = _i64
+    L.or_csr_to_bsr.argtypes = [_i64, _i64, _i, _i, _p, _p, _p, _i, _i, _p, _p, _p]
+    L.or_csr_to_bsr.restype = _i64
+    L.or_coo_to_bsr.argtypes = [_i64, _i64, _i64, _i, _i, _p, _p, _p, _i, _i, _p, _p, _p]
+    L.or_coo_to_bsr.restype = _i64
+
+
+def _ptr(a):
+    return None if a is None else a.ctypes.data
+
+
+def _c(a, dtype=None):
+    a = np.asarray(a)
+    if dtype is not None and a.dtype != dtype:
+        a = a.astype(dtype)
+    return np.ascontiguousarray(a)
+
+
+def _layout(a):
+    """(order, ld) of a 2-D numpy array: order 0 row-major, 1 column-major."""
+    if a.flags.c_contiguous:
+        return 0, (a.shape[1] if a.shape[1] > 0 else 1)
+    if a.flags.f_contiguous:
+        return 1, (a.shape[0] if a.shape[0] > 0 else 1)
+    raise ValueError("dense operand must be C- or Fortran-contiguous")
+
+
+def dtype_code(dt) -> int:
+    dt = np.dtype(dt)
+    if dt == np.float64:
+        return F64
+    if dt == np.float32:
+        return F32
+    if dt == np.uint16:
+        return BF16
+    raise TypeError(f"oracle: unsupported value type {dt}")
+
+
+def set_threads(n: int) -> None:
+    lib().or_set_threads(int(n))
+
+
+def max_threads() -> int:
+    return int(lib().or_max_threads())
+
+
+# ---------------------------------------------------------------- SpMV -------
+def spmv(rowptr, colind, val, x, y=None, alpha=1.0, beta=0.0, base=0):
+    """y = alpha*A*x + beta*y in the reference's row order and value type."""
+    rowptr, colind = _c(rowptr, np.int32), _c(colind, np.int32)
+    val = _c(val)
+    x = _c(x, val.dtype)
+    m = rowptr.shape[0] - 1
+    y = np.zeros(m, val.dtype) if y is None else _c(y, val.dtype).copy()
+    fn = {np.dtype(np.float64): lib().or_csr_spmv_f64,
+          np.dtype(np.float32): lib().or_csr_spmv_f32}[val.dtype]
+    fn(m, _ptr(rowptr), _ptr(colind), _ptr(val), _ptr(x), _ptr(y), alpha, beta, base)
+    return y
+
+
+def spmv_ref64(rowptr, colind, val, x, y=None, alpha=1.0, beta=0.0, base=0):
+    """fp64 y and the per-row bound |alpha|*sum|v*x| + |beta*y|."""
+    rowptr, colind = _c(rowptr, np.int32), _c(colind, np.int32)
+    val = _c(val)
+    x = _c(x, val.dtype)
+    m = rowptr.shape[0] - 1
+    yin = None if y is None else _c(y, val.dtype)
+    out = np.empty(m, np.float64)
+    bound = np.empty(m, np.float64)
+    lib().or_csr_spmv_ref64(dtype_code(val.dtype), m, _ptr(rowptr), _ptr(colind), _ptr(val),
+                            _ptr(x), _ptr(yin), _ptr(out), _ptr(bound), alpha, beta, base)
+    return out, bound
+
+
+# ---------------------------------------------------------------- SpMM -------
+def spmm(rowptr, colind, val, B, C=None, alpha=1.0, beta=0.0, base=0, c_order=0):
+    """C = alpha*A*B + beta*C (Tiled per-(row,col) order).  B keeps its layout;
+    C is returned in `c_order` (0 row-major, 1 column-major) unless given."""
+    rowptr, colind = _c(rowptr, np.int32), _c(colind, np.int32)
+    val = _c(val)
+    B = np.asarray(B)
+    assert B.dtype == val.dtype
+    m, k = rowptr.shape[0] - 1, B.shape[1]
+    if C is None:
+        C = np.zeros((m, k), val.dtype, order="C" if c_order == 0 else "F")
+    else:
+        C = C.copy(order="K")
+    bo, ldb = _layout(B)
+    co, ldc = _layout(C)
+    fn = {np.dtype(np.float32): lib().or_csr_spmm_f32,
+          np.dtype(np.float64): lib().or_csr_spmm_f64}[val.dtype]
+    fn(m, k, _ptr(rowptr), _ptr(colind), _ptr(val), _ptr(B), ldb, bo, _ptr(C), ldc, co,
+       alpha, beta, base)
+    return C
+
+
+def spmm_ref64(rowptr, colind, val, B, C=None, alpha=1.0, beta=0.0, base=0):
+    """fp64 C (row-major) and bound, fp32 inputs."""
+    rowptr, colind = _c(rowptr, np.int32), _c(colind, np.int32)
+    val = _c(val, np.float32)
+    B = np.asarray(B)
+    m, k = rowptr.shape[0] - 1, B.shape[1]
+    bo, ldb = _layout(B)
+    if C is not None:
+        co, ldc = _layout(C)
+    else:
+        co, ldc = 0, max(k, 1)
+    out = np.empty((m, k), np.float64)
+    bound = np.empty((m, k), np.float64)
+    lib().or_csr_spmm_ref64_f32(m, k, _ptr(rowptr), _ptr(colind), _ptr(val), _ptr(B), ldb, bo,
+                                _ptr(C), ldc, co, _ptr(out), _ptr(bound), alpha, beta, base)
+    return out, bound
+
+
+# ---------------------------------------------------------------- SDDMM ------
+def sddmm(rowptr, colind, A, B_kn, out, S=None, mode=0, alpha=1.0, beta=0.0, base=0):
+    """Sampled product over the CSR pattern.  A is m x K, B_kn is the logical
+    K x n operand (a row-major n x K array enters as its transpose view).
+    mode 0: out = alpha*dot + beta*out;  mode 1: out = (alpha*dot)*S + beta*out."""
+    rowptr, colind = _c(rowptr, np.int32), _c(colind, np.int32)
+    A, B_kn = np.asarray(A), np.asarray(B_kn)
+    out = _c(out, A.dtype).copy()
+    S = None if S is None else _c(S, A.dtype)
+    m, K = rowptr.shape[0] - 1, A.shape[1]
+    ao, lda = _layout(A)
+    bo, ldb = _layout(B_kn)
+    fn = {np.dtype(np.float32): lib().or_sddmm_f32,
+          np.dtype(np.float64): lib().or_sddmm_f64}[A.dtype]
+    fn(m, K, _ptr(rowptr), _ptr(colind), _ptr(A), lda, ao, _ptr(B_kn), ldb, bo, _ptr(S),
+       _ptr(out), mode, alpha, beta, base)
+    return out
+
+
+def sddmm_ref64(rowptr, colind, A, B_kn, out_in=None, S=None, mode=0, alpha=1.0, beta=0.0,
+                base=0):
+    rowptr, colind = _c(rowptr, np.int32), _c(colind, np.int32)
+    A, B_kn = np.asarray(A), np.asarray(B_kn)
+    m, K = rowptr.shape[0] - 1, A.shape[1]
+    nnz = colind.shape[0]
+    ao, lda = _layout(A)
+    bo, ldb = _layout(B_kn)
+    S = None if S is None else _c(S, np.float32)
+    out_in = None if out_in is None else _c(out_in, np.float32)
+    out = np.empty(nnz, np.float64)
+    bound = np.empty(nnz, np.float64)
+    lib().or_sddmm_ref64_f32(m, K, _ptr(rowptr), _ptr(colind), _ptr(A), lda, ao, _ptr(B_kn),
+                             ldb, bo, _ptr(S), _ptr(out_in), _ptr(out), _ptr(bound), mode,
+                             alpha, beta, base)
+    return out, bound
+
+
+# ---------------------------------------------------------------- BSR SpMM ---
+def bsr_spmm(browptr, bcolind, bval_u16, X_u16, b1=64, b2=64, Y=None, alpha=1.0, beta=0.0,
+             base=0):
+    """fp32 Y = alpha*A*X + beta*Y for a BSRRight matrix with bf16 values/X."""
+    browptr, bcolind = _c(browptr, np.int32), _c(bcolind, np.int32)
+    bval = _c(bval_u16, np.uint16)
+    X = _c(X_u16, np.uint16)
+    mb, N = browptr.shape[0] - 1, X.shape[1]
+    Y = np.zeros((mb * b1, N), np.float32) if Y is None else _c(Y, np.float32).copy()
+    lib().or_bsr_spmm_bf16(mb, N, b1, b2, _ptr(browptr), _ptr(bcolind), _ptr(bval), _ptr(X),
+                           N, _ptr(Y), N, alpha, beta, base)
+    return Y
+
+
+def bsr_spmm_ref64(browptr, bcolind, bval_u16, X_u16, b1=64, b2=64, Y=None, alpha=1.0,
+                   beta=0.0, base=0):
+    browptr, bcolind = _c(browptr, np.int32), _c(bcolind, np.int32)
+    bval = _c(bval_u16, np.uint16)
+    X = _c(X_u16, np.uint16)
+    mb, N = browptr.shape[0] - 1, X.shape[1]
+    Yin = None if Y is None else _c(Y, np.float32)
+    out = np.empty((mb * b1, N), np.float64)
+    bound = np.empty((mb * b1, N), np.float64)
+    lib().or_bsr_spmm_ref64_bf16(mb, N, b1, b2, _ptr(browptr), _ptr(bcolind), _ptr(bval),
+                                 _ptr(X), N, _ptr(Yin), N, _ptr(out), _ptr(bound), alpha, beta,
+                                 base)
+    return out, bound
+
+
+# ---------------------------------------------------------------- scans ------
+def exclusive_scan(counts, base=0):
+    counts = _c(counts, np.int32)
+    out = np.empty(counts.shape[0] + 1, np.int32)
+    tot = lib().or_exclusive_scan_i32(counts.shape[0], _ptr(counts), _ptr(out), base)
+    if tot < 0:
+        raise OverflowError("exclusive_scan: running total exceeds int32")
+    return out
+
+
+# ---------------------------------------------------------------- conversion -
+def _bsr_alloc(mb, nnzb, b1, b2, dt):
+    return (np.empty(mb + 1, np.int32), np.empty(max(nnzb, 0), np.int32),
+            np.empty(max(nnzb, 0) * b1 * b2, dt))
+
+
+def csr_to_bsr(m, n, rowptr, colind, val, b1, b2, base=0):
+    """(browptr, bcolind, bval) of BSRRight((b1,b2)) with ceil(m/b1) block rows."""
+    rowptr, colind, val = _c(rowptr, np.int32), _c(colind, np.int32), _c(val)
+    dt = dtype_code(val.dtype)
+    nnzb = lib().or_csr_to_bsr(m, n, b1, b2, _ptr(rowptr), _ptr(colind), _ptr(val), dt, base,
+                               None, None, None)
+    mb = (m + b1 - 1) // b1
+    bp, bc, bv = _bsr_alloc(mb, nnzb, b1, b2, val.dtype)
+    lib().or_csr_to_bsr(m, n, b1, b2, _ptr(rowptr), _ptr(colind), _ptr(val), dt, base,
+                        _ptr(bp), _ptr(bc), _ptr(bv))
+    return bp, bc, bv
+
+
+def coo_to_bsr(m, n, rows, cols, val, b1, b2, base=0):
+    rows, cols, val = _c(rows, np.int32), _c(cols, np.int32), _c(val)
+    dt = dtype_code(val.dtype)
+    nnz = rows.shape[0]
+    nnzb = lib().or_coo_to_bsr(m, n, nnz, b1, b2, _ptr(rows), _ptr(cols), _ptr(val), dt, base,
+                               None, None, None)
+    mb = (m + b1 - 1) // b1
+    bp, bc, bv = _bsr_alloc(mb, nnzb, b1, b2, val.dtype)
+    lib().or_coo_to_bsr(m, n, nnz, b1, b2, _ptr(rows), _ptr(cols), _ptr(val), dt, base,
+                        _ptr(bp), _ptr(bc), _ptr(bv))
+    return bp, bc, bv

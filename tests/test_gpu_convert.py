@@ -1,0 +1,116 @@
+"""GPU CSR/COO -> BSR conversion and position scans: bit-exact against the
+CPU composer restatement (indices, patterns and values)."""
+import numpy as np
+import pytest
+import torch
+
+import jlust_b200 as J
+from jlust_b200 import synth
+from oracle import oracle as O
+from _helpers import DEV, bf16_dev, random_csr, to_dev
+
+pytestmark = pytest.mark.gpu
+
+
+def _host(t):
+    t = t.cpu()
+    if t.dtype == torch.bfloat16:
+        return t.view(torch.int16).numpy().view(np.uint16)
+    return t.numpy()
+
+
+def _dev_vals(v):
+    return bf16_dev(v) if v.dtype == np.uint16 else to_dev(v)
+
+
+def check_csr(m, n, rp, ci, val, b1, b2, base):
+    A = J.csr_tensor(to_dev(rp), to_dev(ci), _dev_vals(val), (m, n), origin=base)
+    Bt = J.convert_format(A, J.Formats.BSRRight((b1, b2)))
+    J.device_status()
+    bp, bc, bv = O.csr_to_bsr(m, n, rp, ci, val, b1, b2, base=base)
+    assert np.array_equal(_host(J.positions(Bt, 2)), bp)
+    assert np.array_equal(_host(J.coordinates(Bt, 2)), bc)
+    assert np.array_equal(_host(J.nonzeros(Bt)).view(np.uint8), bv.view(np.uint8))
+    assert Bt.origin == A.origin and Bt.extents == (m, n)
+
+
+def test_fixture(golden):
+    g = golden["convert_fixture_3x4"]["A"]
+    check_csr(3, 4, np.array(g["rowptr"], np.int32), np.array(g["colind"], np.int32),
+              np.array(g["val"], np.float32), 2, 2, 0)
+
+
+@pytest.mark.parametrize("dtype", [np.float64, np.float32, np.uint16])
+@pytest.mark.parametrize("base", [0, 1])
+@pytest.mark.parametrize("b1,b2", [(4, 4), (3, 5), (64, 64), (1, 7)])
+def test_csr_random(dtype, base, b1, b2):
+    rng = np.random.default_rng(61)
+    m, n = 301, 257                                    # not multiples of the block size
+    rp, ci, val = random_csr(m, n, rng.integers(0, 25, size=m), seed=62, base=base,
+                             zero_frac=0.2)
+    if dtype == np.uint16:
+        val = synth.f32_to_bf16_bits(val.astype(np.float32))
+    else:
+        val = val.astype(dtype)
+    val[::17] = -0.0 if dtype != np.uint16 else np.uint16(0x8000)   # negative zeros drop too
+    check_csr(m, n, rp, ci, val, b1, b2, base)
+
+
+def test_csr_wide_matrix_windows():
+    """More block columns than one shared-memory bitmap window holds."""
+    rng = np.random.default_rng(63)
+    m, n = 40, 400_000
+    rp, ci, val = random_csr(m, n, rng.integers(0, 200, size=m), seed=64)
+    check_csr(m, n, rp, ci, val, 2, 1, 0)
+
+
+def test_config5_round_trip():
+    bp, bc, bv, _ = synth.config5(nbr=128)
+    rp, ci, vals = synth.bsr_to_csr(bp, bc, bv, 64, 128)
+    A = J.csr_tensor(to_dev(rp), to_dev(ci), bf16_dev(vals), (8192, 8192), origin=0)
+    Bt = J.convert_format(A, J.Formats.BSRRight((64, 64)))
+    J.device_status()
+    assert np.array_equal(_host(J.positions(Bt, 2)), bp)
+    assert np.array_equal(_host(J.coordinates(Bt, 2)), bc)
+    assert np.array_equal(_host(J.nonzeros(Bt)), bv)
+
+
+@pytest.mark.parametrize("base", [0, 1])
+def test_coo_duplicates_and_order(base):
+    rng = np.random.default_rng(65)
+    m, n, nnz = 200, 150, 6000                          # many duplicate coordinates
+    rows = rng.integers(0, m, nnz).astype(np.int32)
+    cols = rng.integers(0, n, nnz).astype(np.int32)
+    vals = rng.uniform(-1, 1, nnz)
+    vals[rng.random(nnz) < 0.1] = 0
+    A = J.coo_tensor(to_dev(rows + base), to_dev(cols + base), to_dev(vals), (m, n), origin=base)
+    Bt = J.convert_format(A, J.Formats.BSRRight((8, 4)))
+    J.device_status()
+    bp, bc, bv = O.coo_to_bsr(m, n, rows + base, cols + base, vals, 8, 4, base=base)
+    assert np.array_equal(_host(J.positions(Bt, 2)), bp)
+    assert np.array_equal(_host(J.coordinates(Bt, 2)), bc)
+    assert np.array_equal(_host(J.nonzeros(Bt)), bv)
+
+
+def test_coo_bounds_error():
+    A = J.coo_tensor(to_dev(np.array([0, 9], np.int32)), to_dev(np.array([0, 1], np.int32)),
+                     to_dev(np.ones(2)), (4, 4), origin=0)
+    with pytest.raises(J.NonCanonicalStorage):
+        J.convert_format(A, J.Formats.BSRRight((2, 2)))
+    J.device_status()
+
+
+@pytest.mark.parametrize("n", [0, 1, 2047, 2048, 2049, 3_000_001])
+def test_scan(n):
+    rng = np.random.default_rng(66)
+    c = rng.integers(0, 300, size=n).astype(np.int32)
+    out = J.exclusive_scan(to_dev(c), base=1)
+    J.device_status()
+    assert np.array_equal(out.cpu().numpy(), O.exclusive_scan(c, base=1))
+
+
+def test_empty_matrix():
+    A = J.csr_tensor(to_dev(np.zeros(11, np.int32)), to_dev(np.zeros(0, np.int32)),
+                     to_dev(np.zeros(0)), (10, 10), origin=0)
+    Bt = J.convert_format(A, J.Formats.BSRRight((4, 4)))
+    assert _host(J.positions(Bt, 2)).tolist() == [0, 0, 0, 0] and J.nnz(Bt) == 0

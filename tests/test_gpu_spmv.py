@@ -1,0 +1,136 @@
+"""CSR SpMV on the GPU against the CPU oracle: bit-exact for rows of up to 32
+entries (same operations in the same order), within tolerance for longer rows."""
+import numpy as np
+import pytest
+import torch
+
+import jlust_b200 as J
+from jlust_b200 import synth
+from oracle import oracle as O
+from _helpers import DEV, assert_within, random_csr, to_dev
+
+pytestmark = pytest.mark.gpu
+TOL = {np.float64: 1e-12, np.float32: 1e-5}
+
+
+def run_spmv(rp, ci, val, x, m, n, base, y0=None, alpha=1.0, beta=0.0, prepared=False):
+    A = J.csr_tensor(to_dev(rp), to_dev(ci), to_dev(val), (m, n), origin=base)
+    xd = to_dev(x)
+    yd = to_dev(y0) if y0 is not None else torch.zeros(m, dtype=xd.dtype, device=DEV)
+    if prepared:
+        h = J.prepare(J.B200Backend(), J.SpMVOp, A)
+        J.execute(J.SpMVOp, h, xd, yd, alpha=alpha, beta=beta)
+    else:
+        J.execute(J.SpMVOp, A, xd, yd, alpha=alpha, beta=beta)
+    J.device_status()
+    return yd.cpu().numpy()
+
+
+def test_kat(golden):
+    for name in ("spmv_csr_onebased", "spmv_csr_zerobased"):
+        g = golden[name]
+        A = g["A"]
+        y = run_spmv(np.array(A["rowptr"], np.int32), np.array(A["colind"], np.int32),
+                     np.array(A["val"]), np.array(g["x"]), 3, 3, A["base"])
+        assert y.tolist() == g["y"]
+
+
+@pytest.mark.parametrize("dtype", [np.float64, np.float32])
+@pytest.mark.parametrize("base", [0, 1])
+@pytest.mark.parametrize("ab", [(1.0, 0.0), (0.5, 0.0), (-1.5, 2.0), (1.0, 1.0)])
+def test_short_rows_bit_exact(dtype, base, ab):
+    rng = np.random.default_rng(11)
+    m, n = 5000, 3000
+    lengths = rng.integers(0, 33, size=m)
+    lengths[::97] = 0                                  # empty rows
+    rp, ci, val = random_csr(m, n, lengths, seed=12, base=base, dtype=dtype)
+    x = rng.uniform(-1, 1, n).astype(dtype)
+    y0 = rng.uniform(-1, 1, m).astype(dtype)
+    alpha, beta = ab
+    got = run_spmv(rp, ci, val, x, m, n, base, y0, alpha, beta)
+    ref = O.spmv(rp, ci, val, x, y0, alpha, beta, base)
+    assert np.array_equal(got, ref)
+
+
+@pytest.mark.parametrize("dtype", [np.float64, np.float32])
+def test_long_rows_within_tolerance(dtype):
+    rng = np.random.default_rng(13)
+    m, n = 3000, 20000
+    lengths = rng.integers(0, 20, size=m)
+    lengths[::50] = rng.integers(33, 3000, size=lengths[::50].shape[0])   # warp rows
+    lengths[7] = 12000                                                      # unstaged tile
+    rp, ci, val = random_csr(m, n, lengths, seed=14, dtype=dtype)
+    x = rng.uniform(-1, 1, n).astype(dtype)
+    got = run_spmv(rp, ci, val, x, m, n, 0, alpha=2.0)
+    ref, bound = O.spmv_ref64(rp, ci, val, x, alpha=2.0)
+    assert_within(got, ref, bound, TOL[dtype])
+    # rows of up to 32 entries are summed by one thread in storage order, from
+    # shared memory or (in tiles too large to stage) from global memory alike
+    short = np.diff(rp) <= 32
+    exact = O.spmv(rp, ci, val, x, alpha=2.0)
+    assert np.array_equal(got[short], exact[short])
+
+
+def test_prepared_handle_and_update_values():
+    rp, ci, val, x = synth.config1(seed=21, n=20000, k=10)
+    A = J.csr_tensor(to_dev(rp), to_dev(ci), to_dev(val), (20000, 20000), origin=0)
+    h = J.prepare(J.B200Backend(), J.SpMVOp, A)
+    info = h.info()
+    assert info["max_row"] == 10 and info["variant"] == 0
+    y = torch.zeros(20000, dtype=torch.float64, device=DEV)
+    J.execute(J.SpMVOp, h, to_dev(x), y)
+    assert np.array_equal(y.cpu().numpy(), O.spmv(rp, ci, val, x))
+    val2 = val * 3
+    J.update_values(h, J.csr_tensor(A.pos[1], A.crd[1], to_dev(val2), (20000, 20000), origin=0))
+    J.execute(h, to_dev(x), y)
+    assert np.array_equal(y.cpu().numpy(), O.spmv(rp, ci, val2, x))
+
+
+def test_validation_rejects_noncanonical():
+    rp = np.array([0, 2, 1, 3], np.int32)       # decreasing row pointer
+    ci = np.array([0, 1, 2], np.int32)
+    A = J.csr_tensor(to_dev(rp), to_dev(ci), to_dev(np.ones(3)), (3, 3), origin=0)
+    with pytest.raises(J.NonCanonicalStorage):
+        J.validate_storage(A)
+    with pytest.raises(J.NonCanonicalStorage):
+        J.prepare(J.B200Backend(), J.SpMVOp, A)
+    ci_bad = np.array([0, 5, 2], np.int32)      # column out of range
+    A2 = J.csr_tensor(to_dev(np.array([0, 2, 2, 3], np.int32)), to_dev(ci_bad),
+                      to_dev(np.ones(3)), (3, 3), origin=0)
+    with pytest.raises(J.NonCanonicalStorage):
+        J.validate_storage(A2)
+    J.validate_storage(J.csr_tensor(to_dev(np.array([0, 2, 2, 3], np.int32)),
+                                    to_dev(np.array([0, 2, 1], np.int32)), to_dev(np.ones(3)),
+                                    (3, 3), origin=0))
+
+
+def test_empty_and_degenerate():
+    # m = 0
+    got = run_spmv(np.array([0], np.int32), np.zeros(0, np.int32), np.zeros(0), np.ones(4), 0, 4, 0)
+    assert got.shape == (0,)
+    # nnz = 0 with beta
+    y0 = np.arange(5, dtype=np.float64)
+    got = run_spmv(np.zeros(6, np.int32), np.zeros(0, np.int32), np.zeros(0), np.ones(3), 5, 3, 0,
+                   y0, 1.0, 2.0)
+    assert got.tolist() == (2 * y0).tolist()
+
+
+def test_config1_full_size_bit_exact():
+    rp, ci, val, x = synth.config1()
+    got = run_spmv(rp, ci, val, x, 100_000, 100_000, 0)
+    assert np.array_equal(got, O.spmv(rp, ci, val, x))
+
+
+def test_laplacian_iterations_bit_exact():
+    """20 iterations x <- A x on a 1024^2 grid stay bit-identical to the oracle."""
+    rp, ci, val, x = synth.config2(g=1024)
+    n = 1024 * 1024
+    A = J.csr_tensor(to_dev(rp), to_dev(ci), to_dev(val), (n, n), origin=0)
+    xa, xb = to_dev(x), torch.empty(n, dtype=torch.float64, device=DEV)
+    xr = x.copy()
+    for _ in range(20):
+        J.execute(J.SpMVOp, A, xa, xb)
+        xa, xb = xb, xa
+        xr = O.spmv(rp, ci, val, xr)
+    J.device_status()
+    assert np.array_equal(xa.cpu().numpy(), xr)

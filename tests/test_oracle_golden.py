@@ -1,0 +1,125 @@
+"""The CPU oracle against the reference's known-answer vectors, and its own
+invariants (thread-count independence, fp64 agreement, conversion round trip)."""
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from jlust_b200 import synth
+
+
+def _csr(d, dtype=np.float64):
+    return (np.array(d["rowptr"], np.int32), np.array(d["colind"], np.int32),
+            np.array(d["val"], dtype), d["base"])
+
+
+@pytest.mark.parametrize("name", ["spmv_csr_onebased", "spmv_csr_zerobased"])
+@pytest.mark.parametrize("dtype", [np.float64, np.float32])
+def test_spmv_kat(golden, name, dtype):
+    g = golden[name]
+    rp, ci, v, base = _csr(g["A"], dtype)
+    y = O.spmv(rp, ci, v, np.array(g["x"], dtype), alpha=g["alpha"], beta=g["beta"], base=base)
+    assert np.array_equal(y, np.array(g["y"], dtype))
+
+
+@pytest.mark.parametrize("order", ["C", "F"])
+def test_spmm_kat(golden, order):
+    g = golden["spmm_csr_onebased"]
+    rp, ci, v, base = _csr(g["A"])
+    B = np.array(g["B"], np.float64, order=order)
+    C = O.spmm(rp, ci, v, B, base=base, c_order=0 if order == "C" else 1)
+    assert np.array_equal(C, np.array(g["C"]))
+
+
+def test_sddmm_kat(golden):
+    g = golden["sddmm_csr_onebased"]
+    rp, ci, v, base = _csr(g["C"], np.float32)
+    A = np.array(g["A"], np.float32)
+    B = np.array(g["B"], np.float32)      # K x n as the reference passes it
+    out = O.sddmm(rp, ci, A, B, v, mode=0, alpha=g["alpha"], beta=g["beta"], base=base)
+    assert np.array_equal(out, np.array(g["out"], np.float32))
+    # sampled-product mode with S = 1 gives the same values
+    out1 = O.sddmm(rp, ci, A, B, v, S=np.ones(5, np.float32), mode=1, base=base)
+    assert np.array_equal(out1, out)
+
+
+def test_conversion_fixture_blocks(golden):
+    """CSR fixture of test_convert.jl to BSRRight((2,2)) with the level extents
+    of dim2lvl(as_size=true): ceil(3/2) = 2 block rows."""
+    g = golden["convert_fixture_3x4"]
+    rp, ci, v, base = _csr(g["A"], np.float32)
+    bp, bc, bv = O.csr_to_bsr(3, 4, rp, ci, v, 2, 2, base=base)
+    assert bp.tolist() == [0, 2, 4]
+    assert bc.tolist() == [0, 1, 0, 1]
+    assert bv.tolist() == [1, 0, 0, 3, 2, 0, 0, 0, 4, 0, 0, 0, 5, 0, 0, 0]
+    # the decomposer's visit set is recovered from the blocks
+    visits = []
+    for I in range(2):
+        for q in range(bp[I], bp[I + 1]):
+            tile = bv[q * 4:(q + 1) * 4].reshape(2, 2)
+            for r in range(2):
+                for c in range(2):
+                    if tile[r, c] != 0:
+                        visits.append([[I * 2 + r, int(bc[q]) * 2 + c], float(tile[r, c])])
+    assert sorted(visits) == sorted(g["decomposer_visits"])
+
+
+def test_conversion_origin_preserved():
+    rp = np.array([1, 3, 4, 6], np.int32)
+    ci = np.array([1, 3, 2, 1, 3], np.int32)
+    v = np.array([1, 2, 3, 4, 5], np.float32)
+    bp, bc, bv = O.csr_to_bsr(3, 4, rp, ci, v, 2, 2, base=1)
+    assert bp.tolist() == [1, 3, 5] and bc.tolist() == [1, 2, 1, 2]
+
+
+def test_coo_duplicates_first_wins_and_zeros_dropped():
+    rows = np.array([2, 0, 0, 1, 0], np.int32)
+    cols = np.array([3, 1, 1, 0, 1], np.int32)
+    vals = np.array([5, 0, 7, 9, 8], np.float64)   # (0,1): 0 dropped, then 7 wins over 8
+    bp, bc, bv = O.coo_to_bsr(3, 4, rows, cols, vals, 2, 2)
+    assert bp.tolist() == [0, 1, 2]
+    assert bc.tolist() == [0, 1]
+    assert bv.tolist() == [0, 7, 9, 0, 0, 5, 0, 0]
+
+
+def test_scan():
+    c = np.array([3, 0, 2, 5], np.int32)
+    assert O.exclusive_scan(c, base=1).tolist() == [1, 4, 4, 6, 11]
+
+
+def test_thread_count_independent():
+    rp, ci, v, x = synth.config1(seed=5, n=3000, k=7)
+    outs = []
+    for t in (1, 4):
+        O.set_threads(t)
+        outs.append(O.spmv(rp, ci, v, x))
+    O.set_threads(O.max_threads())
+    assert np.array_equal(outs[0], outs[1])
+
+
+def test_spmv_matches_fp64_reference():
+    rp, ci, v, x = synth.config1(seed=6, n=2000, k=9)
+    y = O.spmv(rp, ci, v, x, alpha=0.5)
+    y64, bound = O.spmv_ref64(rp, ci, v, x, alpha=0.5)
+    assert np.all(np.abs(y - y64) <= 1e-14 * bound + 1e-300)
+
+
+def test_bsr_oracle_vs_dense():
+    bp, bc, bv, B = synth.config5(seed=7, nbr=6, bs=8, band=1, p_off=0.3, N=16)
+    Y = O.bsr_spmm(bp, bc, bv, B, b1=8, b2=8)
+    dense = np.zeros((48, 48), np.float64)
+    for I in range(6):
+        for q in range(bp[I], bp[I + 1]):
+            dense[I * 8:(I + 1) * 8, bc[q] * 8:(bc[q] + 1) * 8] = synth.bf16_bits_to_f32(
+                bv[q * 64:(q + 1) * 64]).reshape(8, 8)
+    ref = dense @ synth.bf16_bits_to_f32(B).astype(np.float64)
+    assert np.allclose(Y, ref, rtol=1e-5, atol=1e-5)
+    y64, bound = O.bsr_spmm_ref64(bp, bc, bv, B, b1=8, b2=8)
+    assert np.allclose(y64, ref, rtol=1e-12, atol=1e-12)
+
+
+def test_csr_bsr_round_trip():
+    bp, bc, bv, _ = synth.config5(seed=8, nbr=5, bs=4, band=1, p_off=0.4, N=8)
+    rp, ci, vals = synth.bsr_to_csr(bp, bc, bv, 4, 5)
+    bp2, bc2, bv2 = O.csr_to_bsr(20, 20, rp, ci, vals, 4, 4)
+    # blocks whose values are all zero after bf16 rounding would vanish; none here
+    assert np.array_equal(bp2, bp) and np.array_equal(bc2, bc) and np.array_equal(bv2, bv)
