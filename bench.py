@@ -97,16 +97,21 @@ class ClockSampler:
         self.reasons = set()
         self.max_mhz = None
         self.h = None
+        self.err = None
         try:
             import pynvml as N
             import torch
             N.nvmlInit()
             pr = torch.cuda.get_device_properties(torch_device)
             bus = f"{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0"
-            self.h = N.nvmlDeviceGetHandleByPciBusId_v2(bus)
+            try:
+                self.h = N.nvmlDeviceGetHandleByPciBusId(bus.encode())
+            except Exception:
+                self.h = N.nvmlDeviceGetHandleByPciBusId(bus)
             self.N = N
             self.max_mhz = N.nvmlDeviceGetMaxClockInfo(self.h, N.NVML_CLOCK_SM)
         except Exception as e:  # NVML missing: report no clocks rather than fail
+            self.h = None
             self.err = repr(e)
         self._stop = threading.Event()
         self._t = None
@@ -138,7 +143,7 @@ class ClockSampler:
     def summary(self):
         if not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
-                    "samples": 0}
+                    "samples": 0, "error": self.err}
         return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
                 "reasons": sorted(self.reasons), "samples": len(self.samples)}
 
@@ -209,7 +214,7 @@ def timed(ctx, fn, steps, stream):
 class Laplacian:
     """Config 2: x <- A x on the 5-point Laplacian of a g x g grid, fp64."""
 
-    kernel = "spmv_tiles"
+    kernel = "spmv_rows"
     dtype = "f64"
 
     def __init__(self, ctx):
@@ -318,10 +323,342 @@ class Laplacian:
         return f"full iterations x <- A x of the {self.g}^2 Laplacian (fp64, oracle row order)"
 
 
-WORKLOADS = {"laplacian": Laplacian}
+class Single:
+    """Base of the single-GPU workloads (configs 1, 3, 4, 5 and conversion)."""
+
+    flush_l2 = False
+    launches_per_step = 1
+    bound = "hbm"
+
+    def __init__(self, ctx):
+        import torch
+
+        import jlust_b200 as J
+        from jlust_b200 import synth
+        if ctx.world > 1:
+            raise SystemExit(f"workload {ctx.args.workload} runs on one GPU")
+        self.ctx, self.J, self.synth, self.torch = ctx, J, synth, torch
+        self.dev = ctx.device
+        self.setup()
+
+    def d(self, a):
+        return self.torch.from_numpy(np.ascontiguousarray(a)).to(self.dev)
+
+    def bf(self, bits):
+        return self.torch.from_numpy(np.ascontiguousarray(bits).view(np.int16)).to(self.dev).view(
+            self.torch.bfloat16)
+
+    def reset(self):
+        pass
+
+    def e2e_setup(self):
+        self.e2e_inputs = [t.cpu().pin_memory() for t in self.e2e_in()]
+        self.e2e_outputs = [self.torch.empty_like(t, device="cpu").pin_memory() for t in self.e2e_out()]
+        self.h2d = sum(t.numel() * t.element_size() for t in self.e2e_inputs)
+        self.d2h = sum(t.numel() * t.element_size() for t in self.e2e_outputs)
+
+    def e2e_step(self):
+        for hd, dv in zip(self.e2e_inputs, self.e2e_in()):
+            dv.copy_(hd, non_blocking=True)
+        self.api_call()
+        for hd, dv in zip(self.e2e_outputs, self.e2e_out()):
+            hd.copy_(dv, non_blocking=True)
+
+    def step(self):
+        self.api_call()
+
+
+class SpMV1(Single):
+    """Config 1: CSR SpMV fp64, n = 100,000, 10 uniform columns per row."""
+
+    kernel, dtype, flush_l2 = "spmv_rows", "f64", True
+
+    def setup(self):
+        J = self.J
+        rp, ci, val, x = self.synth.config1()
+        self.h = (rp, ci, val, x)
+        self.nnz, self.m = int(rp[-1]), rp.shape[0] - 1
+        self.A = J.csr_tensor(self.d(rp), self.d(ci), self.d(val), (self.m, self.m), origin=0)
+        self.x, self.y = self.d(x), self.torch.zeros(self.m, dtype=self.torch.float64, device=self.dev)
+
+    def api_call(self):
+        self.J.execute(self.J.SpMVOp, self.A, self.x, self.y)
+
+    def e2e_in(self):
+        return [self.x]
+
+    def e2e_out(self):
+        return [self.y]
+
+    def flops(self):
+        return 2.0 * self.nnz
+
+    def bytes(self):
+        return 12.0 * self.nnz + 4.0 * (self.m + 1) + 16.0 * self.m
+
+    def config(self):
+        return {"workload": f"cfg1: CSR SpMV fp64, n={self.m}, 10 nnz/row (nnz={self.nnz}), y = A x",
+                "l2": "256 MB buffer written between timed launches (inputs 14 MB < L2)"}
+
+    def cpu_setup(self):
+        pass
+
+    def cpu_step(self):
+        from oracle import oracle as O
+        rp, ci, val, x = self.h
+        O.spmv(rp, ci, val, x)
+
+    def cpu_sample(self):
+        return "full y = A x (fp64, oracle row order)"
+
+
+class SpMM(Single):
+    """Config 3: CSR SpMM fp32, power-law A (4M x 4M), B 4M x 64 row-major."""
+
+    kernel, dtype = "spmm_rowmajor", "f32"
+
+    def setup(self):
+        J = self.J
+        rp, ci, val, B = self.synth.config3()
+        self.h = (rp, ci, val, B)
+        self.nnz, self.m = int(rp[-1]), rp.shape[0] - 1
+        self.k = B.shape[1]
+        self.deg = np.diff(rp)
+        self.A = J.csr_tensor(self.d(rp), self.d(ci), self.d(val), (self.m, self.m), origin=0)
+        self.B = self.d(B)
+        self.C = self.torch.zeros(self.m, self.k, dtype=self.torch.float32, device=self.dev)
+
+    def api_call(self):
+        self.J.execute(self.J.SpMMOp, self.A, self.B, self.C)
+
+    def e2e_in(self):
+        return [self.B]
+
+    def e2e_out(self):
+        return [self.C]
+
+    def flops(self):
+        return 2.0 * self.nnz * self.k
+
+    def bytes(self):  # gather model: one B row per stored entry, C written once
+        return 8.0 * self.nnz + 4.0 * (self.m + 1) + 4.0 * self.k * (self.nnz + self.m)
+
+    def config(self):
+        return {"workload": f"cfg3: CSR SpMM fp32, power-law {self.m}x{self.m} (Zipf 2.0 on "
+                            f"[1,4096], nnz={self.nnz}, mean {self.nnz / self.m:.2f}/row), "
+                            f"B {self.m}x{self.k} row-major",
+                "bytes_model": "gather (8 nnz + 4 (m+1) + 256 nnz + 256 m)",
+                "compulsory_bytes": 8.0 * self.nnz + 4.0 * (self.m + 1) + 8.0 * self.k * self.m,
+                "l2": "inputs larger than L2"}
+
+    def cpu_setup(self):
+        pass
+
+    def cpu_step(self):
+        from oracle import oracle as O
+        rp, ci, val, B = self.h
+        O.spmm(rp, ci, val, B)
+
+    def cpu_sample(self):
+        return "full C = A B (fp32, Tiled per-(row,col) order)"
+
+
+class SDDMM(Single):
+    """Config 4: SDDMM fp32, 1M x 1M pattern with 32 entries per row, K = 128."""
+
+    kernel, dtype = "sddmm_fast", "f32"
+
+    def setup(self):
+        J = self.J
+        rp, ci, A, B, S = self.synth.config4()
+        self.h = (rp, ci, A, B, S)
+        self.nnz, self.m = int(rp[-1]), rp.shape[0] - 1
+        self.K = A.shape[1]
+        self.S = self.d(S)
+        self.Cs = J.csr_tensor(self.d(rp), self.d(ci), self.S.clone(), (self.m, self.m), origin=0)
+        self.A, self.Bt = self.d(A), self.d(B)
+
+    def api_call(self):
+        J = self.J
+        J.execute(J.SDDMMOp, self.A, self.Bt.t(), self.Cs, mode="mul", S=self.S)
+
+    def e2e_in(self):
+        return [self.A, self.Bt]
+
+    def e2e_out(self):
+        return [self.Cs.val]
+
+    def flops(self):
+        return 2.0 * self.nnz * self.K
+
+    def bytes(self):  # gather model: A rows once, one B row per entry
+        return 4.0 * self.K * (self.m + self.nnz) + 4.0 * self.nnz + 4.0 * (self.m + 1) + 8.0 * self.nnz
+
+    def config(self):
+        return {"workload": f"cfg4: SDDMM fp32, pattern {self.m}x{self.m} with 32 uniform "
+                            f"entries/row (nnz={self.nnz}), A, B {self.m}x{self.K} N(0,1), "
+                            "out = dot(A_i, B_j) * S_ij",
+                "bytes_model": "gather (512 m + 512 nnz + 12 nnz + 4 (m+1))",
+                "l2": "inputs larger than L2"}
+
+    def cpu_setup(self):
+        pass
+
+    def cpu_step(self):
+        from oracle import oracle as O
+        rp, ci, A, B, S = self.h
+        rows = self.m // 16
+        O.sddmm(rp[:rows + 1], ci, A, B.T, S, S=S, mode=1)
+
+    def cpu_flops(self):
+        return 2.0 * int(self.h[0][self.m // 16]) * self.K
+
+    def cpu_sample(self):
+        return "the first 1/16 of the pattern rows per step (fp32, sequential K loop)"
+
+
+class BSR(Single):
+    """Config 5: BSR SpMM bf16 -> fp32, 65,536^2 with 64x64 blocks, band +-8 + 2%."""
+
+    kernel, dtype, bound = "bsr_spmm_tc", "bf16 in, f32 accumulate", "tensor"
+
+    def setup(self):
+        J = self.J
+        bp, bc, bv, B = self.synth.config5()
+        self.h = (bp, bc, bv, B)
+        self.nnzb, self.mb = bc.shape[0], bp.shape[0] - 1
+        self.N = B.shape[1]
+        n = self.mb * 64
+        self.A = J.bsr_tensor(self.d(bp), self.d(bc), self.bf(bv), (n, n), (64, 64), origin=0)
+        self.B = self.bf(B)
+        self.C = self.torch.zeros(n, self.N, dtype=self.torch.float32, device=self.dev)
+
+    def api_call(self):
+        self.J.execute(self.J.BlockSpMMOp, self.A, self.B, self.C)
+
+    def e2e_in(self):
+        return [self.B]
+
+    def e2e_out(self):
+        return [self.C]
+
+    def flops(self):
+        return 2.0 * self.nnzb * 64 * 64 * self.N
+
+    def bytes(self):
+        n = self.mb * 64
+        return 8192.0 * self.nnzb + 2.0 * n * self.N + 4.0 * n * self.N + 4.0 * (self.nnzb + self.mb + 1)
+
+    def config(self):
+        return {"workload": f"cfg5: BSR SpMM bf16 (fp32 accumulate), {self.mb * 64}^2 with 64x64 "
+                            f"blocks, band +-8 + 2% off-band (nnzb={self.nnzb}), B "
+                            f"{self.mb * 64}x{self.N} bf16 row-major",
+                "l2": "A values (311 MB) larger than L2; B (33.5 MB) L2-resident by design"}
+
+    def cpu_setup(self):
+        pass
+
+    def cpu_step(self):
+        from oracle import oracle as O
+        bp, bc, bv, B = self.h
+        rows = self.mb // 16
+        O.bsr_spmm(bp[:rows + 1], bc, bv, B)
+
+    def cpu_flops(self):
+        return 2.0 * int(self.h[0][self.mb // 16]) * 64 * 64 * self.N
+
+    def cpu_sample(self):
+        return "the first 1/16 of the block rows per step (fp32, fused-loop order)"
+
+
+class Convert(Single):
+    """CSR -> BSRRight((64, 64)) of the config-5 matrix (bf16 values)."""
+
+    kernel, dtype = "fill_blocks", "bf16 values, int32 indices"
+
+    def setup(self):
+        J = self.J
+        bp, bc, bv, _ = self.synth.config5(N=64)
+        rp, ci, vals = self.synth.bsr_to_csr(bp, bc, bv, 64, bp.shape[0] - 1)
+        self.h = (rp, ci, vals)
+        self.m = rp.shape[0] - 1
+        self.nnz = int(rp[-1])
+        self.nnzb, self.mb = bc.shape[0], bp.shape[0] - 1
+        self.A = J.csr_tensor(self.d(rp), self.d(ci), self.bf(vals), (self.m, self.m), origin=0)
+
+    def api_call(self):
+        self.out = self.J.convert_format(self.A, self.J.Formats.BSRRight((64, 64)))
+
+    def e2e_setup(self):
+        torch = self.torch
+        self.hv = self.A.val.cpu().pin_memory()
+        self.hout = torch.empty(self.nnzb * 4096, dtype=torch.bfloat16).pin_memory()
+        self.h2d = self.hv.numel() * 2
+        self.d2h = self.hout.numel() * 2
+
+    def e2e_step(self):
+        self.A.val.copy_(self.hv, non_blocking=True)
+        self.api_call()
+        self.hout.copy_(self.out.val, non_blocking=True)
+
+    def flops(self):  # reported as entries converted per second (GFLOP/s field = Gentries/s)
+        return float(self.nnz)
+
+    def bytes(self):
+        return (4.0 * (self.m + 1) + 6.0 * self.nnz) + (8192.0 * self.nnzb + 4.0 * self.nnzb +
+                                                         4.0 * (self.mb + 1))
+
+    def config(self):
+        return {"workload": f"CSR -> BSR 64x64 of the cfg5 matrix ({self.m}^2, nnz={self.nnz}, "
+                            f"nnzb={self.nnzb}), count + fill (host sync between)",
+                "value_unit_note": "value = G stored entries converted per second"}
+
+    def cpu_setup(self):
+        pass
+
+    def cpu_step(self):
+        from oracle import oracle as O
+        rp, ci, vals = self.h
+        rows = self.m // 64
+        O.csr_to_bsr(rows, self.m, rp[:rows + 1], ci, vals, 64, 64)
+
+    def cpu_flops(self):
+        return float(self.h[0][self.m // 64])
+
+    def cpu_sample(self):
+        return "the first 1/64 of the rows per step (single-threaded composer)"
+
+
+WORKLOADS = {"laplacian": Laplacian, "spmv1": SpMV1, "spmm": SpMM, "sddmm": SDDMM, "bsr": BSR,
+             "convert": Convert}
 
 
 # ------------------------------------------------------------------- arms --
+def unit_of(W):
+    return "Gentries/s" if isinstance(W, Convert) else "GFLOP/s"
+
+
+def timed_flushed(ctx, fn, steps, stream):
+    """Like timed(), for inputs smaller than L2: a 256 MB buffer is written
+    before every launch and only the launches are timed (CUDA events around
+    each one on `stream`, summed)."""
+    torch = ctx.torch
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=ctx.device)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(steps)]
+    ctx.barrier()
+    with ClockSampler(ctx.device) as clk:
+        for a, b in evs:
+            flush.zero_()
+            a.record(stream)
+            fn()
+            b.record(stream)
+        torch.cuda.synchronize(ctx.device)
+    secs = sum(a.elapsed_time(b) for a, b in evs) / 1e3
+    ctx.barrier()
+    return ctx.max_over_ranks(secs), clk.summary()
+
+
 def cpu_time(step, flops_per_step, min_steps=2, max_steps=20, budget_s=20.0):
     """Times `step` on the host: one untimed call, then up to max_steps calls
     or budget_s seconds.  Returns (GFLOP/s, steps timed)."""
@@ -345,19 +682,31 @@ def run_ours(args):
         W.step()
     J.device_status()
     W.reset()
-    secs, clocks = timed(ctx, W.step, args.steps, stream)
-    J.device_status()
     K = args.steps
+    if getattr(W, "flush_l2", False):
+        secs, clocks = timed_flushed(ctx, W.step, K, stream)
+    else:
+        secs, clocks = timed(ctx, W.step, K, stream)
+    J.device_status()
     value = W.flops() * K / secs / 1e9
     eff_gbs = W.bytes() * K / secs / 1e9
     pk = peaks()
     per_launch_s = secs / K
-    achieved = (W.bytes() / ctx.world) / per_launch_s / 1e9
     traffic = profile_traffic(f"{W.kernel}_{args.workload}")
-    roof = {"bound": "hbm", "kernel": W.kernel, "achieved": round(achieved, 1),
-            "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
-            "traffic": traffic, "peak_source": pk["source"] + " (hbm_gbs, copy burst)",
-            "algorithmic_bytes_per_launch": W.bytes() / ctx.world}
+    if getattr(W, "bound", "hbm") == "tensor":
+        achieved = W.flops() / per_launch_s / 1e12
+        roof = {"bound": "tensor", "kernel": W.kernel, "achieved": round(achieved, 2),
+                "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                "frac": round(achieved / pk["bf16_tflops"], 4), "traffic": traffic,
+                "peak_source": pk["source"] + " (bf16_tflops, cuBLAS burst)",
+                "hbm_achieved_gbs": round(W.bytes() / per_launch_s / 1e9, 1),
+                "hbm_frac": round(W.bytes() / per_launch_s / 1e9 / pk["hbm_gbs"], 4)}
+    else:
+        achieved = (W.bytes() / ctx.world) / per_launch_s / 1e9
+        roof = {"bound": "hbm", "kernel": W.kernel, "achieved": round(achieved, 1),
+                "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
+                "traffic": traffic, "peak_source": pk["source"] + " (hbm_gbs, copy burst)",
+                "algorithmic_bytes_per_launch": W.bytes() / ctx.world}
     if ctx.world > 1:
         roof["note"] = "per-rank bytes over the whole step, halo exchange included"
 
@@ -370,20 +719,21 @@ def run_ours(args):
         J.device_status()
         e_secs, _ = timed(ctx, W.e2e_step, K, stream)
         J.device_status()
-        e2e = {"value": round(W.flops() * K / e_secs / 1e9, 3), "unit": "GFLOP/s",
+        e2e = {"value": round(W.flops() * K / e_secs / 1e9, 3), "unit": unit_of(W),
                "h2d_bytes_per_step": W.h2d, "d2h_bytes_per_step": W.d2h,
-               "ms_per_step": round(e_secs * 1e3 / K, 4), "api": "jlust_b200.execute(SpMVOp, ...)"}
+               "ms_per_step": round(e_secs * 1e3 / K, 4), "api": "jlust_b200.execute / convert_format"}
 
     cpu = None
     if ctx.rank == 0 and ctx.world == 1 and not args.no_cpu:
         from oracle import oracle as O
         W.cpu_setup()
-        v, k = cpu_time(W.cpu_step, W.flops())
-        cpu = {"value": round(v, 3), "unit": "GFLOP/s", "cores": O.max_threads(), "kind": "port",
-               "sample": f"{k} {W.cpu_sample()}"}
+        cf = W.cpu_flops() if hasattr(W, "cpu_flops") else W.flops()
+        v, k = cpu_time(W.cpu_step, cf)
+        cpu = {"value": round(v, 3), "unit": unit_of(W), "cores": O.max_threads(), "kind": "port",
+               "sample": f"{k} steps, {W.cpu_sample()}"}
 
     launches = int(ctx.sum_over_ranks(W.launches_per_step * K))
-    line = {"metric": METRIC, "value": round(value, 3), "unit": "GFLOP/s", "n_gpus": ctx.world,
+    line = {"metric": METRIC, "value": round(value, 3), "unit": unit_of(W), "n_gpus": ctx.world,
             "steps": K, "warmup": args.warmup, "ms_per_step": round(secs * 1e3 / K, 5),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": W.dtype, "data": "synthetic (numpy PCG64, seeds of the configs)",

@@ -125,7 +125,9 @@ JLB_API int jlb_spmv_plan_create(jlb_spmv_plan *plan, void *stream, int dtype, i
 JLB_API int jlb_spmv_plan_execute(jlb_spmv_plan plan, void *stream, const void *val,
                                   const void *x, void *y, double alpha, double beta);
 /* Row-length profile recorded by the plan: max and mean entries per row and
- * the variant code used by execute (0 staged thread-per-row, 1 mixed). */
+ * the variant (0: every row summed by one thread in storage order, i.e.
+ * bit-exact with the CPU walker; 1: some rows longer than 32 entries are
+ * summed by a warp). */
 JLB_API int jlb_spmv_plan_info(jlb_spmv_plan plan, int64_t *max_row, double *mean_row,
                                int *variant);
 JLB_API int jlb_spmv_plan_destroy(jlb_spmv_plan plan);

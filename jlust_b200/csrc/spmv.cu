@@ -1,22 +1,24 @@
 // spmv.cu -- CSR SpMV for sm_100a, plus CSR structure validation.
 //
-// One CTA owns a tile of kRows consecutive rows (one thread per row).  The
-// tile's slice of the value and column arrays is contiguous, so the CTA first
-// stages it into shared memory with 16-byte vector loads (cache-streaming, so
-// the gathered x keeps L2), then:
-//   phase A  rows of <= kShortMax entries: one thread sums its row in storage
-//            order with separately rounded products and sums -- the same
-//            operations, in the same order, as JLUST's CPU walker
-//            (ext/KernelAbstractionsExt/ops/_walker.jl:111-146 and
-//            ops/spmv.jl:154,161-178), hence bit-identical results;
-//   phase B  longer rows: one warp per row, lane-strided partial sums and a
-//            fixed xor-butterfly (deterministic, within tolerance).
-// A tile whose slice exceeds kCap entries (it holds long rows) runs the same
-// two phases straight from global memory.  This replaces the reference's
-// per-row walker kernels with their VS heuristic (KA spmv.jl:296-323) and its
-// atomic merge-based kernel (ext/CUDAExt/ops/spmv.jl:129-191): the choice of
-// thread / warp per row is made per row from its length, and no atomics touch
-// y, so results are deterministic.
+// One thread per row.  A row of up to kShortMax entries is summed by its
+// thread in storage order with separately rounded products and sums -- the
+// same operations, in the same order, as JLUST's CPU walker
+// (ext/KernelAbstractionsExt/ops/_walker.jl:111-146 and ops/spmv.jl:154,
+// 161-178), hence bit-identical results.  The thread reads its entries
+// directly through the read-only path: the 32 rows of a warp occupy one
+// contiguous slice of the value and column arrays, so the L1 turns the
+// threads' strided reads into whole-line fetches and every byte of the
+// slice crosses HBM once (measured on B200: 95% of the copy bandwidth on the
+// 4096^2 Laplacian; staging the slice in shared memory first was slower).
+// The x gathers of four entries are issued before their sums.
+//
+// Rows longer than kShortMax are found with a warp ballot and summed by the
+// whole warp: lane-strided partial sums and a fixed xor-butterfly
+// (deterministic, within tolerance).  No atomics touch y.  This replaces the
+// reference's per-row walker kernels with their VS heuristic
+// (KA spmv.jl:296-323) and its atomic merge-based kernel
+// (ext/CUDAExt/ops/spmv.jl:129-191): thread or warp per row is chosen per row
+// from its length.
 #include "common.cuh"
 
 #include <new>
@@ -27,48 +29,8 @@ JLB_DEFINE_DEV_ERROR(spmv)
 
 namespace spmv {
 
-constexpr int kRows = 256;      // rows per tile == threads per CTA
-constexpr int kCap = 2048;      // entries staged per tile
+constexpr int kThreads = 256;
 constexpr int kShortMax = 32;   // longest row summed by a single thread
-
-template <typename T>
-struct Vec16;
-template <>
-struct Vec16<double> { using type = double2; };
-template <>
-struct Vec16<float> { using type = float4; };
-template <>
-struct Vec16<int32_t> { using type = int4; };
-
-// Copies src[p0, p1) into dst[p - pa], pa <= p0.  With `vec`, pa must be a
-// multiple of the 16-byte vector width and src 16-byte aligned; whole vectors
-// below p1 are moved with 16-byte loads, the ragged end element by element.
-// Every load stays inside [pa, p1), which lies inside the caller's array.
-template <typename T>
-__device__ __forceinline__ void stage_range(T *dst, const T *__restrict__ src, int64_t pa,
-                                            int64_t p0, int64_t p1, bool vec) {
-    constexpr int E = 16 / (int)sizeof(T);
-    using V = typename Vec16<T>::type;
-    const int tid = threadIdx.x, nt = blockDim.x;
-    int64_t tail = p0;
-    if (vec) {
-        const int64_t vb = pa / E, ve = p1 / E;
-        const V *s = reinterpret_cast<const V *>(src);
-        V *d = reinterpret_cast<V *>(dst);
-        for (int64_t v = vb + tid; v < ve; v += nt) d[v - vb] = __ldcs(s + v);
-        tail = ve * E > p0 ? ve * E : p0;
-    }
-    for (int64_t p = tail + tid; p < p1; p += nt) dst[p - pa] = __ldcs(src + p);
-}
-
-template <typename T>
-struct __align__(16) Smem {
-    T val[kCap + 16 / sizeof(T)];
-    int32_t col[kCap + 4];
-    int32_t rp[kRows + 1];
-    int32_t longrows[kRows];
-    int nlong;
-};
 
 template <typename T, bool kBeta>
 __device__ __forceinline__ void write_row(T *y, int64_t r, T acc, T alpha, T beta) {
@@ -77,81 +39,68 @@ __device__ __forceinline__ void write_row(T *y, int64_t r, T acc, T alpha, T bet
     y[r] = out;
 }
 
+// Sum of entries [lo, hi) in storage order.
+template <typename T>
+__device__ __forceinline__ T row_sum(int lo, int hi, const int32_t *__restrict__ colind,
+                                     const T *__restrict__ val, const T *__restrict__ x, int base) {
+    T acc = T(0);
+    int k = lo;
+    for (; k + 4 <= hi; k += 4) {
+        const int c0 = ldg(colind + k), c1 = ldg(colind + k + 1);
+        const int c2 = ldg(colind + k + 2), c3 = ldg(colind + k + 3);
+        const T v0 = ldg(val + k), v1 = ldg(val + k + 1), v2 = ldg(val + k + 2), v3 = ldg(val + k + 3);
+        const T x0 = ldg(x + (c0 - base)), x1 = ldg(x + (c1 - base));
+        const T x2 = ldg(x + (c2 - base)), x3 = ldg(x + (c3 - base));
+        acc = add_rn(acc, mul_rn(v0, x0));
+        acc = add_rn(acc, mul_rn(v1, x1));
+        acc = add_rn(acc, mul_rn(v2, x2));
+        acc = add_rn(acc, mul_rn(v3, x3));
+    }
+    for (; k < hi; ++k) acc = add_rn(acc, mul_rn(ldg(val + k), ldg(x + (ldg(colind + k) - base))));
+    return acc;
+}
+
 template <typename T, bool kBeta>
-__global__ void __launch_bounds__(kRows)
-spmv_tiles(int64_t m, const int32_t *__restrict__ rowptr, const int32_t *__restrict__ colind,
-           const T *__restrict__ val, const T *__restrict__ x, T *__restrict__ y, T alpha,
-           T beta, int base, int vec_ok) {
-    __shared__ Smem<T> s;
-    const int tid = threadIdx.x;
-    const int64_t r0 = (int64_t)blockIdx.x * kRows;
-    const int nrows = (int)((m - r0) < kRows ? (m - r0) : kRows);
-    for (int i = tid; i <= nrows; i += kRows) s.rp[i] = rowptr[r0 + i] - base;
-    if (tid == 0) s.nlong = 0;
-    __syncthreads();
-
-    const int64_t p0 = s.rp[0], p1 = s.rp[nrows];
-    constexpr int EV = 16 / (int)sizeof(T);
-    const bool staged = (p1 - p0) <= kCap;
-    const int64_t pav = vec_ok ? (p0 & ~(int64_t)(EV - 1)) : p0;
-    const int64_t pac = vec_ok ? (p0 & ~(int64_t)3) : p0;
-    if (staged) {
-        stage_range<T>(s.val, val, pav, p0, p1, vec_ok);
-        stage_range<int32_t>(s.col, colind, pac, p0, p1, vec_ok);
-        __syncthreads();
+__global__ void __launch_bounds__(kThreads)
+spmv_rows(int64_t m, const int32_t *__restrict__ rowptr, const int32_t *__restrict__ colind,
+          const T *__restrict__ val, const T *__restrict__ x, T *__restrict__ y, T alpha, T beta,
+          int base) {
+    const int64_t r = (int64_t)blockIdx.x * kThreads + threadIdx.x;
+    const int lane = threadIdx.x % kWarp;
+    int lo = 0, hi = 0;
+    if (r < m) {
+        lo = ldg(rowptr + r) - base;
+        hi = ldg(rowptr + r + 1) - base;
     }
-
-    // Phase A: short rows, one thread each, storage order.
-    if (tid < nrows) {
-        const int lo = s.rp[tid], hi = s.rp[tid + 1];
-        if (hi - lo <= kShortMax) {
-            T acc = T(0);
-            if (staged) {
-                for (int k = lo; k < hi; ++k)
-                    acc = add_rn(acc, mul_rn(s.val[k - pav], ldg(x + (s.col[k - pac] - base))));
-            } else {
-                for (int k = lo; k < hi; ++k)
-                    acc = add_rn(acc, mul_rn(ldg(val + k), ldg(x + (ldg(colind + k) - base))));
-            }
-            write_row<T, kBeta>(y, r0 + tid, acc, alpha, beta);
-        } else {
-            s.longrows[atomicAdd(&s.nlong, 1)] = tid;
-        }
-    }
-    __syncthreads();
-
-    // Phase B: long rows, one warp each.
-    const int warp = tid / kWarp, lane = tid % kWarp;
-    for (int i = warp; i < s.nlong; i += kRows / kWarp) {
-        const int t = s.longrows[i];
-        const int lo = s.rp[t], hi = s.rp[t + 1];
+    const bool is_long = hi - lo > kShortMax;
+    if (r < m && !is_long) write_row<T, kBeta>(y, r, row_sum<T>(lo, hi, colind, val, x, base), alpha, beta);
+    unsigned longs = __ballot_sync(0xffffffffu, r < m && is_long);
+    while (longs) {
+        const int src = __ffs(longs) - 1;
+        longs &= longs - 1;
+        const int l = __shfl_sync(0xffffffffu, lo, src), h = __shfl_sync(0xffffffffu, hi, src);
         T acc = T(0);
-        if (staged) {
-            for (int k = lo + lane; k < hi; k += kWarp)
-                acc = add_rn(acc, mul_rn(s.val[k - pav], ldg(x + (s.col[k - pac] - base))));
-        } else {
-            for (int k = lo + lane; k < hi; k += kWarp)
-                acc = add_rn(acc, mul_rn(__ldcs(val + k), ldg(x + (__ldcs(colind + k) - base))));
-        }
+        for (int k = l + lane; k < h; k += kWarp)
+            acc = add_rn(acc, mul_rn(__ldcs(val + k), ldg(x + (__ldcs(colind + k) - base))));
         acc = warp_sum(acc);
-        if (lane == 0) write_row<T, kBeta>(y, r0 + t, acc, alpha, beta);
+        if (lane == src) write_row<T, kBeta>(y, r, acc, alpha, beta);
     }
 }
 
 template <typename T>
-int launch(cudaStream_t st, int base, int64_t m, const int32_t *rowptr, const int32_t *colind,
-           const void *val, const void *x, void *y, double alpha, double beta) {
+int launch(cudaStream_t st, int base, int64_t m, int64_t nnz, const int32_t *rowptr,
+           const int32_t *colind, const void *val, const void *x, void *y, double alpha,
+           double beta) {
     if (m == 0) return ok();
-    const int vec_ok = aligned16(val) && aligned16(colind);
     const T a = (T)alpha, b = (T)beta;
-    const unsigned grid = (unsigned)ceil_div(m, kRows);
+    const unsigned grid = (unsigned)ceil_div(m, kThreads);
     if (b == T(0))
-        spmv_tiles<T, false><<<grid, kRows, 0, st>>>(m, rowptr, colind, (const T *)val,
-                                                      (const T *)x, (T *)y, a, b, base, vec_ok);
+        spmv_rows<T, false><<<grid, kThreads, 0, st>>>(m, rowptr, colind, (const T *)val,
+                                                        (const T *)x, (T *)y, a, b, base);
     else
-        spmv_tiles<T, true><<<grid, kRows, 0, st>>>(m, rowptr, colind, (const T *)val,
-                                                     (const T *)x, (T *)y, a, b, base, vec_ok);
-    JLB_LAUNCH_CHECK("spmv_tiles");
+        spmv_rows<T, true><<<grid, kThreads, 0, st>>>(m, rowptr, colind, (const T *)val,
+                                                       (const T *)x, (T *)y, a, b, base);
+    JLB_LAUNCH_CHECK("spmv_rows");
     return ok();
 }
 
@@ -162,7 +111,7 @@ __global__ void csr_validate_kernel(int64_t m, int64_t n, int64_t nnz,
                                     const int32_t *__restrict__ rowptr,
                                     const int32_t *__restrict__ colind, int base,
                                     int require_sorted, int32_t *__restrict__ stats) {
-    // stats[0] = max row length, stats[1] = number of tiles above kCap entries
+    // stats[0] = max row length, stats[1] = rows longer than kShortMax
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < m; r += stride) {
         const int64_t lo = (int64_t)rowptr[r] - base, hi = (int64_t)rowptr[r + 1] - base;
@@ -171,11 +120,7 @@ __global__ void csr_validate_kernel(int64_t m, int64_t n, int64_t nnz,
         if (hi < lo || lo < 0 || hi > nnz) { atomicOr(&g_validate_flags, 4); continue; }
         if (stats) {
             atomicMax(&stats[0], (int32_t)(hi - lo));
-            if (r % kRows == 0) {
-                const int64_t re = (r + kRows < m) ? r + kRows : m;
-                const int64_t tn = (int64_t)rowptr[re] - base - lo;
-                if (tn > kCap) atomicAdd(&stats[1], 1);
-            }
+            if (hi - lo > kShortMax) atomicAdd(&stats[1], 1);
         }
         int64_t prev = -1;
         for (int64_t k = lo; k < hi; ++k) {
@@ -189,8 +134,8 @@ __global__ void csr_validate_kernel(int64_t m, int64_t n, int64_t nnz,
 
 }  // namespace spmv
 
-// Runs the validation kernel; on success optionally returns (max row, tiles
-// above the staging capacity) through stats_host.
+// Runs the validation kernel; on success optionally returns (max row length,
+// rows longer than kShortMax) through stats_host.
 int csr_validate_impl(cudaStream_t st, int base, int64_t m, int64_t n, int64_t nnz,
                       const int32_t *rowptr, const int32_t *colind, int require_sorted,
                       int32_t *stats_dev, int32_t *stats_host) {
@@ -260,10 +205,10 @@ extern "C" JLB_API int jlb_csr_spmv(void *stream, int dtype, int idx_base, int64
     int st = spmv_args(dtype, idx_base, m, n, nnz, rowptr, colind, val, x, y);
     if (st) return st;
     if (dtype == JLB_F64)
-        return spmv::launch<double>(as_stream(stream), idx_base, m, rowptr, colind, val, x, y,
-                                    alpha, beta);
-    return spmv::launch<float>(as_stream(stream), idx_base, m, rowptr, colind, val, x, y, alpha,
-                               beta);
+        return spmv::launch<double>(as_stream(stream), idx_base, m, nnz, rowptr, colind, val, x,
+                                    y, alpha, beta);
+    return spmv::launch<float>(as_stream(stream), idx_base, m, nnz, rowptr, colind, val, x, y,
+                               alpha, beta);
 }
 
 struct jlb_spmv_plan_s {
@@ -271,7 +216,7 @@ struct jlb_spmv_plan_s {
     int64_t m, n, nnz;
     const int32_t *rowptr, *colind;
     int64_t max_row;
-    int64_t wide_tiles;
+    int64_t long_rows;
     int variant;
 };
 
@@ -295,8 +240,8 @@ extern "C" JLB_API int jlb_spmv_plan_create(jlb_spmv_plan *plan, void *stream, i
     p->dtype = dtype; p->base = idx_base; p->m = m; p->n = n; p->nnz = nnz;
     p->rowptr = rowptr; p->colind = colind;
     p->max_row = stats[0];
-    p->wide_tiles = stats[1];
-    p->variant = (stats[0] <= spmv::kShortMax && stats[1] == 0) ? 0 : 1;
+    p->long_rows = stats[1];
+    p->variant = stats[1] == 0 ? 0 : 1;
     *plan = p;
     return ok();
 }
@@ -307,10 +252,10 @@ extern "C" JLB_API int jlb_spmv_plan_execute(jlb_spmv_plan p, void *stream, cons
     int st = spmv_args(p->dtype, p->base, p->m, p->n, p->nnz, p->rowptr, p->colind, val, x, y);
     if (st) return st;
     if (p->dtype == JLB_F64)
-        return spmv::launch<double>(as_stream(stream), p->base, p->m, p->rowptr, p->colind, val,
-                                    x, y, alpha, beta);
-    return spmv::launch<float>(as_stream(stream), p->base, p->m, p->rowptr, p->colind, val, x, y,
-                               alpha, beta);
+        return spmv::launch<double>(as_stream(stream), p->base, p->m, p->nnz, p->rowptr,
+                                    p->colind, val, x, y, alpha, beta);
+    return spmv::launch<float>(as_stream(stream), p->base, p->m, p->nnz, p->rowptr, p->colind,
+                               val, x, y, alpha, beta);
 }
 
 extern "C" JLB_API int jlb_spmv_plan_info(jlb_spmv_plan p, int64_t *max_row, double *mean_row,

@@ -64,8 +64,7 @@ def test_long_rows_within_tolerance(dtype):
     got = run_spmv(rp, ci, val, x, m, n, 0, alpha=2.0)
     ref, bound = O.spmv_ref64(rp, ci, val, x, alpha=2.0)
     assert_within(got, ref, bound, TOL[dtype])
-    # rows of up to 32 entries are summed by one thread in storage order, from
-    # shared memory or (in tiles too large to stage) from global memory alike
+    # rows of up to 32 entries are summed by one thread in storage order
     short = np.diff(rp) <= 32
     exact = O.spmv(rp, ci, val, x, alpha=2.0)
     assert np.array_equal(got[short], exact[short])
