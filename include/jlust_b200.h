@@ -191,6 +191,22 @@ JLB_API size_t jlb_scan_workspace_size(int64_t n);
 JLB_API int jlb_exclusive_scan_i32(void *stream, int64_t n, const int32_t *counts, int32_t *out,
                                    int idx_base, void *workspace, size_t workspace_bytes);
 
+/* Allocation-free variant of jlb_exclusive_scan_i32, with no counterpart in
+ * the reference.  It is for callers that cannot call cudaMalloc -- for
+ * example code that must not re-enter a memory pool (Julia finalizers and
+ * callbacks run while CUDA.jl's allocator may be busy) or that runs on a
+ * device whose memory is entirely handed to another allocator.  Its scratch
+ * is a static 128 KB device array inside the library (present on every GPU
+ * that loads it, until the process exits), so n is limited to 33,554,432
+ * counts; larger n fails with JLB_ERR_INVALID_ARGUMENT.  The first call on a
+ * device looks up that array's device address (cudaGetSymbolAddress), so
+ * make the first call on each device before any stream capture.  All calls
+ * share the one array: calls that may run concurrently on the GPU (other
+ * streams, other host threads) race and must be serialised by the caller.
+ * Same result and semantics as jlb_exclusive_scan_i32; allocates nothing. */
+JLB_API int jlb_exclusive_scan_i32_noalloc(void *stream, int64_t n, const int32_t *counts,
+                                           int32_t *out, int idx_base);
+
 /* CSR -> BSRRight((b1, b2)) on the GPU, bit-exact with JLUST's convert_format
  * (src/convert.jl:302-388) using the block-row level extent ceil(m/b1):
  * explicit zeros dropped, block columns ascending, b1 x b2 row-major tiles

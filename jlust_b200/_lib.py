@@ -45,6 +45,7 @@ SIGNATURES = {
                           _d, _d]),
     "jlb_scan_workspace_size": (_sz, [_i64]),
     "jlb_exclusive_scan_i32": (_i, [_p, _i64, _p, _p, _i, _p, _sz]),
+    "jlb_exclusive_scan_i32_noalloc": (_i, [_p, _i64, _p, _p, _i]),
     "jlb_csr_to_bsr_workspace_size": (_sz, [_i64, _i64, _i64, _i, _i]),
     "jlb_csr_to_bsr_count": (_i, [_p, _i, _i, _i64, _i64, _i64, _p, _p, _p, _i, _i, _p, _pi64,
                                   _p, _sz]),

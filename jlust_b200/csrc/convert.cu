@@ -20,6 +20,8 @@
 // writes the winner's value.
 #include "common.cuh"
 
+#include <mutex>
+
 namespace jlb {
 
 JLB_DEFINE_DEV_ERROR(convert)
@@ -611,4 +613,60 @@ extern "C" JLB_API int jlb_coo_to_bsr_fill(void *stream, int dtype, int idx_base
         browptr, bcolind, bval, winner);
     JLB_LAUNCH_CHECK("fill_blocks");
     return ok();
+}
+
+// ------------------------------------------------- allocation-free scan
+// A variant of jlb_exclusive_scan_i32 for callers that cannot allocate device
+// memory: its scratch (one int64 partial sum per 2048 counts) lives in this
+// file-scope device array instead of a caller workspace.  The array exists on
+// every GPU that loads the library, for the life of the process.
+namespace jlb {
+namespace conv {
+
+constexpr int64_t kNoAllocTiles = 16384;                    // 128 KB of scratch
+constexpr int64_t kNoAllocMaxN = kNoAllocTiles * kScanTile; // 33,554,432 counts
+
+static __device__ __align__(256) int64_t g_scan_noalloc_sums[kNoAllocTiles];
+
+// Device address of g_scan_noalloc_sums on the current device.  The name of
+// the array is only a host-side stand-in, so the address is looked up once
+// per device (with that device current) and cached.
+static int noalloc_scratch(void **ptr) {
+    constexpr int kMaxDevices = 64;
+    static void *cache[kMaxDevices] = {nullptr};
+    static std::mutex mu;
+    int dev = 0;
+    JLB_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kMaxDevices) return fail(JLB_ERR_DEVICE_MISMATCH, "device %d out of range", dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (!cache[dev]) {
+        void *p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_scan_noalloc_sums);
+        if (e != cudaSuccess) return cuda_check(e, "cudaGetSymbolAddress(g_scan_noalloc_sums)");
+        cache[dev] = p;
+    }
+    *ptr = cache[dev];
+    return JLB_OK;
+}
+
+}  // namespace conv
+}  // namespace jlb
+
+extern "C" JLB_API int jlb_exclusive_scan_i32_noalloc(void *stream, int64_t n,
+                                                      const int32_t *counts, int32_t *out,
+                                                      int idx_base) {
+    if (n < 0) return fail(JLB_ERR_INVALID_ARGUMENT, "negative length");
+    if (n > conv::kNoAllocMaxN)
+        return fail(JLB_ERR_INVALID_ARGUMENT,
+                    "jlb_exclusive_scan_i32_noalloc: n = %lld exceeds the static scratch limit of "
+                    "%lld counts; use jlb_exclusive_scan_i32 with a workspace",
+                    (long long)n, (long long)conv::kNoAllocMaxN);
+    if (!out || (n > 0 && !counts)) return fail(JLB_ERR_INVALID_ARGUMENT, "null buffer");
+    void *scratch = nullptr;
+    int r = conv::noalloc_scratch(&scratch);
+    if (r) return r;
+    // Every partial sum the kernels read is written earlier in the same call,
+    // so the scratch needs no clearing between calls.
+    return conv::scan(as_stream(stream), n, counts, out, idx_base, scratch,
+                      (size_t)conv::kNoAllocTiles * sizeof(int64_t));
 }
