@@ -8,9 +8,10 @@
 // sum runs over the row's entries in storage order with separately rounded
 // products and sums: the same operations as JLUST's Tiled SpMM body
 // (ext/KernelAbstractionsExt/ops/spmm.jl:272-292), hence bit-identical.
-// Rows longer than kLong entries are split into 16 contiguous segments, one
-// per group of the CTA, whose partial sums are added in segment order
-// (deterministic, within tolerance).  No atomics touch C.
+// Groups run independently (no block barriers), one row each.  Rows longer
+// than kLong entries go to a second kernel that splits each into 16
+// contiguous segments, one per group of a CTA, whose partial sums are added
+// in segment order (deterministic, within tolerance).  No atomics touch C.
 //
 // Generic path (any order / alignment): one thread per output element, the
 // same storage-order sum.
@@ -25,7 +26,6 @@ namespace spmm {
 constexpr int kThreads = 256;
 constexpr int kGroup = 16;                     // lanes per row
 constexpr int kGroups = kThreads / kGroup;     // rows in flight per CTA
-constexpr int kRowsPerTile = 64;
 constexpr int kLong = 256;                     // longer rows use the whole CTA
 
 template <typename T>
@@ -116,6 +116,10 @@ __device__ __forceinline__ void store_chunk(T *C, int64_t ldc, int64_t row, int6
     *dst = out;
 }
 
+// Short rows: one 16-lane group per row, no block-level synchronisation
+// (rows of a power-law matrix differ widely in length, and a barrier would
+// make every group of a CTA wait for its slowest row).  Rows longer than
+// kLong are left to spmm_long_rows.
 template <typename T, bool kBeta>
 __global__ void __launch_bounds__(kThreads)
 spmm_rowmajor(int64_t m, int64_t k, const int32_t *__restrict__ rowptr,
@@ -124,43 +128,54 @@ spmm_rowmajor(int64_t m, int64_t k, const int32_t *__restrict__ rowptr,
               T beta, int base) {
     constexpr int E = V16<T>::E;
     constexpr int CW = kGroup * E;  // columns per chunk
-    __shared__ int32_t s_rp[kRowsPerTile + 1];
-    __shared__ int32_t s_long[kRowsPerTile];
+    const int tid = threadIdx.x;
+    const int lane = tid % kGroup;
+    const unsigned gmask = (tid % kWarp < kGroup) ? 0x0000ffffu : 0xffff0000u;
+    const int64_t r = (int64_t)blockIdx.x * kGroups + tid / kGroup;
+    if (r >= m) return;
+    const int lo = ldg(rowptr + r) - base, hi = ldg(rowptr + r + 1) - base;
+    if (hi - lo > kLong) return;
+    for (int64_t c0 = 0; c0 < k; c0 += CW) {
+        const int64_t col0 = c0 + (int64_t)lane * E;
+        const bool width_ok = col0 < k;
+        T acc[E];
+#pragma unroll
+        for (int e = 0; e < E; ++e) acc[e] = T(0);
+        group_accumulate<T>(acc, lo, hi, colind, val, B, ldb, col0, width_ok, base, gmask, lane);
+        if (width_ok) store_chunk<T, kBeta>(C, ldc, r, col0, acc, alpha, beta);
+    }
+}
+
+constexpr int kScanRows = 4096;   // rows a long-row CTA inspects
+
+// Long rows: each CTA inspects kScanRows rows and computes every row longer
+// than kLong with all 16 groups, one contiguous segment each, the partial
+// sums added in segment order (deterministic).
+template <typename T, bool kBeta>
+__global__ void __launch_bounds__(kThreads)
+spmm_long_rows(int64_t m, int64_t k, const int32_t *__restrict__ rowptr,
+               const int32_t *__restrict__ colind, const T *__restrict__ val,
+               const T *__restrict__ B, int64_t ldb, T *__restrict__ C, int64_t ldc, T alpha,
+               T beta, int base) {
+    constexpr int E = V16<T>::E;
+    constexpr int CW = kGroup * E;
+    __shared__ int64_t s_long[kScanRows];
     __shared__ int s_nlong;
     __shared__ T s_part[kGroups][CW];
-
     const int tid = threadIdx.x;
     const int g = tid / kGroup, lane = tid % kGroup;
     const unsigned gmask = (tid % kWarp < kGroup) ? 0x0000ffffu : 0xffff0000u;
-    const int64_t r0 = (int64_t)blockIdx.x * kRowsPerTile;
-    const int nrows = (int)((m - r0) < kRowsPerTile ? (m - r0) : kRowsPerTile);
-    for (int i = tid; i <= nrows; i += kThreads) s_rp[i] = rowptr[r0 + i] - base;
+    const int64_t r0 = (int64_t)blockIdx.x * kScanRows;
     if (tid == 0) s_nlong = 0;
     __syncthreads();
-
-    // Phase A: one 16-lane group per row.
-    for (int t = g; t < nrows; t += kGroups) {
-        const int lo = s_rp[t], hi = s_rp[t + 1];
-        if (hi - lo > kLong) {
-            if (lane == 0) s_long[atomicAdd(&s_nlong, 1)] = t;
-            continue;
-        }
-        for (int64_t c0 = 0; c0 < k; c0 += CW) {
-            const int64_t col0 = c0 + (int64_t)lane * E;
-            const bool width_ok = col0 < k;
-            T acc[E];
-#pragma unroll
-            for (int e = 0; e < E; ++e) acc[e] = T(0);
-            group_accumulate<T>(acc, lo, hi, colind, val, B, ldb, col0, width_ok, base, gmask, lane);
-            if (width_ok) store_chunk<T, kBeta>(C, ldc, r0 + t, col0, acc, alpha, beta);
-        }
+    for (int i = tid; i < kScanRows && r0 + i < m; i += kThreads) {
+        const int64_t r = r0 + i;
+        if (ldg(rowptr + r + 1) - ldg(rowptr + r) > kLong) s_long[atomicAdd(&s_nlong, 1)] = r;
     }
     __syncthreads();
-
-    // Phase B: long rows, 16 contiguous segments summed in segment order.
     for (int i = 0; i < s_nlong; ++i) {
-        const int t = s_long[i];
-        const int lo = s_rp[t], hi = s_rp[t + 1];
+        const int64_t r = s_long[i];
+        const int lo = ldg(rowptr + r) - base, hi = ldg(rowptr + r + 1) - base;
         const int seg = (hi - lo + kGroups - 1) / kGroups;
         const int slo = lo + g * seg < hi ? lo + g * seg : hi;
         const int shi = slo + seg < hi ? slo + seg : hi;
@@ -181,7 +196,7 @@ spmm_rowmajor(int64_t m, int64_t k, const int32_t *__restrict__ rowptr,
                     tot[e] = s_part[0][lane * E + e];
                     for (int q = 1; q < kGroups; ++q) tot[e] = add_rn(tot[e], s_part[q][lane * E + e]);
                 }
-                store_chunk<T, kBeta>(C, ldc, r0 + t, col0, tot, alpha, beta);
+                store_chunk<T, kBeta>(C, ldc, r, col0, tot, alpha, beta);
             }
             __syncthreads();
         }
@@ -225,13 +240,19 @@ int launch(cudaStream_t st, int base, int64_t m, int64_t k, const int32_t *rowpt
     const bool fast = b_order == JLB_ROW_MAJOR && c_order == JLB_ROW_MAJOR && k % E == 0 &&
                       ldb % E == 0 && ldc % E == 0 && aligned16(B) && aligned16(C);
     if (fast) {
-        const unsigned grid = (unsigned)ceil_div(m, kRowsPerTile);
-        if (b == T(0))
+        const unsigned grid = (unsigned)ceil_div(m, kGroups);
+        const unsigned grid_long = (unsigned)ceil_div(m, kScanRows);
+        if (b == T(0)) {
             spmm_rowmajor<T, false><<<grid, kThreads, 0, st>>>(m, k, rowptr, colind, (const T *)val,
                                                                (const T *)B, ldb, (T *)C, ldc, a, b, base);
-        else
+            spmm_long_rows<T, false><<<grid_long, kThreads, 0, st>>>(
+                m, k, rowptr, colind, (const T *)val, (const T *)B, ldb, (T *)C, ldc, a, b, base);
+        } else {
             spmm_rowmajor<T, true><<<grid, kThreads, 0, st>>>(m, k, rowptr, colind, (const T *)val,
                                                               (const T *)B, ldb, (T *)C, ldc, a, b, base);
+            spmm_long_rows<T, true><<<grid_long, kThreads, 0, st>>>(
+                m, k, rowptr, colind, (const T *)val, (const T *)B, ldb, (T *)C, ldc, a, b, base);
+        }
         JLB_LAUNCH_CHECK("spmm_rowmajor");
     } else {
         const int64_t total = m * k;
