@@ -47,7 +47,9 @@ def parse_args():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--workload", default="laplacian",
                    choices=["laplacian", "spmv1", "spmm", "sddmm", "bsr", "convert"])
-    p.add_argument("--exchange", choices=["halo", "allgather"], default="halo")
+    p.add_argument("--exchange", choices=["p2p", "halo", "allgather"], default="p2p",
+                   help="p2p: halo fused into the SpMV kernel over NVLink (default); "
+                        "halo: NCCL send/recv; allgather: NCCL all-gather of x")
     p.add_argument("--grid", type=int, default=4096, help="Laplacian grid width")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
@@ -242,21 +244,39 @@ class Laplacian:
         self.A = J.csr_tensor(self.rowptr, self.colind, self.val, (self.R, self.R + 2 * g), origin=0)
         self.x0 = np.random.default_rng(1).uniform(-1.0, 1.0, size=self.n)
         interior = D.interior_rows(rp, lci, self.R, g) if ctx.world > 1 else (0, self.R)
-        self.halo = D.HaloSpMV(self.R, g, self._spmv_rows, dev, mode=ctx.args.exchange,
-                               interior=interior)
-        self.launches_per_step = sum(1 for a, b in ((0, interior[0]), interior, (interior[1], self.R))
-                                     if b > a) if ctx.world > 1 and ctx.args.exchange == "halo" else 1
+        self.p2p = ctx.world > 1 and ctx.args.exchange == "p2p"
+        if self.p2p:
+            self.halo = D.P2PHaloSpMV(self.R, g, self.rowptr, self.colind, self.val, interior, dev)
+            self.launches_per_step = 1
+            self.kernel = "halo_step"
+        else:
+            self.halo = D.HaloSpMV(self.R, g, self._spmv_rows, dev, mode=ctx.args.exchange,
+                                   interior=interior)
+            self.launches_per_step = sum(
+                1 for a, b in ((0, interior[0]), interior, (interior[1], self.R)) if b > a
+            ) if ctx.world > 1 and ctx.args.exchange == "halo" else 1
         self.reset()
 
     def reset(self):
+        """x = x0 on every rank; all ranks call it together, between steps."""
         import torch
         g, r0, r1 = self.g, self.r0, self.r1
         buf = np.zeros(self.R + 2 * g)
         lo, hi = max(r0 - g, 0), min(r1 + g, self.n)
         buf[lo - (r0 - g):hi - (r0 - g)] = self.x0[lo:hi]
-        self.halo.cur = 0
+        self.ctx.barrier()
+        if self.p2p:
+            self.halo.step_no = 0
+            self.halo.flags.zero_()
+        else:
+            self.halo.cur = 0
         self.halo.bufs[0].copy_(torch.from_numpy(buf))
         self.halo.bufs[1].zero_()
+        self.ctx.barrier()
+
+    def close(self):
+        if self.p2p:
+            self.halo.close()
 
     def _spmv_rows(self, lo, hi, x, y):
         """Rows [lo, hi) through the C ABI (row-range view of the local CSR)."""
@@ -282,7 +302,9 @@ class Laplacian:
         return {"workload": f"cfg2: CSR SpMV fp64, 2D 5-point Laplacian {self.g}x{self.g} "
                             f"(n={self.n}, nnz={self.nnz_total}), x <- A x per step",
                 "n": self.n, "nnz": self.nnz_total, "partition": f"rows/{self.ctx.world}",
-                "exchange": "none" if self.ctx.world == 1 else self.ctx.args.exchange,
+                "exchange": "none" if self.ctx.world == 1 else
+                ("halo fused into the SpMV kernel over NVLink peer memory" if self.p2p
+                 else self.ctx.args.exchange),
                 "l2": "inputs larger than L2 (1.34 GB per iteration), no flush"}
 
     # end to end through the public API: x from pinned host memory, y back to it
@@ -296,6 +318,13 @@ class Laplacian:
 
     def e2e_step(self):
         J, h, g, R = self.J, self.halo, self.g, self.R
+        if self.p2p:
+            t = h.step_no
+            h.bufs[t % 2][g:g + R].copy_(self.hx[self.hcur], non_blocking=True)
+            y = h.step()
+            self.hx[1 - self.hcur].copy_(y[g:g + R], non_blocking=True)
+            self.hcur = 1 - self.hcur
+            return
         x, y = h.bufs[h.cur], h.bufs[1 - h.cur]
         x[g:g + R].copy_(self.hx[self.hcur], non_blocking=True)
         if self.ctx.world > 1:
@@ -692,7 +721,10 @@ def run_ours(args):
     eff_gbs = W.bytes() * K / secs / 1e9
     pk = peaks()
     per_launch_s = secs / K
-    traffic = profile_traffic(f"{W.kernel}_{args.workload}")
+    traffic = profile_traffic(f"spmv_rows_{args.workload}" if W.kernel == "halo_step"
+                              else f"{W.kernel}_{args.workload}")
+    if traffic is not None and ctx.world > 1:
+        traffic /= ctx.world        # the capture is of the 1-GPU launch; rows split evenly
     if getattr(W, "bound", "hbm") == "tensor":
         achieved = W.flops() / per_launch_s / 1e12
         roof = {"bound": "tensor", "kernel": W.kernel, "achieved": round(achieved, 2),
@@ -741,6 +773,8 @@ def run_ours(args):
             "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches, "clocks": clocks}
     if ctx.rank == 0:
         print(json.dumps(line), flush=True)
+    if hasattr(W, "close"):
+        W.close()
     ctx.close()
 
 

@@ -15,7 +15,8 @@ Every row's sum is formed exactly as on one GPU (same entries, same order),
 so the partitioned iteration is bit-identical to the single-GPU one.
 
 `allgather` exchange mode replaces the halo exchange by an all-gather of the
-whole x for comparison.
+whole x for comparison.  P2PHaloSpMV fuses the exchange into the SpMV kernel
+over NVLink peer memory (one launch per step, no collective library).
 """
 from __future__ import annotations
 
@@ -132,3 +133,106 @@ class HaloSpMV:
                 self.spmv(i1, self.R, x, y)
         self.cur = 1 - self.cur
         return self.bufs[self.cur]
+
+
+class P2PHaloSpMV:
+    """Distributed x <- A x with the halo exchange fused into the SpMV kernel
+    (jlb_halo_spmv_step): each step is one launch per GPU that computes the
+    local rows, stores the boundary results straight into the neighbours'
+    halo buffers over NVLink (CUDA IPC peer pointers) and publishes them with
+    a system-scope release flag; the neighbour's boundary rows wait for it.
+    No host synchronisation and no collective library on the data path.
+
+    rowptr / colind / val are the local CSR on this rank's GPU (columns in
+    halo-buffer coordinates); interior = (lo, hi) local rows reading no halo.
+    """
+
+    def __init__(self, R: int, h: int, rowptr, colind, val, interior, device, group=None,
+                 timeout_s: float = 2.0):
+        import ctypes as C
+
+        from . import _lib
+        self.C, self._lib = C, _lib
+        self.R, self.h = R, h
+        self.rowptr, self.colind, self.val = rowptr, colind, val
+        self.dtype = {torch.float64: _lib.F64, torch.float32: _lib.F32}[val.dtype]
+        self.interior = interior
+        self.device = torch.device(device)
+        self.group = group
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.timeout_ns = int(timeout_s * 1e9)
+        self.bufs = [torch.zeros(R + 2 * h, dtype=val.dtype, device=self.device) for _ in range(2)]
+        self.flags = torch.zeros(4, dtype=torch.int32, device=self.device)
+        self.step_no = 0
+        self._opened = []
+        self._bases = {}
+        self.lower = self.upper = None   # (bufs ptrs [2], flags ptr) of neighbours
+        if self.world > 1:
+            mine = [self._handle(t) for t in (*self.bufs, self.flags)]
+            allh = [None] * self.world
+            dist.all_gather_object(allh, mine, group=group)
+            torch.cuda.synchronize(self.device)
+            if self.rank > 0:
+                self.lower = self._open(allh[self.rank - 1])
+            if self.rank < self.world - 1:
+                self.upper = self._open(allh[self.rank + 1])
+            dist.barrier(group=group)
+
+    def _handle(self, t):
+        C = self.C
+        hbuf = (C.c_char * 64)()
+        off = C.c_uint64()
+        self._lib.call("jlb_ipc_handle", C.c_void_p(t.data_ptr()), hbuf, C.byref(off))
+        return bytes(hbuf), off.value
+
+    def _open(self, handles):
+        # Several tensors may share one allocation, hence one handle: map each
+        # allocation once.
+        C = self.C
+        ptrs = []
+        for hb, off in handles:
+            if hb not in self._bases:
+                base = C.c_void_p()
+                self._lib.call("jlb_ipc_open", C.c_char_p(hb), C.byref(base))
+                self._bases[hb] = base.value
+                self._opened.append(base.value)
+            ptrs.append(self._bases[hb] + off)
+        return ptrs[:2], ptrs[2]
+
+    @property
+    def x(self) -> torch.Tensor:
+        return self.bufs[self.step_no % 2]
+
+    def own(self, buf=None) -> torch.Tensor:
+        b = self.x if buf is None else buf
+        return b[self.h:self.h + self.R]
+
+    def step(self):
+        C = self.C
+        t = self.step_no
+        cur, nxt = self.bufs[t % 2], self.bufs[(t + 1) % 2]
+        lower_next = C.c_void_p(self.lower[0][(t + 1) % 2]) if self.lower else C.c_void_p(0)
+        upper_next = C.c_void_p(self.upper[0][(t + 1) % 2]) if self.upper else C.c_void_p(0)
+        lower_flag = C.c_void_p(self.lower[1] + 4) if self.lower else C.c_void_p(0)
+        upper_flag = C.c_void_p(self.upper[1]) if self.upper else C.c_void_p(0)
+        st = C.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
+        self._lib.call("jlb_halo_spmv_step", st, self.dtype, 0, self.R, self.h, self.interior[0],
+                       self.interior[1], C.c_void_p(self.rowptr.data_ptr()),
+                       C.c_void_p(self.colind.data_ptr()), C.c_void_p(self.val.data_ptr()),
+                       C.c_void_p(cur.data_ptr()), C.c_void_p(nxt.data_ptr()), lower_next,
+                       upper_next, C.c_void_p(self.flags.data_ptr()), lower_flag, upper_flag, t,
+                       self.timeout_ns)
+        self.step_no += 1
+        return nxt
+
+    def close(self):
+        """Unmap the neighbours' buffers; call on every rank, between steps."""
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        for base in self._opened:
+            self._lib.call("jlb_ipc_close", self.C.c_void_p(base))
+        self._opened = []
+        self._bases = {}
+        self.lower = self.upper = None

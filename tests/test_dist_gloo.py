@@ -1,0 +1,84 @@
+"""Row-partitioned Laplacian iteration with halo exchange (jlust_b200/dist.py)
+on two CPU ranks over gloo; the local SpMV is the oracle, so the check is
+that partitioning and exchange reproduce the single-process iteration bit
+for bit, in both exchange modes."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+G = 48          # grid width: n = 2304 rows, halo = 48
+ITERS = 6
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, mode, out_dir):
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    from jlust_b200 import dist as D
+    from jlust_b200 import synth
+    from oracle import oracle as O
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        n = G * G
+        r0, r1 = D.partition_rows(n, world, rank, align=G)
+        R = r1 - r0
+        rp, ci, val = synth.laplacian_rows(G, r0, r1)
+        lci = (ci.astype(np.int64) - (r0 - G)).astype(np.int32)
+        x0 = np.random.default_rng(1).uniform(-1, 1, n)
+
+        def spmv(lo, hi, x, y):
+            y[G + lo:G + hi] = torch.from_numpy(O.spmv(rp[lo:hi + 1], lci, val, x.numpy()))
+
+        interior = D.interior_rows(rp, lci, R, G)
+        h = D.HaloSpMV(R, G, spmv, "cpu", mode=mode, interior=interior)
+        buf = np.zeros(R + 2 * G)
+        lo, hi = max(r0 - G, 0), min(r1 + G, n)
+        buf[lo - (r0 - G):hi - (r0 - G)] = x0[lo:hi]
+        h.bufs[0].copy_(torch.from_numpy(buf))
+        for _ in range(ITERS):
+            h.step()
+        np.save(os.path.join(out_dir, f"x{rank}.npy"), h.own().numpy())
+        np.save(os.path.join(out_dir, f"interior{rank}.npy"), np.array(interior))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("mode", ["halo", "allgather"])
+def test_two_rank_laplacian_matches_single(tmp_path, mode):
+    from jlust_b200 import synth
+    from oracle import oracle as O
+    O.build()
+    world = 2
+    mp.start_processes(_worker, args=(world, _free_port(), mode, str(tmp_path)), nprocs=world,
+                       start_method="spawn", join=True)
+    got = np.concatenate([np.load(tmp_path / f"x{r}.npy") for r in range(world)])
+    rp, ci, val = synth.laplacian_2d(G)
+    x = np.random.default_rng(1).uniform(-1, 1, G * G)
+    for _ in range(ITERS):
+        x = O.spmv(rp, ci, val, x)
+    assert np.array_equal(got, x)
+    # interior rows exclude exactly the first and last grid line of each rank
+    for r in range(world):
+        i0, i1 = np.load(tmp_path / f"interior{r}.npy")
+        assert (i0, i1) == ((G if r > 0 else 0), (G * G // world - G if r < world - 1 else G * G // world))
+
+
+def test_partition_rows():
+    from jlust_b200 import dist as D
+    n, g = 4096 * 4096, 4096
+    spans = [D.partition_rows(n, 8, r, align=g) for r in range(8)]
+    assert spans[0][0] == 0 and spans[-1][1] == n
+    assert all(b == c for (_, b), (c, _) in zip(spans, spans[1:]))
+    assert all((b - a) % g == 0 for a, b in spans)
