@@ -131,11 +131,14 @@ class ClockSampler:
                 pass
             time.sleep(self.period)
 
-    def __enter__(self):
-        if self.h is not None:
+    def start(self):
+        if self.h is not None and self._t is None:
             self._t = threading.Thread(target=self._run, daemon=True)
             self._t.start()
         return self
+
+    def __enter__(self):
+        return self.start()
 
     def __exit__(self, *a):
         if self._t is not None:
@@ -200,8 +203,11 @@ def timed(ctx, fn, steps, stream):
     torch = ctx.torch
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
+    # NVML set-up and the sampling thread start before the barrier, so every
+    # rank enters the timed region together.
+    clk = ClockSampler(ctx.device).start()
     ctx.barrier()
-    with ClockSampler(ctx.device) as clk:
+    with clk:
         start.record(stream)
         for _ in range(steps):
             fn()
@@ -290,6 +296,13 @@ class Laplacian:
 
     def step(self):
         self.halo.step()
+
+    def run_steps(self, k):
+        if self.p2p:
+            self.halo.steps(k)
+        else:
+            for _ in range(k):
+                self.halo.step()
 
     # algorithmic work, whole job, per step (bench_suitesparse.jl:170-172 form)
     def flops(self):
@@ -675,8 +688,9 @@ def timed_flushed(ctx, fn, steps, stream):
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=ctx.device)
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(steps)]
+    clk = ClockSampler(ctx.device).start()
     ctx.barrier()
-    with ClockSampler(ctx.device) as clk:
+    with clk:
         for a, b in evs:
             flush.zero_()
             a.record(stream)
@@ -714,6 +728,9 @@ def run_ours(args):
     K = args.steps
     if getattr(W, "flush_l2", False):
         secs, clocks = timed_flushed(ctx, W.step, K, stream)
+    elif hasattr(W, "run_steps"):
+        # K launches enqueued by one ABI call (no per-step host overhead)
+        secs, clocks = timed(ctx, lambda: W.run_steps(K), 1, stream)
     else:
         secs, clocks = timed(ctx, W.step, K, stream)
     J.device_status()

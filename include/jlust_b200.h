@@ -245,29 +245,31 @@ JLB_API int jlb_coo_to_bsr_fill(void *stream, int dtype, int idx_base, int64_t m
 
 /* ------------------------------------- row-partitioned SpMV (multi-GPU) */
 
-/* One step x <- A x of a row-partitioned iteration, fused with its halo
- * exchange over NVLink peer memory (one process per GPU).  No counterpart in
- * the reference, which has no multi-GPU layer; it serves the row-partitioned
- * 2-D Laplacian configuration.
+/* Steps first_step .. first_step+nsteps-1 of x <- A x for a row-partitioned
+ * iteration, each fused with its halo exchange over NVLink peer memory (one
+ * process per GPU, one kernel launch per step).  No counterpart in the
+ * reference, which has no multi-GPU layer; it serves the row-partitioned 2-D
+ * Laplacian configuration.
  * This rank owns R rows of A (CSR, columns shifted into the halo buffer) and
- * keeps x in two buffers of R + 2h values laid out [lower halo | own | upper
- * halo]; step t (counting from 0, one call per step) reads x_cur = buffer t%2
- * and writes the own part of x_next = buffer (t+1)%2.  Rows [interior_lo,
- * interior_hi) must read no halo entry.  lower_next / upper_next are the
- * neighbours' buffers (t+1)%2 (peer pointers from jlb_ipc_open), or NULL at
- * the ends; the first h own results are also stored into the lower
- * neighbour's upper halo and the last h into the upper neighbour's lower
- * halo.  my_flags is this rank's int[4] (zeroed once before step 0):
- * [published by lower, published by upper, internal, internal];
- * lower_flag = &lower neighbour's my_flags[1], upper_flag = &upper
- * neighbour's my_flags[0].  Boundary rows wait (at most timeout_ns of GPU
- * time) for the neighbour's step-t publication; on expiry the device error
- * word reports JLB_ERR_DEVICE_TIMEOUT through jlb_device_status(). */
-JLB_API int jlb_halo_spmv_step(void *stream, int dtype, int idx_base, int64_t R, int64_t h,
-                               int64_t interior_lo, int64_t interior_hi, const int32_t *rowptr,
-                               const int32_t *colind, const void *val, const void *x_cur,
-                               void *x_next, void *lower_next, void *upper_next, int *my_flags,
-                               int *lower_flag, int *upper_flag, int step, uint64_t timeout_ns);
+ * keeps x in two buffers x_bufs[0..1] of R + 2h values laid out [lower halo |
+ * own | upper halo]; step t reads x_bufs[t%2] and writes the own part of
+ * x_bufs[(t+1)%2].  Steps count from 0 across calls.  Rows [interior_lo,
+ * interior_hi) must read no halo entry.  lower_bufs / upper_bufs are the
+ * neighbours' two buffers (peer pointers from jlb_ipc_open), or NULL at the
+ * ends: the first h own results of step t are also stored into the lower
+ * neighbour's buffer (t+1)%2 (its upper halo), the last h into the upper
+ * neighbour's (its lower halo).  my_flags is this rank's int[4], zeroed once
+ * before step 0: [published by lower, published by upper, internal,
+ * internal]; lower_flag = &lower neighbour's my_flags[1], upper_flag =
+ * &upper neighbour's my_flags[0].  Boundary rows wait (at most timeout_ns of
+ * GPU time) for the neighbour's publication of step t; on expiry the device
+ * error word reports JLB_ERR_DEVICE_TIMEOUT through jlb_device_status(). */
+JLB_API int jlb_halo_spmv_steps(void *stream, int dtype, int idx_base, int64_t R, int64_t h,
+                                int64_t interior_lo, int64_t interior_hi, const int32_t *rowptr,
+                                const int32_t *colind, const void *val, void *const *x_bufs,
+                                void *const *lower_bufs, void *const *upper_bufs, int *my_flags,
+                                int *lower_flag, int *upper_flag, int first_step, int nsteps,
+                                uint64_t timeout_ns);
 
 /* CUDA IPC for the buffers above (no counterpart in the reference).
  * jlb_ipc_handle writes the 64-byte handle of the allocation containing ptr

@@ -56,8 +56,8 @@ SIGNATURES = {
                                   _p, _sz]),
     "jlb_coo_to_bsr_fill": (_i, [_p, _i, _i, _i64, _i64, _i64, _p, _p, _p, _i, _i, _p, _i64, _p,
                                  _p, _p, _sz]),
-    "jlb_halo_spmv_step": (_i, [_p, _i, _i, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _p,
-                                _p, _p, _p, _i, C.c_uint64]),
+    "jlb_halo_spmv_steps": (_i, [_p, _i, _i, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _p,
+                                 _p, _p, _i, _i, C.c_uint64]),
     "jlb_ipc_handle": (_i, [_p, _p, C.POINTER(C.c_uint64)]),
     "jlb_ipc_open": (_i, [_p, C.POINTER(_p)]),
     "jlb_ipc_close": (_i, [_p]),

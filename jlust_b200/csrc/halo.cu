@@ -21,6 +21,10 @@
 // boundary rows (the only readers of that halo) finished -- so no halo is
 // overwritten while being read.
 //
+// Consecutive steps are launched with programmatic dependent launch: step t+1
+// reads its rows of A while step t drains and waits for step t's completion
+// (griddepcontrol.wait) before reading x.
+//
 // Every wait is bounded (timeout_ns of the GPU's global timer): on expiry the
 // block records DEV_ERR_TIMEOUT, computes with what it has and publishes, so
 // the launch ends and jlb_device_status() reports the failure.
@@ -113,20 +117,50 @@ struct Args {
     uint64_t timeout_ns;
 };
 
+// Programmatic dependent launch: the next step's grid may start while this
+// one drains; it reads its rows of A (independent of x) first and waits for
+// this grid's completion (griddepcontrol.wait) before touching x.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+constexpr int kPre = 8;   // entries per row read before the wait
+
 template <typename T>
 __global__ void __launch_bounds__(kThreads) halo_step(Args a) {
     const T *val = (const T *)a.val;
     const T *x = (const T *)a.x;
     T *y = (T *)a.y;
     const int64_t b = blockIdx.x;
+    pdl_trigger();
     if (b < a.interior_blocks) {
         const int64_t r = a.i0 + b * kThreads + threadIdx.x;
+        int lo = 0, hi = 0;
+        int c[kPre];
+        T v[kPre];
         if (r < a.i1) {
-            const int lo = ldg(a.rowptr + r) - a.base, hi = ldg(a.rowptr + r + 1) - a.base;
-            y[a.h + r] = row_sum_ro<T>(lo, hi, a.colind, val, x, a.base);
+            lo = ldg(a.rowptr + r) - a.base;
+            hi = ldg(a.rowptr + r + 1) - a.base;
+#pragma unroll
+            for (int j = 0; j < kPre; ++j)
+                if (lo + j < hi) {
+                    c[j] = ldg(a.colind + lo + j) - a.base;
+                    v[j] = ldg(val + lo + j);
+                }
+        }
+        pdl_wait();
+        if (r < a.i1) {
+            // storage order: the prefetched entries, then any further ones
+            T acc = T(0);
+#pragma unroll
+            for (int j = 0; j < kPre; ++j)
+                if (lo + j < hi) acc = add_rn(acc, mul_rn(v[j], ldg(x + c[j])));
+            for (int k = lo + kPre; k < hi; ++k)
+                acc = add_rn(acc, mul_rn(ldg(val + k), ldg(x + (ldg(a.colind + k) - a.base))));
+            y[a.h + r] = acc;
         }
         return;
     }
+    pdl_wait();
     // Boundary blocks: side 0 = rows [0, i0) (lower halo), side 1 = [i1, R).
     const int side = (b < a.interior_blocks + a.lower_blocks) ? 0 : 1;
     const int64_t sb = side == 0 ? b - a.interior_blocks : b - a.interior_blocks - a.lower_blocks;
@@ -167,44 +201,62 @@ __global__ void __launch_bounds__(kThreads) halo_step(Args a) {
 
 using namespace jlb;
 
-extern "C" JLB_API int jlb_halo_spmv_step(void *stream, int dtype, int idx_base, int64_t R,
-                                          int64_t h, int64_t interior_lo, int64_t interior_hi,
-                                          const int32_t *rowptr, const int32_t *colind,
-                                          const void *val, const void *x_cur, void *x_next,
-                                          void *lower_next, void *upper_next, int *my_flags,
-                                          int *lower_flag, int *upper_flag, int step,
-                                          uint64_t timeout_ns) {
+extern "C" JLB_API int jlb_halo_spmv_steps(void *stream, int dtype, int idx_base, int64_t R,
+                                           int64_t h, int64_t interior_lo, int64_t interior_hi,
+                                           const int32_t *rowptr, const int32_t *colind,
+                                           const void *val, void *const *x_bufs,
+                                           void *const *lower_bufs, void *const *upper_bufs,
+                                           int *my_flags, int *lower_flag, int *upper_flag,
+                                           int first_step, int nsteps, uint64_t timeout_ns) {
     if (dtype != JLB_F32 && dtype != JLB_F64)
         return fail(JLB_ERR_UNSUPPORTED_VALUE_TYPE, "halo SpMV supports Float32 and Float64");
     if (idx_base != 0 && idx_base != 1) return fail(JLB_ERR_INVALID_ARGUMENT, "idx_base must be 0 or 1");
     if (R < 0 || h < 0 || interior_lo < 0 || interior_hi > R || interior_lo > interior_hi)
         return fail(JLB_ERR_INCOMPATIBLE_EXTENTS, "bad row ranges");
-    if ((interior_lo > 0 && interior_lo < (lower_next ? h : 0)) || (!!lower_next != !!lower_flag) ||
-        (!!upper_next != !!upper_flag))
-        return fail(JLB_ERR_INVALID_ARGUMENT, "neighbour buffer and flag must be given together");
-    if (lower_next && interior_lo < h)
+    if (first_step < 0 || nsteps < 0) return fail(JLB_ERR_INVALID_ARGUMENT, "negative step");
+    if (!x_bufs || !x_bufs[0] || !x_bufs[1])
+        return fail(JLB_ERR_INVALID_ARGUMENT, "x_bufs must hold two buffers");
+    const bool lower = lower_bufs != nullptr, upper = upper_bufs != nullptr;
+    if (lower != (lower_flag != nullptr) || upper != (upper_flag != nullptr))
+        return fail(JLB_ERR_INVALID_ARGUMENT, "neighbour buffers and flag must be given together");
+    if ((lower && (!lower_bufs[0] || !lower_bufs[1])) || (upper && (!upper_bufs[0] || !upper_bufs[1])))
+        return fail(JLB_ERR_INVALID_ARGUMENT, "neighbour buffers must be two pointers");
+    if (lower && interior_lo < h)
         return fail(JLB_ERR_INVALID_ARGUMENT, "rows feeding the lower neighbour must be boundary rows");
-    if (upper_next && R - interior_hi < h)
+    if (upper && R - interior_hi < h)
         return fail(JLB_ERR_INVALID_ARGUMENT, "rows feeding the upper neighbour must be boundary rows");
-    if ((lower_next || upper_next) && R < 2 * h)
+    if ((lower || upper) && R < 2 * h)
         return fail(JLB_ERR_INCOMPATIBLE_EXTENTS, "each rank needs at least 2*h rows");
-    if (R == 0) return ok();
-    if (!rowptr || !colind || !val || !x_cur || !x_next || !my_flags)
-        return fail(JLB_ERR_INVALID_ARGUMENT, "null buffer");
+    if (R == 0 || nsteps == 0) return ok();
+    if (!rowptr || !colind || !val || !my_flags) return fail(JLB_ERR_INVALID_ARGUMENT, "null buffer");
     halo::Args a;
     a.R = R; a.h = h; a.i0 = interior_lo; a.i1 = interior_hi;
     a.interior_blocks = ceil_div(interior_hi - interior_lo, halo::kThreads);
     a.lower_blocks = ceil_div(interior_lo, halo::kThreads);
     a.upper_blocks = ceil_div(R - interior_hi, halo::kThreads);
-    a.rowptr = rowptr; a.colind = colind; a.val = val; a.x = x_cur; a.y = x_next;
-    a.lower_next = lower_next; a.upper_next = upper_next; a.my_flags = my_flags;
+    a.rowptr = rowptr; a.colind = colind; a.val = val; a.my_flags = my_flags;
     a.lower_flag = lower_flag; a.upper_flag = upper_flag;
-    a.step = step; a.base = idx_base; a.timeout_ns = timeout_ns;
+    a.base = idx_base; a.timeout_ns = timeout_ns;
     const int64_t grid = a.interior_blocks + a.lower_blocks + a.upper_blocks;
     cudaStream_t st = as_stream(stream);
-    if (dtype == JLB_F64) halo::halo_step<double><<<(unsigned)grid, halo::kThreads, 0, st>>>(a);
-    else halo::halo_step<float><<<(unsigned)grid, halo::kThreads, 0, st>>>(a);
-    JLB_LAUNCH_CHECK("halo_step");
+    for (int t = first_step; t < first_step + nsteps; ++t) {
+        a.step = t;
+        a.x = x_bufs[t % 2];
+        a.y = x_bufs[(t + 1) % 2];
+        a.lower_next = lower ? lower_bufs[(t + 1) % 2] : nullptr;
+        a.upper_next = upper ? upper_bufs[(t + 1) % 2] : nullptr;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)grid);
+        cfg.blockDim = dim3(halo::kThreads);
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        if (dtype == JLB_F64) JLB_CUDA(cudaLaunchKernelEx(&cfg, halo::halo_step<double>, a));
+        else JLB_CUDA(cudaLaunchKernelEx(&cfg, halo::halo_step<float>, a));
+    }
     return ok();
 }
 

@@ -137,7 +137,7 @@ class HaloSpMV:
 
 class P2PHaloSpMV:
     """Distributed x <- A x with the halo exchange fused into the SpMV kernel
-    (jlb_halo_spmv_step): each step is one launch per GPU that computes the
+    (jlb_halo_spmv_steps): each step is one launch per GPU that computes the
     local rows, stores the boundary results straight into the neighbours'
     halo buffers over NVLink (CUDA IPC peer pointers) and publishes them with
     a system-scope release flag; the neighbour's boundary rows wait for it.
@@ -208,23 +208,31 @@ class P2PHaloSpMV:
         b = self.x if buf is None else buf
         return b[self.h:self.h + self.R]
 
-    def step(self):
+    def _arrays(self):
         C = self.C
-        t = self.step_no
-        cur, nxt = self.bufs[t % 2], self.bufs[(t + 1) % 2]
-        lower_next = C.c_void_p(self.lower[0][(t + 1) % 2]) if self.lower else C.c_void_p(0)
-        upper_next = C.c_void_p(self.upper[0][(t + 1) % 2]) if self.upper else C.c_void_p(0)
-        lower_flag = C.c_void_p(self.lower[1] + 4) if self.lower else C.c_void_p(0)
-        upper_flag = C.c_void_p(self.upper[1]) if self.upper else C.c_void_p(0)
+        P2 = C.c_void_p * 2
+        self._xb = P2(*(b.data_ptr() for b in self.bufs))
+        self._lb = P2(*self.lower[0]) if self.lower else None
+        self._ub = P2(*self.upper[0]) if self.upper else None
+
+    def steps(self, k: int = 1):
+        """Run k iterations (k launches, one ABI call); returns the current x buffer."""
+        C = self.C
+        if not hasattr(self, "_xb"):
+            self._arrays()
         st = C.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
-        self._lib.call("jlb_halo_spmv_step", st, self.dtype, 0, self.R, self.h, self.interior[0],
+        self._lib.call("jlb_halo_spmv_steps", st, self.dtype, 0, self.R, self.h, self.interior[0],
                        self.interior[1], C.c_void_p(self.rowptr.data_ptr()),
                        C.c_void_p(self.colind.data_ptr()), C.c_void_p(self.val.data_ptr()),
-                       C.c_void_p(cur.data_ptr()), C.c_void_p(nxt.data_ptr()), lower_next,
-                       upper_next, C.c_void_p(self.flags.data_ptr()), lower_flag, upper_flag, t,
-                       self.timeout_ns)
-        self.step_no += 1
-        return nxt
+                       self._xb, self._lb, self._ub, C.c_void_p(self.flags.data_ptr()),
+                       C.c_void_p(self.lower[1] + 4) if self.lower else C.c_void_p(0),
+                       C.c_void_p(self.upper[1]) if self.upper else C.c_void_p(0),
+                       self.step_no, k, self.timeout_ns)
+        self.step_no += k
+        return self.bufs[self.step_no % 2]
+
+    def step(self):
+        return self.steps(1)
 
     def close(self):
         """Unmap the neighbours' buffers; call on every rank, between steps."""
@@ -236,3 +244,5 @@ class P2PHaloSpMV:
         self._opened = []
         self._bases = {}
         self.lower = self.upper = None
+        if hasattr(self, "_xb"):
+            del self._xb

@@ -58,9 +58,12 @@ def test_bounded_wait_times_out():
     st = C.c_void_p(torch.cuda.current_stream(0).cuda_stream)
     p = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
     i0, i1 = D.interior_rows(rp, lci, R, g)
-    _lib.call("jlb_halo_spmv_step", st, _lib.F64, 0, R, g, i0, i1, p(d[0]), p(d[1]), p(d[2]),
-              p(bufs[0]), p(bufs[1]), p(fake_peer), C.c_void_p(0), p(flags), p(fake_flag),
-              C.c_void_p(0), 1, int(20e6))     # step 1 needs flag >= 1; limit 20 ms
+    P2 = C.c_void_p * 2
+    xb = P2(bufs[0].data_ptr(), bufs[1].data_ptr())
+    lb = P2(fake_peer.data_ptr(), fake_peer.data_ptr())
+    _lib.call("jlb_halo_spmv_steps", st, _lib.F64, 0, R, g, i0, i1, p(d[0]), p(d[1]), p(d[2]),
+              xb, lb, None, p(flags), p(fake_flag), C.c_void_p(0), 1, 1,
+              int(20e6))     # step 1 needs the lower neighbour's flag >= 1; limit 20 ms
     with pytest.raises(J.DeviceTimeout):
         J.device_status()
     y = torch.zeros(R, dtype=torch.float64, device=DEV)
@@ -70,9 +73,16 @@ def test_bounded_wait_times_out():
 
 def test_argument_checks():
     L = _lib.load()
-    st = L.jlb_halo_spmv_step(None, _lib.F64, 0, 100, 64, 0, 100, None, None, None, None, None,
-                              C.c_void_p(16), None, None, None, None, 0, 1000)
-    assert st != 0
+    P2 = C.c_void_p * 2
+    xb = P2(16, 32)
+    # a neighbour buffer without its flag
+    st = L.jlb_halo_spmv_steps(None, _lib.F64, 0, 200, 64, 64, 136, None, None, None, xb,
+                               P2(16, 32), None, None, None, None, 0, 1, 1000)
+    assert st == 8
+    # rows feeding the lower neighbour declared interior
+    st = L.jlb_halo_spmv_steps(None, _lib.F64, 0, 200, 64, 0, 136, None, None, None, xb,
+                               P2(16, 32), None, None, C.c_void_p(16), None, 0, 1, 1000)
+    assert st == 8
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
