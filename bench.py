@@ -372,16 +372,26 @@ class Single:
     launches_per_step = 1
     bound = "hbm"
 
+    shardable = False
+
     def __init__(self, ctx):
         import torch
 
         import jlust_b200 as J
         from jlust_b200 import synth
-        if ctx.world > 1:
+        if ctx.world > 1 and not self.shardable:
             raise SystemExit(f"workload {ctx.args.workload} runs on one GPU")
         self.ctx, self.J, self.synth, self.torch = ctx, J, synth, torch
         self.dev = ctx.device
+        self.rank, self.world = ctx.rank, ctx.world
         self.setup()
+
+    def shard(self, rowptr):
+        """This rank's rows (balanced by rows + entries) and the rebased CSR
+        pointer of that slice."""
+        from jlust_b200 import dist as D
+        r0, r1 = D.partition_by_nnz(rowptr, self.world, self.rank)
+        return r0, r1, (rowptr[r0:r1 + 1].astype(np.int64) - int(rowptr[r0])).astype(np.int32)
 
     def d(self, a):
         return self.torch.from_numpy(np.ascontiguousarray(a)).to(self.dev)
@@ -396,8 +406,8 @@ class Single:
     def e2e_setup(self):
         self.e2e_inputs = [t.cpu().pin_memory() for t in self.e2e_in()]
         self.e2e_outputs = [self.torch.empty_like(t, device="cpu").pin_memory() for t in self.e2e_out()]
-        self.h2d = sum(t.numel() * t.element_size() for t in self.e2e_inputs)
-        self.d2h = sum(t.numel() * t.element_size() for t in self.e2e_outputs)
+        self.h2d = self.world * sum(t.numel() * t.element_size() for t in self.e2e_inputs)
+        self.d2h = self.world * sum(t.numel() * t.element_size() for t in self.e2e_outputs)
 
     def e2e_step(self):
         for hd, dv in zip(self.e2e_inputs, self.e2e_in()):
@@ -457,7 +467,8 @@ class SpMV1(Single):
 class SpMM(Single):
     """Config 3: CSR SpMM fp32, power-law A (4M x 4M), B 4M x 64 row-major."""
 
-    kernel, dtype = "spmm_rowmajor", "f32"
+    kernel, dtype, shardable = "spmm_stream", "f32", True
+    launches_per_step = 2   # spmm_stream + spmm_long_rows
 
     def setup(self):
         J = self.J
@@ -465,10 +476,13 @@ class SpMM(Single):
         self.h = (rp, ci, val, B)
         self.nnz, self.m = int(rp[-1]), rp.shape[0] - 1
         self.k = B.shape[1]
-        self.deg = np.diff(rp)
-        self.A = J.csr_tensor(self.d(rp), self.d(ci), self.d(val), (self.m, self.m), origin=0)
+        # rows sharded by rows + entries; B replicated on every rank (copied once, untimed)
+        r0, r1, lrp = self.shard(rp)
+        p0, p1 = int(rp[r0]), int(rp[r1])
+        self.A = J.csr_tensor(self.d(lrp), self.d(ci[p0:p1]), self.d(val[p0:p1]), (r1 - r0, self.m),
+                              origin=0)
         self.B = self.d(B)
-        self.C = self.torch.zeros(self.m, self.k, dtype=self.torch.float32, device=self.dev)
+        self.C = self.torch.zeros(r1 - r0, self.k, dtype=self.torch.float32, device=self.dev)
 
     def api_call(self):
         self.J.execute(self.J.SpMMOp, self.A, self.B, self.C)
@@ -491,6 +505,7 @@ class SpMM(Single):
                             f"B {self.m}x{self.k} row-major",
                 "bytes_model": "gather (8 nnz + 4 (m+1) + 256 nnz + 256 m)",
                 "compulsory_bytes": 8.0 * self.nnz + 4.0 * (self.m + 1) + 8.0 * self.k * self.m,
+                "partition": f"rows/{self.world} (balanced by rows + entries), B replicated",
                 "l2": "inputs larger than L2"}
 
     def cpu_setup(self):
@@ -508,7 +523,7 @@ class SpMM(Single):
 class SDDMM(Single):
     """Config 4: SDDMM fp32, 1M x 1M pattern with 32 entries per row, K = 128."""
 
-    kernel, dtype = "sddmm_fast", "f32"
+    kernel, dtype, shardable = "sddmm_fast", "f32", True
 
     def setup(self):
         J = self.J
@@ -516,9 +531,12 @@ class SDDMM(Single):
         self.h = (rp, ci, A, B, S)
         self.nnz, self.m = int(rp[-1]), rp.shape[0] - 1
         self.K = A.shape[1]
-        self.S = self.d(S)
-        self.Cs = J.csr_tensor(self.d(rp), self.d(ci), self.S.clone(), (self.m, self.m), origin=0)
-        self.A, self.Bt = self.d(A), self.d(B)
+        r0, r1, lrp = self.shard(rp)
+        p0, p1 = int(rp[r0]), int(rp[r1])
+        self.S = self.d(S[p0:p1])
+        self.Cs = J.csr_tensor(self.d(lrp), self.d(ci[p0:p1]), self.S.clone(), (r1 - r0, self.m),
+                               origin=0)
+        self.A, self.Bt = self.d(A[r0:r1]), self.d(B)
 
     def api_call(self):
         J = self.J
@@ -541,6 +559,7 @@ class SDDMM(Single):
                             f"entries/row (nnz={self.nnz}), A, B {self.m}x{self.K} N(0,1), "
                             "out = dot(A_i, B_j) * S_ij",
                 "bytes_model": "gather (512 m + 512 nnz + 12 nnz + 4 (m+1))",
+                "partition": f"pattern rows/{self.world}, A rows sharded, B replicated",
                 "l2": "inputs larger than L2"}
 
     def cpu_setup(self):
@@ -562,7 +581,7 @@ class SDDMM(Single):
 class BSR(Single):
     """Config 5: BSR SpMM bf16 -> fp32, 65,536^2 with 64x64 blocks, band +-8 + 2%."""
 
-    kernel, dtype, bound = "bsr_spmm_tc", "bf16 in, f32 accumulate", "tensor"
+    kernel, dtype, bound, shardable = "bsr_spmm_tc", "bf16 in, f32 accumulate", "tensor", True
 
     def setup(self):
         J = self.J
@@ -571,9 +590,12 @@ class BSR(Single):
         self.nnzb, self.mb = bc.shape[0], bp.shape[0] - 1
         self.N = B.shape[1]
         n = self.mb * 64
-        self.A = J.bsr_tensor(self.d(bp), self.d(bc), self.bf(bv), (n, n), (64, 64), origin=0)
+        I0, I1, lbp = self.shard(bp)
+        q0, q1 = int(bp[I0]), int(bp[I1])
+        self.A = J.bsr_tensor(self.d(lbp), self.d(bc[q0:q1]), self.bf(bv[q0 * 4096:q1 * 4096]),
+                              ((I1 - I0) * 64, n), (64, 64), origin=0)
         self.B = self.bf(B)
-        self.C = self.torch.zeros(n, self.N, dtype=self.torch.float32, device=self.dev)
+        self.C = self.torch.zeros((I1 - I0) * 64, self.N, dtype=self.torch.float32, device=self.dev)
 
     def api_call(self):
         self.J.execute(self.J.BlockSpMMOp, self.A, self.B, self.C)
@@ -595,6 +617,7 @@ class BSR(Single):
         return {"workload": f"cfg5: BSR SpMM bf16 (fp32 accumulate), {self.mb * 64}^2 with 64x64 "
                             f"blocks, band +-8 + 2% off-band (nnzb={self.nnzb}), B "
                             f"{self.mb * 64}x{self.N} bf16 row-major",
+                "partition": f"block rows/{self.world} (balanced by rows + blocks), B replicated",
                 "l2": "A values (311 MB) larger than L2; B (33.5 MB) L2-resident by design"}
 
     def cpu_setup(self):

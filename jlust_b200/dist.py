@@ -34,6 +34,24 @@ def partition_rows(n: int, world: int, rank: int, align: int = 1):
     return r0, r1
 
 
+def partition_by_nnz(rowptr: np.ndarray, world: int, rank: int):
+    """Contiguous row range of `rank` with about (m + nnz) / world rows plus
+    entries: each row counts once plus its entries, so power-law rows and
+    empty rows both balance.  Returns (r0, r1)."""
+    rowptr = np.asarray(rowptr, dtype=np.int64)
+    m = rowptr.shape[0] - 1
+    base = int(rowptr[0])
+    work = (rowptr - base) + np.arange(m + 1)
+    total = int(work[-1])
+
+    def cut(k):
+        return int(np.searchsorted(work, total * k / world, side="left"))
+
+    r0 = 0 if rank == 0 else min(cut(rank), m)
+    r1 = m if rank == world - 1 else min(cut(rank + 1), m)
+    return r0, max(r0, r1)
+
+
 def local_csr(rowptr: np.ndarray, colind: np.ndarray, val: np.ndarray, r0: int, r1: int, h: int):
     """Rows [r0, r1) of a global CSR with columns shifted into the local halo
     buffer (column c -> c - (r0 - h)).  Requires every column of those rows to

@@ -82,3 +82,15 @@ def test_partition_rows():
     assert spans[0][0] == 0 and spans[-1][1] == n
     assert all(b == c for (_, b), (c, _) in zip(spans, spans[1:]))
     assert all((b - a) % g == 0 for a, b in spans)
+
+
+def test_partition_by_nnz_balances_power_law():
+    from jlust_b200 import dist as D
+    from jlust_b200 import synth
+    rp, _, _ = synth.power_law(100_000, 100_000, 2.0, 4096, seed=3)
+    for world in (2, 4, 8):
+        spans = [D.partition_by_nnz(rp, world, r) for r in range(world)]
+        assert spans[0][0] == 0 and spans[-1][1] == 100_000
+        assert all(b == c for (_, b), (c, _) in zip(spans, spans[1:]))
+        work = [(rp[b] - rp[a]) + (b - a) for a, b in spans]
+        assert max(work) - min(work) <= 4096 + 2          # at most one long row apart

@@ -91,3 +91,38 @@ def test_power_law_reduced_config3():
     assert_within(got, ref, bound, 1e-5)
     short = np.diff(rp) <= 256
     assert np.array_equal(got[short], O.spmm(rp, ci, val, B)[short])
+
+
+@pytest.mark.parametrize("pattern", ["empty", "all_long", "one_row", "edge256", "sparse_rows", "ragged"])
+def test_row_patterns(pattern):
+    """Row patterns the streaming kernel's partition and cursors must get right:
+    no entries at all, only long rows, a single row, lengths at the long-row
+    threshold (256 vs 257), runs of empty rows, and ragged lengths in 1-based
+    storage with beta != 0."""
+    rng = np.random.default_rng(41)
+    n, k, base = 3000, 64, 0
+    if pattern == "empty":
+        lengths = np.zeros(5000, np.int64)
+    elif pattern == "all_long":
+        lengths = rng.integers(257, 700, size=40)
+    elif pattern == "one_row":
+        lengths = np.array([7])
+    elif pattern == "edge256":
+        lengths = rng.choice([0, 1, 255, 256, 257], size=400)
+    elif pattern == "sparse_rows":
+        lengths = np.where(rng.random(20000) < 0.02, rng.integers(1, 5, size=20000), 0)
+    else:
+        lengths = rng.integers(0, 60, size=9000)
+        base = 1
+    m = lengths.shape[0]
+    rp, ci, val = random_csr(m, n, lengths, seed=42, base=base, dtype=np.float32)
+    B = rng.uniform(-1, 1, size=(n, k)).astype(np.float32)
+    C0 = rng.uniform(-1, 1, size=(m, k)).astype(np.float32)
+    beta = 0.5 if pattern == "ragged" else 0.0
+    got = run(rp, ci, val, B, m, n, base, C0, 1.0, beta)
+    exact = O.spmm(rp, ci, val, B, C0, 1.0, beta, base)
+    short = np.diff(rp) <= 256
+    assert np.array_equal(got[short], exact[short])
+    if (~short).any():
+        ref, bound = O.spmm_ref64(rp - base, ci - base, val, B)
+        assert_within(got[~short], ref[~short], bound[~short], 1e-5)
