@@ -1,27 +1,33 @@
 // spmm.cu -- CSR SpMM (C = alpha*A*B + beta*C) for sm_100a.
 //
-// Fast path (B and C row-major, 16-byte aligned rows).  A group of 8 lanes
-// holds a 256-byte column chunk of one output row (64 fp32 / 32 fp64 columns):
-// each lane owns two 16-byte vectors, so every stored entry of A costs one
-// 256-byte gather of a B row in two coalesced 128-byte halves.
+// Fast path (B and C row-major, 16-byte aligned rows).  The work is one
+// gather of a B row per stored entry of A.  A group of 8 lanes works on a
+// 256-byte column chunk of an output row (64 fp32 / 32 fp64 columns; lane l
+// owns 16-byte vectors l and 8 + l).  Each lane copies its part of an entry's
+// B-row chunk into one of the group's kDepth shared-memory slots with
+// cp.async.cg (L2 only); the lanes add slot i while the copies for the next
+// kDepth - 1 entries are in flight.  Holding the data in flight in shared
+// memory instead of registers keeps registers at 64 and 32 warps resident per
+// SM; measured on config 3 (power-law, k = 64), more resident warps with 3
+// slots each beat deeper pipelines (1.47 ms per SpMM at depth 3, 4 CTAs/SM;
+// 2.5 ms at depth 12, 2 CTAs/SM; 2.0 ms with registers as slots).  The
+// untiled bulk copy (cp.async.bulk, one 256-byte copy per entry) was slower
+// still (3.9 ms): per-copy cost dominates at this size.
 //
-// The work is bound by how many B-row gathers are in flight, and power-law
-// matrices have mostly 1-entry rows, so a group does not work row by row.  It
-// owns a contiguous range of rows, balanced by rows + entries (each group
-// finds its range with an 8-ary search of the row pointer), and streams
-// through the range's entries in storage order with kDepth gathers always in
-// flight, across row boundaries: entry i+kDepth is issued while entry i is
-// accumulated, and a row's chunk of C is stored when its last entry has been
-// added.  Per output element the sum runs over the row's entries in storage
-// order with separately rounded products and sums: the same operations as
-// JLUST's Tiled SpMM body (ext/KernelAbstractionsExt/ops/spmm.jl:272-292),
-// hence bit-identical.  B rows bypass L1 (ld.global.cg); the sequential index
-// streams stay in L1.
+// spmm_stream: each group owns a contiguous range of rows, balanced by rows +
+// entries (each group finds its range with an 8-ary search of the row
+// pointer), and streams through the range's entries in storage order across
+// row boundaries; a row's chunk of C is stored when its last entry is in.
+// Per output element the sum runs over the row's entries in storage order with
+// separately rounded products and sums: the same operations as JLUST's Tiled
+// SpMM body (ext/KernelAbstractionsExt/ops/spmm.jl:272-292), hence
+// bit-identical.
 //
-// Rows longer than kLong entries are skipped by the stream and computed by a
-// second kernel that splits each into contiguous segments, one per group of a
-// CTA, whose partial sums are added in segment order (deterministic, within
-// tolerance).  No atomics touch C.
+// spmm_long_rows: rows longer than kLong entries, which the stream skips.  A
+// CTA lists the long rows among kScanRows rows in ascending order and splits
+// them into contiguous segments, each row getting groups in proportion to its
+// length; the segments' partial sums are added in segment order
+// (deterministic, within tolerance).  No atomics touch C.
 //
 // Generic path (any order / alignment): one thread per output element, the
 // same storage-order sum.
@@ -33,13 +39,20 @@ JLB_DEFINE_DEV_ERROR(spmm)
 
 namespace spmm {
 
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
 constexpr int kThreads = 256;
-constexpr int kGroup = 8;                      // lanes per row
-constexpr int kVec = 2;                        // 16-byte vectors per lane per B row
+constexpr int kGroup = 8;                      // lanes per group
+constexpr int kVec = 2;                        // 16-byte vectors per lane per B-row chunk
 constexpr int kGroups = kThreads / kGroup;     // groups per CTA
+constexpr int kChunkBytes = kGroup * kVec * 16;  // one B-row chunk (256 bytes)
 constexpr int kLong = 256;                     // longer rows go to spmm_long_rows
-constexpr int kDepth = 4;                      // B-row gathers in flight per group
-constexpr int kMinWork = 64;                   // rows + entries per group, at least
+constexpr int kDepth = 3;                      // B-row chunks in flight per group
+constexpr int kMinWork = 64;                   // rows + entries per stream group, at least
+constexpr int kScanRows = 512;                 // rows a long-row CTA inspects
+constexpr int kSlotBytes = kGroups * kDepth * kChunkBytes;
 
 template <typename T>
 struct V16;
@@ -59,8 +72,8 @@ struct V16<double> {
 };
 
 // Columns a lane owns inside a chunk of kGroup*kVec vectors: vector w of lane
-// l sits at vector index w*kGroup + l, so each load instruction of the group
-// covers kGroup consecutive vectors (128 contiguous bytes).
+// l sits at vector index w*kGroup + l (byte offset 16 * (w*kGroup + l) in the
+// chunk), so each access of the group covers 128 contiguous bytes.
 template <typename T>
 struct Lanes {
     static constexpr int E = V16<T>::E;
@@ -68,64 +81,58 @@ struct Lanes {
     __device__ static int64_t col(int64_t c0, int lane, int w) { return c0 + ((int64_t)w * kGroup + lane) * E; }
 };
 
-// One in-flight entry: its value and this lane's part of its B row.
+// A group's slots: kDepth shared-memory chunks of 256 bytes.  Each lane
+// copies its own two 16-byte vectors of an entry's B-row chunk with
+// cp.async.cg (L2 only, no registers held while in flight) and commits one
+// copy group per slot refill, empty when there is no entry left, so that
+// `cp.async.wait_group kDepth-1` before reading slot u means slot u has
+// landed.  A lane reads back only what it copied itself: no barrier.
 template <typename T>
-struct Slot {
-    T v;
-    typename V16<T>::type b[kVec];
+struct Slots {
+    uint32_t buf;      // shared address of this lane's first vector in slot 0
+    const unsigned char *data;   // generic pointer to the same
+    int lane;
+    bool ok[kVec];     // vector w of this lane lies inside the matrix
+
+    __device__ void issue(int u, const T *row_c0) const {
+#pragma unroll
+        for (int w = 0; w < kVec; ++w)
+            if (ok[w])
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                                 buf + (uint32_t)(u * kChunkBytes + w * kGroup * 16)),
+                             "l"(row_c0 + (w * kGroup + lane) * V16<T>::E)
+                             : "memory");
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    }
+    __device__ void skip() const { asm volatile("cp.async.commit_group;" ::: "memory"); }
+    // Waits for slot u (the oldest copy group in flight) and adds v * chunk.
+    __device__ void add(int u, T v, T (&acc)[kVec][V16<T>::E]) const {
+        using VT = typename V16<T>::type;
+        asm volatile("cp.async.wait_group %0;" ::"n"(kDepth - 1) : "memory");
+#pragma unroll
+        for (int w = 0; w < kVec; ++w)
+            if (ok[w]) {
+                const VT b = *reinterpret_cast<const VT *>(data + u * kChunkBytes + w * kGroup * 16);
+#pragma unroll
+                for (int e = 0; e < V16<T>::E; ++e)
+                    acc[w][e] = add_rn(acc[w][e], mul_rn(v, V16<T>::get(b, e)));
+            }
+    }
 };
 
 template <typename T>
-__device__ __forceinline__ void issue(Slot<T> &s, int p, const int32_t *__restrict__ colind,
-                                      const T *__restrict__ val, const T *__restrict__ B,
-                                      int64_t ldb, int64_t c0, int base, int lane,
-                                      const bool (&ok)[kVec]) {
-    using VT = typename V16<T>::type;
-    const int64_t c = (int64_t)(ldg(colind + p) - base);
-    s.v = ldg(val + p);
-    const T *row = B + c * ldb;
-#pragma unroll
-    for (int w = 0; w < kVec; ++w)
-        if (ok[w]) s.b[w] = __ldcg(reinterpret_cast<const VT *>(row + Lanes<T>::col(c0, lane, w)));
+__device__ __forceinline__ Slots<T> group_slots(unsigned char *smem, int group, int lane) {
+    Slots<T> s;
+    s.data = smem + (size_t)group * kDepth * kChunkBytes + lane * 16;
+    s.buf = smem_u32(s.data);
+    s.lane = lane;
+    return s;
 }
 
 template <typename T>
-__device__ __forceinline__ void accumulate(T (&acc)[kVec][V16<T>::E], const Slot<T> &s,
-                                           const bool (&ok)[kVec]) {
+__device__ __forceinline__ void set_chunk(Slots<T> &s, int64_t c0, int64_t k) {
 #pragma unroll
-    for (int w = 0; w < kVec; ++w)
-        if (ok[w]) {
-#pragma unroll
-            for (int e = 0; e < V16<T>::E; ++e)
-                acc[w][e] = add_rn(acc[w][e], mul_rn(s.v, V16<T>::get(s.b[w], e)));
-        }
-}
-
-// Accumulates entries [lo, hi) of one row, in storage order, into acc for the
-// chunk starting at column c0, kDepth gathers in flight.
-template <typename T>
-__device__ __forceinline__ void range_accumulate(T (&acc)[kVec][V16<T>::E], int lo, int hi,
-                                                 const int32_t *__restrict__ colind,
-                                                 const T *__restrict__ val,
-                                                 const T *__restrict__ B, int64_t ldb,
-                                                 int64_t c0, int64_t k, int base, int lane) {
-    bool ok[kVec];
-#pragma unroll
-    for (int w = 0; w < kVec; ++w) ok[w] = Lanes<T>::col(c0, lane, w) < k;
-    Slot<T> s[kDepth];
-#pragma unroll
-    for (int u = 0; u < kDepth; ++u)
-        if (lo + u < hi) issue(s[u], lo + u, colind, val, B, ldb, c0, base, lane, ok);
-    for (int p = lo; p < hi; p += kDepth) {
-#pragma unroll
-        for (int u = 0; u < kDepth; ++u) {
-            const int q = p + u;
-            if (q < hi) {
-                accumulate(acc, s[u], ok);
-                if (q + kDepth < hi) issue(s[u], q + kDepth, colind, val, B, ldb, c0, base, lane, ok);
-            }
-        }
-    }
+    for (int w = 0; w < kVec; ++w) s.ok[w] = Lanes<T>::col(c0, s.lane, w) < k;
 }
 
 template <typename T, bool kBeta>
@@ -220,15 +227,16 @@ __device__ __forceinline__ void issue_seek(int64_t &r, int &p, int &e, int64_t r
 }
 
 // Short rows: each group streams through the entries of its row range (rows
-// longer than kLong excluded) with kDepth B-row gathers in flight, storing
-// each row's chunk of C when its last entry is in, and the chunk of every
-// empty row as alpha * 0 (+ beta * C).
+// longer than kLong excluded) with kDepth B-row chunks in flight, storing each
+// row's chunk of C when its last entry is in, and the chunk of every empty row
+// as alpha * 0 (+ beta * C).
 template <typename T, bool kBeta>
-__global__ void __launch_bounds__(kThreads, 3)
+__global__ void __launch_bounds__(kThreads, 4)
 spmm_stream(int64_t m, int64_t k, const int32_t *__restrict__ rowptr,
             const int32_t *__restrict__ colind, const T *__restrict__ val,
             const T *__restrict__ B, int64_t ldb, T *__restrict__ C, int64_t ldc, T alpha, T beta,
             int base) {
+    extern __shared__ __align__(128) unsigned char smem[];
     const int tid = threadIdx.x;
     const int lane = tid % kGroup;
     const unsigned gmask = group_mask(tid);
@@ -239,13 +247,14 @@ spmm_stream(int64_t m, int64_t k, const int32_t *__restrict__ rowptr,
     int64_t rs, re;
     find_rows(m, rowptr, base, total * g / groups, total * (g + 1) / groups, lane, gmask, shift,
               rs, re);
-    if (rs >= re) return;
+    // no early exit: the whole warp stays in the loops below, which end when
+    // every group of the warp is done, so its four groups reconverge every
+    // iteration instead of running one after another
     const int first = ldg(rowptr + rs) - base;
+    Slots<T> sl = group_slots<T>(smem, tid / kGroup, lane);
 
     for (int64_t c0 = 0; c0 < k; c0 += Lanes<T>::CW) {
-        bool ok[kVec];
-#pragma unroll
-        for (int w = 0; w < kVec; ++w) ok[w] = Lanes<T>::col(c0, lane, w) < k;
+        set_chunk(sl, c0, k);
         T acc[kVec][V16<T>::E];
         zero(acc);
 
@@ -268,21 +277,24 @@ spmm_stream(int64_t m, int64_t k, const int32_t *__restrict__ rowptr,
         // issue cursor, kDepth entries ahead of the consume cursor
         int64_t ri = rc;
         int ip = cp, ie = ce;
-        Slot<T> s[kDepth];
-        bool have[kDepth];
+        T v[kDepth];
+        uint32_t live = 0;   // bit u: slot u holds an entry
 #pragma unroll
         for (int u = 0; u < kDepth; ++u) {
-            have[u] = ri < re;
-            if (have[u]) {
-                issue(s[u], ip, colind, val, B, ldb, c0, base, lane, ok);
+            if (ri < re) {
+                live |= 1u << u;
+                v[u] = ldg(val + ip);
+                sl.issue(u, B + (int64_t)(ldg(colind + ip) - base) * ldb + c0);
                 if (++ip >= ie) issue_seek(ri, ip, ie, re, rowptr, base);
+            } else {
+                sl.skip();
             }
         }
-        while (have[0]) {
+        while (__any_sync(0xffffffffu, live & 1u)) {
 #pragma unroll
             for (int u = 0; u < kDepth; ++u) {
-                if (!have[u]) continue;
-                accumulate(acc, s[u], ok);
+                if (!(live >> u & 1u)) continue;
+                sl.add(u, v[u], acc);
                 if (++cp >= ce) {
                     store_chunk<T, kBeta>(C, ldc, rc, c0, k, acc, alpha, beta, lane);
                     zero(acc);
@@ -299,87 +311,185 @@ spmm_stream(int64_t m, int64_t k, const int32_t *__restrict__ rowptr,
                         break;
                     }
                 }
-                have[u] = ri < re;
-                if (have[u]) {
-                    issue(s[u], ip, colind, val, B, ldb, c0, base, lane, ok);
+                if (ri < re) {
+                    v[u] = ldg(val + ip);
+                    sl.issue(u, B + (int64_t)(ldg(colind + ip) - base) * ldb + c0);
                     if (++ip >= ie) issue_seek(ri, ip, ie, re, rowptr, base);
+                } else {
+                    live &= ~(1u << u);
+                    sl.skip();
                 }
             }
         }
     }
 }
 
-template <typename T, bool kBeta>
-int stream_grid() {
-    static int per_sm = 0, sms = 0;
-    if (!per_sm) {
-        int dev = 0;
-        if (cudaGetDevice(&dev) != cudaSuccess ||
-            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
-            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, spmm_stream<T, kBeta>, kThreads, 0) != cudaSuccess ||
-            per_sm < 1) {
-            per_sm = 1;
-            sms = 148;
+// Adds entries [lo, hi) of one row, in storage order, into acc with kDepth
+// chunks in flight.
+template <typename T>
+__device__ __forceinline__ void range_accumulate(const Slots<T> &sl, T (&acc)[kVec][V16<T>::E],
+                                                 int lo, int hi,
+                                                 const int32_t *__restrict__ colind,
+                                                 const T *__restrict__ val,
+                                                 const T *__restrict__ B, int64_t ldb, int64_t c0,
+                                                 int base) {
+    T v[kDepth];
+#pragma unroll
+    for (int u = 0; u < kDepth; ++u) {
+        if (lo + u < hi) {
+            v[u] = ldg(val + lo + u);
+            sl.issue(u, B + (int64_t)(ldg(colind + lo + u) - base) * ldb + c0);
+        } else {
+            sl.skip();
         }
     }
-    return per_sm * sms;
+    for (int p = lo; p < hi; p += kDepth) {
+#pragma unroll
+        for (int u = 0; u < kDepth; ++u) {
+            if (p + u >= hi) break;
+            sl.add(u, v[u], acc);
+            const int q = p + u + kDepth;
+            if (q < hi) {
+                v[u] = ldg(val + q);
+                sl.issue(u, B + (int64_t)(ldg(colind + q) - base) * ldb + c0);
+            } else {
+                sl.skip();
+            }
+        }
+    }
 }
 
-constexpr int kScanRows = 4096;   // rows a long-row CTA inspects
-
-// Long rows: each CTA inspects kScanRows rows and computes every row longer
-// than kLong with all of its groups, one contiguous segment each, the partial
-// sums added in segment order (deterministic).
+// Long rows.  The CTA lists the rows longer than kLong among its kScanRows
+// rows in ascending order (block scan of per-thread counts), then works
+// through the list in rounds of up to kGroups rows.  In a round row i gets
+// g_i = 1 + (kGroups - n) * L_i / E groups (n rows, L_i entries, E their sum),
+// each taking one contiguous segment of ceil(L_i / g_i) entries; the first
+// group of the row adds the g_i partial sums in segment order and stores the
+// chunk.  Allocation and order depend only on the matrix: deterministic.
 template <typename T, bool kBeta>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 4)
 spmm_long_rows(int64_t m, int64_t k, const int32_t *__restrict__ rowptr,
                const int32_t *__restrict__ colind, const T *__restrict__ val,
                const T *__restrict__ B, int64_t ldb, T *__restrict__ C, int64_t ldc, T alpha,
                T beta, int base) {
     constexpr int E = V16<T>::E;
-    __shared__ int64_t s_long[kScanRows];
-    __shared__ int s_nlong;
-    __shared__ T s_part[kGroups][kVec * kGroup * E];
+    constexpr int kPer = kScanRows / kThreads;   // rows each thread inspects
+    extern __shared__ __align__(128) unsigned char smem[];
+    T(*s_part)[kVec * kGroup * E] = reinterpret_cast<T(*)[kVec * kGroup * E]>(smem + kSlotBytes);
+    int *s_row = reinterpret_cast<int *>(smem + kSlotBytes + kGroups * kChunkBytes);
+    int *s_len = s_row + kScanRows;
+    __shared__ int s_warp[kThreads / kWarp];
+    __shared__ int s_n;
     const int tid = threadIdx.x;
-    const int g = tid / kGroup, lane = tid % kGroup;
+    const int gi = tid / kGroup, lane = tid % kGroup;
+    const unsigned gmask = group_mask(tid);
     const int64_t r0 = (int64_t)blockIdx.x * kScanRows;
-    if (tid == 0) s_nlong = 0;
-    __syncthreads();
-    for (int i = tid; i < kScanRows && r0 + i < m; i += kThreads) {
-        const int64_t r = r0 + i;
-        if (ldg(rowptr + r + 1) - ldg(rowptr + r) > kLong) s_long[atomicAdd(&s_nlong, 1)] = r;
+
+    // ascending list of long rows: per-thread counts, warp scan, block offsets
+    int lens[kPer];
+    int cnt = 0;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+        const int64_t r = r0 + (int64_t)tid * kPer + j;
+        lens[j] = r < m ? ldg(rowptr + r + 1) - ldg(rowptr + r) : 0;
+        cnt += lens[j] > kLong;
     }
+    int incl = cnt;
+#pragma unroll
+    for (int d = 1; d < kWarp; d <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, incl, d);
+        if (tid % kWarp >= d) incl += t;
+    }
+    if (tid % kWarp == kWarp - 1) s_warp[tid / kWarp] = incl;
     __syncthreads();
-    for (int i = 0; i < s_nlong; ++i) {
-        const int64_t r = s_long[i];
-        const int lo = ldg(rowptr + r) - base, hi = ldg(rowptr + r + 1) - base;
-        const int seg = (hi - lo + kGroups - 1) / kGroups;
-        const int slo = lo + g * seg < hi ? lo + g * seg : hi;
-        const int shi = slo + seg < hi ? slo + seg : hi;
+    int off = incl - cnt;
+    for (int w = 0; w < tid / kWarp; ++w) off += s_warp[w];
+    if (tid == kThreads - 1) s_n = off + cnt;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j)
+        if (lens[j] > kLong) {
+            s_row[off] = tid * kPer + j;
+            s_len[off] = lens[j];
+            ++off;
+        }
+    __syncthreads();
+    const int n = s_n;
+    if (n == 0) return;
+
+    Slots<T> sl = group_slots<T>(smem, gi, lane);
+    for (int i0 = 0; i0 < n; i0 += kGroups) {
+        const int nr = n - i0 < kGroups ? n - i0 : kGroups;
+        int64_t tot = 0;
+        for (int i = 0; i < nr; ++i) tot += s_len[i0 + i];
+        // this group's row, its first group and its group count
+        int row = -1, first = 0, cnt_g = 0, acc_g = 0;
+        for (int i = 0; i < nr; ++i) {
+            const int gcount = 1 + (int)((int64_t)(kGroups - nr) * s_len[i0 + i] / tot);
+            if (gi >= acc_g && gi < acc_g + gcount) {
+                row = i0 + i;
+                first = acc_g;
+                cnt_g = gcount;
+            }
+            acc_g += gcount;
+        }
+        int slo = 0, shi = 0;
+        int64_t r = 0;
+        if (row >= 0) {
+            r = r0 + s_row[row];
+            const int lo = ldg(rowptr + r) - base, hi = ldg(rowptr + r + 1) - base;
+            const int seg = (hi - lo + cnt_g - 1) / cnt_g;
+            const int s = gi - first;
+            slo = lo + s * seg < hi ? lo + s * seg : hi;
+            shi = slo + seg < hi ? slo + seg : hi;
+        }
         for (int64_t c0 = 0; c0 < k; c0 += Lanes<T>::CW) {
+            set_chunk(sl, c0, k);
             T acc[kVec][E];
             zero(acc);
-            range_accumulate<T>(acc, slo, shi, colind, val, B, ldb, c0, k, base, lane);
+            if (row >= 0) range_accumulate<T>(sl, acc, slo, shi, colind, val, B, ldb, c0, base);
 #pragma unroll
             for (int w = 0; w < kVec; ++w)
 #pragma unroll
-                for (int e = 0; e < E; ++e) s_part[g][(w * kGroup + lane) * E + e] = acc[w][e];
+                for (int e = 0; e < E; ++e) s_part[gi][(w * kGroup + lane) * E + e] = acc[w][e];
             __syncthreads();
-            if (g == 0) {
-                T tot[kVec][E];
+            if (row >= 0 && gi == first) {
+                T sum[kVec][E];
 #pragma unroll
                 for (int w = 0; w < kVec; ++w)
 #pragma unroll
                     for (int e = 0; e < E; ++e) {
                         const int idx = (w * kGroup + lane) * E + e;
-                        tot[w][e] = s_part[0][idx];
-                        for (int q = 1; q < kGroups; ++q) tot[w][e] = add_rn(tot[w][e], s_part[q][idx]);
+                        sum[w][e] = s_part[first][idx];
+                        for (int q = 1; q < cnt_g; ++q) sum[w][e] = add_rn(sum[w][e], s_part[first + q][idx]);
                     }
-                store_chunk<T, kBeta>(C, ldc, r, c0, k, tot, alpha, beta, lane);
+                store_chunk<T, kBeta>(C, ldc, r, c0, k, sum, alpha, beta, lane);
             }
             __syncthreads();
         }
     }
+}
+
+constexpr int kStreamSmem = kSlotBytes;
+constexpr int kLongSmem = kSlotBytes + kGroups * kChunkBytes + 2 * kScanRows * 4;
+
+// Opts the kernels into their dynamic shared memory once per device and
+// returns the stream kernel's resident CTAs per SM times the SM count.
+template <typename T, bool kBeta>
+int prepare_kernels(int *grid_full) {
+    static int per_sm[64] = {0}, sms[64] = {0};
+    int dev = 0;
+    JLB_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return fail(JLB_ERR_DEVICE_MISMATCH, "device ordinal %d", dev);
+    if (!per_sm[dev]) {
+        JLB_CUDA(cudaFuncSetAttribute(spmm_stream<T, kBeta>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmem));
+        JLB_CUDA(cudaFuncSetAttribute(spmm_long_rows<T, kBeta>, cudaFuncAttributeMaxDynamicSharedMemorySize, kLongSmem));
+        JLB_CUDA(cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev));
+        int p = 0;
+        JLB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&p, spmm_stream<T, kBeta>, kThreads, kStreamSmem));
+        per_sm[dev] = p < 1 ? 1 : p;
+    }
+    *grid_full = per_sm[dev] * sms[dev];
+    return JLB_OK;
 }
 
 // Generic layouts: one thread per output element.
@@ -409,6 +519,23 @@ __global__ void spmm_generic(int64_t m, int64_t k, const int32_t *__restrict__ r
     }
 }
 
+template <typename T, bool kBeta>
+int launch_fast(cudaStream_t st, int base, int64_t m, int64_t nnz, int64_t k,
+                const int32_t *rowptr, const int32_t *colind, const T *val, const T *B,
+                int64_t ldb, T *C, int64_t ldc, T a, T b) {
+    int full = 0;
+    const int rc = prepare_kernels<T, kBeta>(&full);
+    if (rc != JLB_OK) return rc;
+    const int64_t need = ceil_div(m + nnz, (int64_t)kGroups * kMinWork);
+    const unsigned grid = (unsigned)(need < full ? need : full);
+    spmm_stream<T, kBeta><<<grid, kThreads, kStreamSmem, st>>>(m, k, rowptr, colind, val, B, ldb,
+                                                               C, ldc, a, b, base);
+    spmm_long_rows<T, kBeta><<<(unsigned)ceil_div(m, kScanRows), kThreads, kLongSmem, st>>>(
+        m, k, rowptr, colind, val, B, ldb, C, ldc, a, b, base);
+    JLB_LAUNCH_CHECK("spmm_stream");
+    return ok();
+}
+
 template <typename T>
 int launch(cudaStream_t st, int base, int64_t m, int64_t nnz, int64_t k, const int32_t *rowptr,
            const int32_t *colind, const void *val, const void *B, int64_t ldb, int b_order,
@@ -419,30 +546,18 @@ int launch(cudaStream_t st, int base, int64_t m, int64_t nnz, int64_t k, const i
     const bool fast = b_order == JLB_ROW_MAJOR && c_order == JLB_ROW_MAJOR && k % E == 0 &&
                       ldb % E == 0 && ldc % E == 0 && aligned16(B) && aligned16(C);
     if (fast) {
-        const unsigned grid_long = (unsigned)ceil_div(m, kScanRows);
-        const int64_t need = ceil_div(m + nnz, (int64_t)kGroups * kMinWork);
-        if (b == T(0)) {
-            const int64_t full = stream_grid<T, false>();
-            spmm_stream<T, false><<<(unsigned)(need < full ? need : full), kThreads, 0, st>>>(
-                m, k, rowptr, colind, (const T *)val, (const T *)B, ldb, (T *)C, ldc, a, b, base);
-            spmm_long_rows<T, false><<<grid_long, kThreads, 0, st>>>(
-                m, k, rowptr, colind, (const T *)val, (const T *)B, ldb, (T *)C, ldc, a, b, base);
-        } else {
-            const int64_t full = stream_grid<T, true>();
-            spmm_stream<T, true><<<(unsigned)(need < full ? need : full), kThreads, 0, st>>>(
-                m, k, rowptr, colind, (const T *)val, (const T *)B, ldb, (T *)C, ldc, a, b, base);
-            spmm_long_rows<T, true><<<grid_long, kThreads, 0, st>>>(
-                m, k, rowptr, colind, (const T *)val, (const T *)B, ldb, (T *)C, ldc, a, b, base);
-        }
-        JLB_LAUNCH_CHECK("spmm_stream");
-    } else {
-        const int64_t total = m * k;
-        const unsigned grid = (unsigned)(ceil_div(total, 256) < 148 * 32 ? ceil_div(total, 256) : 148 * 32);
-        spmm_generic<T><<<grid, 256, 0, st>>>(m, k, rowptr, colind, (const T *)val, (const T *)B,
-                                              ldb, b_order, (T *)C, ldc, c_order, a, b, base,
-                                              b != T(0));
-        JLB_LAUNCH_CHECK("spmm_generic");
+        if (b == T(0))
+            return launch_fast<T, false>(st, base, m, nnz, k, rowptr, colind, (const T *)val,
+                                         (const T *)B, ldb, (T *)C, ldc, a, b);
+        return launch_fast<T, true>(st, base, m, nnz, k, rowptr, colind, (const T *)val,
+                                    (const T *)B, ldb, (T *)C, ldc, a, b);
     }
+    const int64_t total = m * k;
+    const unsigned grid = (unsigned)(ceil_div(total, 256) < 148 * 32 ? ceil_div(total, 256) : 148 * 32);
+    spmm_generic<T><<<grid, 256, 0, st>>>(m, k, rowptr, colind, (const T *)val, (const T *)B,
+                                          ldb, b_order, (T *)C, ldc, c_order, a, b, base,
+                                          b != T(0));
+    JLB_LAUNCH_CHECK("spmm_generic");
     return ok();
 }
 
