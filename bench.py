@@ -51,6 +51,9 @@ def parse_args():
                    help="p2p: halo fused into the SpMV kernel over NVLink (default); "
                         "halo: NCCL send/recv; allgather: NCCL all-gather of x")
     p.add_argument("--grid", type=int, default=4096, help="Laplacian grid width")
+    p.add_argument("--l2-persist", type=int, default=1,
+                   help="Laplacian: persisting L2 window over the local CSR: 1 = where the "
+                        "set-aside holds half of it, 2 = always, 0 = never")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
     return p.parse_args()
@@ -244,9 +247,28 @@ class Laplacian:
         self.nnz_local = int(rp[-1])
         self.nnz_total = 5 * self.n - 4 * g
         dev = ctx.device
-        self.rowptr = torch.from_numpy(rp).to(dev)
-        self.colind = torch.from_numpy(lci).to(dev)
-        self.val = torch.from_numpy(val).to(dev)
+        # the local CSR in one allocation (row pointer | columns | values, 256-byte
+        # aligned parts) so that one L2 access-policy window covers it
+        parts = [rp, lci, val]
+        offs, tot = [], 0
+        for a in parts:
+            offs.append(tot)
+            tot += -(-a.nbytes // 256) * 256
+        self.csr_buf = torch.empty(tot, dtype=torch.uint8, device=dev)
+        views = []
+        for a, o in zip(parts, offs):
+            v = self.csr_buf[o:o + a.nbytes].view(getattr(torch, str(a.dtype)))
+            v.copy_(torch.from_numpy(a))
+            views.append(v)
+        self.rowptr, self.colind, self.val = views
+        self.persisted = 0
+        if ctx.args.l2_persist:
+            # kept only where the set-aside holds at least half of the local CSR
+            # (8 ranks at 4096^2); on larger shards it would only shrink L2
+            self.persisted = J.l2_persist(self.csr_buf, tot, device=dev)
+            if ctx.args.l2_persist == 1 and 2 * self.persisted < tot:
+                self.persisted = J.l2_persist(0, 0, device=dev)
+        self.csr_bytes = tot
         self.A = J.csr_tensor(self.rowptr, self.colind, self.val, (self.R, self.R + 2 * g), origin=0)
         self.x0 = np.random.default_rng(1).uniform(-1.0, 1.0, size=self.n)
         interior = D.interior_rows(rp, lci, self.R, g) if ctx.world > 1 else (0, self.R)
@@ -283,6 +305,8 @@ class Laplacian:
     def close(self):
         if self.p2p:
             self.halo.close()
+        if self.persisted:
+            self.J.l2_persist(0, 0, device=self.ctx.device)
 
     def _spmv_rows(self, lo, hi, x, y):
         """Rows [lo, hi) through the C ABI (row-range view of the local CSR)."""
@@ -318,7 +342,9 @@ class Laplacian:
                 "exchange": "none" if self.ctx.world == 1 else
                 ("halo fused into the SpMV kernel over NVLink peer memory" if self.p2p
                  else self.ctx.args.exchange),
-                "l2": "inputs larger than L2 (1.34 GB per iteration), no flush"}
+                "l2": (f"per-rank CSR {self.csr_bytes} B under a persisting L2 window "
+                       f"({self.persisted} B set-aside), x and y not; no flush"
+                       if self.persisted else "inputs larger than L2, no flush")}
 
     # end to end through the public API: x from pinned host memory, y back to it
     def e2e_setup(self):

@@ -279,6 +279,17 @@ JLB_API int jlb_ipc_handle(void *ptr, void *handle_out, uint64_t *offset_out);
 JLB_API int jlb_ipc_open(const void *handle, void **base_out);
 JLB_API int jlb_ipc_close(void *base);
 
+/* L2 residency for iterative solves (no counterpart in the reference).
+ * Marks [base, base + bytes) as a persisting access-policy window on
+ * `stream`: kernels launched on the stream afterwards keep up to the device's
+ * persisting L2 set-aside of that range in L2 across launches (the window is
+ * clipped to the device's maximum window size and the hit ratio set to
+ * set-aside / window).  The set-aside is reserved for the calling process's
+ * context and released with it.  bytes == 0 clears the window on the stream,
+ * resets persisting lines to normal and returns the set-aside.  *persisted_out
+ * (may be NULL) receives the bytes the set-aside covers. */
+JLB_API int jlb_l2_persist(void *stream, const void *base, size_t bytes, size_t *persisted_out);
+
 #ifdef __cplusplus
 }
 #endif

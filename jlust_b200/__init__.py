@@ -37,3 +37,21 @@ def device_status(device=None) -> None:
     from . import _lib
     s = torch.cuda.current_stream(device).cuda_stream
     _lib.call("jlb_device_status", C.c_void_p(s))
+
+
+def l2_persist(base, nbytes: int, device=None) -> int:
+    """Keep [base, base + nbytes) in L2 across the kernels launched afterwards
+    on the current stream (jlb_l2_persist): base is a device pointer or a
+    tensor.  Returns the bytes the persisting set-aside covers.  nbytes == 0
+    clears the window and returns the set-aside."""
+    import ctypes as C
+
+    import torch
+
+    from . import _lib
+    ptr = base.data_ptr() if hasattr(base, "data_ptr") else int(base)
+    s = torch.cuda.current_stream(device).cuda_stream
+    out = C.c_size_t(0)
+    _lib.call("jlb_l2_persist", C.c_void_p(s), C.c_void_p(ptr), C.c_size_t(int(nbytes)),
+              C.byref(out))
+    return out.value

@@ -61,6 +61,7 @@ SIGNATURES = {
     "jlb_ipc_handle": (_i, [_p, _p, C.POINTER(C.c_uint64)]),
     "jlb_ipc_open": (_i, [_p, C.POINTER(_p)]),
     "jlb_ipc_close": (_i, [_p]),
+    "jlb_l2_persist": (_i, [_p, _p, _sz, C.POINTER(_sz)]),
 }
 
 _lib = None

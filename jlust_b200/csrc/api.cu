@@ -94,3 +94,36 @@ extern "C" JLB_API int jlb_device_status(void *stream) {
                     "a device bounds/overflow check failed (error bits 0x%x)", bits);
     return ok();
 }
+
+extern "C" JLB_API int jlb_l2_persist(void *stream, const void *base, size_t bytes,
+                                      size_t *persisted_out) {
+    cudaStream_t st = as_stream(stream);
+    if (persisted_out) *persisted_out = 0;
+    cudaStreamAttrValue v;
+    memset(&v, 0, sizeof(v));
+    if (bytes == 0 || base == nullptr) {
+        v.accessPolicyWindow.num_bytes = 0;
+        JLB_CUDA(cudaStreamSetAttribute(st, cudaStreamAttributeAccessPolicyWindow, &v));
+        JLB_CUDA(cudaCtxResetPersistingL2Cache());
+        JLB_CUDA(cudaDeviceSetLimit(cudaLimitPersistingL2CacheSize, 0));
+        return ok();
+    }
+    int dev = 0, max_persist = 0, max_window = 0;
+    JLB_CUDA(cudaGetDevice(&dev));
+    JLB_CUDA(cudaDeviceGetAttribute(&max_persist, cudaDevAttrMaxPersistingL2CacheSize, dev));
+    JLB_CUDA(cudaDeviceGetAttribute(&max_window, cudaDevAttrMaxAccessPolicyWindowSize, dev));
+    if (max_persist <= 0 || max_window <= 0)
+        return fail(JLB_ERR_CUDA, "device %d has no persisting L2 (set-aside %d, window %d)", dev,
+                    max_persist, max_window);
+    const size_t window = bytes < (size_t)max_window ? bytes : (size_t)max_window;
+    const size_t setaside = window < (size_t)max_persist ? window : (size_t)max_persist;
+    JLB_CUDA(cudaDeviceSetLimit(cudaLimitPersistingL2CacheSize, setaside));
+    v.accessPolicyWindow.base_ptr = const_cast<void *>(base);
+    v.accessPolicyWindow.num_bytes = window;
+    v.accessPolicyWindow.hitRatio = (float)((double)setaside / (double)window);
+    v.accessPolicyWindow.hitProp = cudaAccessPropertyPersisting;
+    v.accessPolicyWindow.missProp = cudaAccessPropertyStreaming;
+    JLB_CUDA(cudaStreamSetAttribute(st, cudaStreamAttributeAccessPolicyWindow, &v));
+    if (persisted_out) *persisted_out = setaside;
+    return ok();
+}

@@ -5,10 +5,14 @@
 // Rank r keeps x in two device buffers (double buffering), each laid out as
 // [lower halo (h) | own rows (R) | upper halo (h)].  Step t reads buffer t%2
 // and writes buffer (t+1)%2.  In one launch:
-//   * blocks over the interior rows (which read no halo entry) compute;
-//   * the last blocks compute the boundary rows: a block whose rows read the
+//   * the first blocks compute the boundary rows: a block whose rows read the
 //     lower halo first waits until the lower neighbour has published step t's
 //     halo (flag from_lower >= t), likewise for the upper halo;
+//   * the remaining blocks compute the interior rows (which read no halo
+//     entry).  Boundary blocks go first so that each step publishes its halo
+//     early, with the peer stores and system-scope fences overlapping the
+//     interior rows instead of adding to the end of the step; a neighbour's
+//     next step then finds the flag already raised;
 //   * every boundary row's result is stored into this rank's next buffer and,
 //     for the first h rows, into the lower neighbour's next buffer (its upper
 //     halo), for the last h rows into the upper neighbour's (its lower halo),
@@ -131,9 +135,10 @@ __global__ void __launch_bounds__(kThreads) halo_step(Args a) {
     const T *x = (const T *)a.x;
     T *y = (T *)a.y;
     const int64_t b = blockIdx.x;
+    const int64_t nbound = a.lower_blocks + a.upper_blocks;
     pdl_trigger();
-    if (b < a.interior_blocks) {
-        const int64_t r = a.i0 + b * kThreads + threadIdx.x;
+    if (b >= nbound) {
+        const int64_t r = a.i0 + (b - nbound) * kThreads + threadIdx.x;
         int lo = 0, hi = 0;
         int c[kPre];
         T v[kPre];
@@ -162,8 +167,8 @@ __global__ void __launch_bounds__(kThreads) halo_step(Args a) {
     }
     pdl_wait();
     // Boundary blocks: side 0 = rows [0, i0) (lower halo), side 1 = [i1, R).
-    const int side = (b < a.interior_blocks + a.lower_blocks) ? 0 : 1;
-    const int64_t sb = side == 0 ? b - a.interior_blocks : b - a.interior_blocks - a.lower_blocks;
+    const int side = b < a.lower_blocks ? 0 : 1;
+    const int64_t sb = side == 0 ? b : b - a.lower_blocks;
     const int64_t nb = side == 0 ? a.lower_blocks : a.upper_blocks;
     const int64_t first = side == 0 ? 0 : a.i1, last = side == 0 ? a.i0 : a.R;
     if (threadIdx.x == 0) {

@@ -73,3 +73,26 @@ def test_reduced_config5():
     assert_within(got, ref, bound, 1e-5)
     f32 = O.bsr_spmm(bp, bc, bv, B)
     assert np.linalg.norm(got - f32) / np.linalg.norm(f32) < 1e-5
+
+
+@pytest.mark.parametrize("nbr_rows,nbr_cols,N", [(41, 37, 64), (41, 37, 192), (33, 50, 320), (1, 5, 256), (41, 37, 256)])
+def test_shapes_and_order(nbr_rows, nbr_cols, N):
+    """Odd and rectangular block grids, N that the tensor path does not take
+    (64, 192, 320: the SIMT kernel) and that it does (256), runs of empty
+    block rows, and block columns stored out of order inside a row."""
+    rng = np.random.default_rng(55 + N)
+    present = rng.random((nbr_rows, nbr_cols)) < 0.2
+    if nbr_rows > 6:
+        present[[2, 3, 6]] = False                            # empty block rows
+    bp = np.zeros(nbr_rows + 1, np.int32)
+    bp[1:] = np.cumsum(present.sum(axis=1))
+    bc = np.nonzero(present)[1].astype(np.int32)
+    for r in range(0, nbr_rows, 5):                           # unsorted columns in some rows
+        seg = bc[bp[r]:bp[r + 1]]
+        bc[bp[r]:bp[r + 1]] = seg[::-1]
+    bv = synth.f32_to_bf16_bits(rng.standard_normal(bc.shape[0] * 4096, dtype=np.float32))
+    B = synth.f32_to_bf16_bits(rng.standard_normal((nbr_cols * 64, N), dtype=np.float32))
+    Y0 = rng.standard_normal((nbr_rows * 64, N), dtype=np.float32)
+    got = run(bp, bc, bv, B, 64, nbr_rows, nbr_cols, Y0, alpha=1.5, beta=0.25)
+    ref, bound = O.bsr_spmm_ref64(bp, bc, bv, B, Y=Y0, alpha=1.5, beta=0.25)
+    assert_within(got, ref, bound, 1e-5)

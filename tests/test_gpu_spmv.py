@@ -133,3 +133,25 @@ def test_laplacian_iterations_bit_exact():
         xr = O.spmv(rp, ci, val, xr)
     J.device_status()
     assert np.array_equal(xa.cpu().numpy(), xr)
+
+
+def test_l2_persisting_window_same_results():
+    """Iterations under a persisting L2 window over the matrix (jlb_l2_persist)
+    give the same bits as without it; clearing the window releases the
+    set-aside."""
+    rp, ci, val, x = synth.config2(g=1024)
+    n = 1024 * 1024
+    A = J.csr_tensor(to_dev(rp), to_dev(ci), to_dev(val), (n, n), origin=0)
+    persisted = J.l2_persist(A.val, val.nbytes)
+    assert persisted > 0
+    try:
+        xa, xb = to_dev(x), torch.empty(n, dtype=torch.float64, device=DEV)
+        xr = x.copy()
+        for _ in range(10):
+            J.execute(J.SpMVOp, A, xa, xb)
+            xa, xb = xb, xa
+            xr = O.spmv(rp, ci, val, xr)
+        J.device_status()
+        assert np.array_equal(xa.cpu().numpy(), xr)
+    finally:
+        assert J.l2_persist(0, 0) == 0
