@@ -52,6 +52,40 @@ def partition_by_nnz(rowptr: np.ndarray, world: int, rank: int):
     return r0, max(r0, r1)
 
 
+def exclusive_scan(counts: torch.Tensor, base: int = 0, scan=None, group=None) -> torch.Tensor:
+    """Exclusive scan of counts split across ranks in rank order (rank r holds
+    a contiguous slice): returns this rank's part of the global position
+    buffer, out[0] = base + (counts of lower ranks), out[i+1] = out[i] +
+    counts[i] -- len(counts) + 1 entries, so rank r's last entry equals rank
+    r+1's first.  Each rank scans its slice locally (`scan`, default the
+    library's jlb_exclusive_scan_i32 on the slice's GPU; any callable with the
+    same contract on CPU ranks), then one all-gather of the slice totals gives
+    the offsets.  The result is int32 like every position buffer; a global
+    total past Int32 raises OverflowError on every rank."""
+    if scan is None:
+        from .convert import exclusive_scan as scan
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    rank = dist.get_rank(group) if dist.is_initialized() else 0
+    # the shard total as an int64 sum (not the scan's last entry, which would
+    # wrap); every rank takes the all-gather, also one whose shard alone
+    # overflows, so that all ranks raise together
+    mine = int(counts.sum(dtype=torch.int64).item())
+    local = scan(counts, 0) if base + mine <= 2**31 - 1 else None
+    total = torch.tensor([mine], dtype=torch.int64)
+    if counts.is_cuda and world > 1 and dist.get_backend(group) == "nccl":
+        total = total.to(counts.device)
+    totals = [torch.zeros_like(total) for _ in range(world)]
+    if world > 1:
+        dist.all_gather(totals, total, group=group)
+    else:
+        totals = [total]
+    totals = [int(t.item()) for t in totals]
+    if local is None or base + sum(totals) > 2**31 - 1:
+        raise OverflowError("exclusive_scan: global total exceeds Int32 positions")
+    offset = base + sum(totals[:rank])
+    return local + offset if offset else local
+
+
 def local_csr(rowptr: np.ndarray, colind: np.ndarray, val: np.ndarray, r0: int, r1: int, h: int):
     """Rows [r0, r1) of a global CSR with columns shifted into the local halo
     buffer (column c -> c - (r0 - h)).  Requires every column of those rows to

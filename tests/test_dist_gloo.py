@@ -94,3 +94,49 @@ def test_partition_by_nnz_balances_power_law():
         assert all(b == c for (_, b), (c, _) in zip(spans, spans[1:]))
         work = [(rp[b] - rp[a]) + (b - a) for a, b in spans]
         assert max(work) - min(work) <= 4096 + 2          # at most one long row apart
+
+
+def _scan_worker(rank, world, port, out_dir):
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    from jlust_b200 import dist as D
+    from oracle import oracle as O
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        counts = np.random.default_rng(7).integers(0, 50, size=1001).astype(np.int32)
+        lo, hi = D.partition_rows(counts.shape[0], world, rank)
+        part = torch.from_numpy(counts[lo:hi].copy())
+
+        def cpu_scan(c, base):   # the oracle's scan stands in for the GPU's on gloo ranks
+            return torch.from_numpy(O.exclusive_scan(c.numpy(), base).astype(np.int32))
+
+        out = D.exclusive_scan(part, base=1, scan=cpu_scan)
+        np.save(os.path.join(out_dir, f"scan{rank}.npy"), out.numpy())
+        # rank 0's slice overflows by itself, the others only together
+        big = torch.full((4,), 2**29 if rank == 0 else 2**28, dtype=torch.int32)
+        try:
+            D.exclusive_scan(big, scan=cpu_scan)
+            np.save(os.path.join(out_dir, f"ovf{rank}.npy"), np.array([0]))
+        except OverflowError:
+            np.save(os.path.join(out_dir, f"ovf{rank}.npy"), np.array([1]))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_distributed_scan_matches_global(tmp_path, world):
+    """Local scans + all-gather of shard totals reproduce the global exclusive
+    scan bit for bit (origin 1, an uneven split); a global total past Int32
+    raises on every rank."""
+    from oracle import oracle as O
+    mp.spawn(_scan_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    counts = np.random.default_rng(7).integers(0, 50, size=1001).astype(np.int32)
+    ref = O.exclusive_scan(counts, 1)
+    from jlust_b200 import dist as D
+    for r in range(world):
+        lo, hi = D.partition_rows(counts.shape[0], world, r)
+        got = np.load(tmp_path / f"scan{r}.npy")
+        assert np.array_equal(got, ref[lo:hi + 1])
+        assert np.load(tmp_path / f"ovf{r}.npy")[0] == 1

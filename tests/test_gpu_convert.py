@@ -114,3 +114,12 @@ def test_empty_matrix():
                      to_dev(np.zeros(0)), (10, 10), origin=0)
     Bt = J.convert_format(A, J.Formats.BSRRight((4, 4)))
     assert _host(J.positions(Bt, 2)).tolist() == [0, 0, 0, 0] and J.nnz(Bt) == 0
+
+
+def test_distributed_scan_single_process_gpu():
+    """jlust_b200.dist.exclusive_scan with one rank runs the library scan on
+    the GPU and equals the oracle (the multi-rank offsets are covered on gloo)."""
+    from jlust_b200 import dist as D
+    counts = np.random.default_rng(61).integers(0, 9, size=300_001).astype(np.int32)
+    got = D.exclusive_scan(torch.from_numpy(counts).to(DEV), base=1)
+    assert np.array_equal(got.cpu().numpy(), O.exclusive_scan(counts, 1))
