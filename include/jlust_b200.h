@@ -214,7 +214,11 @@ JLB_API int jlb_exclusive_scan_i32_noalloc(void *stream, int64_t n, const int32_
  * Phase 1 (count) fills browptr (ceil(m/b1)+1 entries) and returns nnzb in
  * *nnzb (synchronises `stream`); the caller allocates bcolind (nnzb) and bval
  * (nnzb*b1*b2 values of dtype); phase 2 (fill) writes them.  `workspace`
- * holds jlb_to_bsr_workspace_size(...) bytes for both phases.
+ * holds jlb_csr_to_bsr_workspace_size(...) bytes for both phases; passing the
+ * same workspace to fill lets it reuse the block-column bitmaps that count
+ * left there (matrices of up to 163,840 block columns), so fill reads the CSR
+ * once.  Any other workspace, or a smaller one, is also correct: fill then
+ * rebuilds the bitmaps.
  * Replaces convert_format(u, Formats.BSRRight((b1,b2))) for CSR sources and
  * cuSPARSE csr2bsr (supports_convert, ext/CUDAExt/CUDAExt.jl:330-339). */
 JLB_API size_t jlb_csr_to_bsr_workspace_size(int64_t m, int64_t n, int64_t nnz, int b1, int b2);

@@ -176,7 +176,56 @@ struct Src {
     const int32_t *bent;     // COO: bucketed storage indices
     int64_t m, n;
     int b1, b2, base, es;
+    int sh1, sh2;            // log2(b1), log2(b2) when a power of two, else -1
+
+    __device__ __forceinline__ int64_t blk_col(int64_t j) const { return sh2 >= 0 ? j >> sh2 : j / b2; }
+    __device__ __forceinline__ int64_t in_col(int64_t j) const { return sh2 >= 0 ? j & (b2 - 1) : j % b2; }
+    __device__ __forceinline__ int64_t in_row(int64_t i) const { return sh1 >= 0 ? i & (b1 - 1) : i % b1; }
 };
+
+inline int log2_exact(int b) {
+    int k = 0;
+    while ((1 << k) < b) ++k;
+    return (1 << k) == b ? k : -1;
+}
+
+constexpr int kUnrollEntries = 4;   // entries per lane loaded before use
+
+// CSR rows of block row I, warp-synchronously: every lane of the warp calls
+// f(p, i, j, ok) for kUnrollEntries entries at a time (ok false for padding,
+// explicit zeros and out-of-range columns), so f may use warp shuffles.  The
+// loads of a batch are issued before any use.
+template <typename F>
+__device__ __forceinline__ void for_each_csr_row_sync(const Src &s, int64_t I, F f) {
+    const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
+    const int64_t i0 = I * s.b1;
+    for (int r = warp; r < s.b1; r += kThreads / kWarp) {
+        const int64_t i = i0 + r;
+        if (i >= s.m) break;
+        const int64_t lo = (int64_t)s.rowptr[i] - s.base, hi = (int64_t)s.rowptr[i + 1] - s.base;
+        for (int64_t p0 = lo; p0 < hi; p0 += (int64_t)kWarp * kUnrollEntries) {
+            int64_t jj[kUnrollEntries];
+            bool nz[kUnrollEntries];
+#pragma unroll
+            for (int u = 0; u < kUnrollEntries; ++u) {
+                const int64_t p = p0 + u * kWarp + lane;
+                nz[u] = p < hi;
+                jj[u] = nz[u] ? (int64_t)__ldg(s.cols + p) - s.base : -1;
+                if (nz[u]) nz[u] = !is_zero(s.val, s.es, p);
+            }
+#pragma unroll
+            for (int u = 0; u < kUnrollEntries; ++u) {
+                const int64_t p = p0 + u * kWarp + lane;
+                bool ok = nz[u];
+                if (ok && (jj[u] < 0 || jj[u] >= s.n)) {
+                    dev_error(DEV_ERR_BOUNDS);
+                    ok = false;
+                }
+                f(p, i, jj[u], ok);
+            }
+        }
+    }
+}
 
 // Calls f(p, i, j) for every nonzero entry of block row I (storage index p,
 // 0-based row i and column j).  CSR: one warp per row, lanes over entries.
@@ -209,8 +258,21 @@ __device__ __forceinline__ void for_each_entry(const Src &s, int64_t I, F f) {
 
 // Marks the block columns of window [w0, w0 + kWinBits) hit by block row I.
 __device__ __forceinline__ void mark_window(const Src &s, int64_t I, int64_t w0, uint32_t *bits) {
+    if (s.rowptr) {
+        // CSR: a row's columns ascend, so one atomic per run of equal block
+        // columns across the lanes (compare with the previous lane; unsorted
+        // rows stay correct, with more atomics)
+        for_each_csr_row_sync(s, I, [&](int64_t, int64_t, int64_t j, bool ok) {
+            const int64_t J = ok ? s.blk_col(j) - w0 : -1;
+            const bool in = ok && J >= 0 && J < kWinBits;
+            const int64_t prev = __shfl_up_sync(0xffffffffu, in ? J : -1, 1);
+            const bool lead = (threadIdx.x % kWarp) == 0 || prev != J;
+            if (in && lead) atomicOr(&bits[J >> 5], 1u << (J & 31));
+        });
+        return;
+    }
     for_each_entry(s, I, [&](int64_t p, int64_t i, int64_t j) {
-        const int64_t J = j / s.b2 - w0;
+        const int64_t J = s.blk_col(j) - w0;
         const bool in = J >= 0 && J < kWinBits;
         // one atomic per distinct J among the lanes that agree on it
         const unsigned act = __activemask();
@@ -231,9 +293,20 @@ __device__ __forceinline__ int64_t block_sum(int64_t v, int64_t *s_red) {
     return t;
 }
 
+// Block-column bitmaps handed from the count pass to the fill pass through the
+// caller's workspace (one window only, i.e. at most kWinBits block columns):
+// the fill pass then reads the CSR once instead of twice.  `stamp` holds a
+// key of the count call's arguments; the fill pass uses the bitmaps only when
+// its own key matches, and marks them again otherwise.
+struct Carry {
+    uint32_t *bits;      // mb x words, or null: no hand-over
+    uint64_t *stamp;
+    uint64_t key;
+};
+
 // Count pass: counts[I] (= browptr[I+1]) = number of distinct nonzero blocks.
 __global__ void __launch_bounds__(kThreads)
-count_blocks(Src s, int64_t mb, int64_t nb, int32_t *__restrict__ counts) {
+count_blocks(Src s, int64_t mb, int64_t nb, int32_t *__restrict__ counts, Carry carry) {
     __shared__ uint32_t bits[kWinWords];
     __shared__ int64_t s_red[kThreads / kWarp];
     for (int64_t I = blockIdx.x; I < mb; I += gridDim.x) {
@@ -245,7 +318,10 @@ count_blocks(Src s, int64_t mb, int64_t nb, int32_t *__restrict__ counts) {
             mark_window(s, I, w0, bits);
             __syncthreads();
             int64_t c = 0;
-            for (int w = threadIdx.x; w < nw; w += kThreads) c += __popc(bits[w]);
+            for (int w = threadIdx.x; w < nw; w += kThreads) {
+                c += __popc(bits[w]);
+                if (carry.bits) carry.bits[I * nw + w] = bits[w];
+            }
             total += block_sum(c, s_red);
         }
         if (threadIdx.x == 0) {
@@ -254,12 +330,15 @@ count_blocks(Src s, int64_t mb, int64_t nb, int32_t *__restrict__ counts) {
         }
         __syncthreads();
     }
+    if (carry.bits && blockIdx.x == 0 && threadIdx.x == 0) *carry.stamp = carry.key;
 }
 
 // Fill pass.  winner == nullptr means the source has unique coordinates.
 __global__ void __launch_bounds__(kThreads)
 fill_blocks(Src s, int64_t mb, int64_t nb, int64_t nnzb, const int32_t *__restrict__ browptr,
-            int32_t *__restrict__ bcolind, void *__restrict__ bval, int32_t *__restrict__ winner) {
+            int32_t *__restrict__ bcolind, void *__restrict__ bval, int32_t *__restrict__ winner,
+            Carry carry) {
+    const bool handed = carry.bits && *carry.stamp == carry.key;
     __shared__ uint32_t bits[kWinWords];
     __shared__ int32_t pref[kWinWords];
     __shared__ int64_t s_warp[kThreads / kWarp];
@@ -277,10 +356,15 @@ fill_blocks(Src s, int64_t mb, int64_t nb, int64_t nnzb, const int32_t *__restri
         int64_t rank0 = 0;  // blocks in earlier windows
         for (int64_t w0 = 0; w0 < nb; w0 += kWinBits) {
             const int nw = (int)ceil_div((nb - w0) < kWinBits ? (nb - w0) : kWinBits, 32);
-            for (int w = threadIdx.x; w < nw; w += kThreads) bits[w] = 0;
-            __syncthreads();
-            mark_window(s, I, w0, bits);
-            __syncthreads();
+            if (handed) {
+                for (int w = threadIdx.x; w < nw; w += kThreads) bits[w] = carry.bits[I * nw + w];
+                __syncthreads();
+            } else {
+                for (int w = threadIdx.x; w < nw; w += kThreads) bits[w] = 0;
+                __syncthreads();
+                mark_window(s, I, w0, bits);
+                __syncthreads();
+            }
             // exclusive prefix of the word popcounts, kThreads words at a time
             int64_t carry = 0;
             for (int c0 = 0; c0 < nw; c0 += kThreads) {
@@ -307,12 +391,12 @@ fill_blocks(Src s, int64_t mb, int64_t nb, int64_t nnzb, const int32_t *__restri
                 }
             }
             auto cell_of = [&](int64_t i, int64_t j) -> int64_t {
-                const int64_t J = j / s.b2 - w0;
+                const int64_t J = s.blk_col(j) - w0;
                 if (J < 0 || J >= kWinBits) return -1;
                 const uint32_t word = bits[J >> 5];
                 const int64_t rk = rank0 + pref[J >> 5] + __popc(word & ((1u << (J & 31)) - 1u));
                 if (q0 + rk >= q1) { dev_error(DEV_ERR_BOUNDS); return -1; }
-                return (q0 + rk) * bsz + (i % s.b1) * s.b2 + (j % s.b2);
+                return (q0 + rk) * bsz + s.in_row(i) * s.b2 + s.in_col(j);
             };
             if (winner) {
                 for_each_entry(s, I, [&](int64_t p, int64_t i, int64_t j) {
@@ -323,6 +407,11 @@ fill_blocks(Src s, int64_t mb, int64_t nb, int64_t nnzb, const int32_t *__restri
                 for_each_entry(s, I, [&](int64_t p, int64_t i, int64_t j) {
                     const int64_t c = cell_of(i, j);
                     if (c >= 0 && winner[c] == (int32_t)p) copy_val(bval, c, s.val, p, s.es);
+                });
+            } else if (s.rowptr) {
+                for_each_csr_row_sync(s, I, [&](int64_t p, int64_t i, int64_t j, bool ok) {
+                    const int64_t c = ok ? cell_of(i, j) : -1;
+                    if (c >= 0) copy_val(bval, c, s.val, p, s.es);
                 });
             } else {
                 for_each_entry(s, I, [&](int64_t p, int64_t i, int64_t j) {
@@ -417,11 +506,58 @@ extern "C" JLB_API int jlb_exclusive_scan_i32(void *stream, int64_t n, const int
 }
 
 // ------------------------------------------------------------------ CSR -> BSR
-static size_t csr_ws(int64_t m, int b1) { return conv::scan_ws(ceil_div(m, b1)) + 256; }
+// Workspace: [scan scratch | stamp | block-column bitmaps (when handed over)].
+constexpr size_t kMaxCarryBytes = (size_t)256 << 20;
+
+static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+static size_t carry_bytes(int64_t m, int64_t n, int b1, int b2) {
+    const int64_t mb = ceil_div(m, b1), nb = ceil_div(n, b2);
+    if (nb > conv::kWinBits || mb <= 0) return 0;
+    const size_t bytes = (size_t)mb * (size_t)ceil_div(nb, 32) * 4;
+    return bytes <= kMaxCarryBytes ? bytes : 0;
+}
+
+static size_t csr_scan_ws(int64_t m, int b1) { return align256(conv::scan_ws(ceil_div(m, b1)) + 256); }
+
+static size_t csr_ws(int64_t m, int64_t n, int b1, int b2) {
+    const size_t cb = carry_bytes(m, n, b1, b2);
+    return cb ? csr_scan_ws(m, b1) + 256 + cb : csr_scan_ws(m, b1);
+}
+
+static uint64_t carry_key(int64_t m, int64_t n, int64_t nnz, int b1, int b2, int base, int dtype,
+                          const void *rowptr, const void *colind, const void *val) {
+    uint64_t h = 0x9e3779b97f4a7c15ull;
+    const uint64_t parts[10] = {(uint64_t)m, (uint64_t)n, (uint64_t)nnz, (uint64_t)b1,
+                                (uint64_t)b2, (uint64_t)base, (uint64_t)dtype,
+                                (uint64_t)(uintptr_t)rowptr, (uint64_t)(uintptr_t)colind,
+                                (uint64_t)(uintptr_t)val};
+    for (uint64_t v : parts) {
+        h ^= v + 0x9e3779b97f4a7c15ull + (h << 6) + (h >> 2);
+        h *= 0xbf58476d1ce4e5b9ull;
+    }
+    return h | 1ull;   // never 0: a zeroed workspace never matches
+}
+
+// The hand-over region of a CSR workspace, or {null} when it is too small or
+// the matrix needs more than one bitmap window.
+static conv::Carry csr_carry(void *ws, size_t wsb, int64_t m, int64_t n, int64_t nnz, int b1,
+                             int b2, int base, int dtype, const void *rowptr, const void *colind,
+                             const void *val) {
+    conv::Carry c{nullptr, nullptr, 0};
+    const size_t cb = carry_bytes(m, n, b1, b2);
+    const size_t scan = csr_scan_ws(m, b1);
+    if (!cb || !ws || wsb < scan + 256 + cb) return c;
+    char *p = reinterpret_cast<char *>(ws);
+    c.stamp = reinterpret_cast<uint64_t *>(p + scan);
+    c.bits = reinterpret_cast<uint32_t *>(p + scan + 256);
+    c.key = carry_key(m, n, nnz, b1, b2, base, dtype, rowptr, colind, val);
+    return c;
+}
 
 extern "C" JLB_API size_t jlb_csr_to_bsr_workspace_size(int64_t m, int64_t n, int64_t nnz, int b1,
                                                         int b2) {
-    return b1 > 0 ? csr_ws(m, b1) : 0;
+    return b1 > 0 && b2 > 0 ? csr_ws(m, n, b1, b2) : 0;
 }
 
 static conv::Src csr_src(int dtype, int idx_base, int64_t m, int64_t n, const int32_t *rowptr,
@@ -430,6 +566,7 @@ static conv::Src csr_src(int dtype, int idx_base, int64_t m, int64_t n, const in
     s.rowptr = rowptr; s.rows = nullptr; s.cols = colind; s.val = val;
     s.boffs = nullptr; s.bent = nullptr; s.m = m; s.n = n;
     s.b1 = b1; s.b2 = b2; s.base = idx_base; s.es = (int)dtype_size(dtype);
+    s.sh1 = conv::log2_exact(b1); s.sh2 = conv::log2_exact(b2);
     return s;
 }
 
@@ -461,12 +598,14 @@ extern "C" JLB_API int jlb_csr_to_bsr_count(void *stream, int dtype, int idx_bas
     if (r) return r;
     if (!browptr || !nnzb || !rowptr || (nnz > 0 && (!colind || !val)))
         return fail(JLB_ERR_INVALID_ARGUMENT, "null buffer");
-    if (workspace_bytes < csr_ws(m, b1)) return fail(JLB_ERR_WORKSPACE, "workspace too small");
+    if (workspace_bytes < csr_scan_ws(m, b1)) return fail(JLB_ERR_WORKSPACE, "workspace too small");
     cudaStream_t st = as_stream(stream);
     const int64_t mb = ceil_div(m, b1), nb = ceil_div(n, b2);
     if (mb > 0) {
         conv::count_blocks<<<conv::grid_rows(mb), conv::kThreads, 0, st>>>(
-            csr_src(dtype, idx_base, m, n, rowptr, colind, val, b1, b2), mb, nb, browptr + 1);
+            csr_src(dtype, idx_base, m, n, rowptr, colind, val, b1, b2), mb, nb, browptr + 1,
+            csr_carry(workspace, workspace_bytes, m, n, nnz, b1, b2, idx_base, dtype, rowptr,
+                      colind, val));
         JLB_LAUNCH_CHECK("count_blocks");
     }
     return finish_count(st, mb, idx_base, browptr, nnzb, workspace, workspace_bytes, nullptr);
@@ -487,7 +626,9 @@ extern "C" JLB_API int jlb_csr_to_bsr_fill(void *stream, int dtype, int idx_base
     cudaStream_t st = as_stream(stream);
     conv::fill_blocks<<<conv::grid_rows(mb), conv::kThreads, 0, st>>>(
         csr_src(dtype, idx_base, m, n, rowptr, colind, val, b1, b2), mb, nb, nnzb, browptr,
-        bcolind, bval, nullptr);
+        bcolind, bval, nullptr,
+        csr_carry(workspace, workspace_bytes, m, n, nnz, b1, b2, idx_base, dtype, rowptr, colind,
+                  val));
     JLB_LAUNCH_CHECK("fill_blocks");
     return ok();
 }
@@ -549,6 +690,7 @@ static conv::Src coo_src(int dtype, int idx_base, int64_t m, int64_t n, const in
     s.rowptr = nullptr; s.rows = rows; s.cols = cols; s.val = val;
     s.boffs = boffs; s.bent = bent; s.m = m; s.n = n;
     s.b1 = b1; s.b2 = b2; s.base = idx_base; s.es = (int)dtype_size(dtype);
+    s.sh1 = conv::log2_exact(b1); s.sh2 = conv::log2_exact(b2);
     return s;
 }
 
@@ -571,7 +713,7 @@ extern "C" JLB_API int jlb_coo_to_bsr_count(void *stream, int dtype, int idx_bas
     if (mb > 0) {
         conv::count_blocks<<<conv::grid_rows(mb), conv::kThreads, 0, st>>>(
             coo_src(dtype, idx_base, m, n, rows, cols, val, b1, b2, boffs, bent), mb, nb,
-            browptr + 1);
+            browptr + 1, conv::Carry{nullptr, nullptr, 0});
         JLB_LAUNCH_CHECK("count_blocks");
     }
     // The bucket scan already used the scan workspace; reuse it for browptr.
@@ -610,7 +752,7 @@ extern "C" JLB_API int jlb_coo_to_bsr_fill(void *stream, int dtype, int idx_base
     int32_t *winner = k.take<int32_t>((size_t)nnzb * (size_t)b1 * (size_t)b2);
     conv::fill_blocks<<<conv::grid_rows(mb), conv::kThreads, 0, st>>>(
         coo_src(dtype, idx_base, m, n, rows, cols, val, b1, b2, boffs, bent), mb, nb, nnzb,
-        browptr, bcolind, bval, winner);
+        browptr, bcolind, bval, winner, conv::Carry{nullptr, nullptr, 0});
     JLB_LAUNCH_CHECK("fill_blocks");
     return ok();
 }

@@ -123,3 +123,44 @@ def test_distributed_scan_single_process_gpu():
     counts = np.random.default_rng(61).integers(0, 9, size=300_001).astype(np.int32)
     got = D.exclusive_scan(torch.from_numpy(counts).to(DEV), base=1)
     assert np.array_equal(got.cpu().numpy(), O.exclusive_scan(counts, 1))
+
+
+@pytest.mark.parametrize("fill_ws", ["same", "fresh", "small"])
+def test_csr_fill_workspace_handover(fill_ws):
+    """The fill phase reuses the count phase's bitmaps only from the same
+    workspace; a fresh (zeroed) workspace or one too small to hold them makes
+    it rebuild them -- all three give the oracle's bits."""
+    import ctypes as C
+    from jlust_b200 import _lib
+    rng = np.random.default_rng(65)
+    m, n, b1, b2 = 700, 900, 16, 16
+    rp, ci, val = random_csr(m, n, rng.integers(0, 40, size=m), seed=66, zero_frac=0.1)
+    val = val.astype(np.float32)
+    rpd, cid, vd = to_dev(rp), to_dev(ci), to_dev(val)
+    mb = -(-m // b1)
+    st = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    L = _lib.load()
+    wsb = L.jlb_csr_to_bsr_workspace_size(m, n, ci.shape[0], b1, b2)
+    ws = torch.zeros(wsb, dtype=torch.uint8, device=DEV)
+    browptr = torch.empty(mb + 1, dtype=torch.int32, device=DEV)
+    nnzb = C.c_int64()
+
+    def P(t):
+        return C.c_void_p(t.data_ptr())
+
+    _lib.call("jlb_csr_to_bsr_count", st, _lib.F32, 0, m, n, ci.shape[0], P(rpd), P(cid), P(vd),
+              b1, b2, P(browptr), C.byref(nnzb), P(ws), wsb)
+    if fill_ws == "fresh":
+        ws = torch.zeros(wsb, dtype=torch.uint8, device=DEV)
+    elif fill_ws == "small":
+        wsb = 4096
+        ws = torch.zeros(wsb, dtype=torch.uint8, device=DEV)
+    bcol = torch.empty(nnzb.value, dtype=torch.int32, device=DEV)
+    bval = torch.empty(nnzb.value * b1 * b2, dtype=torch.float32, device=DEV)
+    _lib.call("jlb_csr_to_bsr_fill", st, _lib.F32, 0, m, n, ci.shape[0], P(rpd), P(cid), P(vd),
+              b1, b2, P(browptr), nnzb.value, P(bcol), P(bval), P(ws), wsb)
+    J.device_status()
+    bp, bc, bv = O.csr_to_bsr(m, n, rp, ci, val, b1, b2)
+    assert np.array_equal(browptr.cpu().numpy(), bp)
+    assert np.array_equal(bcol.cpu().numpy(), bc)
+    assert np.array_equal(bval.cpu().numpy().view(np.uint8), bv.view(np.uint8))
