@@ -9,7 +9,7 @@
 // kDepth - 1 entries are in flight.  Holding the data in flight in shared
 // memory instead of registers keeps registers at 64 and 32 warps resident per
 // SM; measured on config 3 (power-law, k = 64), more resident warps with 3
-// slots each beat deeper pipelines (1.47 ms per SpMM at depth 3, 4 CTAs/SM;
+// slots each beat deeper pipelines (1.40 ms per SpMM at depth 3, 4 CTAs/SM;
 // 2.5 ms at depth 12, 2 CTAs/SM; 2.0 ms with registers as slots).  The
 // untiled bulk copy (cp.async.bulk, one 256-byte copy per entry) was slower
 // still (3.9 ms): per-copy cost dominates at this size.
@@ -213,7 +213,7 @@ __device__ __forceinline__ void find_rows(int64_t m, const int32_t *__restrict__
 // Moves the issue cursor to the first entry of the next row in (r, re) that
 // has entries and at most kLong of them; r == re when there is none.  e holds
 // the end of row r on entry.
-__device__ __forceinline__ void issue_seek(int64_t &r, int &p, int &e, int64_t re,
+__device__ __forceinline__ void issue_seek(int &r, int &p, int &e, int re,
                                            const int32_t *__restrict__ rowptr, int base) {
     for (;;) {
         if (++r >= re) return;
@@ -244,9 +244,11 @@ spmm_stream(int64_t m, int64_t k, const int32_t *__restrict__ rowptr,
     const int64_t groups = (int64_t)gridDim.x * kGroups;
     const int64_t g = (int64_t)blockIdx.x * kGroups + tid / kGroup;
     const int64_t total = m + (int64_t)(ldg(rowptr + m) - base);
-    int64_t rs, re;
+    int64_t rs64, re64;
     find_rows(m, rowptr, base, total * g / groups, total * (g + 1) / groups, lane, gmask, shift,
-              rs, re);
+              rs64, re64);
+    // row cursors in 32 bits (the launcher takes this path for m < 2^31 only)
+    const int rs = (int)rs64, re = (int)re64;
     // no early exit: the whole warp stays in the loops below, which end when
     // every group of the warp is done, so its four groups reconverge every
     // iteration instead of running one after another
@@ -260,7 +262,7 @@ spmm_stream(int64_t m, int64_t k, const int32_t *__restrict__ rowptr,
 
         // consume cursor: row rc, next entry cp, row end ce.  Rows before the
         // first short non-empty one are stored now (empty) or skipped (long).
-        int64_t rc = rs - 1;
+        int rc = rs - 1;
         int cp = first, ce = first;
         for (;;) {
             if (++rc >= re) break;
@@ -275,7 +277,7 @@ spmm_stream(int64_t m, int64_t k, const int32_t *__restrict__ rowptr,
             break;
         }
         // issue cursor, kDepth entries ahead of the consume cursor
-        int64_t ri = rc;
+        int ri = rc;
         int ip = cp, ie = ce;
         T v[kDepth];
         uint32_t live = 0;   // bit u: slot u holds an entry
@@ -543,7 +545,7 @@ int launch(cudaStream_t st, int base, int64_t m, int64_t nnz, int64_t k, const i
     if (m == 0 || k == 0) return ok();
     constexpr int E = V16<T>::E;
     const T a = (T)alpha, b = (T)beta;
-    const bool fast = b_order == JLB_ROW_MAJOR && c_order == JLB_ROW_MAJOR && k % E == 0 &&
+    const bool fast = m < INT32_MAX && b_order == JLB_ROW_MAJOR && c_order == JLB_ROW_MAJOR && k % E == 0 &&
                       ldb % E == 0 && ldc % E == 0 && aligned16(B) && aligned16(C);
     if (fast) {
         if (b == T(0))
