@@ -29,12 +29,14 @@ JLB_DEFINE_DEV_ERROR(convert)
 namespace conv {
 
 constexpr int kThreads = 256;
+constexpr int kConvThreads = 1024;   // threads of the CSR/COO -> BSR kernels (one CTA per block row)
 constexpr int kScanItems = 8;
 constexpr int kScanTile = kThreads * kScanItems;
 constexpr int64_t kWinBits = 163840;  // block columns per bitmap window (bitmap + prefix = 40 KB)
 constexpr int kWinWords = (int)(kWinBits / 32);
 
 // ------------------------------------------------------------------ scans
+template <int NT = kThreads>
 __device__ __forceinline__ int64_t block_exclusive_scan(int64_t v, int64_t *s_warp, int64_t &total) {
     const int lane = threadIdx.x % kWarp, warp = threadIdx.x / kWarp;
     int64_t x = v;
@@ -46,16 +48,16 @@ __device__ __forceinline__ int64_t block_exclusive_scan(int64_t v, int64_t *s_wa
     if (lane == kWarp - 1) s_warp[warp] = x;
     __syncthreads();
     if (warp == 0) {
-        int64_t w = lane < kThreads / kWarp ? s_warp[lane] : 0;
+        int64_t w = lane < NT / kWarp ? s_warp[lane] : 0;
 #pragma unroll
         for (int o = 1; o < kWarp; o <<= 1) {
             const int64_t y = __shfl_up_sync(0xffffffffu, w, o);
             if (lane >= o) w += y;
         }
-        if (lane < kThreads / kWarp) s_warp[lane] = w;
+        if (lane < NT / kWarp) s_warp[lane] = w;
     }
     __syncthreads();
-    total = s_warp[kThreads / kWarp - 1];
+    total = s_warp[NT / kWarp - 1];
     const int64_t before = warp > 0 ? s_warp[warp - 1] : 0;
     __syncthreads();
     return before + x - v;
@@ -199,7 +201,7 @@ template <typename F>
 __device__ __forceinline__ void for_each_csr_row_sync(const Src &s, int64_t I, F f) {
     const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
     const int64_t i0 = I * s.b1;
-    for (int r = warp; r < s.b1; r += kThreads / kWarp) {
+    for (int r = warp; r < s.b1; r += kConvThreads / kWarp) {
         const int64_t i = i0 + r;
         if (i >= s.m) break;
         const int64_t lo = (int64_t)s.rowptr[i] - s.base, hi = (int64_t)s.rowptr[i + 1] - s.base;
@@ -234,7 +236,7 @@ __device__ __forceinline__ void for_each_entry(const Src &s, int64_t I, F f) {
     if (s.rowptr) {
         const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
         const int64_t i0 = I * s.b1;
-        for (int r = warp; r < s.b1; r += kThreads / kWarp) {
+        for (int r = warp; r < s.b1; r += kConvThreads / kWarp) {
             const int64_t i = i0 + r;
             if (i >= s.m) break;
             const int64_t lo = (int64_t)s.rowptr[i] - s.base, hi = (int64_t)s.rowptr[i + 1] - s.base;
@@ -247,7 +249,7 @@ __device__ __forceinline__ void for_each_entry(const Src &s, int64_t I, F f) {
         }
     } else {
         const int64_t e0 = s.boffs[I], e1 = s.boffs[I + 1];
-        for (int64_t e = e0 + threadIdx.x; e < e1; e += kThreads) {
+        for (int64_t e = e0 + threadIdx.x; e < e1; e += kConvThreads) {
             const int64_t p = s.bent[e];
             const int64_t i = (int64_t)s.rows[p] - s.base, j = (int64_t)s.cols[p] - s.base;
             if (i < 0 || i >= s.m || j < 0 || j >= s.n) { dev_error(DEV_ERR_BOUNDS); continue; }
@@ -288,7 +290,7 @@ __device__ __forceinline__ int64_t block_sum(int64_t v, int64_t *s_red) {
     if (threadIdx.x % kWarp == 0) s_red[threadIdx.x / kWarp] = v;
     __syncthreads();
     int64_t t = 0;
-    for (int w = 0; w < kThreads / kWarp; ++w) t += s_red[w];
+    for (int w = 0; w < kConvThreads / kWarp; ++w) t += s_red[w];
     __syncthreads();
     return t;
 }
@@ -305,20 +307,20 @@ struct Carry {
 };
 
 // Count pass: counts[I] (= browptr[I+1]) = number of distinct nonzero blocks.
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kConvThreads)
 count_blocks(Src s, int64_t mb, int64_t nb, int32_t *__restrict__ counts, Carry carry) {
     __shared__ uint32_t bits[kWinWords];
-    __shared__ int64_t s_red[kThreads / kWarp];
+    __shared__ int64_t s_red[kConvThreads / kWarp];
     for (int64_t I = blockIdx.x; I < mb; I += gridDim.x) {
         int64_t total = 0;
         for (int64_t w0 = 0; w0 < nb; w0 += kWinBits) {
             const int nw = (int)ceil_div((nb - w0) < kWinBits ? (nb - w0) : kWinBits, 32);
-            for (int w = threadIdx.x; w < nw; w += kThreads) bits[w] = 0;
+            for (int w = threadIdx.x; w < nw; w += kConvThreads) bits[w] = 0;
             __syncthreads();
             mark_window(s, I, w0, bits);
             __syncthreads();
             int64_t c = 0;
-            for (int w = threadIdx.x; w < nw; w += kThreads) {
+            for (int w = threadIdx.x; w < nw; w += kConvThreads) {
                 c += __popc(bits[w]);
                 if (carry.bits) carry.bits[I * nw + w] = bits[w];
             }
@@ -334,14 +336,14 @@ count_blocks(Src s, int64_t mb, int64_t nb, int32_t *__restrict__ counts, Carry 
 }
 
 // Fill pass.  winner == nullptr means the source has unique coordinates.
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kConvThreads)
 fill_blocks(Src s, int64_t mb, int64_t nb, int64_t nnzb, const int32_t *__restrict__ browptr,
             int32_t *__restrict__ bcolind, void *__restrict__ bval, int32_t *__restrict__ winner,
             Carry carry) {
     const bool handed = carry.bits && *carry.stamp == carry.key;
     __shared__ uint32_t bits[kWinWords];
     __shared__ int32_t pref[kWinWords];
-    __shared__ int64_t s_warp[kThreads / kWarp];
+    __shared__ int64_t s_warp[kConvThreads / kWarp];
     const int64_t bsz = (int64_t)s.b1 * s.b2;
     for (int64_t I = blockIdx.x; I < mb; I += gridDim.x) {
         int64_t q0 = (int64_t)browptr[I] - s.base, q1 = (int64_t)browptr[I + 1] - s.base;
@@ -351,33 +353,33 @@ fill_blocks(Src s, int64_t mb, int64_t nb, int64_t nnzb, const int32_t *__restri
         }
         zero_bytes(reinterpret_cast<char *>(bval), q0 * bsz * s.es, q1 * bsz * s.es);
         if (winner)
-            for (int64_t c = q0 * bsz + threadIdx.x; c < q1 * bsz; c += kThreads) winner[c] = INT32_MAX;
+            for (int64_t c = q0 * bsz + threadIdx.x; c < q1 * bsz; c += kConvThreads) winner[c] = INT32_MAX;
         __syncthreads();
         int64_t rank0 = 0;  // blocks in earlier windows
         for (int64_t w0 = 0; w0 < nb; w0 += kWinBits) {
             const int nw = (int)ceil_div((nb - w0) < kWinBits ? (nb - w0) : kWinBits, 32);
             if (handed) {
-                for (int w = threadIdx.x; w < nw; w += kThreads) bits[w] = carry.bits[I * nw + w];
+                for (int w = threadIdx.x; w < nw; w += kConvThreads) bits[w] = carry.bits[I * nw + w];
                 __syncthreads();
             } else {
-                for (int w = threadIdx.x; w < nw; w += kThreads) bits[w] = 0;
+                for (int w = threadIdx.x; w < nw; w += kConvThreads) bits[w] = 0;
                 __syncthreads();
                 mark_window(s, I, w0, bits);
                 __syncthreads();
             }
-            // exclusive prefix of the word popcounts, kThreads words at a time
+            // exclusive prefix of the word popcounts, kConvThreads words at a time
             int64_t carry = 0;
-            for (int c0 = 0; c0 < nw; c0 += kThreads) {
+            for (int c0 = 0; c0 < nw; c0 += kConvThreads) {
                 const int w = c0 + threadIdx.x;
                 const int64_t v = w < nw ? __popc(bits[w]) : 0;
                 int64_t tot;
-                const int64_t ex = block_exclusive_scan(v, s_warp, tot);
+                const int64_t ex = block_exclusive_scan<kConvThreads>(v, s_warp, tot);
                 if (w < nw) pref[w] = (int32_t)(carry + ex);
                 carry += tot;
             }
             __syncthreads();
             // block column array, ascending
-            for (int w = threadIdx.x; w < nw; w += kThreads) {
+            for (int w = threadIdx.x; w < nw; w += kConvThreads) {
                 uint32_t word = bits[w];
                 int r = pref[w];
                 while (word) {
@@ -602,7 +604,7 @@ extern "C" JLB_API int jlb_csr_to_bsr_count(void *stream, int dtype, int idx_bas
     cudaStream_t st = as_stream(stream);
     const int64_t mb = ceil_div(m, b1), nb = ceil_div(n, b2);
     if (mb > 0) {
-        conv::count_blocks<<<conv::grid_rows(mb), conv::kThreads, 0, st>>>(
+        conv::count_blocks<<<conv::grid_rows(mb), conv::kConvThreads, 0, st>>>(
             csr_src(dtype, idx_base, m, n, rowptr, colind, val, b1, b2), mb, nb, browptr + 1,
             csr_carry(workspace, workspace_bytes, m, n, nnz, b1, b2, idx_base, dtype, rowptr,
                       colind, val));
@@ -624,7 +626,7 @@ extern "C" JLB_API int jlb_csr_to_bsr_fill(void *stream, int dtype, int idx_base
     const int64_t mb = ceil_div(m, b1), nb = ceil_div(n, b2);
     if (mb == 0) return ok();
     cudaStream_t st = as_stream(stream);
-    conv::fill_blocks<<<conv::grid_rows(mb), conv::kThreads, 0, st>>>(
+    conv::fill_blocks<<<conv::grid_rows(mb), conv::kConvThreads, 0, st>>>(
         csr_src(dtype, idx_base, m, n, rowptr, colind, val, b1, b2), mb, nb, nnzb, browptr,
         bcolind, bval, nullptr,
         csr_carry(workspace, workspace_bytes, m, n, nnz, b1, b2, idx_base, dtype, rowptr, colind,
@@ -711,7 +713,7 @@ extern "C" JLB_API int jlb_coo_to_bsr_count(void *stream, int dtype, int idx_bas
     r = coo_bucket(st, dtype, idx_base, m, n, nnz, rows, cols, val, b1, workspace, &boffs, &bent);
     if (r) return r;
     if (mb > 0) {
-        conv::count_blocks<<<conv::grid_rows(mb), conv::kThreads, 0, st>>>(
+        conv::count_blocks<<<conv::grid_rows(mb), conv::kConvThreads, 0, st>>>(
             coo_src(dtype, idx_base, m, n, rows, cols, val, b1, b2, boffs, bent), mb, nb,
             browptr + 1, conv::Carry{nullptr, nullptr, 0});
         JLB_LAUNCH_CHECK("count_blocks");
@@ -750,7 +752,7 @@ extern "C" JLB_API int jlb_coo_to_bsr_fill(void *stream, int dtype, int idx_base
     k.take<int32_t>((size_t)(nnz > 0 ? nnz : 1));
     k.take<char>(conv::scan_ws(mb));
     int32_t *winner = k.take<int32_t>((size_t)nnzb * (size_t)b1 * (size_t)b2);
-    conv::fill_blocks<<<conv::grid_rows(mb), conv::kThreads, 0, st>>>(
+    conv::fill_blocks<<<conv::grid_rows(mb), conv::kConvThreads, 0, st>>>(
         coo_src(dtype, idx_base, m, n, rows, cols, val, b1, b2, boffs, bent), mb, nb, nnzb,
         browptr, bcolind, bval, winner, conv::Carry{nullptr, nullptr, 0});
     JLB_LAUNCH_CHECK("fill_blocks");
