@@ -143,15 +143,23 @@ int scan(cudaStream_t st, int64_t n, const int32_t *counts, int32_t *out, int ba
 }
 
 // ------------------------------------------------------------ value helpers
-__device__ __forceinline__ bool is_zero(const void *val, int es, int64_t p) {
-    if (es == 8) return reinterpret_cast<const double *>(val)[p] == 0.0;
-    if (es == 4) return reinterpret_cast<const float *>(val)[p] == 0.0f;
+// ES = bytes per value (8 fp64, 4 fp32, 2 bf16); the conversion kernels are
+// compiled per value size so that these are single loads and stores.
+template <int ES>
+__device__ __forceinline__ bool is_zero(const void *val, int64_t p) {
+    if (ES == 8) return reinterpret_cast<const double *>(val)[p] == 0.0;
+    if (ES == 4) return reinterpret_cast<const float *>(val)[p] == 0.0f;
     return (reinterpret_cast<const uint16_t *>(val)[p] & 0x7fffu) == 0;
 }
 
-__device__ __forceinline__ void copy_val(void *dst, int64_t q, const void *src, int64_t p, int es) {
-    if (es == 8) reinterpret_cast<uint64_t *>(dst)[q] = reinterpret_cast<const uint64_t *>(src)[p];
-    else if (es == 4) reinterpret_cast<uint32_t *>(dst)[q] = reinterpret_cast<const uint32_t *>(src)[p];
+__device__ __forceinline__ bool is_zero(const void *val, int es, int64_t p) {
+    return es == 8 ? is_zero<8>(val, p) : es == 4 ? is_zero<4>(val, p) : is_zero<2>(val, p);
+}
+
+template <int ES>
+__device__ __forceinline__ void copy_val(void *dst, int64_t q, const void *src, int64_t p) {
+    if (ES == 8) reinterpret_cast<uint64_t *>(dst)[q] = reinterpret_cast<const uint64_t *>(src)[p];
+    else if (ES == 4) reinterpret_cast<uint32_t *>(dst)[q] = reinterpret_cast<const uint32_t *>(src)[p];
     else reinterpret_cast<uint16_t *>(dst)[q] = reinterpret_cast<const uint16_t *>(src)[p];
 }
 
@@ -197,29 +205,31 @@ constexpr int kUnrollEntries = 4;   // entries per lane loaded before use
 // f(p, i, j, ok) for kUnrollEntries entries at a time (ok false for padding,
 // explicit zeros and out-of-range columns), so f may use warp shuffles.  The
 // loads of a batch are issued before any use.
-template <typename F>
+// Entry indices and columns fit 32 bits (nnz < 2^31, Int32 coordinates).
+template <int ES, typename F>
 __device__ __forceinline__ void for_each_csr_row_sync(const Src &s, int64_t I, F f) {
     const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
     const int64_t i0 = I * s.b1;
+    const int n = (int)(s.n < INT32_MAX ? s.n : INT32_MAX);
     for (int r = warp; r < s.b1; r += kConvThreads / kWarp) {
         const int64_t i = i0 + r;
         if (i >= s.m) break;
-        const int64_t lo = (int64_t)s.rowptr[i] - s.base, hi = (int64_t)s.rowptr[i + 1] - s.base;
-        for (int64_t p0 = lo; p0 < hi; p0 += (int64_t)kWarp * kUnrollEntries) {
-            int64_t jj[kUnrollEntries];
+        const int lo = s.rowptr[i] - s.base, hi = s.rowptr[i + 1] - s.base;
+        for (int p0 = lo; p0 < hi; p0 += kWarp * kUnrollEntries) {
+            int jj[kUnrollEntries];
             bool nz[kUnrollEntries];
 #pragma unroll
             for (int u = 0; u < kUnrollEntries; ++u) {
-                const int64_t p = p0 + u * kWarp + lane;
+                const int p = p0 + u * kWarp + lane;
                 nz[u] = p < hi;
-                jj[u] = nz[u] ? (int64_t)__ldg(s.cols + p) - s.base : -1;
-                if (nz[u]) nz[u] = !is_zero(s.val, s.es, p);
+                jj[u] = nz[u] ? __ldg(s.cols + p) - s.base : -1;
+                if (nz[u]) nz[u] = !is_zero<ES>(s.val, p);
             }
 #pragma unroll
             for (int u = 0; u < kUnrollEntries; ++u) {
-                const int64_t p = p0 + u * kWarp + lane;
+                const int p = p0 + u * kWarp + lane;
                 bool ok = nz[u];
-                if (ok && (jj[u] < 0 || jj[u] >= s.n)) {
+                if (ok && (jj[u] < 0 || jj[u] >= n)) {
                     dev_error(DEV_ERR_BOUNDS);
                     ok = false;
                 }
@@ -231,7 +241,7 @@ __device__ __forceinline__ void for_each_csr_row_sync(const Src &s, int64_t I, F
 
 // Calls f(p, i, j) for every nonzero entry of block row I (storage index p,
 // 0-based row i and column j).  CSR: one warp per row, lanes over entries.
-template <typename F>
+template <int ES, typename F>
 __device__ __forceinline__ void for_each_entry(const Src &s, int64_t I, F f) {
     if (s.rowptr) {
         const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
@@ -241,7 +251,7 @@ __device__ __forceinline__ void for_each_entry(const Src &s, int64_t I, F f) {
             if (i >= s.m) break;
             const int64_t lo = (int64_t)s.rowptr[i] - s.base, hi = (int64_t)s.rowptr[i + 1] - s.base;
             for (int64_t p = lo + lane; p < hi; p += kWarp) {
-                if (is_zero(s.val, s.es, p)) continue;
+                if (is_zero<ES>(s.val, p)) continue;
                 const int64_t j = (int64_t)s.cols[p] - s.base;
                 if (j < 0 || j >= s.n) { dev_error(DEV_ERR_BOUNDS); continue; }
                 f(p, i, j);
@@ -259,12 +269,13 @@ __device__ __forceinline__ void for_each_entry(const Src &s, int64_t I, F f) {
 }
 
 // Marks the block columns of window [w0, w0 + kWinBits) hit by block row I.
+template <int ES>
 __device__ __forceinline__ void mark_window(const Src &s, int64_t I, int64_t w0, uint32_t *bits) {
     if (s.rowptr) {
         // CSR: a row's columns ascend, so one atomic per run of equal block
         // columns across the lanes (compare with the previous lane; unsorted
         // rows stay correct, with more atomics)
-        for_each_csr_row_sync(s, I, [&](int64_t, int64_t, int64_t j, bool ok) {
+        for_each_csr_row_sync<ES>(s, I, [&](int64_t, int64_t, int64_t j, bool ok) {
             const int64_t J = ok ? s.blk_col(j) - w0 : -1;
             const bool in = ok && J >= 0 && J < kWinBits;
             const int64_t prev = __shfl_up_sync(0xffffffffu, in ? J : -1, 1);
@@ -273,7 +284,7 @@ __device__ __forceinline__ void mark_window(const Src &s, int64_t I, int64_t w0,
         });
         return;
     }
-    for_each_entry(s, I, [&](int64_t p, int64_t i, int64_t j) {
+    for_each_entry<ES>(s, I, [&](int64_t p, int64_t i, int64_t j) {
         const int64_t J = s.blk_col(j) - w0;
         const bool in = J >= 0 && J < kWinBits;
         // one atomic per distinct J among the lanes that agree on it
@@ -307,6 +318,7 @@ struct Carry {
 };
 
 // Count pass: counts[I] (= browptr[I+1]) = number of distinct nonzero blocks.
+template <int ES>
 __global__ void __launch_bounds__(kConvThreads)
 count_blocks(Src s, int64_t mb, int64_t nb, int32_t *__restrict__ counts, Carry carry) {
     __shared__ uint32_t bits[kWinWords];
@@ -317,7 +329,7 @@ count_blocks(Src s, int64_t mb, int64_t nb, int32_t *__restrict__ counts, Carry 
             const int nw = (int)ceil_div((nb - w0) < kWinBits ? (nb - w0) : kWinBits, 32);
             for (int w = threadIdx.x; w < nw; w += kConvThreads) bits[w] = 0;
             __syncthreads();
-            mark_window(s, I, w0, bits);
+            mark_window<ES>(s, I, w0, bits);
             __syncthreads();
             int64_t c = 0;
             for (int w = threadIdx.x; w < nw; w += kConvThreads) {
@@ -336,7 +348,8 @@ count_blocks(Src s, int64_t mb, int64_t nb, int32_t *__restrict__ counts, Carry 
 }
 
 // Fill pass.  winner == nullptr means the source has unique coordinates.
-__global__ void __launch_bounds__(kConvThreads)
+template <int ES>
+__global__ void __launch_bounds__(kConvThreads, 2)
 fill_blocks(Src s, int64_t mb, int64_t nb, int64_t nnzb, const int32_t *__restrict__ browptr,
             int32_t *__restrict__ bcolind, void *__restrict__ bval, int32_t *__restrict__ winner,
             Carry carry) {
@@ -364,7 +377,7 @@ fill_blocks(Src s, int64_t mb, int64_t nb, int64_t nnzb, const int32_t *__restri
             } else {
                 for (int w = threadIdx.x; w < nw; w += kConvThreads) bits[w] = 0;
                 __syncthreads();
-                mark_window(s, I, w0, bits);
+                mark_window<ES>(s, I, w0, bits);
                 __syncthreads();
             }
             // exclusive prefix of the word popcounts, kConvThreads words at a time
@@ -401,24 +414,24 @@ fill_blocks(Src s, int64_t mb, int64_t nb, int64_t nnzb, const int32_t *__restri
                 return (q0 + rk) * bsz + s.in_row(i) * s.b2 + s.in_col(j);
             };
             if (winner) {
-                for_each_entry(s, I, [&](int64_t p, int64_t i, int64_t j) {
+                for_each_entry<ES>(s, I, [&](int64_t p, int64_t i, int64_t j) {
                     const int64_t c = cell_of(i, j);
                     if (c >= 0) atomicMin(&winner[c], (int32_t)p);
                 });
                 __syncthreads();
-                for_each_entry(s, I, [&](int64_t p, int64_t i, int64_t j) {
+                for_each_entry<ES>(s, I, [&](int64_t p, int64_t i, int64_t j) {
                     const int64_t c = cell_of(i, j);
-                    if (c >= 0 && winner[c] == (int32_t)p) copy_val(bval, c, s.val, p, s.es);
+                    if (c >= 0 && winner[c] == (int32_t)p) copy_val<ES>(bval, c, s.val, p);
                 });
             } else if (s.rowptr) {
-                for_each_csr_row_sync(s, I, [&](int64_t p, int64_t i, int64_t j, bool ok) {
+                for_each_csr_row_sync<ES>(s, I, [&](int64_t p, int64_t i, int64_t j, bool ok) {
                     const int64_t c = ok ? cell_of(i, j) : -1;
-                    if (c >= 0) copy_val(bval, c, s.val, p, s.es);
+                    if (c >= 0) copy_val<ES>(bval, c, s.val, p);
                 });
             } else {
-                for_each_entry(s, I, [&](int64_t p, int64_t i, int64_t j) {
+                for_each_entry<ES>(s, I, [&](int64_t p, int64_t i, int64_t j) {
                     const int64_t c = cell_of(i, j);
-                    if (c >= 0) copy_val(bval, c, s.val, p, s.es);
+                    if (c >= 0) copy_val<ES>(bval, c, s.val, p);
                 });
             }
             rank0 += carry;
@@ -465,6 +478,14 @@ inline unsigned grid_for(int64_t items, int per = 256) {
     const int64_t g = ceil_div(items > 0 ? items : 1, per);
     return (unsigned)(g < 148 * 32 ? g : 148 * 32);
 }
+
+// Instantiates a conversion kernel for the value size of `es`.
+#define JLB_CONV_LAUNCH(kernel, es, grid, st, ...)                                      \
+    do {                                                                                 \
+        if ((es) == 8) conv::kernel<8><<<(grid), conv::kConvThreads, 0, (st)>>>(__VA_ARGS__); \
+        else if ((es) == 4) conv::kernel<4><<<(grid), conv::kConvThreads, 0, (st)>>>(__VA_ARGS__); \
+        else conv::kernel<2><<<(grid), conv::kConvThreads, 0, (st)>>>(__VA_ARGS__);      \
+    } while (0)
 
 inline unsigned grid_rows(int64_t mb) { return (unsigned)(mb < 148 * 64 ? (mb > 0 ? mb : 1) : 148 * 64); }
 
@@ -604,10 +625,11 @@ extern "C" JLB_API int jlb_csr_to_bsr_count(void *stream, int dtype, int idx_bas
     cudaStream_t st = as_stream(stream);
     const int64_t mb = ceil_div(m, b1), nb = ceil_div(n, b2);
     if (mb > 0) {
-        conv::count_blocks<<<conv::grid_rows(mb), conv::kConvThreads, 0, st>>>(
-            csr_src(dtype, idx_base, m, n, rowptr, colind, val, b1, b2), mb, nb, browptr + 1,
-            csr_carry(workspace, workspace_bytes, m, n, nnz, b1, b2, idx_base, dtype, rowptr,
-                      colind, val));
+        JLB_CONV_LAUNCH(count_blocks, dtype_size(dtype), conv::grid_rows(mb), st,
+                        csr_src(dtype, idx_base, m, n, rowptr, colind, val, b1, b2), mb, nb,
+                        browptr + 1,
+                        csr_carry(workspace, workspace_bytes, m, n, nnz, b1, b2, idx_base, dtype,
+                                  rowptr, colind, val));
         JLB_LAUNCH_CHECK("count_blocks");
     }
     return finish_count(st, mb, idx_base, browptr, nnzb, workspace, workspace_bytes, nullptr);
@@ -626,11 +648,11 @@ extern "C" JLB_API int jlb_csr_to_bsr_fill(void *stream, int dtype, int idx_base
     const int64_t mb = ceil_div(m, b1), nb = ceil_div(n, b2);
     if (mb == 0) return ok();
     cudaStream_t st = as_stream(stream);
-    conv::fill_blocks<<<conv::grid_rows(mb), conv::kConvThreads, 0, st>>>(
-        csr_src(dtype, idx_base, m, n, rowptr, colind, val, b1, b2), mb, nb, nnzb, browptr,
-        bcolind, bval, nullptr,
-        csr_carry(workspace, workspace_bytes, m, n, nnz, b1, b2, idx_base, dtype, rowptr, colind,
-                  val));
+    JLB_CONV_LAUNCH(fill_blocks, dtype_size(dtype), conv::grid_rows(mb), st,
+                    csr_src(dtype, idx_base, m, n, rowptr, colind, val, b1, b2), mb, nb, nnzb,
+                    browptr, bcolind, bval, nullptr,
+                    csr_carry(workspace, workspace_bytes, m, n, nnz, b1, b2, idx_base, dtype,
+                              rowptr, colind, val));
     JLB_LAUNCH_CHECK("fill_blocks");
     return ok();
 }
@@ -713,9 +735,9 @@ extern "C" JLB_API int jlb_coo_to_bsr_count(void *stream, int dtype, int idx_bas
     r = coo_bucket(st, dtype, idx_base, m, n, nnz, rows, cols, val, b1, workspace, &boffs, &bent);
     if (r) return r;
     if (mb > 0) {
-        conv::count_blocks<<<conv::grid_rows(mb), conv::kConvThreads, 0, st>>>(
-            coo_src(dtype, idx_base, m, n, rows, cols, val, b1, b2, boffs, bent), mb, nb,
-            browptr + 1, conv::Carry{nullptr, nullptr, 0});
+        JLB_CONV_LAUNCH(count_blocks, dtype_size(dtype), conv::grid_rows(mb), st,
+                        coo_src(dtype, idx_base, m, n, rows, cols, val, b1, b2, boffs, bent), mb,
+                        nb, browptr + 1, conv::Carry{nullptr, nullptr, 0});
         JLB_LAUNCH_CHECK("count_blocks");
     }
     // The bucket scan already used the scan workspace; reuse it for browptr.
@@ -752,9 +774,9 @@ extern "C" JLB_API int jlb_coo_to_bsr_fill(void *stream, int dtype, int idx_base
     k.take<int32_t>((size_t)(nnz > 0 ? nnz : 1));
     k.take<char>(conv::scan_ws(mb));
     int32_t *winner = k.take<int32_t>((size_t)nnzb * (size_t)b1 * (size_t)b2);
-    conv::fill_blocks<<<conv::grid_rows(mb), conv::kConvThreads, 0, st>>>(
-        coo_src(dtype, idx_base, m, n, rows, cols, val, b1, b2, boffs, bent), mb, nb, nnzb,
-        browptr, bcolind, bval, winner, conv::Carry{nullptr, nullptr, 0});
+    JLB_CONV_LAUNCH(fill_blocks, dtype_size(dtype), conv::grid_rows(mb), st,
+                    coo_src(dtype, idx_base, m, n, rows, cols, val, b1, b2, boffs, bent), mb, nb,
+                    nnzb, browptr, bcolind, bval, winner, conv::Carry{nullptr, nullptr, 0});
     JLB_LAUNCH_CHECK("fill_blocks");
     return ok();
 }
