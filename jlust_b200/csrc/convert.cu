@@ -191,6 +191,9 @@ struct Src {
     __device__ __forceinline__ int64_t blk_col(int64_t j) const { return sh2 >= 0 ? j >> sh2 : j / b2; }
     __device__ __forceinline__ int64_t in_col(int64_t j) const { return sh2 >= 0 ? j & (b2 - 1) : j % b2; }
     __device__ __forceinline__ int64_t in_row(int64_t i) const { return sh1 >= 0 ? i & (b1 - 1) : i % b1; }
+    // 32-bit forms for CSR columns (Int32 coordinates)
+    __device__ __forceinline__ int blk_col32(int j) const { return sh2 >= 0 ? j >> sh2 : j / b2; }
+    __device__ __forceinline__ int in_col32(int j) const { return sh2 >= 0 ? j & (b2 - 1) : j % b2; }
 };
 
 inline int log2_exact(int b) {
@@ -275,10 +278,11 @@ __device__ __forceinline__ void mark_window(const Src &s, int64_t I, int64_t w0,
         // CSR: a row's columns ascend, so one atomic per run of equal block
         // columns across the lanes (compare with the previous lane; unsorted
         // rows stay correct, with more atomics)
-        for_each_csr_row_sync<ES>(s, I, [&](int64_t, int64_t, int64_t j, bool ok) {
-            const int64_t J = ok ? s.blk_col(j) - w0 : -1;
+        const int w0i = (int)w0;   // block columns fit 32 bits
+        for_each_csr_row_sync<ES>(s, I, [&](int, int64_t, int j, bool ok) {
+            const int J = ok ? s.blk_col32(j) - w0i : -1;
             const bool in = ok && J >= 0 && J < kWinBits;
-            const int64_t prev = __shfl_up_sync(0xffffffffu, in ? J : -1, 1);
+            const int prev = __shfl_up_sync(0xffffffffu, in ? J : -1, 1);
             const bool lead = (threadIdx.x % kWarp) == 0 || prev != J;
             if (in && lead) atomicOr(&bits[J >> 5], 1u << (J & 31));
         });
@@ -424,9 +428,16 @@ fill_blocks(Src s, int64_t mb, int64_t nb, int64_t nnzb, const int32_t *__restri
                     if (c >= 0 && winner[c] == (int32_t)p) copy_val<ES>(bval, c, s.val, p);
                 });
             } else if (s.rowptr) {
-                for_each_csr_row_sync<ES>(s, I, [&](int64_t p, int64_t i, int64_t j, bool ok) {
-                    const int64_t c = ok ? cell_of(i, j) : -1;
-                    if (c >= 0) copy_val<ES>(bval, c, s.val, p);
+                // CSR: the same cell in 32-bit arithmetic (block ranks < nnzb < 2^31)
+                const int w0i = (int)w0, rank0i = (int)rank0;
+                for_each_csr_row_sync<ES>(s, I, [&](int p, int64_t i, int j, bool ok) {
+                    if (!ok) return;
+                    const int J = s.blk_col32(j) - w0i;
+                    if ((unsigned)J >= (unsigned)kWinBits) return;
+                    const uint32_t word = bits[J >> 5];
+                    const int rk = rank0i + pref[J >> 5] + __popc(word & ((1u << (J & 31)) - 1u));
+                    if (q0 + rk >= q1) { dev_error(DEV_ERR_BOUNDS); return; }
+                    copy_val<ES>(bval, (q0 + rk) * bsz + s.in_row(i) * s.b2 + s.in_col32(j), s.val, p);
                 });
             } else {
                 for_each_entry<ES>(s, I, [&](int64_t p, int64_t i, int64_t j) {
