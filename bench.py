@@ -792,13 +792,14 @@ def run_ours(args):
     if traffic is not None and ctx.world > 1:
         traffic /= ctx.world        # the capture is of the 1-GPU launch; rows split evenly
     if getattr(W, "bound", "hbm") == "tensor":
-        achieved = W.flops() / per_launch_s / 1e12
+        # per GPU, like the HBM roofline: the job's work / N over the step time
+        achieved = (W.flops() / ctx.world) / per_launch_s / 1e12
+        hbm = (W.bytes() / ctx.world) / per_launch_s / 1e9
         roof = {"bound": "tensor", "kernel": W.kernel, "achieved": round(achieved, 2),
                 "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                 "frac": round(achieved / pk["bf16_tflops"], 4), "traffic": traffic,
                 "peak_source": pk["source"] + " (bf16_tflops, cuBLAS burst)",
-                "hbm_achieved_gbs": round(W.bytes() / per_launch_s / 1e9, 1),
-                "hbm_frac": round(W.bytes() / per_launch_s / 1e9 / pk["hbm_gbs"], 4)}
+                "hbm_achieved_gbs": round(hbm, 1), "hbm_frac": round(hbm / pk["hbm_gbs"], 4)}
     else:
         achieved = (W.bytes() / ctx.world) / per_launch_s / 1e9
         roof = {"bound": "hbm", "kernel": W.kernel, "achieved": round(achieved, 1),
@@ -806,7 +807,8 @@ def run_ours(args):
                 "traffic": traffic, "peak_source": pk["source"] + " (hbm_gbs, copy burst)",
                 "algorithmic_bytes_per_launch": W.bytes() / ctx.world}
     if ctx.world > 1:
-        roof["note"] = "per-rank bytes over the whole step, halo exchange included"
+        roof["note"] = ("per GPU: the job's work / N over the step time (max over ranks)"
+                        + (", halo exchange included" if args.workload == "laplacian" else ""))
 
     e2e = None
     if not args.no_e2e:
