@@ -155,3 +155,21 @@ def test_l2_persisting_window_same_results():
         assert np.array_equal(xa.cpu().numpy(), xr)
     finally:
         assert J.l2_persist(0, 0) == 0
+
+
+def test_row_range_views_match_whole():
+    """SpMV through row-range views of one CSR (row pointer slices over the
+    same columns and values, as a chunked pipeline uses them) gives the same
+    bits as the whole matrix."""
+    rp, ci, val, x = synth.config2(g=512)
+    n = 512 * 512
+    rpd, cid, vd, xd = to_dev(rp), to_dev(ci), to_dev(val), to_dev(x)
+    whole = torch.empty(n, dtype=torch.float64, device=DEV)
+    J.execute(J.SpMVOp, J.csr_tensor(rpd, cid, vd, (n, n), origin=0), xd, whole)
+    parts = torch.empty(n, dtype=torch.float64, device=DEV)
+    b = [n * c // 7 for c in range(8)]
+    for lo, hi in zip(b[:-1], b[1:]):
+        J.execute(J.SpMVOp, J.csr_tensor(rpd[lo:hi + 1], cid, vd, (hi - lo, n), origin=0), xd,
+                  parts[lo:hi])
+    J.device_status()
+    assert torch.equal(whole, parts)
