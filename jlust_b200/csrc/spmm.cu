@@ -15,7 +15,7 @@
 // still (3.9 ms): per-copy cost dominates at this size.
 //
 // spmm_stream: each group owns a contiguous range of rows, balanced by rows +
-// entries (each group finds its range with an 8-ary search of the row
+// entries (each group finds its range with a 9-ary search of the row
 // pointer), and streams through the range's entries in storage order across
 // row boundaries; a row's chunk of C is stored when its last entry is in.
 // Per output element the sum runs over the row's entries in storage order with
@@ -172,15 +172,15 @@ __device__ __forceinline__ unsigned group_mask(int tid) {
 }
 
 // Smallest rows r0, r1 in [0, m] with r + rowptr[r] - base >= t0 (resp. t1):
-// both 8-ary searches run together, each lane of the group probing one point
+// both (kGroup+1)-ary searches run together, each lane of the group probing one point
 // of each interval per step (about log9(m) dependent loads).
 __device__ __forceinline__ void find_rows(int64_t m, const int32_t *__restrict__ rowptr, int base,
                                           int64_t t0, int64_t t1, int lane, unsigned gmask,
                                           int shift, int64_t &r0, int64_t &r1) {
     int64_t lo0 = 0, hi0 = m, lo1 = 0, hi1 = m;
     while (lo0 < hi0 || lo1 < hi1) {
-        const int64_t p0 = lo0 + (hi0 - lo0) * (lane + 1) / 9;
-        const int64_t p1 = lo1 + (hi1 - lo1) * (lane + 1) / 9;
+        const int64_t p0 = lo0 + (hi0 - lo0) * (lane + 1) / (kGroup + 1);
+        const int64_t p1 = lo1 + (hi1 - lo1) * (lane + 1) / (kGroup + 1);
         const bool q0 = lo0 < hi0 && p0 + (ldg(rowptr + p0) - base) >= t0;
         const bool q1 = lo1 < hi1 && p1 + (ldg(rowptr + p1) - base) >= t1;
         const unsigned b0 = (__ballot_sync(gmask, q0) >> shift) & ((1u << kGroup) - 1u);
@@ -189,20 +189,20 @@ __device__ __forceinline__ void find_rows(int64_t m, const int32_t *__restrict__
             const int64_t span = hi0 - lo0;
             if (b0) {
                 const int f = __ffs(b0) - 1;
-                hi0 = lo0 + span * (f + 1) / 9;
-                if (f > 0) lo0 = lo0 + span * f / 9 + 1;
+                hi0 = lo0 + span * (f + 1) / (kGroup + 1);
+                if (f > 0) lo0 = lo0 + span * f / (kGroup + 1) + 1;
             } else {
-                lo0 = lo0 + span * 8 / 9 + 1;
+                lo0 = lo0 + span * kGroup / (kGroup + 1) + 1;
             }
         }
         if (lo1 < hi1) {
             const int64_t span = hi1 - lo1;
             if (b1) {
                 const int f = __ffs(b1) - 1;
-                hi1 = lo1 + span * (f + 1) / 9;
-                if (f > 0) lo1 = lo1 + span * f / 9 + 1;
+                hi1 = lo1 + span * (f + 1) / (kGroup + 1);
+                if (f > 0) lo1 = lo1 + span * f / (kGroup + 1) + 1;
             } else {
-                lo1 = lo1 + span * 8 / 9 + 1;
+                lo1 = lo1 + span * kGroup / (kGroup + 1) + 1;
             }
         }
     }
