@@ -9,7 +9,7 @@
 // kDepth - 1 entries are in flight.  Holding the data in flight in shared
 // memory instead of registers keeps registers at 64 and 32 warps resident per
 // SM; measured on config 3 (power-law, k = 64), more resident warps with 3
-// slots each beat deeper pipelines (1.40 ms per SpMM at depth 3, 4 CTAs/SM;
+// slots each beat deeper pipelines (1.37 ms per SpMM at depth 3, 4 CTAs/SM;
 // 2.5 ms at depth 12, 2 CTAs/SM; 2.0 ms with registers as slots).  The
 // untiled bulk copy (cp.async.bulk, one 256-byte copy per entry) was slower
 // still (3.9 ms): per-copy cost dominates at this size.
@@ -51,7 +51,7 @@ constexpr int kChunkBytes = kGroup * kVec * 16;  // one B-row chunk (256 bytes)
 constexpr int kLong = 256;                     // longer rows go to spmm_long_rows
 constexpr int kDepth = 3;                      // B-row chunks in flight per group
 constexpr int kMinWork = 64;                   // rows + entries per stream group, at least
-constexpr int kScanRows = 512;                 // rows a long-row CTA inspects
+constexpr int kScanRows = 256;                 // rows a long-row CTA inspects
 constexpr int kSlotBytes = kGroups * kDepth * kChunkBytes;
 
 template <typename T>
