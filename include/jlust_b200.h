@@ -114,6 +114,33 @@ JLB_API int jlb_csr_spmv(void *stream, int dtype, int idx_base, int64_t m, int64
                          int64_t nnz, const int32_t *rowptr, const int32_t *colind,
                          const void *val, const void *x, void *y, double alpha, double beta);
 
+/* y = alpha * A * x + beta * y for an m x n DCSR matrix: nfib stored rows,
+ * row_ids[f] (nfib, the outer level's coordinates) the row of stored row f,
+ * fibptr (nfib + 1, the inner level's positions) and colind / val its
+ * entries.  Stored rows are summed exactly as jlb_csr_spmv sums a CSR row;
+ * rows that are not stored are not written (JLUST's DCSR walk,
+ * ext/KernelAbstractionsExt/ops/_walker.jl:323-342, dispatched from
+ * ops/spmv.jl:371-504; KAT test/test_emitter.jl:127-157). */
+JLB_API int jlb_dcsr_spmv(void *stream, int dtype, int idx_base, int64_t m, int64_t n,
+                          int64_t nfib, int64_t nnz, const int32_t *fibptr,
+                          const int32_t *row_ids, const int32_t *colind, const void *val,
+                          const void *x, void *y, double alpha, double beta);
+
+/* y = alpha * A * x + beta * y for COO (row and column coordinates per entry,
+ * any order, duplicates add) and for CSC (column pointer n + 1, row
+ * coordinates).  As in JLUST's COO and scatter paths
+ * (ext/KernelAbstractionsExt/ops/spmv.jl:386-420, ops/_walker.jl:343-375),
+ * y is scaled by beta first (set to 0 when beta == 0) and every entry adds
+ * alpha * v * x[col] to its row with an atomic add, so the order of a row's
+ * terms is not fixed: results agree within floating-point tolerance, not
+ * bit for bit.  KAT test/test_emitter.jl:161-192 (COO). */
+JLB_API int jlb_coo_spmv(void *stream, int dtype, int idx_base, int64_t m, int64_t n,
+                         int64_t nnz, const int32_t *rows, const int32_t *cols, const void *val,
+                         const void *x, void *y, double alpha, double beta);
+JLB_API int jlb_csc_spmv(void *stream, int dtype, int idx_base, int64_t m, int64_t n,
+                         int64_t nnz, const int32_t *colptr, const int32_t *rowind,
+                         const void *val, const void *x, void *y, double alpha, double beta);
+
 /* Prepared SpMV: validates the structure once, records the row-length
  * profile and picks the kernel variant.  Replaces prepare(backend, SpMVOp,
  * u_A) (src/ops.jl:187-202; EmitterSpMVHandle, KA spmv.jl:518-531). */

@@ -58,7 +58,8 @@ def supports_backend(backend, op: Op) -> bool:
         return False
     f = op.formats
     if op.tag == "SpMV" and len(f) == 3:
-        return f[0].family == "CSR" and _dense_n(f[1], 1) and _dense_n(f[2], 1)
+        return (f[0].family in ("CSR", "DCSR", "COO", "CSC") and _dense_n(f[1], 1)
+                and _dense_n(f[2], 1))
     if op.tag == "SpMM" and len(f) == 3:
         return f[0].family in ("CSR", "BSR") and _dense_n(f[1], 2) and _dense_n(f[2], 2)
     if op.tag == "SDDMM" and len(f) == 3:
@@ -117,16 +118,41 @@ def spmv(A: USTensor, x, y, alpha=1.0, beta=0.0, input_fn=None, output_fn=None):
     if input_fn is not None or output_fn is not None:
         raise UnsupportedFormat("B200Backend: input_fn/output_fn closures cannot cross the C ABI")
     x, y = ust(x).val, ust(y).val
-    m, n, rowptr, colind, val = _csr_parts(A)
+    fam = A.format.family
+    if fam not in ("CSR", "DCSR", "COO", "CSC"):
+        raise UnsupportedFormat(f"B200Backend SpMV: format {A.format.name} is not supported")
+    m, n = A.extents
+    val = nonzeros(A)
+    if val.dim() != 1 or not val.is_contiguous():
+        raise IncompatibleExtents("SpMV: values must be a contiguous vector")
     dt = _value_type(val, (torch.float32, torch.float64), "SpMV")
     if x.dtype != val.dtype or y.dtype != val.dtype:
         raise UnsupportedValueType("SpMV: A, x and y must share one value type")
     _vec(x, "x"), _vec(y, "y")
     if x.numel() != n or y.numel() != m:
         raise IncompatibleExtents(f"SpMV: A is {m}x{n}, x has {x.numel()}, y has {y.numel()}")
-    dev = _same_device(rowptr, colind, val, x, y)
-    _lib.call("jlb_csr_spmv", _stream(dev), dt, A.origin.offset, m, n, val.numel(), _ptr(rowptr),
-              _ptr(colind), _ptr(val), _ptr(x), _ptr(y), float(alpha), float(beta))
+    base, nnz, a, b = A.origin.offset, val.numel(), float(alpha), float(beta)
+    if fam == "CSR":
+        rowptr, colind = positions(A, 2), coordinates(A, 2)
+        dev = _same_device(rowptr, colind, val, x, y)
+        _lib.call("jlb_csr_spmv", _stream(dev), dt, base, m, n, nnz, _ptr(rowptr), _ptr(colind),
+                  _ptr(val), _ptr(x), _ptr(y), a, b)
+    elif fam == "DCSR":
+        # outer level: stored rows (coordinates); inner level: positions + columns
+        row_ids, fibptr, colind = coordinates(A, 1), positions(A, 2), coordinates(A, 2)
+        dev = _same_device(row_ids, fibptr, colind, val, x, y)
+        _lib.call("jlb_dcsr_spmv", _stream(dev), dt, base, m, n, row_ids.numel(), nnz,
+                  _ptr(fibptr), _ptr(row_ids), _ptr(colind), _ptr(val), _ptr(x), _ptr(y), a, b)
+    elif fam == "COO":
+        rows, cols = coordinates(A, 1), coordinates(A, 2)
+        dev = _same_device(rows, cols, val, x, y)
+        _lib.call("jlb_coo_spmv", _stream(dev), dt, base, m, n, nnz, _ptr(rows), _ptr(cols),
+                  _ptr(val), _ptr(x), _ptr(y), a, b)
+    else:  # CSC: dense outer level over columns, compressed rows inside
+        colptr, rowind = positions(A, 2), coordinates(A, 2)
+        dev = _same_device(colptr, rowind, val, x, y)
+        _lib.call("jlb_csc_spmv", _stream(dev), dt, base, m, n, nnz, _ptr(colptr), _ptr(rowind),
+                  _ptr(val), _ptr(x), _ptr(y), a, b)
     return y
 
 

@@ -60,21 +60,35 @@ __device__ __forceinline__ T row_sum(int lo, int hi, const int32_t *__restrict__
     return acc;
 }
 
-template <typename T, bool kBeta>
+// kRowIds: DCSR, whose compressed outer level stores only the non-empty rows:
+// `m` counts the stored rows, rowptr is the inner level's position buffer and
+// row_ids[f] the row of stored row f (JLUST's DCSR walk,
+// ext/KernelAbstractionsExt/ops/_walker.jl:323-342: rows not stored are not
+// written).  Otherwise plain CSR with row_ids unused.
+template <typename T, bool kBeta, bool kRowIds = false>
 __global__ void __launch_bounds__(kThreads)
 spmv_rows(int64_t m, const int32_t *__restrict__ rowptr, const int32_t *__restrict__ colind,
           const T *__restrict__ val, const T *__restrict__ x, T *__restrict__ y, T alpha, T beta,
-          int base) {
-    const int64_t r = (int64_t)blockIdx.x * kThreads + threadIdx.x;
+          int base, const int32_t *__restrict__ row_ids = nullptr, int64_t nrows = 0) {
+    const int64_t f = (int64_t)blockIdx.x * kThreads + threadIdx.x;
     const int lane = threadIdx.x % kWarp;
     int lo = 0, hi = 0;
-    if (r < m) {
-        lo = ldg(rowptr + r) - base;
-        hi = ldg(rowptr + r + 1) - base;
+    int64_t r = f;
+    bool live = f < m;
+    if (live) {
+        lo = ldg(rowptr + f) - base;
+        hi = ldg(rowptr + f + 1) - base;
+        if (kRowIds) {
+            r = (int64_t)ldg(row_ids + f) - base;
+            if (r < 0 || r >= nrows) {
+                dev_error(DEV_ERR_BOUNDS);
+                live = false;
+            }
+        }
     }
     const bool is_long = hi - lo > kShortMax;
-    if (r < m && !is_long) write_row<T, kBeta>(y, r, row_sum<T>(lo, hi, colind, val, x, base), alpha, beta);
-    unsigned longs = __ballot_sync(0xffffffffu, r < m && is_long);
+    if (live && !is_long) write_row<T, kBeta>(y, r, row_sum<T>(lo, hi, colind, val, x, base), alpha, beta);
+    unsigned longs = __ballot_sync(0xffffffffu, live && is_long);
     while (longs) {
         const int src = __ffs(longs) - 1;
         longs &= longs - 1;
@@ -85,6 +99,25 @@ spmv_rows(int64_t m, const int32_t *__restrict__ rowptr, const int32_t *__restri
         acc = warp_sum(acc);
         if (lane == src) write_row<T, kBeta>(y, r, acc, alpha, beta);
     }
+}
+
+template <typename T>
+int launch_dcsr(cudaStream_t st, int base, int64_t nrows, int64_t nfib, const int32_t *fibptr,
+                const int32_t *row_ids, const int32_t *colind, const void *val, const void *x,
+                void *y, double alpha, double beta) {
+    if (nfib == 0) return ok();
+    const T a = (T)alpha, b = (T)beta;
+    const unsigned grid = (unsigned)ceil_div(nfib, kThreads);
+    if (b == T(0))
+        spmv_rows<T, false, true><<<grid, kThreads, 0, st>>>(nfib, fibptr, colind, (const T *)val,
+                                                              (const T *)x, (T *)y, a, b, base,
+                                                              row_ids, nrows);
+    else
+        spmv_rows<T, true, true><<<grid, kThreads, 0, st>>>(nfib, fibptr, colind, (const T *)val,
+                                                             (const T *)x, (T *)y, a, b, base,
+                                                             row_ids, nrows);
+    JLB_LAUNCH_CHECK("spmv_rows (DCSR)");
+    return ok();
 }
 
 template <typename T>
@@ -209,6 +242,22 @@ extern "C" JLB_API int jlb_csr_spmv(void *stream, int dtype, int idx_base, int64
                                     y, alpha, beta);
     return spmv::launch<float>(as_stream(stream), idx_base, m, nnz, rowptr, colind, val, x, y,
                                alpha, beta);
+}
+
+extern "C" JLB_API int jlb_dcsr_spmv(void *stream, int dtype, int idx_base, int64_t m, int64_t n,
+                                     int64_t nfib, int64_t nnz, const int32_t *fibptr,
+                                     const int32_t *row_ids, const int32_t *colind,
+                                     const void *val, const void *x, void *y, double alpha,
+                                     double beta) {
+    int st = spmv_args(dtype, idx_base, nfib, n, nnz, fibptr, colind, val, x, y);
+    if (st) return st;
+    if (m < 0 || nfib > m) return fail(JLB_ERR_INCOMPATIBLE_EXTENTS, "more stored rows than rows");
+    if (nfib > 0 && !row_ids) return fail(JLB_ERR_INVALID_ARGUMENT, "null row coordinates");
+    if (dtype == JLB_F64)
+        return spmv::launch_dcsr<double>(as_stream(stream), idx_base, m, nfib, fibptr, row_ids,
+                                         colind, val, x, y, alpha, beta);
+    return spmv::launch_dcsr<float>(as_stream(stream), idx_base, m, nfib, fibptr, row_ids, colind,
+                                    val, x, y, alpha, beta);
 }
 
 struct jlb_spmv_plan_s {

@@ -87,6 +87,59 @@ OR_EXPORT void NAME(int64_t m, const int32_t *rowptr, const int32_t *colind,    
 DEFINE_SPMV(or_csr_spmv_f64, double)
 DEFINE_SPMV(or_csr_spmv_f32, float)
 
+/* DCSR SpMV: JLUST's DCSR walk (ext/KernelAbstractionsExt/ops/_walker.jl:
+ * 323-342, dispatched from ops/spmv.jl:371-504).  Stored row f is row
+ * row_ids[f]; its entries fibptr[f] .. fibptr[f+1]-1 are summed in storage
+ * order as a CSR row is; rows that are not stored are not written. */
+#define DEFINE_DCSR_SPMV(NAME, T)                                               \
+OR_EXPORT void NAME(int64_t nfib, const int32_t *fibptr, const int32_t *row_ids, \
+                    const int32_t *colind, const T *val, const T *x, T *y,      \
+                    double alpha_d, double beta_d, int base) {                  \
+    const T alpha = (T)alpha_d, beta = (T)beta_d;                               \
+    const int zero_beta = (beta == (T)0);                                       \
+    for (int64_t f = 0; f < nfib; ++f) {                                        \
+        const int64_t r = (int64_t)row_ids[f] - base;                           \
+        T acc = (T)0;                                                           \
+        for (int64_t k = (int64_t)fibptr[f] - base; k < (int64_t)fibptr[f + 1] - base; ++k) { \
+            T prod = val[k] * x[(int64_t)colind[k] - base];                     \
+            acc = acc + prod;                                                   \
+        }                                                                       \
+        T out = alpha * acc;                                                    \
+        if (!zero_beta) { T by = beta * y[r]; out = out + by; }                 \
+        y[r] = out;                                                             \
+    }                                                                           \
+}
+
+DEFINE_DCSR_SPMV(or_dcsr_spmv_f64, double)
+DEFINE_DCSR_SPMV(or_dcsr_spmv_f32, float)
+
+/* COO and CSC SpMV: JLUST's COO and scatter paths (ops/spmv.jl:386-420):
+ * y scaled by beta (set to 0 when beta is 0), then every entry, in storage
+ * order here, adds (alpha * v) * x[col] to its row.  The reference and the
+ * GPU add the same terms in an order that is not fixed (atomics). */
+#define DEFINE_ENTRY_SPMV(NAME, T)                                              \
+OR_EXPORT void NAME(int64_t m, int64_t n, int64_t nnz, const int32_t *rows,     \
+                    const int32_t *cols, const int32_t *colptr, const T *val,   \
+                    const T *x, T *y, double alpha_d, double beta_d, int base) { \
+    const T alpha = (T)alpha_d, beta = (T)beta_d;                               \
+    for (int64_t r = 0; r < m; ++r) y[r] = (beta == (T)0) ? (T)0 : beta * y[r]; \
+    if (colptr) {                                                               \
+        for (int64_t j = 0; j < n; ++j)                                         \
+            for (int64_t p = (int64_t)colptr[j] - base; p < (int64_t)colptr[j + 1] - base; ++p) { \
+                T t = alpha * val[p];                                           \
+                y[(int64_t)rows[p] - base] += t * x[j];                         \
+            }                                                                   \
+    } else {                                                                    \
+        for (int64_t p = 0; p < nnz; ++p) {                                     \
+            T t = alpha * val[p];                                               \
+            y[(int64_t)rows[p] - base] += t * x[(int64_t)cols[p] - base];       \
+        }                                                                       \
+    }                                                                           \
+}
+
+DEFINE_ENTRY_SPMV(or_entry_spmv_f64, double)
+DEFINE_ENTRY_SPMV(or_entry_spmv_f32, float)
+
 /* fp64 reference of the same product plus the per-row magnitude bound
  * sum_k |v_k * x_k|, used for tolerance checks of any value type. */
 OR_EXPORT void or_csr_spmv_ref64(int dtype, int64_t m, const int32_t *rowptr,

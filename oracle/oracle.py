@@ -54,6 +54,10 @@ def _declare(L):
     for n in ("or_csr_spmv_f64", "or_csr_spmv_f32"):
         getattr(L, n).argtypes = [_i64, _p, _p, _p, _p, _p, _d, _d, _i]
     L.or_csr_spmv_ref64.argtypes = [_i, _i64, _p, _p, _p, _p, _p, _p, _p, _d, _d, _i]
+    for n in ("or_dcsr_spmv_f64", "or_dcsr_spmv_f32"):
+        getattr(L, n).argtypes = [_i64, _p, _p, _p, _p, _p, _p, _d, _d, _i]
+    for n in ("or_entry_spmv_f64", "or_entry_spmv_f32"):
+        getattr(L, n).argtypes = [_i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _d, _d, _i]
     for n in ("or_csr_spmm_f32", "or_csr_spmm_f64"):
         getattr(L, n).argtypes = [_i64, _i64, _p, _p, _p, _p, _i64, _i, _p, _i64, _i, _d, _d, _i]
     L.or_csr_spmm_ref64_f32.argtypes = [_i64, _i64, _p, _p, _p, _p, _i64, _i, _p, _i64, _i,
@@ -126,6 +130,51 @@ def spmv(rowptr, colind, val, x, y=None, alpha=1.0, beta=0.0, base=0):
           np.dtype(np.float32): lib().or_csr_spmv_f32}[val.dtype]
     fn(m, _ptr(rowptr), _ptr(colind), _ptr(val), _ptr(x), _ptr(y), alpha, beta, base)
     return y
+
+
+def dcsr_spmv(m, fibptr, row_ids, colind, val, x, y=None, alpha=1.0, beta=0.0, base=0):
+    """DCSR y = alpha*A*x + beta*y on the stored rows only (JLUST's DCSR walk,
+    ext/KernelAbstractionsExt/ops/_walker.jl:323-342); other rows keep y."""
+    fibptr, row_ids, colind = (_c(a, np.int32) for a in (fibptr, row_ids, colind))
+    val = _c(val)
+    x = _c(x, val.dtype)
+    y = np.zeros(m, val.dtype) if y is None else _c(y, val.dtype).copy()
+    fn = {np.dtype(np.float64): lib().or_dcsr_spmv_f64,
+          np.dtype(np.float32): lib().or_dcsr_spmv_f32}[val.dtype]
+    fn(row_ids.shape[0], _ptr(fibptr), _ptr(row_ids), _ptr(colind), _ptr(val), _ptr(x), _ptr(y),
+       alpha, beta, base)
+    return y
+
+
+def entry_spmv(m, n, rows, val, x, cols=None, colptr=None, y=None, alpha=1.0, beta=0.0, base=0):
+    """COO (rows, cols) or CSC (colptr, rows) SpMV as JLUST's COO / scatter
+    paths (ops/spmv.jl:386-420): y scaled by beta, then each entry adds
+    (alpha*v)*x[col] to its row, here in storage order."""
+    rows = _c(rows, np.int32)
+    val = _c(val)
+    x = _c(x, val.dtype)
+    cols = None if cols is None else _c(cols, np.int32)
+    colptr = None if colptr is None else _c(colptr, np.int32)
+    y = np.zeros(m, val.dtype) if y is None else _c(y, val.dtype).copy()
+    fn = {np.dtype(np.float64): lib().or_entry_spmv_f64,
+          np.dtype(np.float32): lib().or_entry_spmv_f32}[val.dtype]
+    fn(m, n, val.shape[0], _ptr(rows), _ptr(cols), _ptr(colptr), _ptr(val), _ptr(x), _ptr(y),
+       alpha, beta, base)
+    return y
+
+
+def entry_spmv_ref64(m, rows, cols, val, x, y=None, alpha=1.0, beta=0.0, base=0):
+    """fp64 y and the bound |alpha|*sum|v*x| + |beta*y| per row, from the
+    (row, col) list of the entries (COO, or CSC with cols expanded)."""
+    r = np.asarray(rows, np.int64) - base
+    c = np.asarray(cols, np.int64) - base
+    t = np.asarray(val, np.float64) * np.asarray(x, np.float64)[c]
+    acc = np.zeros(m)
+    mag = np.zeros(m)
+    np.add.at(acc, r, t)
+    np.add.at(mag, r, np.abs(t))
+    yo = np.zeros(m) if y is None or beta == 0 else np.asarray(y, np.float64)
+    return alpha * acc + beta * yo, abs(alpha) * mag + np.abs(beta * yo)
 
 
 def spmv_ref64(rowptr, colind, val, x, y=None, alpha=1.0, beta=0.0, base=0):

@@ -24,6 +24,16 @@ KATS = {
     "spmv_csr_zerobased": {
         "source": "test/test_emitter.jl:106-123",
         "A": A_ZERO, "x": [1.0, 2.0, 3.0], "alpha": 1.0, "beta": 0.0, "y": [7.0, 6.0, 19.0]},
+    "spmv_dcsr_onebased": {
+        "source": "test/test_emitter.jl:127-157 (row 2 not stored, y starts at zero)",
+        "m": 3, "n": 3, "row_ids": [1, 3], "fibptr": [1, 3, 5], "colind": [1, 3, 1, 3],
+        "val": [1.0, 2.0, 4.0, 5.0], "base": 1, "x": [1.0, 2.0, 3.0], "y0": [0.0, 0.0, 0.0],
+        "alpha": 1.0, "beta": 0.0, "y": [7.0, 0.0, 19.0]},
+    "spmv_coo_onebased": {
+        "source": "test/test_emitter.jl:161-192",
+        "m": 3, "n": 3, "rows": [1, 1, 2, 3, 3], "cols": [1, 3, 2, 1, 3],
+        "val": [1.0, 2.0, 3.0, 4.0, 5.0], "base": 1, "x": [1.0, 2.0, 3.0],
+        "alpha": 1.0, "beta": 0.0, "y": [7.0, 6.0, 19.0]},
     "spmm_csr_onebased": {
         "source": "test/test_emitter.jl:196-228; test/test_cuda.jl:304-314",
         "A": A_ONE, "B": [[1.0, 0.0], [2.0, 1.0], [0.0, 3.0]], "alpha": 1.0, "beta": 0.0,

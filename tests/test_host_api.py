@@ -40,6 +40,9 @@ def test_supports_backend_table():
     be = J.B200Backend()
     d1, d2 = F.DensedRight(1), F.DensedRight(2)
     assert J.supports_backend(be, J.SpMVOp(F.CSR, d1, d1))
+    for fmt in (F.DCSR, F.COO, F.CSC):
+        assert J.supports_backend(be, J.SpMVOp(fmt, d1, d1))
+    assert not J.supports_backend(be, J.SpMVOp(F.DCSC, d1, d1))
     assert not J.supports_backend(be, J.SpMVOp(d2, d1, d1))
     assert not J.supports_backend(be, J.SpMVOp(F.CSR, d1, F.CSR))
     assert J.supports_backend(be, J.SpMMOp(F.CSR, d2, d2))

@@ -123,3 +123,35 @@ def test_csr_bsr_round_trip():
     bp2, bc2, bv2 = O.csr_to_bsr(20, 20, rp, ci, vals, 4, 4)
     # blocks whose values are all zero after bf16 rounding would vanish; none here
     assert np.array_equal(bp2, bp) and np.array_equal(bc2, bc) and np.array_equal(bv2, bv)
+
+
+@pytest.mark.parametrize("dtype", [np.float64, np.float32])
+def test_dcsr_and_coo_spmv_kats(golden, dtype):
+    """The reference's DCSR (row 2 not stored, left as it was) and COO SpMV
+    answers, and the same matrix stored as CSC."""
+    g = golden["spmv_dcsr_onebased"]
+    y = O.dcsr_spmv(g["m"], g["fibptr"], g["row_ids"], g["colind"], np.array(g["val"], dtype),
+                    np.array(g["x"], dtype), np.array(g["y0"], dtype), g["alpha"], g["beta"],
+                    g["base"])
+    assert y.tolist() == g["y"]
+    g = golden["spmv_coo_onebased"]
+    y = O.entry_spmv(g["m"], g["n"], g["rows"], np.array(g["val"], dtype),
+                     np.array(g["x"], dtype), cols=g["cols"], base=g["base"])
+    assert y.tolist() == g["y"]
+    # column-major storage of the same entries
+    order = np.lexsort((g["rows"], g["cols"]))
+    rows = np.array(g["rows"])[order]
+    cols = np.array(g["cols"])[order]
+    colptr = np.searchsorted(cols, np.arange(1, g["n"] + 2)) + 1
+    y = O.entry_spmv(g["m"], g["n"], rows, np.array(g["val"], dtype)[order],
+                     np.array(g["x"], dtype), colptr=colptr, base=1)
+    assert y.tolist() == g["y"]
+
+
+def test_dcsr_rows_not_stored_keep_y():
+    """With beta != 0 the stored rows get alpha*A x + beta*y and the others
+    keep y unscaled, as the reference's DCSR walk writes stored rows only."""
+    y0 = np.array([10.0, 20.0, 30.0])
+    y = O.dcsr_spmv(3, [0, 2, 4], [0, 2], [0, 2, 0, 2], [1.0, 2.0, 4.0, 5.0], [1.0, 2.0, 3.0],
+                    y0, 1.0, 0.5)
+    assert y.tolist() == [12.0, 20.0, 34.0]
