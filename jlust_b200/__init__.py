@@ -14,6 +14,7 @@ from .backend import (AbstractKernelHandle, AbstractUSTBackend, B200Backend,  # 
                       B200SpMVHandle, default_backend, execute, mul, prepare,
                       supports_backend, update_values, validate_storage)
 from .convert import convert_format, exclusive_scan  # noqa: F401
+from .block import BlockSparseMatrix, mul, update_block_values  # noqa: F401
 from .errors import (DeviceMismatch, DeviceTimeout, IncompatibleExtents,  # noqa: F401
                      IndexOriginMismatch, InvalidLevelAccess, NonCanonicalStorage,
                      UnsupportedFormat, UnsupportedIndexType, UnsupportedValueType)

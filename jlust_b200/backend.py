@@ -252,6 +252,13 @@ def execute(op_or_type, *args, backend=None, **kw):
     if isinstance(op_or_type, OpType):
         if args and isinstance(args[0], AbstractKernelHandle):
             return args[0].execute(*args[1:], **kw)
+        from .block import BlockSparseMatrix, block_spmm, block_spmv
+        if args and isinstance(args[0], BlockSparseMatrix):
+            if op_or_type.tag == "BlockSpMV":
+                return block_spmv(args[0], args[1], args[2], backend=backend)
+            if op_or_type.tag == "BlockSpMM":
+                return block_spmm(args[0], args[1], args[2], backend=backend)
+            raise UnsupportedFormat(f"{op_or_type} does not take a BlockSparseMatrix")
         tensors = [ust(a) for a in args]
         primary = tensors[2] if op_or_type.tag == "SDDMM" else tensors[0]
         be = backend if backend is not None else default_backend(primary, op_or_type)

@@ -337,3 +337,36 @@ def coo_to_bsr(m, n, rows, cols, val, b1, b2, base=0):
     lib().or_coo_to_bsr(m, n, nnz, b1, b2, _ptr(rows), _ptr(cols), _ptr(val), dt, base,
                         _ptr(bp), _ptr(bc), _ptr(bv))
     return bp, bc, bv
+
+
+# ------------------------------------------------------ block sparse matrix --
+def bsm_assemble(row_sizes, col_sizes, blocks):
+    """The one CSR the reference compiles a BlockSparseMatrix of CSR blocks to
+    (ext/CUDAExt/ops/block_mul.jl:128-229): blocks = {(i, j): (rowptr,
+    colind, val, base)} with 0-based block indices; rows of block row i
+    follow row_off[i], and block (i, j)'s entries of each of its rows are
+    appended, blocks visited in (i, j) order, columns shifted by col_off[j].
+    Returns (rowptr, colind, val), 0-based."""
+    row_off = np.concatenate([[0], np.cumsum(row_sizes)]).astype(np.int64)
+    col_off = np.concatenate([[0], np.cumsum(col_sizes)]).astype(np.int64)
+    n_rows = int(row_off[-1])
+    row_nnz = [0] * n_rows
+    for (i, j), (rp, ci, v, base) in blocks.items():
+        for r in range(row_sizes[i]):
+            row_nnz[row_off[i] + r] += int(rp[r + 1]) - int(rp[r])
+    rowptr = [0] * (n_rows + 1)
+    for r in range(n_rows):
+        rowptr[r + 1] = rowptr[r] + row_nnz[r]
+    colind = [0] * rowptr[-1]
+    dtype = next(iter(blocks.values()))[2].dtype
+    val = np.zeros(rowptr[-1], dtype)
+    cursor = list(rowptr[:-1])
+    for (i, j) in sorted(blocks):
+        rp, ci, v, base = blocks[(i, j)]
+        for r in range(row_sizes[i]):
+            for k in range(int(rp[r]) - base, int(rp[r + 1]) - base):
+                slot = cursor[row_off[i] + r]
+                cursor[row_off[i] + r] += 1
+                colind[slot] = int(ci[k]) - base + int(col_off[j])
+                val[slot] = v[k]
+    return np.array(rowptr, np.int32), np.array(colind, np.int32), val
