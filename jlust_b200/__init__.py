@@ -14,12 +14,12 @@ from .backend import (AbstractKernelHandle, AbstractUSTBackend, B200Backend,  # 
                       B200SpMVHandle, default_backend, execute, mul, prepare,
                       supports_backend, update_values, validate_storage)
 from .convert import convert_format, exclusive_scan  # noqa: F401
-from .block import BlockSparseMatrix, mul, update_block_values  # noqa: F401
+from .block import BlockBandedMatrix, BlockSparseMatrix, mul, update_block_values  # noqa: F401
 from .errors import (DeviceMismatch, DeviceTimeout, IncompatibleExtents,  # noqa: F401
                      IndexOriginMismatch, InvalidLevelAccess, NonCanonicalStorage,
                      UnsupportedFormat, UnsupportedIndexType, UnsupportedValueType)
 from .formats import Formats, TensorFormat, dim2lvl, format_family, lvl2dim  # noqa: F401
-from .ops import (BlockSpMMOp, BlockSpMVOp, Op, SDDMMOp, SpGEMMOp, SpMMOp,  # noqa: F401
+from .ops import (BBMSpMVOp, BlockSpMMOp, BlockSpMVOp, Op, SDDMMOp, SpGEMMOp, SpMMOp,  # noqa: F401
                   SpMVOp, SpSMOp, SpSVOp, SparseToDenseOp)
 from .tensor import (OneBased, USTensor, ZeroBased, bsr_tensor, coo_tensor,  # noqa: F401
                      coordinates, csr_tensor, extents, has_coordinates, has_positions,

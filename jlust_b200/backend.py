@@ -252,7 +252,11 @@ def execute(op_or_type, *args, backend=None, **kw):
     if isinstance(op_or_type, OpType):
         if args and isinstance(args[0], AbstractKernelHandle):
             return args[0].execute(*args[1:], **kw)
-        from .block import BlockSparseMatrix, block_spmm, block_spmv
+        from .block import BlockBandedMatrix, BlockSparseMatrix, bbm_spmv, block_spmm, block_spmv
+        if args and isinstance(args[0], BlockBandedMatrix):
+            if op_or_type.tag != "BBMSpMV":
+                raise UnsupportedFormat(f"{op_or_type} does not take a BlockBandedMatrix")
+            return bbm_spmv(args[0], args[1], args[2])
         if args and isinstance(args[0], BlockSparseMatrix):
             if op_or_type.tag == "BlockSpMV":
                 return block_spmv(args[0], args[1], args[2], backend=backend)

@@ -97,43 +97,48 @@ class BlockSparseMatrix:
         return all(b.format.family == "CSR" for _, _, b in self.stored())
 
 
-class _Compiled:
-    """The assembled CSR, the per-block slot maps and the captured graphs."""
+def _host_csr(b: USTensor):
+    base = b.origin.offset
+    rp = positions(b, 2).cpu().numpy().astype(np.int64) - base
+    ci = coordinates(b, 2).cpu().numpy().astype(np.int64) - base
+    return rp, ci
 
-    def __init__(self, A: BlockSparseMatrix):
-        m, n = A.shape
-        dev = nonzeros(next(A.stored())[2]).device
+
+class _Assembled:
+    """One CSR of m x n assembled from parts (key, row offset, column offset,
+    CSR block) in order: each part's rows append their entries, in storage
+    order, to the rows at its row offset, columns shifted by its column offset
+    (the order of ext/CUDAExt/ops/block_mul.jl:128-229).  Keeps a slot map per
+    keyed part and the CUDA graphs of its SpMV per (y, x) buffer pair."""
+
+    def __init__(self, m, n, parts, dtype):
+        dev = nonzeros(parts[0][3]).device
         row_nnz = np.zeros(m, np.int64)
-        host = {}
-        for i, j, b in A.stored():
-            base = b.origin.offset
-            rp = positions(b, 2).cpu().numpy().astype(np.int64) - base
-            ci = coordinates(b, 2).cpu().numpy().astype(np.int64) - base
-            host[(i, j)] = (rp, ci)
-            r0 = A.row_off[i]
-            row_nnz[r0:r0 + A.row_sizes[i]] += np.diff(rp)
+        host = []
+        for key, r0, c0, b in parts:
+            rp, ci = _host_csr(b)
+            host.append((key, r0, c0, b, rp, ci))
+            row_nnz[r0:r0 + rp.shape[0] - 1] += np.diff(rp)
         rowptr = np.zeros(m + 1, np.int64)
         np.cumsum(row_nnz, out=rowptr[1:])
         if rowptr[-1] > np.iinfo(np.int32).max - 1:
-            raise IncompatibleExtents("BlockSparseMatrix: assembled nnz exceeds Int32 positions")
+            raise IncompatibleExtents("assembled nnz exceeds Int32 positions")
         colind = np.zeros(int(rowptr[-1]), np.int32)
         cursor = rowptr[:-1].copy()
-        maps = {}
-        # blocks in (block row, block column) order, so a row's entries follow
-        # its blocks left to right, each block's in its own storage order
-        for (i, j), (rp, ci) in sorted(host.items()):
-            r0, c0 = A.row_off[i], A.col_off[j]
+        self.val = torch.empty(int(rowptr[-1]), dtype=dtype, device=dev)
+        self.maps = {}
+        for key, r0, c0, b, rp, ci in host:
+            nr = rp.shape[0] - 1
             lens = np.diff(rp)
-            rows = np.repeat(np.arange(A.row_sizes[i]), lens)
+            rows = np.repeat(np.arange(nr), lens)
             within = np.arange(ci.shape[0]) - np.repeat(rp[:-1], lens)
-            slots = cursor[r0 + rows] + within
-            colind[slots] = (ci + c0).astype(np.int32)
-            cursor[r0:r0 + A.row_sizes[i]] += lens
-            maps[(i, j)] = torch.from_numpy(slots).to(dev)
-        self.maps = maps
-        self.val = torch.empty(int(rowptr[-1]), dtype=A.dtype, device=dev)
-        for (i, j), slots in maps.items():
-            self.val[slots] = nonzeros(A.blocks[i][j])
+            slots_np = cursor[r0 + rows] + within
+            colind[slots_np] = (ci + c0).astype(np.int32)
+            cursor[r0:r0 + nr] += lens
+            slots = torch.from_numpy(slots_np).to(dev)
+            self.val[slots] = nonzeros(b)
+            if key is not None:
+                self.maps[key] = slots
         self.csr = csr_tensor(torch.from_numpy(rowptr.astype(np.int32)).to(dev),
                               torch.from_numpy(colind).to(dev), self.val, (m, n), origin=0)
         self.graphs = {}
@@ -156,6 +161,16 @@ class _Compiled:
                 self.spmv(x, y)
             self.graphs[key] = g
         g.replay()
+
+
+def _bsm_parts(A: "BlockSparseMatrix", r0=0, c0=0, key=True):
+    return [((i, j) if key else None, r0 + int(A.row_off[i]), c0 + int(A.col_off[j]), b)
+            for i, j, b in sorted(A.stored(), key=lambda t: (t[0], t[1]))]
+
+
+def _Compiled(A: "BlockSparseMatrix") -> _Assembled:
+    m, n = A.shape
+    return _Assembled(m, n, _bsm_parts(A), A.dtype)
 
 
 def _vec(t, what):
@@ -231,8 +246,97 @@ def update_block_values(A: BlockSparseMatrix, i: int, j: int, new_val: torch.Ten
     return A
 
 
-def mul(y, A: BlockSparseMatrix, x, backend=None):
-    """mul!(y, A, x) / mul!(Y, A, X) for a BlockSparseMatrix."""
+def mul(y, A, x, backend=None):
+    """mul!(y, A, x) / mul!(Y, A, X) for a BlockSparseMatrix, mul!(y, M, x)
+    for a BlockBandedMatrix."""
+    if isinstance(A, BlockBandedMatrix):
+        return bbm_spmv(A, x, y)
     if ust(x).val.dim() == 1:
         return block_spmv(A, x, y, backend)
     return block_spmm(A, x, y, backend)
+
+
+class BlockBandedMatrix:
+    """`BlockBandedMatrix(diags, off_diags, T, bw, n_diag_rows, n_off_rows,
+    n_cols)` (src/block_banded.jl): T periods of n_cols columns each; `diags`
+    is one diagonal block (a CSR USTensor or an all-CSR BlockSparseMatrix of
+    n_diag_rows x n_cols) shared by every period, or a list of T of them;
+    `off_diags[k-1]` couples period t with period t+k for k = 1..bw, as one
+    (neg, pos) pair of n_off_rows[k-1] x n_cols CSR blocks shared by every
+    transition or a list of T-k pairs.  Rows run period by period: period t's
+    n_diag_rows diagonal rows, then for each k <= min(bw, T-t) its coupling
+    rows, which compute neg x_t + pos x_{t+k} (block_banded.jl:79-122)."""
+
+    def __init__(self, diags, off_diags, T, bw, n_diag_rows, n_off_rows, n_cols):
+        if T < 1 or bw < 0 or len(off_diags) != bw or len(n_off_rows) != bw:
+            raise ValueError("BlockBandedMatrix: need T >= 1 and bw levels of (neg, pos) blocks "
+                             "and row counts")
+        self.diags = diags if isinstance(diags, (list, tuple)) else [diags] * T
+        if len(self.diags) != T:
+            raise ValueError(f"BlockBandedMatrix: {len(self.diags)} diagonal blocks for T = {T}")
+        self.off = []
+        for k in range(1, bw + 1):
+            lv = off_diags[k - 1]
+            pairs = [lv] * (T - k) if isinstance(lv, tuple) else list(lv)
+            if len(pairs) != T - k:
+                raise ValueError(f"BlockBandedMatrix: level {k} needs {T - k} (neg, pos) pairs")
+            self.off.append(pairs)
+        self.T, self.bw, self.n_cols = T, bw, n_cols
+        self.n_diag_rows, self.n_off_rows = n_diag_rows, list(n_off_rows)
+        for t, d in enumerate(self.diags):
+            if tuple(d.shape if isinstance(d, BlockSparseMatrix) else d.extents) != (n_diag_rows, n_cols):
+                raise ValueError(f"BlockBandedMatrix: diagonal block of period {t + 1} is not "
+                                 f"{n_diag_rows}x{n_cols}")
+        for k, pairs in enumerate(self.off, start=1):
+            for neg, pos in pairs:
+                if neg.extents != (self.n_off_rows[k - 1], n_cols) or pos.extents != neg.extents:
+                    raise ValueError(f"BlockBandedMatrix: level-{k} blocks are not "
+                                     f"{self.n_off_rows[k - 1]}x{n_cols}")
+        # first row of each period (block_banded.jl _bbm_diag_starts)
+        cum = np.concatenate([[0], np.cumsum(self.n_off_rows)]).astype(np.int64)
+        starts = [0]
+        for t in range(1, T):
+            starts.append(starts[-1] + n_diag_rows + int(cum[min(bw, T - t)]))
+        self.starts, self.cum_off = starts, cum
+        self._compiled = None
+
+    @property
+    def shape(self):
+        rows = self.T * self.n_diag_rows + sum((self.T - k) * self.n_off_rows[k - 1]
+                                               for k in range(1, self.bw + 1))
+        return rows, self.T * self.n_cols
+
+    def parts(self):
+        parts = []
+        for t in range(self.T):
+            r0, c0 = self.starts[t], t * self.n_cols
+            d = self.diags[t]
+            if isinstance(d, BlockSparseMatrix):
+                if not d.compilable():
+                    raise UnsupportedFormat("BlockBandedMatrix: diagonal blocks must be CSR")
+                parts += _bsm_parts(d, r0, c0, key=False)
+            else:
+                parts.append((None, r0, c0, d))
+            for k in range(1, min(self.bw, self.T - 1 - t) + 1):
+                neg, pos = self.off[k - 1][t]
+                rk = r0 + self.n_diag_rows + int(self.cum_off[k - 1])
+                parts.append((None, rk, c0, neg))
+                parts.append((None, rk, (t + k) * self.n_cols, pos))
+        for _, _, _, b in parts:
+            if b.format.family != "CSR":
+                raise UnsupportedFormat("BlockBandedMatrix: blocks must be CSR")
+        return parts
+
+
+def bbm_spmv(M: BlockBandedMatrix, x, y):
+    """y = M x (execute(BBMSpMVOp, M, x, y), src/block_banded.jl:79-122) as
+    one assembled CSR, its SpMV replayed from a CUDA graph per buffer pair."""
+    x, y = _vec(x, "x"), _vec(y, "y")
+    m, n = M.shape
+    if x.numel() != n or y.numel() != m:
+        raise IncompatibleExtents(f"BBMSpMV: M is {m}x{n}, x has {x.numel()}, y has {y.numel()}")
+    if M._compiled is None:
+        parts = M.parts()
+        M._compiled = _Assembled(m, n, parts, nonzeros(parts[0][3]).dtype)
+    M._compiled.run(x, y)
+    return y

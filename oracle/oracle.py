@@ -370,3 +370,42 @@ def bsm_assemble(row_sizes, col_sizes, blocks):
                 colind[slot] = int(ci[k]) - base + int(col_off[j])
                 val[slot] = v[k]
     return np.array(rowptr, np.int32), np.array(colind, np.int32), val
+
+
+def _csr_mv64(rp, ci, v, x, base):
+    rp = np.asarray(rp, np.int64) - base
+    ci = np.asarray(ci, np.int64) - base
+    t = np.asarray(v, np.float64) * np.asarray(x, np.float64)[ci]
+    rows = np.repeat(np.arange(rp.shape[0] - 1), np.diff(rp))
+    acc = np.zeros(rp.shape[0] - 1)
+    mag = np.zeros(rp.shape[0] - 1)
+    np.add.at(acc, rows, t)
+    np.add.at(mag, rows, np.abs(t))
+    return acc, mag
+
+
+def bbm_spmv_ref64(diags, off, T, bw, n_diag_rows, n_off_rows, n_cols, x):
+    """fp64 y = M x for a BlockBandedMatrix and the per-row bound, period by
+    period as the reference's execute(BBMSpMVOp) (src/block_banded.jl:79-122):
+    diags[t] and off[k-1][t] = (neg, pos) are host CSR tuples (rowptr, colind,
+    val, base); period t's diagonal rows get D_t x_t, its level-k coupling
+    rows neg x_t + pos x_{t+k}."""
+    x = np.asarray(x, np.float64)
+    cum = np.concatenate([[0], np.cumsum(n_off_rows)]).astype(np.int64)
+    starts = [0]
+    for t in range(1, T):
+        starts.append(starts[-1] + n_diag_rows + int(cum[min(bw, T - t)]))
+    m = T * n_diag_rows + sum((T - k) * n_off_rows[k - 1] for k in range(1, bw + 1))
+    y, bound = np.zeros(m), np.zeros(m)
+    for t in range(T):
+        xt = x[t * n_cols:(t + 1) * n_cols]
+        a, g = _csr_mv64(*diags[t][:3], xt, diags[t][3])
+        y[starts[t]:starts[t] + n_diag_rows], bound[starts[t]:starts[t] + n_diag_rows] = a, g
+        for k in range(1, min(bw, T - 1 - t) + 1):
+            neg, pos = off[k - 1][t]
+            r0 = starts[t] + n_diag_rows + int(cum[k - 1])
+            a1, g1 = _csr_mv64(*neg[:3], xt, neg[3])
+            a2, g2 = _csr_mv64(*pos[:3], x[(t + k) * n_cols:(t + k + 1) * n_cols], pos[3])
+            y[r0:r0 + n_off_rows[k - 1]] = a1 + a2
+            bound[r0:r0 + n_off_rows[k - 1]] = g1 + g2
+    return y, bound

@@ -49,3 +49,34 @@ def test_assembly_matches_reference_order():
     assert np.array_equal(c.csr.pos[1].numpy(), rp)
     assert np.array_equal(c.csr.crd[1].numpy(), ci)
     assert np.array_equal(c.val.numpy(), v)
+
+
+def _bbm_case(dev=None, dtype=np.float64):
+    """T = 5 periods, bw = 2, per-period diagonal blocks, level 1 shared,
+    level 2 per transition."""
+    T, bw, nd, no, nc = 5, 2, 40, [7, 5], 30
+    dh, dt = [], []
+    for t in range(T):
+        h, u = _blk(nd, nc, 200 + t, base=t % 2, dtype=dtype)
+        dh.append(h), dt.append(u)
+    n1h, n1 = _blk(no[0], nc, 300, dtype=dtype)
+    p1h, p1 = _blk(no[0], nc, 301, base=1, dtype=dtype)
+    lvl2h, lvl2 = [], []
+    for t in range(T - 2):
+        a, ua = _blk(no[1], nc, 400 + t, dtype=dtype)
+        b, ub = _blk(no[1], nc, 500 + t, dtype=dtype)
+        lvl2h.append((a, b)), lvl2.append((ua, ub))
+    offh = [[(n1h, p1h)] * (T - 1), lvl2h]
+    M = J.BlockBandedMatrix(dt, [(n1, p1), lvl2], T, bw, nd, no, nc)
+    return M, dh, offh, (T, bw, nd, no, nc)
+
+
+def test_bbm_shape_and_assembly():
+    M, dh, offh, (T, bw, nd, no, nc) = _bbm_case()
+    assert M.shape == (T * nd + (T - 1) * no[0] + (T - 2) * no[1], T * nc)
+    from jlust_b200.block import _Assembled
+    c = _Assembled(*M.shape, M.parts(), torch.float64)
+    x = np.random.default_rng(9).uniform(-1, 1, M.shape[1])
+    got = O.spmv(c.csr.pos[1].numpy(), c.csr.crd[1].numpy(), c.val.numpy(), x)
+    ref, bound = O.bbm_spmv_ref64(dh, offh, T, bw, nd, no, nc, x)
+    assert np.all(np.abs(got - ref) <= 1e-12 * bound + 1e-300)

@@ -3,7 +3,8 @@ path (one assembled CSR, its SpMV replayed from a CUDA graph): bit-exact with
 the oracle's SpMV of the reference's assembly (rows of up to 32 entries),
 also after new buffers, after update_block_values and inside a capture the
 caller started. Other block formats take the per-block path, and BlockSpMM
-adds every block into its slice of Y: both within tolerance of fp64."""
+adds every block into its slice of Y: both within tolerance of fp64. A
+BlockBandedMatrix is assembled the same way."""
 import numpy as np
 import pytest
 import torch
@@ -122,3 +123,43 @@ def test_block_spmm():
     D = _dense(host)
     assert_within(Y.cpu().numpy(), D @ X.astype(np.float64),
                   np.abs(D) @ np.abs(X.astype(np.float64)), 1e-5)
+
+
+def test_block_banded_spmv():
+    """BlockBandedMatrix y = M x (shared BlockSparseMatrix diagonal, a shared
+    level-1 coupling pair, per-transition level-2 pairs): within tolerance of
+    the reference's period-by-period product, and bit-exact with the oracle's
+    SpMV of the same assembled CSR; a second call replays the graph."""
+    T, bw, no = 6, 2, [300, 200]
+    host, D = _blocks()                                # 2100 x 1400 BlockSparseMatrix
+    nd, nc = D.shape
+    dh_rp, dh_ci, dh_v = O.bsm_assemble(SIZES_R, SIZES_C, host)
+    dh = (dh_rp, dh_ci, dh_v, 0)
+
+    def pair(seed, rows):
+        rng = np.random.default_rng(seed)
+        out = []
+        for s in (0, 1):
+            rp, ci, v = random_csr(rows, nc, rng.integers(0, 9, rows), seed=seed + s)
+            out.append(((rp, ci, v, 0), J.csr_tensor(to_dev(rp), to_dev(ci), to_dev(v), (rows, nc),
+                                                     origin=0)))
+        return out
+    (n1h, n1), (p1h, p1) = pair(600, no[0])
+    lvl2h, lvl2 = [], []
+    for t in range(T - 2):
+        (ah, a), (bh, b) = pair(700 + 2 * t, no[1])
+        lvl2h.append((ah, bh)), lvl2.append((a, b))
+    M = J.BlockBandedMatrix(D, [(n1, p1), lvl2], T, bw, nd, no, nc)
+    m, n = M.shape
+    x = np.random.default_rng(8).uniform(-1, 1, n)
+    xd, yd = to_dev(x), torch.full((m,), np.nan, dtype=torch.float64, device=DEV)
+    J.mul(yd, M, xd)
+    ref, bound = O.bbm_spmv_ref64([dh] * T, [[(n1h, p1h)] * (T - 1), lvl2h], T, bw, nd, no, nc, x)
+    assert_within(yd.cpu().numpy(), ref, bound, 1e-12)
+    c = M._compiled
+    exact = O.spmv(c.csr.pos[1].cpu().numpy(), c.csr.crd[1].cpu().numpy(), c.val.cpu().numpy(), x)
+    assert np.array_equal(yd.cpu().numpy(), exact)
+    yd.fill_(np.nan)
+    J.execute(J.BBMSpMVOp, M, xd, yd)
+    torch.cuda.synchronize()
+    assert np.array_equal(yd.cpu().numpy(), exact)
