@@ -141,6 +141,24 @@ JLB_API int jlb_csc_spmv(void *stream, int dtype, int idx_base, int64_t m, int64
                          int64_t nnz, const int32_t *colptr, const int32_t *rowind,
                          const void *val, const void *x, void *y, double alpha, double beta);
 
+/* y = alpha * M * x + beta * y for a periodic block-banded matrix M with T
+ * periods of n_cols columns: one n_diag x n_cols CSR diagonal block shared by
+ * every period and one coupling pair (neg, pos; n_off x n_cols CSR) shared by
+ * every transition.  Rows run period by period -- period t's diagonal rows
+ * (D x_t), then for t < T-1 its coupling rows (neg x_t + pos x_{t+1}) --
+ * T*n_diag + (T-1)*n_off rows in all, without storing the T-fold matrix.
+ * Each row is summed in storage order (neg entries, then pos entries),
+ * matching JLUST's fused periodic kernel
+ * (ext/KernelAbstractionsExt/ops/block_periodic.jl:126-163, launched from
+ * ext/CUDAExt/ops/block_mul.jl:660-680) without its selector patches. */
+JLB_API int jlb_bbm_periodic_spmv(void *stream, int dtype, int idx_base, int64_t T, int64_t n_diag,
+                                  int64_t n_off, int64_t n_cols, const int32_t *diag_rowptr,
+                                  const int32_t *diag_colind, const void *diag_val,
+                                  const int32_t *neg_rowptr, const int32_t *neg_colind,
+                                  const void *neg_val, const int32_t *pos_rowptr,
+                                  const int32_t *pos_colind, const void *pos_val, const void *x,
+                                  void *y, double alpha, double beta);
+
 /* Prepared SpMV: validates the structure once, records the row-length
  * profile and picks the kernel variant.  Replaces prepare(backend, SpMVOp,
  * u_A) (src/ops.jl:187-202; EmitterSpMVHandle, KA spmv.jl:518-531). */

@@ -104,7 +104,27 @@ def _host_csr(b: USTensor):
     return rp, ci
 
 
-class _Assembled:
+class _Graphed:
+    """Replays self.spmv(x, y) from a CUDA graph captured per (y, x) buffer
+    pair; inside a capture the caller started, launches it directly."""
+
+    def run(self, x, y):
+        if torch.cuda.is_current_stream_capturing():
+            self.spmv(x, y)          # a capture the caller started records the launch
+            return
+        key = (y.data_ptr(), x.data_ptr())
+        g = self.graphs.get(key)
+        if g is None:
+            self.spmv(x, y)          # first use outside the graph, then capture
+            torch.cuda.current_stream(y.device).synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self.spmv(x, y)
+            self.graphs[key] = g
+        g.replay()
+
+
+class _Assembled(_Graphed):
     """One CSR of m x n assembled from parts (key, row offset, column offset,
     CSR block) in order: each part's rows append their entries, in storage
     order, to the rows at its row offset, columns shifted by its column offset
@@ -146,21 +166,6 @@ class _Assembled:
     def spmv(self, x, y):
         from .backend import spmv
         spmv(self.csr, x, y)
-
-    def run(self, x, y):
-        if torch.cuda.is_current_stream_capturing():
-            self.spmv(x, y)          # a capture the caller started records the launch
-            return
-        key = (y.data_ptr(), x.data_ptr())
-        g = self.graphs.get(key)
-        if g is None:
-            self.spmv(x, y)          # first use outside the graph, then capture
-            torch.cuda.current_stream(y.device).synchronize()
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
-                self.spmv(x, y)
-            self.graphs[key] = g
-        g.replay()
 
 
 def _bsm_parts(A: "BlockSparseMatrix", r0=0, c0=0, key=True):
@@ -329,14 +334,73 @@ class BlockBandedMatrix:
 
 
 def bbm_spmv(M: BlockBandedMatrix, x, y):
-    """y = M x (execute(BBMSpMVOp, M, x, y), src/block_banded.jl:79-122) as
-    one assembled CSR, its SpMV replayed from a CUDA graph per buffer pair."""
+    """y = M x (execute(BBMSpMVOp, M, x, y), src/block_banded.jl:79-122): the
+    periodic kernel when one diagonal block and one coupling pair are shared
+    (bw = 1), otherwise one assembled CSR; either replayed from a CUDA graph
+    per buffer pair."""
     x, y = _vec(x, "x"), _vec(y, "y")
     m, n = M.shape
     if x.numel() != n or y.numel() != m:
         raise IncompatibleExtents(f"BBMSpMV: M is {m}x{n}, x has {x.numel()}, y has {y.numel()}")
     if M._compiled is None:
-        parts = M.parts()
-        M._compiled = _Assembled(m, n, parts, nonzeros(parts[0][3]).dtype)
+        if _Periodic.eligible(M):
+            M._compiled = _Periodic(M)
+        else:
+            parts = M.parts()
+            M._compiled = _Assembled(m, n, parts, nonzeros(parts[0][3]).dtype)
     M._compiled.run(x, y)
     return y
+
+
+class _Periodic(_Graphed):
+    """A periodic BlockBandedMatrix (one shared diagonal block, bw = 1, one
+    shared coupling pair) through jlb_bbm_periodic_spmv: the shared blocks are
+    stored once, not T times (JLUST's fused periodic path,
+    ext/CUDAExt/ops/block_mul.jl:584-680)."""
+
+    def __init__(self, M: "BlockBandedMatrix"):
+        d = M.diags[0]
+        if isinstance(d, BlockSparseMatrix):
+            self.diag_asm = _Compiled(d)          # the diagonal assembled once
+            d = self.diag_asm.csr
+        neg, pos = M.off[0][0]
+        self.blocks = (d, neg, pos)
+        self.M = M
+        self.graphs = {}
+
+    @staticmethod
+    def eligible(M: "BlockBandedMatrix") -> bool:
+        if M.bw != 1 or M.T < 2 or any(d is not M.diags[0] for d in M.diags):
+            return False
+        if any(p is not M.off[0][0] for p in M.off[0]):
+            return False
+        d = M.diags[0]
+        if isinstance(d, BlockSparseMatrix):
+            if not d.compilable():
+                return False
+            base = 0
+        else:
+            if d.format.family != "CSR":
+                return False
+            base = d.origin.offset
+        neg, pos = M.off[0][0]
+        return all(b.format.family == "CSR" and b.origin.offset == base for b in (neg, pos))
+
+    def spmv(self, x, y):
+        import ctypes as C
+
+        from . import _lib
+        from .backend import _DTYPE, _same_device, _stream
+        d, neg, pos = self.blocks
+        M = self.M
+        val = nonzeros(d)
+        dev = _same_device(nonzeros(neg), nonzeros(pos), val, x, y)
+
+        def p(t):
+            return C.c_void_p(t.data_ptr())
+        _lib.call("jlb_bbm_periodic_spmv", _stream(dev), _DTYPE[val.dtype], d.origin.offset, M.T,
+                  M.n_diag_rows, M.n_off_rows[0], M.n_cols,
+                  p(positions(d, 2)), p(coordinates(d, 2)), p(val),
+                  p(positions(neg, 2)), p(coordinates(neg, 2)), p(nonzeros(neg)),
+                  p(positions(pos, 2)), p(coordinates(pos, 2)), p(nonzeros(pos)),
+                  p(x), p(y), 1.0, 0.0)

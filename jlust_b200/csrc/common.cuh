@@ -59,6 +59,7 @@ int take_dev_error_bsr();
 int take_dev_error_convert();
 int take_dev_error_halo();
 int take_dev_error_spmvfmt();
+int take_dev_error_bbm();
 
 #define JLB_DEFINE_DEV_ERROR(unit)                                           \
     static __device__ int g_dev_error;                                       \

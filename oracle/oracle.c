@@ -140,6 +140,41 @@ OR_EXPORT void NAME(int64_t m, int64_t n, int64_t nnz, const int32_t *rows,     
 DEFINE_ENTRY_SPMV(or_entry_spmv_f64, double)
 DEFINE_ENTRY_SPMV(or_entry_spmv_f32, float)
 
+/* Periodic block-banded SpMV: JLUST's fused periodic kernel
+ * (ext/KernelAbstractionsExt/ops/block_periodic.jl:126-163).  Row r of
+ * T*n_diag + (T-1)*n_off: period t = r / (n_diag + n_off); a diagonal row sums
+ * D's row with columns shifted by t*n_cols, a coupling row sums neg's row
+ * (shift t*n_cols) then pos's row (shift (t+1)*n_cols) into the same sum. */
+#define DEFINE_BBM_PERIODIC(NAME, T)                                            \
+OR_EXPORT void NAME(int64_t Tp, int64_t n_diag, int64_t n_off, int64_t n_cols,  \
+                    const int32_t *drp, const int32_t *dci, const T *dv,        \
+                    const int32_t *nrp, const int32_t *nci, const T *nv,        \
+                    const int32_t *prp, const int32_t *pci, const T *pv,        \
+                    const T *x, T *y, double alpha_d, double beta_d, int base) { \
+    const T alpha = (T)alpha_d, beta = (T)beta_d;                               \
+    const int64_t rows = Tp * n_diag + (Tp - 1) * n_off;                        \
+    for (int64_t r = 0; r < rows; ++r) {                                        \
+        const int64_t t = r / (n_diag + n_off);                                 \
+        int64_t rem = r - t * (n_diag + n_off);                                 \
+        T acc = (T)0;                                                           \
+        const int32_t *rp[2], *ci[2]; const T *v[2]; int64_t off[2]; int nb;    \
+        if (rem < n_diag) { rp[0] = drp; ci[0] = dci; v[0] = dv; off[0] = t * n_cols; nb = 1; } \
+        else { rem -= n_diag; rp[0] = nrp; ci[0] = nci; v[0] = nv; off[0] = t * n_cols;        \
+               rp[1] = prp; ci[1] = pci; v[1] = pv; off[1] = (t + 1) * n_cols; nb = 2; }        \
+        for (int b = 0; b < nb; ++b)                                            \
+            for (int64_t k = (int64_t)rp[b][rem] - base; k < (int64_t)rp[b][rem + 1] - base; ++k) { \
+                T prod = v[b][k] * x[off[b] + (int64_t)ci[b][k] - base];        \
+                acc = acc + prod;                                               \
+            }                                                                   \
+        T out = alpha * acc;                                                    \
+        if (beta != (T)0) { T by = beta * y[r]; out = out + by; }               \
+        y[r] = out;                                                             \
+    }                                                                           \
+}
+
+DEFINE_BBM_PERIODIC(or_bbm_periodic_spmv_f64, double)
+DEFINE_BBM_PERIODIC(or_bbm_periodic_spmv_f32, float)
+
 /* fp64 reference of the same product plus the per-row magnitude bound
  * sum_k |v_k * x_k|, used for tolerance checks of any value type. */
 OR_EXPORT void or_csr_spmv_ref64(int dtype, int64_t m, const int32_t *rowptr,

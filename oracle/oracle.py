@@ -58,6 +58,8 @@ def _declare(L):
         getattr(L, n).argtypes = [_i64, _p, _p, _p, _p, _p, _p, _d, _d, _i]
     for n in ("or_entry_spmv_f64", "or_entry_spmv_f32"):
         getattr(L, n).argtypes = [_i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _d, _d, _i]
+    for n in ("or_bbm_periodic_spmv_f64", "or_bbm_periodic_spmv_f32"):
+        getattr(L, n).argtypes = [_i64, _i64, _i64, _i64] + [_p] * 11 + [_d, _d, _i]
     for n in ("or_csr_spmm_f32", "or_csr_spmm_f64"):
         getattr(L, n).argtypes = [_i64, _i64, _p, _p, _p, _p, _i64, _i, _p, _i64, _i, _d, _d, _i]
     L.or_csr_spmm_ref64_f32.argtypes = [_i64, _i64, _p, _p, _p, _p, _i64, _i, _p, _i64, _i,
@@ -409,3 +411,22 @@ def bbm_spmv_ref64(diags, off, T, bw, n_diag_rows, n_off_rows, n_cols, x):
             y[r0:r0 + n_off_rows[k - 1]] = a1 + a2
             bound[r0:r0 + n_off_rows[k - 1]] = g1 + g2
     return y, bound
+
+
+def bbm_periodic_spmv(T, n_diag, n_off, n_cols, diag, neg, pos, x, y=None, alpha=1.0, beta=0.0,
+                      base=0):
+    """Periodic block-banded y = alpha*M*x + beta*y in the order of JLUST's
+    fused periodic kernel (ext/KernelAbstractionsExt/ops/block_periodic.jl:
+    126-163); diag / neg / pos are (rowptr, colind, val) CSR tuples."""
+    d, ng, ps = ([_c(a[0], np.int32), _c(a[1], np.int32), _c(a[2])] for a in (diag, neg, pos))
+    dt = d[2].dtype
+    x = _c(x, dt)
+    rows = T * n_diag + (T - 1) * n_off
+    y = np.zeros(rows, dt) if y is None else _c(y, dt).copy()
+    fn = {np.dtype(np.float64): lib().or_bbm_periodic_spmv_f64,
+          np.dtype(np.float32): lib().or_bbm_periodic_spmv_f32}[dt]
+    fn(T, n_diag, n_off, n_cols, *(_ptr(a) for a in d + [_c(ng[0], np.int32), _c(ng[1], np.int32),
+                                                        _c(ng[2], dt)] +
+                                   [_c(ps[0], np.int32), _c(ps[1], np.int32), _c(ps[2], dt)]),
+       _ptr(x), _ptr(y), alpha, beta, base)
+    return y

@@ -163,3 +163,45 @@ def test_block_banded_spmv():
     J.execute(J.BBMSpMVOp, M, xd, yd)
     torch.cuda.synchronize()
     assert np.array_equal(yd.cpu().numpy(), exact)
+
+
+@pytest.mark.parametrize("diag_kind", ["csr", "bsm"])
+def test_block_banded_periodic_kernel(diag_kind):
+    """One diagonal block and one coupling pair shared over T periods (bw = 1)
+    take jlb_bbm_periodic_spmv, which never stores the T-fold matrix:
+    bit-exact with the oracle's restatement of JLUST's fused periodic kernel,
+    within tolerance of the reference's period-by-period product."""
+    from jlust_b200.block import _Periodic
+    T, no = 24, 350
+    if diag_kind == "csr":
+        nd, nc, base = 900, 800, 1
+        rng = np.random.default_rng(120)
+        rp, ci, v = random_csr(nd, nc, rng.integers(0, 12, nd), seed=121, base=base)
+        dh = (rp, ci, v, base)
+        D = J.csr_tensor(to_dev(rp), to_dev(ci), to_dev(v), (nd, nc), origin=base)
+    else:
+        host, D = _blocks()
+        nd, nc = D.shape
+        base = 0
+        dh = (*O.bsm_assemble(SIZES_R, SIZES_C, host), 0)
+    pair_h, pair_d = [], []
+    for s in (0, 1):
+        rng = np.random.default_rng(130 + s)
+        rp, ci, v = random_csr(no, nc, rng.integers(0, 7, no), seed=131 + s, base=base)
+        pair_h.append((rp, ci, v, base))
+        pair_d.append(J.csr_tensor(to_dev(rp), to_dev(ci), to_dev(v), (no, nc), origin=base))
+    M = J.BlockBandedMatrix(D, [tuple(pair_d)], T, 1, nd, [no], nc)
+    m, n = M.shape
+    x = np.random.default_rng(9).uniform(-1, 1, n)
+    xd, yd = to_dev(x), torch.full((m,), np.nan, dtype=torch.float64, device=DEV)
+    J.mul(yd, M, xd)
+    J.device_status()
+    assert isinstance(M._compiled, _Periodic)
+    exact = O.bbm_periodic_spmv(T, nd, no, nc, dh[:3], pair_h[0][:3], pair_h[1][:3], x, base=base)
+    assert np.array_equal(yd.cpu().numpy(), exact)
+    ref, bound = O.bbm_spmv_ref64([dh] * T, [[tuple(pair_h)] * (T - 1)], T, 1, nd, [no], nc, x)
+    assert_within(yd.cpu().numpy(), ref, bound, 1e-12)
+    yd.fill_(np.nan)
+    J.execute(J.BBMSpMVOp, M, xd, yd)                 # graph replay
+    torch.cuda.synchronize()
+    assert np.array_equal(yd.cpu().numpy(), exact)
