@@ -23,13 +23,35 @@ namespace bbm {
 
 constexpr int kThreads = 256;
 
+// Adds row `row` of a shared block into acc in storage order, columns
+// shifted by col_off; four entries' loads are issued before their sums.  A
+// column outside the block is reported and skipped.
 template <typename T>
 __device__ __forceinline__ T walk(int64_t row, const int32_t *__restrict__ rowptr,
                                   const int32_t *__restrict__ colind, const T *__restrict__ val,
                                   const T *__restrict__ x, int64_t col_off, int64_t n_cols,
                                   int base, T acc) {
     const int lo = ldg(rowptr + row) - base, hi = ldg(rowptr + row + 1) - base;
-    for (int k = lo; k < hi; ++k) {
+    int k = lo;
+    for (; k + 4 <= hi; k += 4) {
+        int c[4];
+        T v[4], xv[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            c[u] = ldg(colind + k + u) - base;
+            v[u] = ldg(val + k + u);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const bool in = c[u] >= 0 && c[u] < n_cols;
+            if (!in) dev_error(DEV_ERR_BOUNDS);
+            xv[u] = in ? ldg(x + col_off + c[u]) : T(0);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+            if (c[u] >= 0 && c[u] < n_cols) acc = add_rn(acc, mul_rn(v[u], xv[u]));
+    }
+    for (; k < hi; ++k) {
         const int64_t c = (int64_t)(ldg(colind + k) - base);
         if (c < 0 || c >= n_cols) {
             dev_error(DEV_ERR_BOUNDS);
