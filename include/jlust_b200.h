@@ -126,6 +126,23 @@ JLB_API int jlb_dcsr_spmv(void *stream, int dtype, int idx_base, int64_t m, int6
                           const int32_t *row_ids, const int32_t *colind, const void *val,
                           const void *x, void *y, double alpha, double beta);
 
+/* y = alpha * (A * x + P * x) + beta * y: a CSR A (m x n) plus npatch
+ * selector patches P, patch p adding patch_vals[p] * x[r - patch_rows[2p] +
+ * patch_cols[p]] to each row r in patch_rows[2p] .. patch_rows[2p+1]
+ * (0-based, inclusive; the patch arrays are device memory).  Each row's CSR
+ * entries are summed in storage order by one thread, the patches into a
+ * second sum in patch order, and the two added: JLUST's BlockSparseMatrix
+ * kernel with selector patches (ext/KernelAbstractionsExt/ops/
+ * block_periodic.jl:40-79, launched from ext/CUDAExt/ops/block_mul.jl:275-288,
+ * which has alpha = 1).  rowptr may be NULL when nnz = 0: no CSR entries, as
+ * for a standalone ShiftedDiag tensor (one patch over all rows; JLUST's
+ * walker with a ShiftedDiag leaf, src/backends.jl:223-227). */
+JLB_API int jlb_csr_patched_spmv(void *stream, int dtype, int idx_base, int64_t m, int64_t n,
+                                 int64_t nnz, const int32_t *rowptr, const int32_t *colind,
+                                 const void *val, int npatch, const int64_t *patch_rows,
+                                 const int64_t *patch_cols, const double *patch_vals,
+                                 const void *x, void *y, double alpha, double beta);
+
 /* y = alpha * A * x + beta * y for COO (row and column coordinates per entry,
  * any order, duplicates add) and for CSC (column pointer n + 1, row
  * coordinates).  As in JLUST's COO and scatter paths
@@ -142,22 +159,29 @@ JLB_API int jlb_csc_spmv(void *stream, int dtype, int idx_base, int64_t m, int64
                          const void *val, const void *x, void *y, double alpha, double beta);
 
 /* y = alpha * M * x + beta * y for a periodic block-banded matrix M with T
- * periods of n_cols columns: one n_diag x n_cols CSR diagonal block shared by
- * every period and one coupling pair (neg, pos; n_off x n_cols CSR) shared by
- * every transition.  Rows run period by period -- period t's diagonal rows
- * (D x_t), then for t < T-1 its coupling rows (neg x_t + pos x_{t+1}) --
- * T*n_diag + (T-1)*n_off rows in all, without storing the T-fold matrix.
- * Each row is summed in storage order (neg entries, then pos entries),
- * matching JLUST's fused periodic kernel
- * (ext/KernelAbstractionsExt/ops/block_periodic.jl:126-163, launched from
- * ext/CUDAExt/ops/block_mul.jl:660-680) without its selector patches. */
+ * periods of n_cols columns: one n_diag x n_cols diagonal block shared by
+ * every period (a CSR plus npatch selector patches, encoded as for
+ * jlb_csr_patched_spmv with rows and columns relative to the block) and one
+ * coupling pair (neg, pos; n_off x n_cols) shared by every transition, each
+ * a CSR or, when its rowptr is NULL, a ShiftedDiag selector whose row r holds
+ * *_sel at column r + *_shift.  Rows run period by period -- period t's
+ * diagonal rows (D x_t), then for t < T-1 its coupling rows
+ * (neg x_t + pos x_{t+1}) -- T*n_diag + (T-1)*n_off rows in all, without
+ * storing the T-fold matrix.  A diagonal row sums its CSR entries in storage
+ * order, then adds its patches' sum; a coupling row sums neg's entries, then
+ * pos's, into one sum: JLUST's fused periodic kernel
+ * (ext/KernelAbstractionsExt/ops/block_periodic.jl:114-163, launched from
+ * ext/CUDAExt/ops/block_mul.jl:660-680). */
 JLB_API int jlb_bbm_periodic_spmv(void *stream, int dtype, int idx_base, int64_t T, int64_t n_diag,
                                   int64_t n_off, int64_t n_cols, const int32_t *diag_rowptr,
-                                  const int32_t *diag_colind, const void *diag_val,
-                                  const int32_t *neg_rowptr, const int32_t *neg_colind,
-                                  const void *neg_val, const int32_t *pos_rowptr,
-                                  const int32_t *pos_colind, const void *pos_val, const void *x,
-                                  void *y, double alpha, double beta);
+                                  const int32_t *diag_colind, const void *diag_val, int npatch,
+                                  const int64_t *patch_rows, const int64_t *patch_cols,
+                                  const double *patch_vals, const int32_t *neg_rowptr,
+                                  const int32_t *neg_colind, const void *neg_val,
+                                  int64_t neg_shift, double neg_sel, const int32_t *pos_rowptr,
+                                  const int32_t *pos_colind, const void *pos_val,
+                                  int64_t pos_shift, double pos_sel, const void *x, void *y,
+                                  double alpha, double beta);
 
 /* Prepared SpMV: validates the structure once, records the row-length
  * profile and picks the kernel variant.  Replaces prepare(backend, SpMVOp,

@@ -21,7 +21,7 @@ from .errors import (DeviceMismatch, DeviceTimeout, IncompatibleExtents,  # noqa
 from .formats import Formats, TensorFormat, dim2lvl, format_family, lvl2dim  # noqa: F401
 from .ops import (BBMSpMVOp, BlockSpMMOp, BlockSpMVOp, Op, SDDMMOp, SpGEMMOp, SpMMOp,  # noqa: F401
                   SpMVOp, SpSMOp, SpSVOp, SparseToDenseOp)
-from .tensor import (OneBased, USTensor, ZeroBased, bsr_tensor, coo_tensor,  # noqa: F401
+from .tensor import (OneBased, USTensor, ZeroBased, bsr_tensor, coo_tensor, shifted_diag_tensor,  # noqa: F401
                      coordinates, csr_tensor, extents, has_coordinates, has_positions,
                      index_origin, nnz, nonzeros, positions, ust)
 

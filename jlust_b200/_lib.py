@@ -36,7 +36,9 @@ SIGNATURES = {
     "jlb_dcsr_spmv": (_i, [_p, _i, _i, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _d, _d]),
     "jlb_coo_spmv": (_i, [_p, _i, _i, _i64, _i64, _i64, _p, _p, _p, _p, _p, _d, _d]),
     "jlb_csc_spmv": (_i, [_p, _i, _i, _i64, _i64, _i64, _p, _p, _p, _p, _p, _d, _d]),
-    "jlb_bbm_periodic_spmv": (_i, [_p, _i, _i, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _d, _d]),
+    "jlb_csr_patched_spmv": (_i, [_p, _i, _i, _i64, _i64, _i64, _p, _p, _p, _i, _p, _p, _p, _p, _p, _d, _d]),
+    "jlb_bbm_periodic_spmv": (_i, [_p, _i, _i, _i64, _i64, _i64, _i64, _p, _p, _p, _i, _p, _p, _p,
+                                    _p, _p, _p, _i64, _d, _p, _p, _p, _i64, _d, _p, _p, _d, _d]),
     "jlb_spmv_plan_create": (_i, [C.POINTER(_p), _p, _i, _i, _i64, _i64, _i64, _p, _p]),
     "jlb_spmv_plan_execute": (_i, [_p, _p, _p, _p, _p, _d, _d]),
     "jlb_spmv_plan_info": (_i, [_p, _pi64, C.POINTER(_d), C.POINTER(_i)]),

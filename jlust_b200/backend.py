@@ -58,7 +58,7 @@ def supports_backend(backend, op: Op) -> bool:
         return False
     f = op.formats
     if op.tag == "SpMV" and len(f) == 3:
-        return (f[0].family in ("CSR", "DCSR", "COO", "CSC") and _dense_n(f[1], 1)
+        return (f[0].family in ("CSR", "DCSR", "COO", "CSC", "ShiftedDiag") and _dense_n(f[1], 1)
                 and _dense_n(f[2], 1))
     if op.tag == "SpMM" and len(f) == 3:
         return f[0].family in ("CSR", "BSR") and _dense_n(f[1], 2) and _dense_n(f[2], 2)
@@ -119,6 +119,8 @@ def spmv(A: USTensor, x, y, alpha=1.0, beta=0.0, input_fn=None, output_fn=None):
         raise UnsupportedFormat("B200Backend: input_fn/output_fn closures cannot cross the C ABI")
     x, y = ust(x).val, ust(y).val
     fam = A.format.family
+    if fam == "ShiftedDiag":
+        return _shifted_diag_spmv(A, x, y, alpha, beta)
     if fam not in ("CSR", "DCSR", "COO", "CSC"):
         raise UnsupportedFormat(f"B200Backend SpMV: format {A.format.name} is not supported")
     m, n = A.extents
@@ -153,6 +155,44 @@ def spmv(A: USTensor, x, y, alpha=1.0, beta=0.0, input_fn=None, output_fn=None):
         dev = _same_device(colptr, rowind, val, x, y)
         _lib.call("jlb_csc_spmv", _stream(dev), dt, base, m, n, nnz, _ptr(colptr), _ptr(rowind),
                   _ptr(val), _ptr(x), _ptr(y), a, b)
+    return y
+
+
+_PATCHES = {}
+
+
+def _patch_buffers(dev, patches):
+    """Device copies of selector patches (first row, last row, column of the
+    first row, value), kept per device and patch list."""
+    key = (str(dev), tuple(patches))
+    buf = _PATCHES.get(key)
+    if buf is None:
+        rows = torch.tensor([v for p in patches for v in (p[0], p[1])], dtype=torch.int64)
+        cols = torch.tensor([p[2] for p in patches], dtype=torch.int64)
+        vals = torch.tensor([p[3] for p in patches], dtype=torch.float64)
+        buf = _PATCHES[key] = (rows.to(dev), cols.to(dev), vals.to(dev))
+    return buf
+
+
+def _shifted_diag_spmv(A: USTensor, x, y, alpha, beta):
+    """y = alpha * S x + beta * y for a ShiftedDiag tensor S: row r gets
+    val * x[r + shift] (JLUST's walker with a ShiftedDiag leaf,
+    src/backends.jl:223-227), through the patched SpMV kernel with no CSR
+    entries and one patch over all rows."""
+    m, n = A.extents
+    shift, v = A.format.diag
+    dt = _value_type(x, (torch.float32, torch.float64), "SpMV")
+    if y.dtype != x.dtype or A.val.dtype != x.dtype:
+        raise UnsupportedValueType("SpMV: A, x and y must share one value type")
+    _vec(x, "x"), _vec(y, "y")
+    if x.numel() != n or y.numel() != m:
+        raise IncompatibleExtents(f"SpMV: A is {m}x{n}, x has {x.numel()}, y has {y.numel()}")
+    if m > 0 and (shift < 0 or m - 1 + shift >= n):
+        raise IncompatibleExtents(f"SpMV: ShiftedDiag shift {shift} reaches outside {m}x{n}")
+    dev = _same_device(x, y)
+    pr, pc, pv = _patch_buffers(dev, [(0, m - 1, shift, v)])
+    _lib.call("jlb_csr_patched_spmv", _stream(dev), dt, 0, m, n, 0, None, None, None, 1,
+              _ptr(pr), _ptr(pc), _ptr(pv), _ptr(x), _ptr(y), float(alpha), float(beta))
     return y
 
 

@@ -17,9 +17,9 @@ Two paths, as in the reference:
   `update_block_values` copies new values into a block and, through the slot
   map, into the assembled CSR in place, so captured graphs see them.
 
-The reference treats constant-value selector blocks through a separate patch
-kernel; here such blocks are assembled like any other CSR block (this library
-has no ShiftedDiag format).
+ShiftedDiag blocks and CSR blocks that are a constant times the identity
+become selector patches (ext/CUDAExt/ops/block_mul.jl:89-229): they are kept
+out of the assembled CSR and added by the patched SpMV kernel.
 """
 from __future__ import annotations
 
@@ -94,7 +94,7 @@ class BlockSparseMatrix:
                     yield i, j, b
 
     def compilable(self) -> bool:
-        return all(b.format.family == "CSR" for _, _, b in self.stored())
+        return all(b.format.family in ("CSR", "ShiftedDiag") for _, _, b in self.stored())
 
 
 def _host_csr(b: USTensor):
@@ -131,8 +131,8 @@ class _Assembled(_Graphed):
     (the order of ext/CUDAExt/ops/block_mul.jl:128-229).  Keeps a slot map per
     keyed part and the CUDA graphs of its SpMV per (y, x) buffer pair."""
 
-    def __init__(self, m, n, parts, dtype):
-        dev = nonzeros(parts[0][3]).device
+    def __init__(self, m, n, parts, dtype, dev=None, patches=()):
+        dev = nonzeros(parts[0][3]).device if dev is None else dev
         row_nnz = np.zeros(m, np.int64)
         host = []
         for key, r0, c0, b in parts:
@@ -161,11 +161,33 @@ class _Assembled(_Graphed):
                 self.maps[key] = slots
         self.csr = csr_tensor(torch.from_numpy(rowptr.astype(np.int32)).to(dev),
                               torch.from_numpy(colind).to(dev), self.val, (m, n), origin=0)
+        # selector patches (first row, last row, column of the first row, value)
+        self.patches = list(patches)
+        if self.patches:
+            pr = np.array([[p[0], p[1]] for p in self.patches], np.int64).reshape(-1)
+            self.p_rows = torch.from_numpy(pr).to(dev)
+            self.p_cols = torch.from_numpy(np.array([p[2] for p in self.patches], np.int64)).to(dev)
+            self.p_vals = torch.from_numpy(np.array([p[3] for p in self.patches], np.float64)).to(dev)
         self.graphs = {}
 
     def spmv(self, x, y):
-        from .backend import spmv
-        spmv(self.csr, x, y)
+        if not self.patches:
+            from .backend import spmv
+            spmv(self.csr, x, y)
+            return
+        import ctypes as C
+
+        from . import _lib
+        from .backend import _DTYPE, _same_device, _stream
+        m, n = self.csr.extents
+        dev = _same_device(self.val, x, y)
+
+        def p(t):
+            return C.c_void_p(t.data_ptr())
+        _lib.call("jlb_csr_patched_spmv", _stream(dev), _DTYPE[self.val.dtype], 0, m, n,
+                  self.val.numel(), p(positions(self.csr, 2)), p(coordinates(self.csr, 2)),
+                  p(self.val), len(self.patches), p(self.p_rows), p(self.p_cols), p(self.p_vals),
+                  p(x), p(y), 1.0, 0.0)
 
 
 def _bsm_parts(A: "BlockSparseMatrix", r0=0, c0=0, key=True):
@@ -173,9 +195,47 @@ def _bsm_parts(A: "BlockSparseMatrix", r0=0, c0=0, key=True):
             for i, j, b in sorted(A.stored(), key=lambda t: (t[0], t[1]))]
 
 
+def _selector_value(b: USTensor):
+    """(True, v) when CSR block b is v times the identity on its rows: one
+    entry per row, at the row's own column, all equal (ext/CUDAExt/ops/
+    block_mul.jl:89-115); else (False, 0)."""
+    if b.format.family != "CSR":
+        return False, 0.0
+    m = b.extents[0]
+    rp, ci = _host_csr(b)
+    if rp.shape[0] != m + 1 or rp[-1] - rp[0] != m or np.any(np.diff(rp) != 1):
+        return False, 0.0
+    if np.any(ci[rp[:-1]] != np.arange(m)):
+        return False, 0.0
+    v = nonzeros(b).cpu().numpy()
+    if v.size == 0 or np.any(v != v[0]):
+        return False, 0.0
+    return True, float(v[0])
+
+
 def _Compiled(A: "BlockSparseMatrix") -> _Assembled:
+    """The reference's compile of a BlockSparseMatrix (block_mul.jl:128-229):
+    ShiftedDiag blocks and CSR blocks that are constant multiples of the
+    identity become selector patches, the other CSR blocks one CSR."""
     m, n = A.shape
-    return _Assembled(m, n, _bsm_parts(A), A.dtype)
+    parts, patches = [], []
+    for i, j, b in sorted(A.stored(), key=lambda t: (t[0], t[1])):
+        r0, c0, rows = int(A.row_off[i]), int(A.col_off[j]), A.row_sizes[i]
+        if b.format.family == "ShiftedDiag":
+            shift, v = b.format.diag
+            if shift < 0 or rows - 1 + shift >= A.col_sizes[j]:
+                raise IncompatibleExtents(f"BlockSparseMatrix: ShiftedDiag block ({i + 1},{j + 1}) "
+                                          f"with shift {shift} reaches outside its columns")
+            patches.append((r0, r0 + rows - 1, c0 + shift, v))
+            continue
+        sel, v = _selector_value(b)
+        if sel:
+            patches.append((r0, r0 + rows - 1, c0, v))
+        else:
+            parts.append(((i, j), r0, c0, b))
+    # the CSR blocks' device; a matrix of patches only takes its first block's
+    dev = nonzeros(parts[0][3] if parts else next(A.stored())[2]).device
+    return _Assembled(m, n, parts, A.dtype, dev, patches)
 
 
 def _vec(t, what):
@@ -246,8 +306,11 @@ def update_block_values(A: BlockSparseMatrix, i: int, j: int, new_val: torch.Ten
                                   f"!= nnz {v.numel()}")
     v.copy_(new_val)
     c = A._compiled
-    if c is not None and (i - 1, j - 1) in c.maps:
-        c.val[c.maps[(i - 1, j - 1)]] = v
+    if c is not None:
+        if (i - 1, j - 1) in c.maps:
+            c.val[c.maps[(i - 1, j - 1)]] = v
+        else:
+            A._compiled = None       # a block compiled into a patch: rebuild next time
     return A
 
 
@@ -318,7 +381,7 @@ class BlockBandedMatrix:
             d = self.diags[t]
             if isinstance(d, BlockSparseMatrix):
                 if not d.compilable():
-                    raise UnsupportedFormat("BlockBandedMatrix: diagonal blocks must be CSR")
+                    raise UnsupportedFormat("BlockBandedMatrix: diagonal blocks must be CSR or ShiftedDiag")
                 parts += _bsm_parts(d, r0, c0, key=False)
             else:
                 parts.append((None, r0, c0, d))
@@ -328,9 +391,26 @@ class BlockBandedMatrix:
                 parts.append((None, rk, c0, neg))
                 parts.append((None, rk, (t + k) * self.n_cols, pos))
         for _, _, _, b in parts:
-            if b.format.family != "CSR":
-                raise UnsupportedFormat("BlockBandedMatrix: blocks must be CSR")
+            if b.format.family not in ("CSR", "ShiftedDiag"):
+                raise UnsupportedFormat("BlockBandedMatrix: blocks must be CSR or ShiftedDiag")
         return parts
+
+
+def _split_patches(parts):
+    """Parts (key, row offset, column offset, block) split into CSR parts and
+    selector patches, one per ShiftedDiag block (first row, last row, column
+    of the first row, value)."""
+    csr, patches = [], []
+    for key, r0, c0, b in parts:
+        if b.format.family != "ShiftedDiag":
+            csr.append((key, r0, c0, b))
+            continue
+        (rows, cols), (shift, v) = b.extents, b.format.diag
+        if shift < 0 or rows - 1 + shift >= cols:
+            raise IncompatibleExtents(f"ShiftedDiag block with shift {shift} reaches outside "
+                                      f"its {cols} columns")
+        patches.append((r0, r0 + rows - 1, c0 + shift, v))
+    return csr, patches
 
 
 def bbm_spmv(M: BlockBandedMatrix, x, y):
@@ -346,8 +426,10 @@ def bbm_spmv(M: BlockBandedMatrix, x, y):
         if _Periodic.eligible(M):
             M._compiled = _Periodic(M)
         else:
-            parts = M.parts()
-            M._compiled = _Assembled(m, n, parts, nonzeros(parts[0][3]).dtype)
+            parts, patches = _split_patches(M.parts())
+            first = parts[0][3] if parts else M.parts()[0][3]
+            M._compiled = _Assembled(m, n, parts, nonzeros(first).dtype, nonzeros(first).device,
+                                     patches)
     M._compiled.run(x, y)
     return y
 
@@ -356,14 +438,24 @@ class _Periodic(_Graphed):
     """A periodic BlockBandedMatrix (one shared diagonal block, bw = 1, one
     shared coupling pair) through jlb_bbm_periodic_spmv: the shared blocks are
     stored once, not T times (JLUST's fused periodic path,
-    ext/CUDAExt/ops/block_mul.jl:584-680)."""
+    ext/CUDAExt/ops/block_mul.jl:584-680).  A BlockSparseMatrix diagonal is
+    compiled once, its selector blocks kept as patches; a coupling block may
+    be CSR or ShiftedDiag."""
 
     def __init__(self, M: "BlockBandedMatrix"):
         d = M.diags[0]
+        self.patches = []
         if isinstance(d, BlockSparseMatrix):
             self.diag_asm = _Compiled(d)          # the diagonal assembled once
+            self.patches = self.diag_asm.patches
             d = self.diag_asm.csr
         neg, pos = M.off[0][0]
+        for b in (neg, pos):
+            if b.format.family == "ShiftedDiag":
+                shift, _ = b.format.diag
+                if shift < 0 or M.n_off_rows[0] - 1 + shift >= M.n_cols:
+                    raise IncompatibleExtents(f"BlockBandedMatrix: ShiftedDiag coupling block "
+                                              f"with shift {shift} reaches outside its columns")
         self.blocks = (d, neg, pos)
         self.M = M
         self.graphs = {}
@@ -384,7 +476,8 @@ class _Periodic(_Graphed):
                 return False
             base = d.origin.offset
         neg, pos = M.off[0][0]
-        return all(b.format.family == "CSR" and b.origin.offset == base for b in (neg, pos))
+        return all(b.format.family == "ShiftedDiag"
+                   or (b.format.family == "CSR" and b.origin.offset == base) for b in (neg, pos))
 
     def spmv(self, x, y):
         import ctypes as C
@@ -394,13 +487,21 @@ class _Periodic(_Graphed):
         d, neg, pos = self.blocks
         M = self.M
         val = nonzeros(d)
-        dev = _same_device(nonzeros(neg), nonzeros(pos), val, x, y)
+        dev = _same_device(val, x, y)
 
         def p(t):
-            return C.c_void_p(t.data_ptr())
+            return C.c_void_p(t.data_ptr()) if t is not None else C.c_void_p(0)
+
+        def blk(b):
+            if b.format.family == "ShiftedDiag":
+                shift, v = b.format.diag
+                return [None, None, None, shift, v]
+            _same_device(nonzeros(b), val)
+            return [p(positions(b, 2)), p(coordinates(b, 2)), p(nonzeros(b)), 0, 0.0]
+        a = getattr(self, "diag_asm", None)
+        pr, pc, pv = (a.p_rows, a.p_cols, a.p_vals) if self.patches else (None, None, None)
         _lib.call("jlb_bbm_periodic_spmv", _stream(dev), _DTYPE[val.dtype], d.origin.offset, M.T,
                   M.n_diag_rows, M.n_off_rows[0], M.n_cols,
                   p(positions(d, 2)), p(coordinates(d, 2)), p(val),
-                  p(positions(neg, 2)), p(coordinates(neg, 2)), p(nonzeros(neg)),
-                  p(positions(pos, 2)), p(coordinates(pos, 2)), p(nonzeros(pos)),
-                  p(x), p(y), 1.0, 0.0)
+                  len(self.patches), p(pr), p(pc), p(pv),
+                  *blk(neg), *blk(pos), p(x), p(y), 1.0, 0.0)

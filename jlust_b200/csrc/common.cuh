@@ -107,4 +107,28 @@ constexpr int kWarp = 32;
 
 __host__ __device__ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
+// Sum over selector patches of row r in patch order, from zero: patch p
+// covers rows rows[2p] .. rows[2p+1] (inclusive) and adds
+// vals[p] * x[col_off + r - rows[2p] + cols[p]] (JLUST's _apply_patches,
+// ext/KernelAbstractionsExt/ops/block_periodic.jl:39-49).  A column outside
+// [0, n) is skipped and sets bad.
+template <typename T>
+__device__ __forceinline__ T patch_sum(int64_t r, int npatch, const int64_t *__restrict__ rows,
+                                       const int64_t *__restrict__ cols,
+                                       const double *__restrict__ vals, const T *__restrict__ x,
+                                       int64_t col_off, int64_t n, bool &bad) {
+    T acc = T(0);
+    for (int p = 0; p < npatch; ++p) {
+        const int64_t r0 = ldg(rows + 2 * p), r1 = ldg(rows + 2 * p + 1);
+        if (r < r0 || r > r1) continue;
+        const int64_t c = r - r0 + ldg(cols + p);
+        if (c < 0 || c >= n) {
+            bad = true;
+            continue;
+        }
+        acc = add_rn(acc, mul_rn((T)ldg(vals + p), ldg(x + col_off + c)));
+    }
+    return acc;
+}
+
 }  // namespace jlb

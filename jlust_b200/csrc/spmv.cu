@@ -101,6 +101,57 @@ spmv_rows(int64_t m, const int32_t *__restrict__ rowptr, const int32_t *__restri
     }
 }
 
+// CSR SpMV plus selector patches: the assembled CSR of a BlockSparseMatrix
+// whose constant shifted-identity blocks were kept out of it.  Patch p adds
+// val[p] * x[row - rows[2p] + cols[p]] to rows rows[2p] .. rows[2p+1].  Each
+// row sums its CSR entries in storage order (one thread per row, also for
+// long rows), the patches in patch order into a second sum, then adds the
+// two: the operations of JLUST's patched kernel
+// (ext/KernelAbstractionsExt/ops/block_periodic.jl:40-79).  A null rowptr
+// means no CSR entries (a standalone ShiftedDiag tensor, whose one patch
+// gives each row val * x[r + shift] as JLUST's walker does with a
+// ShiftedDiag leaf, src/backends.jl:223-227); alpha scales the row (exact
+// for alpha = 1, the BlockSparseMatrix case).
+template <typename T, bool kBeta>
+__global__ void __launch_bounds__(kThreads)
+patched_rows(int64_t m, int64_t n, const int32_t *__restrict__ rowptr,
+             const int32_t *__restrict__ colind, const T *__restrict__ val, int npatch,
+             const int64_t *__restrict__ prows, const int64_t *__restrict__ pcols,
+             const double *__restrict__ pvals, const T *__restrict__ x, T *__restrict__ y,
+             T alpha, T beta, int base) {
+    const int64_t r = (int64_t)blockIdx.x * kThreads + threadIdx.x;
+    if (r >= m) return;
+    T acc = rowptr ? row_sum<T>(ldg(rowptr + r) - base, ldg(rowptr + r + 1) - base, colind, val,
+                                x, base)
+                   : T(0);
+    bool bad = false;
+    const T pacc = patch_sum<T>(r, npatch, prows, pcols, pvals, x, 0, n, bad);
+    if (bad) dev_error(DEV_ERR_BOUNDS);
+    T out = mul_rn(alpha, add_rn(acc, pacc));
+    if (kBeta) out = add_rn(out, mul_rn(beta, y[r]));
+    y[r] = out;
+}
+
+template <typename T>
+int launch_patched(cudaStream_t st, int base, int64_t m, int64_t n, const int32_t *rowptr,
+                   const int32_t *colind, const void *val, int npatch, const int64_t *prows,
+                   const int64_t *pcols, const double *pvals, const void *x, void *y,
+                   double alpha, double beta) {
+    if (m == 0) return ok();
+    const unsigned grid = (unsigned)ceil_div(m, kThreads);
+    const T a = (T)alpha, b = (T)beta;
+    if (b == T(0))
+        patched_rows<T, false><<<grid, kThreads, 0, st>>>(m, n, rowptr, colind, (const T *)val,
+                                                          npatch, prows, pcols, pvals,
+                                                          (const T *)x, (T *)y, a, b, base);
+    else
+        patched_rows<T, true><<<grid, kThreads, 0, st>>>(m, n, rowptr, colind, (const T *)val,
+                                                         npatch, prows, pcols, pvals,
+                                                         (const T *)x, (T *)y, a, b, base);
+    JLB_LAUNCH_CHECK("patched_rows");
+    return ok();
+}
+
 template <typename T>
 int launch_dcsr(cudaStream_t st, int base, int64_t nrows, int64_t nfib, const int32_t *fibptr,
                 const int32_t *row_ids, const int32_t *colind, const void *val, const void *x,
@@ -258,6 +309,28 @@ extern "C" JLB_API int jlb_dcsr_spmv(void *stream, int dtype, int idx_base, int6
                                          colind, val, x, y, alpha, beta);
     return spmv::launch_dcsr<float>(as_stream(stream), idx_base, m, nfib, fibptr, row_ids, colind,
                                     val, x, y, alpha, beta);
+}
+
+extern "C" JLB_API int jlb_csr_patched_spmv(void *stream, int dtype, int idx_base, int64_t m,
+                                            int64_t n, int64_t nnz, const int32_t *rowptr,
+                                            const int32_t *colind, const void *val, int npatch,
+                                            const int64_t *patch_rows, const int64_t *patch_cols,
+                                            const double *patch_vals, const void *x, void *y,
+                                            double alpha, double beta) {
+    if (!rowptr && nnz > 0) return fail(JLB_ERR_INVALID_ARGUMENT, "null rowptr with entries");
+    static const int32_t no_rows = 0;   // lets a null rowptr pass the common checks
+    int st = spmv_args(dtype, idx_base, m, n, nnz, rowptr ? rowptr : &no_rows, colind, val, x, y);
+    if (st) return st;
+    if (npatch < 0 || (npatch > 0 && (!patch_rows || !patch_cols || !patch_vals)))
+        return fail(JLB_ERR_INVALID_ARGUMENT, "bad patch arrays");
+    if (npatch > 0 && !x) return fail(JLB_ERR_INVALID_ARGUMENT, "null x");
+    if (dtype == JLB_F64)
+        return spmv::launch_patched<double>(as_stream(stream), idx_base, m, n, rowptr, colind,
+                                            val, npatch, patch_rows, patch_cols, patch_vals, x,
+                                            y, alpha, beta);
+    return spmv::launch_patched<float>(as_stream(stream), idx_base, m, n, rowptr, colind, val,
+                                       npatch, patch_rows, patch_cols, patch_vals, x, y, alpha,
+                                       beta);
 }
 
 struct jlb_spmv_plan_s {

@@ -39,6 +39,7 @@ class TensorFormat:
     keys: tuple
     levels: tuple
     block: tuple | None = None   # (b1, b2) for block formats
+    diag: tuple | None = None    # (shift, val) for ShiftedDiag
 
     def __eq__(self, other):
         return (isinstance(other, TensorFormat) and self.dimensions == other.dimensions
@@ -112,6 +113,15 @@ class Formats:
     CSC = TensorFormat("CSC", "CSC", ("i", "j"), (Key("j"), Key("i")), (DENSE, COMPRESSED))
     DCSR = TensorFormat("DCSR", "DCSR", ("i", "j"), (Key("i"), Key("j")), (COMPRESSED, COMPRESSED))
     DCSC = TensorFormat("DCSC", "DCSC", ("i", "j"), (Key("j"), Key("i")), (COMPRESSED, COMPRESSED))
+
+    @staticmethod
+    def ShiftedDiag(shift: int = 0, val: float = 1.0) -> TensorFormat:
+        """Shifted scaled identity (src/named_formats.jl:53-60): row r holds one
+        entry, `val` at column r + shift, and the tensor stores no buffers."""
+        return TensorFormat(f"ShiftedDiag(shift={int(shift)},val={float(val)})", "ShiftedDiag",
+                            ("i", "j"), (Key("i"), Key("j")),
+                            (DENSE, f"shifted_diag({int(shift)},{float(val)!r})"),
+                            None, (int(shift), float(val)))
 
     @staticmethod
     def BSRRight(blocksize) -> TensorFormat:

@@ -144,6 +144,15 @@ def csr_tensor(rowptr, colind, nzval, dims, origin=None) -> USTensor:
     return USTensor((int(m), int(n)), Formats.CSR, (None, rowptr), (None, colind), nzval, origin)
 
 
+def shifted_diag_tensor(dtype, n_rows, n_cols, shift=0, val=1.0, device="cpu") -> USTensor:
+    """A structural shifted scaled identity (src/interop.jl:155-181): row r
+    has one entry, `val` at column r + shift, with no position, coordinate or
+    value buffers (the value lives in the format)."""
+    from .formats import Formats
+    return USTensor((int(n_rows), int(n_cols)), Formats.ShiftedDiag(shift, val), (None, None),
+                    (None, None), torch.empty(0, dtype=dtype, device=device), OneBased())
+
+
 def coo_tensor(rows, cols, nzval, dims, origin=None) -> USTensor:
     """COO from buffers (src/interop.jl:248-260)."""
     origin = _origin(OneBased() if origin is None else origin)

@@ -141,15 +141,24 @@ DEFINE_ENTRY_SPMV(or_entry_spmv_f64, double)
 DEFINE_ENTRY_SPMV(or_entry_spmv_f32, float)
 
 /* Periodic block-banded SpMV: JLUST's fused periodic kernel
- * (ext/KernelAbstractionsExt/ops/block_periodic.jl:126-163).  Row r of
+ * (ext/KernelAbstractionsExt/ops/block_periodic.jl:114-163).  Row r of
  * T*n_diag + (T-1)*n_off: period t = r / (n_diag + n_off); a diagonal row sums
- * D's row with columns shifted by t*n_cols, a coupling row sums neg's row
- * (shift t*n_cols) then pos's row (shift (t+1)*n_cols) into the same sum. */
+ * D's row with columns shifted by t*n_cols, then adds the sum of its selector
+ * patches (npatch of them: rows prows[2p]..prows[2p+1] inclusive, value
+ * pvals[p] times x[t*n_cols + r - prows[2p] + pcols[p]], summed from zero in
+ * patch order, _apply_patches at :39-49); a coupling row sums neg's row (shift
+ * t*n_cols) then pos's row (shift (t+1)*n_cols) into the same sum.  A coupling
+ * block whose rowptr is NULL is a ShiftedDiag selector: its row adds
+ * sel * x[off + row + shift]. */
 #define DEFINE_BBM_PERIODIC(NAME, T)                                            \
 OR_EXPORT void NAME(int64_t Tp, int64_t n_diag, int64_t n_off, int64_t n_cols,  \
                     const int32_t *drp, const int32_t *dci, const T *dv,        \
+                    int64_t npatch, const int64_t *prows, const int64_t *pcols, \
+                    const double *pvals,                                        \
                     const int32_t *nrp, const int32_t *nci, const T *nv,        \
+                    int64_t nshift, double nsel,                                \
                     const int32_t *prp, const int32_t *pci, const T *pv,        \
+                    int64_t pshift, double psel,                                \
                     const T *x, T *y, double alpha_d, double beta_d, int base) { \
     const T alpha = (T)alpha_d, beta = (T)beta_d;                               \
     const int64_t rows = Tp * n_diag + (Tp - 1) * n_off;                        \
@@ -157,15 +166,33 @@ OR_EXPORT void NAME(int64_t Tp, int64_t n_diag, int64_t n_off, int64_t n_cols,  
         const int64_t t = r / (n_diag + n_off);                                 \
         int64_t rem = r - t * (n_diag + n_off);                                 \
         T acc = (T)0;                                                           \
-        const int32_t *rp[2], *ci[2]; const T *v[2]; int64_t off[2]; int nb;    \
+        const int32_t *rp[2], *ci[2]; const T *v[2]; int64_t off[2], sh[2];     \
+        double sel[2]; int nb;                                                  \
         if (rem < n_diag) { rp[0] = drp; ci[0] = dci; v[0] = dv; off[0] = t * n_cols; nb = 1; } \
         else { rem -= n_diag; rp[0] = nrp; ci[0] = nci; v[0] = nv; off[0] = t * n_cols;        \
-               rp[1] = prp; ci[1] = pci; v[1] = pv; off[1] = (t + 1) * n_cols; nb = 2; }        \
-        for (int b = 0; b < nb; ++b)                                            \
+               sh[0] = nshift; sel[0] = nsel;                                   \
+               rp[1] = prp; ci[1] = pci; v[1] = pv; off[1] = (t + 1) * n_cols; nb = 2;          \
+               sh[1] = pshift; sel[1] = psel; }                                 \
+        for (int b = 0; b < nb; ++b) {                                          \
+            if (!rp[b]) {                                                       \
+                T prod = (T)sel[b] * x[off[b] + rem + sh[b]];                   \
+                acc = acc + prod;                                               \
+                continue;                                                       \
+            }                                                                   \
             for (int64_t k = (int64_t)rp[b][rem] - base; k < (int64_t)rp[b][rem + 1] - base; ++k) { \
                 T prod = v[b][k] * x[off[b] + (int64_t)ci[b][k] - base];        \
                 acc = acc + prod;                                               \
             }                                                                   \
+        }                                                                       \
+        if (nb == 1) {                                                          \
+            T pacc = (T)0;                                                      \
+            for (int64_t p = 0; p < npatch; ++p)                                \
+                if (rem >= prows[2 * p] && rem <= prows[2 * p + 1]) {           \
+                    T prod = (T)pvals[p] * x[off[0] + rem - prows[2 * p] + pcols[p]]; \
+                    pacc = pacc + prod;                                         \
+                }                                                               \
+            acc = acc + pacc;                                                   \
+        }                                                                       \
         T out = alpha * acc;                                                    \
         if (beta != (T)0) { T by = beta * y[r]; out = out + by; }               \
         y[r] = out;                                                             \

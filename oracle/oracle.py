@@ -59,7 +59,8 @@ def _declare(L):
     for n in ("or_entry_spmv_f64", "or_entry_spmv_f32"):
         getattr(L, n).argtypes = [_i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _d, _d, _i]
     for n in ("or_bbm_periodic_spmv_f64", "or_bbm_periodic_spmv_f32"):
-        getattr(L, n).argtypes = [_i64, _i64, _i64, _i64] + [_p] * 11 + [_d, _d, _i]
+        getattr(L, n).argtypes = ([_i64, _i64, _i64, _i64, _p, _p, _p, _i64, _p, _p, _p]
+                                  + [_p, _p, _p, _i64, _d] * 2 + [_p, _p, _d, _d, _i])
     for n in ("or_csr_spmm_f32", "or_csr_spmm_f64"):
         getattr(L, n).argtypes = [_i64, _i64, _p, _p, _p, _p, _i64, _i, _p, _i64, _i, _d, _d, _i]
     L.or_csr_spmm_ref64_f32.argtypes = [_i64, _i64, _p, _p, _p, _p, _i64, _i, _p, _i64, _i,
@@ -414,19 +415,95 @@ def bbm_spmv_ref64(diags, off, T, bw, n_diag_rows, n_off_rows, n_cols, x):
 
 
 def bbm_periodic_spmv(T, n_diag, n_off, n_cols, diag, neg, pos, x, y=None, alpha=1.0, beta=0.0,
-                      base=0):
+                      base=0, patches=()):
     """Periodic block-banded y = alpha*M*x + beta*y in the order of JLUST's
     fused periodic kernel (ext/KernelAbstractionsExt/ops/block_periodic.jl:
-    126-163); diag / neg / pos are (rowptr, colind, val) CSR tuples."""
-    d, ng, ps = ([_c(a[0], np.int32), _c(a[1], np.int32), _c(a[2])] for a in (diag, neg, pos))
+    114-163); diag is a (rowptr, colind, val) CSR tuple with selector
+    `patches` (first row, last row, column of the first row, value; relative
+    to the diagonal block), neg / pos each a CSR tuple or a ShiftedDiag
+    selector ("shifted", shift, val)."""
+    d = [_c(diag[0], np.int32), _c(diag[1], np.int32), _c(diag[2])]
     dt = d[2].dtype
     x = _c(x, dt)
     rows = T * n_diag + (T - 1) * n_off
     y = np.zeros(rows, dt) if y is None else _c(y, dt).copy()
     fn = {np.dtype(np.float64): lib().or_bbm_periodic_spmv_f64,
           np.dtype(np.float32): lib().or_bbm_periodic_spmv_f32}[dt]
-    fn(T, n_diag, n_off, n_cols, *(_ptr(a) for a in d + [_c(ng[0], np.int32), _c(ng[1], np.int32),
-                                                        _c(ng[2], dt)] +
-                                   [_c(ps[0], np.int32), _c(ps[1], np.int32), _c(ps[2], dt)]),
-       _ptr(x), _ptr(y), alpha, beta, base)
+    keep = []
+
+    def blk(b):
+        if isinstance(b[0], str):
+            return [None, None, None, int(b[1]), float(b[2])]
+        a = [_c(b[0], np.int32), _c(b[1], np.int32), _c(b[2], dt)]
+        keep.extend(a)
+        return [_ptr(a[0]), _ptr(a[1]), _ptr(a[2]), 0, 0.0]
+    pr = _c(np.array([v for p in patches for v in (p[0], p[1])], np.int64))
+    pc = _c(np.array([p[2] for p in patches], np.int64))
+    pv = _c(np.array([p[3] for p in patches], np.float64))
+    fn(T, n_diag, n_off, n_cols, _ptr(d[0]), _ptr(d[1]), _ptr(d[2]), len(patches), _ptr(pr),
+       _ptr(pc), _ptr(pv), *blk(neg), *blk(pos), _ptr(x), _ptr(y), alpha, beta, base)
     return y
+
+
+def bsm_compile(row_sizes, col_sizes, blocks, shifted=None):
+    """The reference's full BlockSparseMatrix compile (ext/CUDAExt/ops/
+    block_mul.jl:89-229): ShiftedDiag blocks (`shifted` = {(i, j): (shift,
+    val)}) and CSR blocks that are a constant times the identity (one entry
+    per row, at the row's own column, all equal) become selector patches
+    (first row, last row, column of the first row, value), 0-based, in
+    (i, j) order; the other CSR blocks are assembled by bsm_assemble.
+    Returns (rowptr, colind, val, patches)."""
+    row_off = np.concatenate([[0], np.cumsum(row_sizes)]).astype(np.int64)
+    col_off = np.concatenate([[0], np.cumsum(col_sizes)]).astype(np.int64)
+    shifted = shifted or {}
+    keys = sorted(set(blocks) | set(shifted))
+    csr, patches = {}, []
+    for (i, j) in keys:
+        r0, r1 = int(row_off[i]), int(row_off[i]) + row_sizes[i] - 1
+        if (i, j) in shifted:
+            sh, v = shifted[(i, j)]
+            patches.append((r0, r1, int(col_off[j]) + sh, v))
+            continue
+        rp, ci, v, base = blocks[(i, j)]
+        rp0 = np.asarray(rp, np.int64) - base
+        ci0 = np.asarray(ci, np.int64) - base
+        m = row_sizes[i]
+        sel = (rp0.shape[0] == m + 1 and rp0[-1] - rp0[0] == m and np.all(np.diff(rp0) == 1)
+               and np.all(ci0[rp0[:-1]] == np.arange(m)) and np.all(np.asarray(v) == v[0]))
+        if sel:
+            patches.append((r0, r1, int(col_off[j]), float(v[0])))
+        else:
+            csr[(i, j)] = blocks[(i, j)]
+    dtype = next(iter(blocks.values()))[2].dtype
+    if csr:
+        rp, ci, v = bsm_assemble(row_sizes, col_sizes, csr)
+    else:
+        rp, ci, v = np.zeros(int(row_off[-1]) + 1, np.int32), np.zeros(0, np.int32), np.zeros(0, dtype)
+    return rp, ci, v, patches
+
+
+def csr_patched_spmv(rowptr, colind, val, patches, x, y=None, beta=0.0, alpha=1.0):
+    """y = alpha (A x + (patches) x) (+ beta y) in the value type, in the
+    order of JLUST's patched kernel (ext/KernelAbstractionsExt/ops/
+    block_periodic.jl:40-79, alpha = 1 there): per row the CSR entries summed
+    in storage order, the patches summed in patch order into a second sum,
+    then the two added.  Plain loops: small cases only."""
+    val = np.asarray(val)
+    T = val.dtype.type
+    x = np.asarray(x, val.dtype)
+    m = len(rowptr) - 1
+    out = np.zeros(m, val.dtype) if y is None else np.asarray(y, val.dtype).copy()
+    b = T(beta)
+    for r in range(m):
+        acc = T(0)
+        for k in range(int(rowptr[r]), int(rowptr[r + 1])):
+            acc = T(acc + T(val[k] * x[colind[k]]))
+        pacc = T(0)
+        for (r0, r1, c0, v) in patches:
+            if r0 <= r <= r1:
+                pacc = T(pacc + T(T(v) * x[r - r0 + c0]))
+        o = T(T(alpha) * T(acc + pacc))
+        if b != 0:
+            o = T(o + T(b * out[r]))
+        out[r] = o
+    return out

@@ -80,3 +80,36 @@ def test_bbm_shape_and_assembly():
     got = O.spmv(c.csr.pos[1].numpy(), c.csr.crd[1].numpy(), c.val.numpy(), x)
     ref, bound = O.bbm_spmv_ref64(dh, offh, T, bw, nd, no, nc, x)
     assert np.all(np.abs(got - ref) <= 1e-12 * bound + 1e-300)
+
+
+def test_selector_patches_compile():
+    """ShiftedDiag blocks and CSR blocks that are a constant times the
+    identity leave the assembled CSR as selector patches (block_mul.jl:
+    89-229), in (i, j) order, as the oracle's restatement of the compile
+    has them; a block with a column shift past its columns is refused."""
+    h00, b00 = _blk(4, 5, 21)
+    sel = (np.arange(4, dtype=np.int32), np.arange(3, dtype=np.int32), np.full(3, 0.5), 0)
+    b10 = J.csr_tensor(*(torch.from_numpy(a) for a in sel[:3]), (3, 5), origin=0)
+    h11, b11 = _blk(3, 6, 22, base=1)
+    sd = J.shifted_diag_tensor(torch.float64, 4, 6, shift=2, val=3.0)
+    A = J.BlockSparseMatrix([[b00, sd], [b10, b11]])
+    c = _Compiled(A)
+    rp, ci, v, patches = O.bsm_compile([4, 3], [5, 6], {(0, 0): h00, (1, 0): sel, (1, 1): h11},
+                                       {(0, 1): (2, 3.0)})
+    assert c.patches == patches == [(0, 3, 7, 3.0), (4, 6, 0, 0.5)]
+    assert np.array_equal(J.positions(c.csr, 2).numpy(), rp)
+    assert np.array_equal(J.coordinates(c.csr, 2).numpy(), ci)
+    assert np.array_equal(c.val.numpy(), v)
+    bad = J.BlockSparseMatrix([[b00, J.shifted_diag_tensor(torch.float64, 4, 6, shift=3)],
+                               [b10, b11]])
+    with pytest.raises(J.IncompatibleExtents, match="ShiftedDiag"):
+        _Compiled(bad)
+    # the oracle's patched product against a dense product
+    x = np.random.default_rng(23).uniform(-1, 1, 11)
+    D = np.zeros((7, 11))
+    for r in range(7):
+        for k in range(rp[r], rp[r + 1]):
+            D[r, ci[k]] += v[k]
+    for r0, r1, c0, pv in patches:
+        D[np.arange(r0, r1 + 1), c0 + np.arange(r1 - r0 + 1)] += pv
+    assert np.allclose(O.csr_patched_spmv(rp, ci, v, patches, x), D @ x, rtol=1e-14, atol=1e-14)

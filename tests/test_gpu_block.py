@@ -205,3 +205,176 @@ def test_block_banded_periodic_kernel(diag_kind):
     J.execute(J.BBMSpMVOp, M, xd, yd)                 # graph replay
     torch.cuda.synchronize()
     assert np.array_equal(yd.cpu().numpy(), exact)
+
+
+def _patched_matrix(dtype=np.float64):
+    """The LAYOUT blocks with the (0, 1) block replaced by a CSR block that
+    is 2.5 times the identity (a selector) and a ShiftedDiag block (shift 50,
+    value -0.75) added at (1, 0): the compile keeps two patches."""
+    host, _ = _blocks(dtype)
+    blocks = [[None] * len(SIZES_C) for _ in SIZES_R]
+    for (i, j), (rp, ci, v, base) in host.items():
+        blocks[i][j] = J.csr_tensor(to_dev(rp), to_dev(ci), to_dev(v), (SIZES_R[i], SIZES_C[j]),
+                                    origin=base)
+    m01 = SIZES_R[0]
+    sel = (np.arange(m01 + 1, dtype=np.int32) + 1, np.arange(m01, dtype=np.int32) + 1,
+           np.full(m01, 2.5, dtype), 1)
+    host[(0, 1)] = sel
+    blocks[0][1] = J.csr_tensor(to_dev(sel[0]), to_dev(sel[1]), to_dev(sel[2]),
+                                (m01, SIZES_C[1]), origin=1)
+    dt = torch.float64 if dtype == np.float64 else torch.float32
+    blocks[1][0] = J.shifted_diag_tensor(dt, SIZES_R[1], SIZES_C[0], shift=50, val=-0.75,
+                                         device=DEV)
+    return host, {(1, 0): (50, -0.75)}, J.BlockSparseMatrix(blocks)
+
+
+@pytest.mark.parametrize("dtype", [np.float64, np.float32])
+def test_selector_patches_bit_exact(dtype):
+    """A ShiftedDiag block and a CSR block that is 2.5 times the identity are
+    kept out of the assembled CSR as selector patches: bit-exact with the
+    oracle's restatement of the reference's patched kernel, within tolerance
+    of fp64, also on graph replay and after update_block_values turns the
+    selector block back into an ordinary one."""
+    host, shifted, A = _patched_matrix(dtype)
+    m, n = A.shape
+    x = np.random.default_rng(11).uniform(-1, 1, n).astype(dtype)
+    xd = to_dev(x)
+    yd = torch.full((m,), np.nan, dtype=xd.dtype, device=DEV)
+    J.mul(yd, A, xd)
+    J.device_status()
+    rp, ci, v, patches = O.bsm_compile(SIZES_R, SIZES_C, host, shifted)
+    assert sorted(p[:3] for p in patches) == [(0, SIZES_R[0] - 1, SIZES_C[0]),
+                                              (SIZES_R[0], SIZES_R[0] + SIZES_R[1] - 1, 50)]
+    assert len(A._compiled.patches) == 2
+    exact = O.csr_patched_spmv(rp, ci, v, patches, x)
+    assert np.array_equal(yd.cpu().numpy(), exact)
+    D = _dense({k: b for k, b in host.items()}, np.float64)
+    r1, c0 = SIZES_R[0], 50
+    D[r1 + np.arange(SIZES_R[1]), c0 + np.arange(SIZES_R[1])] += -0.75
+    assert_within(yd.cpu().numpy(), D @ x.astype(np.float64),
+                  np.abs(D) @ np.abs(x.astype(np.float64)), TOL_BLOCK[dtype])
+    yd.fill_(np.nan)
+    J.execute(J.BlockSpMVOp, A, xd, yd)                # graph replay
+    torch.cuda.synchronize()
+    assert np.array_equal(yd.cpu().numpy(), exact)
+    # new values that are no longer constant: the block leaves the patches
+    nv = np.linspace(1, 2, SIZES_R[0]).astype(dtype)
+    J.update_block_values(A, 1, 2, to_dev(nv))
+    host[(0, 1)] = (*host[(0, 1)][:2], nv, 1)
+    J.mul(yd, A, xd)
+    torch.cuda.synchronize()
+    assert len(A._compiled.patches) == 1
+    rp, ci, v, patches = O.bsm_compile(SIZES_R, SIZES_C, host, shifted)
+    assert np.array_equal(yd.cpu().numpy(), O.csr_patched_spmv(rp, ci, v, patches, x))
+
+
+TOL_BLOCK = {np.float64: 1e-12, np.float32: 1e-5}
+
+
+@pytest.mark.parametrize("ab", [(1.0, 0.0), (-1.5, 0.5)])
+def test_shifted_diag_standalone_spmv(ab):
+    """y = alpha S x + beta y for a ShiftedDiag tensor alone: bit-exact with
+    the oracle (one patch, no CSR entries)."""
+    m, n, shift, val = 3000, 3400, 123, 1.25
+    S = J.shifted_diag_tensor(torch.float64, m, n, shift=shift, val=val, device=DEV)
+    rng = np.random.default_rng(12)
+    x, y0 = rng.uniform(-1, 1, n), rng.uniform(-1, 1, m)
+    y = to_dev(y0)
+    J.execute(J.SpMVOp, S, to_dev(x), y, alpha=ab[0], beta=ab[1])
+    J.device_status()
+    ref = O.csr_patched_spmv(np.zeros(m + 1, np.int64), np.zeros(0, np.int64), np.zeros(0),
+                             [(0, m - 1, shift, val)], x, y0, beta=ab[1], alpha=ab[0])
+    assert np.array_equal(y.cpu().numpy(), ref)
+    with pytest.raises(J.IncompatibleExtents):
+        J.execute(J.SpMVOp, J.shifted_diag_tensor(torch.float64, m, n, shift=500, device=DEV),
+                  to_dev(x), y)
+
+
+@pytest.mark.parametrize("dtype", [np.float64, np.float32])
+def test_block_banded_periodic_with_selectors(dtype):
+    """The reference's periodic case with selectors: a BlockSparseMatrix
+    diagonal holding a ShiftedDiag block and a CSR selector (kept as patches
+    and added per period with the period's column offset) and a coupling pair
+    of a ShiftedDiag neg and a CSR pos: bit-exact with the oracle's
+    restatement of the fused periodic kernel, within tolerance of fp64."""
+    from jlust_b200.block import _Periodic
+    T, no = 12, 400
+    host, shifted, D = _patched_matrix(dtype)
+    nd, nc = D.shape
+    rp, ci, v, patches = O.bsm_compile(SIZES_R, SIZES_C, host, shifted)
+    rng = np.random.default_rng(140)
+    prp, pci, pv = random_csr(no, nc, rng.integers(0, 7, no), seed=141, dtype=dtype)
+    pos = J.csr_tensor(to_dev(prp), to_dev(pci), to_dev(pv), (no, nc), origin=0)
+    dt = torch.float64 if dtype == np.float64 else torch.float32
+    neg = J.shifted_diag_tensor(dt, no, nc, shift=17, val=-1.0, device=DEV)
+    M = J.BlockBandedMatrix(D, [(neg, pos)], T, 1, nd, [no], nc)
+    m, n = M.shape
+    x = np.random.default_rng(10).uniform(-1, 1, n).astype(dtype)
+    xd = to_dev(x)
+    yd = torch.full((m,), np.nan, dtype=dt, device=DEV)
+    J.mul(yd, M, xd)
+    J.device_status()
+    assert isinstance(M._compiled, _Periodic) and len(M._compiled.patches) == 2
+    exact = O.bbm_periodic_spmv(T, nd, no, nc, (rp, ci, v), ("shifted", 17, -1.0),
+                                (prp, pci, pv), x, patches=patches)
+    assert np.array_equal(yd.cpu().numpy(), exact)
+    # fp64 reference: the dense diagonal and coupling blocks period by period
+    Dd = _dense(host)
+    Dd[SIZES_R[0] + np.arange(SIZES_R[1]), 50 + np.arange(SIZES_R[1])] += -0.75
+    Nd = np.zeros((no, nc))
+    Nd[np.arange(no), 17 + np.arange(no)] = -1.0
+    Pd = np.zeros((no, nc))
+    for r in range(no):
+        Pd[r, pci[prp[r]:prp[r + 1]]] += pv[prp[r]:prp[r + 1]]
+    xs = x.astype(np.float64).reshape(T, nc)
+    ref, bound = [], []
+    for t in range(T):
+        ref.append(Dd @ xs[t]), bound.append(np.abs(Dd) @ np.abs(xs[t]))
+        if t < T - 1:
+            ref.append(Nd @ xs[t] + Pd @ xs[t + 1])
+            bound.append(np.abs(Nd) @ np.abs(xs[t]) + np.abs(Pd) @ np.abs(xs[t + 1]))
+    assert_within(yd.cpu().numpy(), np.concatenate(ref), np.concatenate(bound), TOL_BLOCK[dtype])
+    yd.fill_(np.nan)
+    J.execute(J.BBMSpMVOp, M, xd, yd)                 # graph replay
+    torch.cuda.synchronize()
+    assert np.array_equal(yd.cpu().numpy(), exact)
+
+
+def test_block_banded_assembled_with_shifted_diag():
+    """A BlockBandedMatrix that is not periodic (per-transition pairs) with
+    ShiftedDiag coupling blocks: the ShiftedDiag blocks become selector
+    patches of the assembled CSR; within tolerance of fp64."""
+    T, nd, no, nc = 4, 600, 250, 700
+    rng = np.random.default_rng(150)
+    rp, ci, v = random_csr(nd, nc, rng.integers(0, 10, nd), seed=151)
+    D = J.csr_tensor(to_dev(rp), to_dev(ci), to_dev(v), (nd, nc), origin=0)
+    pairs, dense_pairs = [], []
+    for t in range(T - 1):
+        prp, pci, pv = random_csr(no, nc, rng.integers(0, 6, no), seed=160 + t)
+        pos = J.csr_tensor(to_dev(prp), to_dev(pci), to_dev(pv), (no, nc), origin=0)
+        neg = J.shifted_diag_tensor(torch.float64, no, nc, shift=t * 10, val=0.5 + t, device=DEV)
+        pairs.append((neg, pos))
+        Nd, Pd = np.zeros((no, nc)), np.zeros((no, nc))
+        Nd[np.arange(no), t * 10 + np.arange(no)] = 0.5 + t
+        for r in range(no):
+            Pd[r, pci[prp[r]:prp[r + 1]]] += pv[prp[r]:prp[r + 1]]
+        dense_pairs.append((Nd, Pd))
+    M = J.BlockBandedMatrix(D, [pairs], T, 1, nd, [no], nc)
+    m, n = M.shape
+    x = np.random.default_rng(13).uniform(-1, 1, n)
+    yd = torch.full((m,), np.nan, dtype=torch.float64, device=DEV)
+    J.mul(yd, M, to_dev(x))
+    J.device_status()
+    assert len(M._compiled.patches) == T - 1
+    Dd = np.zeros((nd, nc))
+    for r in range(nd):
+        Dd[r, ci[rp[r]:rp[r + 1]]] += v[rp[r]:rp[r + 1]]
+    xs = x.reshape(T, nc)
+    ref, bound = [], []
+    for t in range(T):
+        ref.append(Dd @ xs[t]), bound.append(np.abs(Dd) @ np.abs(xs[t]))
+        if t < T - 1:
+            Nd, Pd = dense_pairs[t]
+            ref.append(Nd @ xs[t] + Pd @ xs[t + 1])
+            bound.append(np.abs(Nd) @ np.abs(xs[t]) + np.abs(Pd) @ np.abs(xs[t + 1]))
+    assert_within(yd.cpu().numpy(), np.concatenate(ref), np.concatenate(bound), 1e-12)
