@@ -316,6 +316,56 @@ JLB_API int jlb_coo_to_bsr_fill(void *stream, int dtype, int idx_base, int64_t m
                                 int64_t nnzb, int32_t *bcolind, void *bval, void *workspace,
                                 size_t workspace_bytes);
 
+/* COO -> CSR (convert_format(u, Formats.CSR) for a COO u, src/convert.jl:
+ * 302-388).  JLUST's COO declares its rows ordered, so the reference composes
+ * the entries in storage order without sorting: rows must not decrease
+ * (NonCanonicalStorage otherwise, where the composer's assertion fails,
+ * src/convert.jl:246), explicit zeros are dropped, columns keep their storage
+ * order within a row, and an entry whose (row, column) equals that of the
+ * nonzero entry before it is merged into it, keeping the first value.  Count
+ * fills rowptr (m + 1, origin idx_base) and *nnz_out (synchronises `stream`);
+ * the caller allocates colind and csr_val (nnz_out each); fill writes them
+ * (columns keep the origin).  A CSR source converts the same way after
+ * jlb_positions_to_coordinates expands its rows. */
+JLB_API size_t jlb_coo_to_csr_workspace_size(int64_t m, int64_t n, int64_t nnz);
+JLB_API int jlb_coo_to_csr_count(void *stream, int dtype, int idx_base, int64_t m, int64_t n,
+                                 int64_t nnz, const int32_t *rows, const int32_t *cols,
+                                 const void *val, int32_t *rowptr, int64_t *nnz_out,
+                                 void *workspace, size_t workspace_bytes);
+JLB_API int jlb_coo_to_csr_fill(void *stream, int dtype, int idx_base, int64_t m, int64_t n,
+                                int64_t nnz, const int32_t *rows, const int32_t *cols,
+                                const void *val, int64_t nnz_out, int32_t *colind, void *csr_val,
+                                void *workspace, size_t workspace_bytes);
+
+/* Sorted compression: nnz (outer, inner) coordinate pairs compressed along the
+ * outer coordinate with the entries lexsorted by (outer, inner, storage
+ * index), explicit zeros dropped and the first of each run of equal
+ * coordinates kept -- the composer's path when the target's level order
+ * differs from the source's (src/convert.jl:334-345, 419-424): COO -> CSC
+ * (outer = columns, inner = rows), CSR -> CSC (outer = colind, inner = the
+ * expanded rows), CSC -> CSR (outer = rowind, inner = the expanded columns).
+ * Count fills ptr (n_outer + 1, origin idx_base) and *nnz_out (synchronises
+ * `stream`) and leaves the sorted entries in the workspace; fill needs that
+ * same workspace, unchanged (JLB_ERR_WORKSPACE otherwise), and writes
+ * inner_out and val_out (nnz_out each).  Outer indices holding more than
+ * 16,777,216 entries are refused (UnsupportedIndexType). */
+JLB_API size_t jlb_sorted_compress_workspace_size(int64_t n_outer, int64_t nnz);
+JLB_API int jlb_sorted_compress_count(void *stream, int dtype, int idx_base, int64_t n_outer,
+                                      int64_t n_inner, int64_t nnz, const int32_t *outer,
+                                      const int32_t *inner, const void *val, int32_t *ptr,
+                                      int64_t *nnz_out, void *workspace, size_t workspace_bytes);
+JLB_API int jlb_sorted_compress_fill(void *stream, int dtype, int idx_base, int64_t n_outer,
+                                     int64_t n_inner, int64_t nnz, const int32_t *outer,
+                                     const int32_t *inner, const void *val, const int32_t *ptr,
+                                     int64_t nnz_out, int32_t *inner_out, void *val_out,
+                                     void *workspace, size_t workspace_bytes);
+
+/* coords[k] = i + idx_base for every k in [ptr[i], ptr[i+1]) - idx_base: the
+ * outer coordinate of each entry of a compressed level (the decomposer's walk
+ * of a dense-over-compressed level, src/convert.jl:5-111). */
+JLB_API int jlb_positions_to_coordinates(void *stream, int idx_base, int64_t n_outer, int64_t nnz,
+                                         const int32_t *ptr, int32_t *coords);
+
 /* ------------------------------------- row-partitioned SpMV (multi-GPU) */
 
 /* Steps first_step .. first_step+nsteps-1 of x <- A x for a row-partitioned

@@ -62,6 +62,16 @@ SIGNATURES = {
                                   _p, _sz]),
     "jlb_coo_to_bsr_fill": (_i, [_p, _i, _i, _i64, _i64, _i64, _p, _p, _p, _i, _i, _p, _i64, _p,
                                  _p, _p, _sz]),
+    "jlb_coo_to_csr_workspace_size": (_sz, [_i64, _i64, _i64]),
+    "jlb_coo_to_csr_count": (_i, [_p, _i, _i, _i64, _i64, _i64, _p, _p, _p, _p, _pi64, _p, _sz]),
+    "jlb_coo_to_csr_fill": (_i, [_p, _i, _i, _i64, _i64, _i64, _p, _p, _p, _i64, _p, _p, _p,
+                                 _sz]),
+    "jlb_sorted_compress_workspace_size": (_sz, [_i64, _i64]),
+    "jlb_sorted_compress_count": (_i, [_p, _i, _i, _i64, _i64, _i64, _p, _p, _p, _p, _pi64, _p,
+                                       _sz]),
+    "jlb_sorted_compress_fill": (_i, [_p, _i, _i, _i64, _i64, _i64, _p, _p, _p, _p, _i64, _p, _p,
+                                      _p, _sz]),
+    "jlb_positions_to_coordinates": (_i, [_p, _i, _i64, _i64, _p, _p]),
     "jlb_halo_spmv_steps": (_i, [_p, _i, _i, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _p,
                                  _p, _p, _i, _i, C.c_uint64]),
     "jlb_ipc_handle": (_i, [_p, _p, C.POINTER(C.c_uint64)]),

@@ -90,7 +90,7 @@ extern "C" JLB_API int jlb_device_status(void *stream) {
     }
     if (bits & DEV_ERR_TIMEOUT)
         return fail(JLB_ERR_DEVICE_TIMEOUT, "a bounded device wait gave up (error bits 0x%x)", bits);
-    if (bits & (DEV_ERR_BOUNDS | DEV_ERR_OVERFLOW))
+    if (bits & (DEV_ERR_BOUNDS | DEV_ERR_OVERFLOW | DEV_ERR_ORDER))
         return fail(JLB_ERR_NONCANONICAL_STORAGE,
                     "a device bounds/overflow check failed (error bits 0x%x)", bits);
     return ok();

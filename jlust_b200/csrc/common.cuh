@@ -49,6 +49,7 @@ enum DevErr : int {
     DEV_ERR_TIMEOUT = 1,      // an mbarrier / flag wait exceeded its limit
     DEV_ERR_BOUNDS = 2,       // an index outside the declared extents
     DEV_ERR_OVERFLOW = 4,     // an int32 position buffer overflowed
+    DEV_ERR_ORDER = 8,        // coordinates out of the order the format declares
 };
 
 // Per-unit accessors, defined once per .cu file by JLB_DEFINE_DEV_ERROR.

@@ -500,6 +500,325 @@ inline unsigned grid_for(int64_t items, int per = 256) {
 
 inline unsigned grid_rows(int64_t mb) { return (unsigned)(mb < 148 * 64 ? (mb > 0 ? mb : 1) : 148 * 64); }
 
+// ------------------------------------------------- sorted compression
+// COO-style (outer, inner) coordinate pairs compressed along the outer
+// coordinate, the composer's path when the target's level order differs from
+// the source's (CSC targets, CSC -> CSR): the nonzero entries are bucketed by
+// outer coordinate (coo_bucket with one bucket per outer index), each bucket
+// is sorted by (inner coordinate, storage index) -- the order of the
+// composer's stable lexsort (src/convert.jl:334-345, 419-424) -- and the first
+// entry of every run of equal inner coordinates is kept, as the composer keeps
+// the first value of a run (src/convert.jl:222-238).  Sorting is an ascending
+// bitonic network over 64-bit keys column << 32 | storage index (unique, so
+// the network's instability does not matter), run on positions [0, len) of a
+// power-of-two network; positions past len act as +infinity and are never
+// touched.  Buckets ("rows") of up to kWarpKeys entries are sorted by one warp
+// in shared memory, up to kCtaKeys by one CTA in shared memory, longer ones by
+// one CTA in place in global memory (gathering the inner coordinate per
+// comparison).
+constexpr int kSortThreads = 256;
+constexpr int kWarpKeys = 256;
+constexpr int kLongThreads = 1024;
+constexpr int kCtaKeys = 16384;   // 128 KB of keys
+constexpr int64_t kMaxSortKeys = (int64_t)1 << 24;   // longest row the global-memory sort takes
+
+__device__ __forceinline__ uint64_t entry_key(const int32_t *__restrict__ cols, int base,
+                                              int32_t e) {
+    return ((uint64_t)(uint32_t)(ldg(cols + e) - base) << 32) | (uint32_t)e;
+}
+
+// One step pair of the network: the partner of i in step (k, j), or -1.
+template <typename I>
+__device__ __forceinline__ I bitonic_partner(I i, I k, I j, I len) {
+    const I l = j == (k >> 1) ? (i ^ (k - 1)) : (i ^ j);
+    return (l > i && l < len) ? l : I(-1);
+}
+
+struct WarpSync {
+    __device__ __forceinline__ void operator()() const { __syncwarp(); }
+};
+struct BlockSync {
+    __device__ __forceinline__ void operator()() const { __syncthreads(); }
+};
+
+// Ascending sort of s[0, len) by the threads tid, tid + nthr, ...; sync()
+// separates the steps and must be reached by all of them.
+template <typename Sync>
+__device__ void bitonic_smem(uint64_t *s, int len, int tid, int nthr, Sync sync) {
+    int P = 1;
+    while (P < len) P <<= 1;
+    for (int k = 2; k <= P; k <<= 1)
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int i = tid; i < P; i += nthr) {
+                const int l = bitonic_partner<int>(i, k, j, len);
+                if (l < 0) continue;
+                const uint64_t a = s[i], b = s[l];
+                if (a > b) {
+                    s[i] = b;
+                    s[l] = a;
+                }
+            }
+            sync();
+        }
+}
+
+__device__ __forceinline__ int warp_isum(int v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// Sorts every bucket of up to kWarpKeys entries (one warp per row) and counts
+// its distinct columns into cnt[r]; longer rows are appended to `long_rows`.
+__global__ void __launch_bounds__(kSortThreads)
+sort_short_rows(int64_t m, const int32_t *__restrict__ offs, int32_t *__restrict__ ent,
+                const int32_t *__restrict__ cols, int base, int32_t *__restrict__ cnt,
+                int32_t *__restrict__ long_rows, int32_t *__restrict__ n_long, int64_t long_cap) {
+    __shared__ uint64_t s_keys[kSortThreads / kWarp][kWarpKeys];
+    const int lane = threadIdx.x % kWarp, warp = threadIdx.x / kWarp;
+    uint64_t *s = s_keys[warp];
+    const int64_t nwarps = (int64_t)gridDim.x * (kSortThreads / kWarp);
+    for (int64_t r = (int64_t)blockIdx.x * (kSortThreads / kWarp) + warp; r < m; r += nwarps) {
+        const int lo = ldg(offs + r), len = ldg(offs + r + 1) - lo;
+        if (len > kWarpKeys) {
+            if (lane == 0) {
+                const int q = atomicAdd(n_long, 1);
+                if (q < long_cap) long_rows[q] = (int32_t)r;
+                else dev_error(DEV_ERR_OVERFLOW);
+            }
+            continue;
+        }
+        for (int i = lane; i < len; i += kWarp) s[i] = entry_key(cols, base, ent[lo + i]);
+        __syncwarp();
+        bitonic_smem(s, len, lane, kWarp, WarpSync{});
+        int u = 0;
+        for (int i = lane; i < len; i += kWarp) {
+            ent[lo + i] = (int32_t)(uint32_t)s[i];
+            u += (i == 0 || (s[i] >> 32) != (s[i - 1] >> 32));
+        }
+        u = warp_isum(u);
+        if (lane == 0) cnt[r] = u;
+        __syncwarp();
+    }
+}
+
+__device__ __forceinline__ int block_isum(int v, int *s_red) {
+    const int lane = threadIdx.x % kWarp, warp = threadIdx.x / kWarp;
+    v = warp_isum(v);
+    if (lane == 0) s_red[warp] = v;
+    __syncthreads();
+    int t = 0;
+    for (int w = 0; w < (int)(blockDim.x / kWarp); ++w) t += s_red[w];
+    __syncthreads();
+    return t;
+}
+
+// Sorts the buckets listed in long_rows, one CTA per row.
+__global__ void __launch_bounds__(kLongThreads)
+sort_long_rows(const int32_t *__restrict__ offs, int32_t *ent, const int32_t *__restrict__ cols,
+               int base, int32_t *__restrict__ cnt, const int32_t *__restrict__ long_rows,
+               const int32_t *__restrict__ n_long, int64_t long_cap) {
+    extern __shared__ uint64_t s_dyn[];
+    __shared__ int s_red[kLongThreads / kWarp];
+    const int tid = threadIdx.x;
+    int nl = *n_long;
+    if (nl > long_cap) nl = (int)long_cap;
+    for (int b = blockIdx.x; b < nl; b += gridDim.x) {
+        const int32_t r = long_rows[b];
+        const int lo = ldg(offs + r), len = ldg(offs + r + 1) - lo;
+        int u = 0;
+        if (len > kMaxSortKeys) {
+            if (tid == 0) {
+                dev_error(DEV_ERR_OVERFLOW);
+                cnt[r] = 0;
+            }
+            continue;
+        }
+        if (len <= kCtaKeys) {
+            for (int i = tid; i < len; i += kLongThreads) s_dyn[i] = entry_key(cols, base, ent[lo + i]);
+            __syncthreads();
+            bitonic_smem(s_dyn, len, tid, kLongThreads, BlockSync{});
+            for (int i = tid; i < len; i += kLongThreads) {
+                ent[lo + i] = (int32_t)(uint32_t)s_dyn[i];
+                u += (i == 0 || (s_dyn[i] >> 32) != (s_dyn[i - 1] >> 32));
+            }
+        } else {
+            // In place in global memory: the same network on entry indices,
+            // each comparison gathering both columns.
+            int32_t *e = ent + lo;
+            const int64_t n64 = len;
+            int64_t P = 1;
+            while (P < n64) P <<= 1;
+            for (int64_t k = 2; k <= P; k <<= 1)
+                for (int64_t j = k >> 1; j > 0; j >>= 1) {
+                    for (int64_t i = tid; i < P; i += kLongThreads) {
+                        const int64_t l = bitonic_partner<int64_t>(i, k, j, n64);
+                        if (l < 0) continue;
+                        const int32_t ea = e[i], eb = e[l];
+                        if (entry_key(cols, base, ea) > entry_key(cols, base, eb)) {
+                            e[i] = eb;
+                            e[l] = ea;
+                        }
+                    }
+                    __syncthreads();
+                }
+            for (int i = tid; i < len; i += kLongThreads)
+                u += (i == 0 || ldg(cols + e[i]) != ldg(cols + e[i - 1]));
+        }
+        u = block_isum(u, s_red);
+        if (tid == 0) cnt[r] = u;
+        __syncthreads();
+    }
+}
+
+// Writes the first entry of every run of equal columns of each sorted bucket
+// to the CSR (one warp per row): its column (origin kept) and value.
+template <int ES>
+__global__ void __launch_bounds__(kSortThreads)
+emit_csr_rows(int64_t m, const int32_t *__restrict__ offs, const int32_t *__restrict__ ent,
+              const int32_t *__restrict__ cols, const void *__restrict__ val, int base,
+              const int32_t *__restrict__ rowptr, int64_t nnz_out, int32_t *__restrict__ colind,
+              void *__restrict__ out_val) {
+    const int lane = threadIdx.x % kWarp, warp = threadIdx.x / kWarp;
+    const int64_t nwarps = (int64_t)gridDim.x * (kSortThreads / kWarp);
+    for (int64_t r = (int64_t)blockIdx.x * (kSortThreads / kWarp) + warp; r < m; r += nwarps) {
+        const int lo = ldg(offs + r), hi = ldg(offs + r + 1);
+        const int64_t out = (int64_t)ldg(rowptr + r) - base, end = (int64_t)ldg(rowptr + r + 1) - base;
+        int64_t run = 0;
+        int32_t prev = 0;
+        for (int i0 = lo; i0 < hi; i0 += kWarp) {
+            const int i = i0 + lane;
+            const bool in = i < hi;
+            const int32_t e = in ? ent[i] : 0;
+            const int32_t c = in ? ldg(cols + e) : 0;
+            int32_t up = __shfl_up_sync(0xffffffffu, c, 1);
+            if (lane == 0) up = prev;
+            const bool first = in && (i == lo || c != up);
+            const unsigned bal = __ballot_sync(0xffffffffu, first);
+            if (first) {
+                const int64_t q = out + run + __popc(bal & ((1u << lane) - 1u));
+                if (q >= 0 && q < end && q < nnz_out) {
+                    colind[q] = c;
+                    copy_val<ES>(out_val, q, val, e);
+                } else {
+                    dev_error(DEV_ERR_OVERFLOW);
+                }
+            }
+            run += __popc(bal);
+            prev = __shfl_sync(0xffffffffu, c, kWarp - 1);
+        }
+    }
+}
+
+// ------------------------------------------------------------- COO -> CSR
+// JLUST's COO format declares its levels ordered, so convert_format hands a
+// COO source to the composer in storage order without sorting
+// (src/convert.jl:346-355): rows must not decrease (the composer's dense row
+// level asserts it, :246), entries keep their storage order within a row,
+// explicit zeros are dropped (:316) and an entry whose coordinates equal
+// those of the nonzero entry before it is merged into it, keeping the first
+// value (the unique column level's run, :231-238).  So the CSR is a stable
+// compaction of the COO: keep[p] marks the entries that stay, an exclusive
+// scan of keep gives their slots, and the first kept entry of row r writes
+// rowptr for the rows since the previous kept entry's row.
+
+// The last nonzero entry before p, or -1.  Every zero belongs to the run
+// before exactly one nonzero entry, so these walks add up to at most nnz.
+template <int ES>
+__device__ __forceinline__ int64_t prev_nonzero(const void *__restrict__ val, int64_t p) {
+    int64_t q = p - 1;
+    while (q >= 0 && is_zero<ES>(val, q)) --q;
+    return q;
+}
+
+template <int ES>
+__global__ void __launch_bounds__(kThreads)
+coo_keep(int64_t nnz, const int32_t *__restrict__ rows, const int32_t *__restrict__ cols,
+         const void *__restrict__ val, int base, int64_t m, int64_t n, int32_t *__restrict__ keep) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < nnz; p += stride) {
+        int k = 0;
+        if (!is_zero<ES>(val, p)) {
+            const int32_t r = ldg(rows + p), c = ldg(cols + p);
+            if ((int64_t)r - base < 0 || (int64_t)r - base >= m || (int64_t)c - base < 0 ||
+                (int64_t)c - base >= n) {
+                dev_error(DEV_ERR_BOUNDS);
+            } else {
+                const int64_t q = prev_nonzero<ES>(val, p);
+                k = 1;
+                if (q >= 0) {
+                    const int32_t rq = ldg(rows + q);
+                    if (rq > r) dev_error(DEV_ERR_ORDER);
+                    k = (rq != r || ldg(cols + q) != c);
+                }
+            }
+        }
+        keep[p] = k;
+    }
+}
+
+// rowptr[i] = total + base for every i: the rows past the last kept entry.
+__global__ void fill_rowptr(int64_t m, const int32_t *__restrict__ total, int base,
+                            int32_t *__restrict__ rowptr) {
+    const int32_t v = *total + base;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i <= m; i += stride) rowptr[i] = v;
+}
+
+// The first kept entry of row r (slot s) writes rowptr[i] = s + base for the
+// rows i in (row of the nonzero entry before it, r].
+template <int ES>
+__global__ void __launch_bounds__(kThreads)
+coo_rowptr(int64_t nnz, const int32_t *__restrict__ rows, const void *__restrict__ val, int base,
+           int64_t m, const int32_t *__restrict__ keep, const int32_t *__restrict__ slot,
+           int32_t *__restrict__ rowptr) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < nnz; p += stride) {
+        if (!keep[p]) continue;
+        const int64_t r = (int64_t)ldg(rows + p) - base;
+        const int64_t q = prev_nonzero<ES>(val, p);
+        int64_t rp = q < 0 ? -1 : (int64_t)ldg(rows + q) - base;
+        if (rp < -1) rp = -1;
+        for (int64_t i = rp + 1; i <= r && i < m; ++i) rowptr[i] = slot[p] + base;
+    }
+}
+
+template <int ES>
+__global__ void __launch_bounds__(kThreads)
+coo_emit(int64_t nnz, const int32_t *__restrict__ cols, const void *__restrict__ val,
+         const int32_t *__restrict__ keep, const int32_t *__restrict__ slot, int64_t nnz_out,
+         int32_t *__restrict__ colind, void *__restrict__ out_val) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < nnz; p += stride) {
+        if (!keep[p]) continue;
+        const int64_t q = slot[p];
+        if (q < 0 || q >= nnz_out) {
+            dev_error(DEV_ERR_OVERFLOW);
+            continue;
+        }
+        colind[q] = ldg(cols + p);
+        copy_val<ES>(out_val, q, val, p);
+    }
+}
+
+// coordinates[k] = i + base for k in [ptr[i], ptr[i+1]) - base: the outer
+// coordinate of every entry of a compressed level (one warp per outer index).
+__global__ void __launch_bounds__(kThreads)
+expand_positions(int64_t n_outer, int64_t nnz, const int32_t *__restrict__ ptr, int base,
+                 int32_t *__restrict__ coords) {
+    const int lane = threadIdx.x % kWarp;
+    const int64_t nwarps = (int64_t)gridDim.x * (kThreads / kWarp);
+    for (int64_t i = (int64_t)blockIdx.x * (kThreads / kWarp) + threadIdx.x / kWarp; i < n_outer;
+         i += nwarps) {
+        const int64_t lo = (int64_t)ldg(ptr + i) - base, hi = (int64_t)ldg(ptr + i + 1) - base;
+        if (lo < 0 || hi > nnz || lo > hi) {
+            if (lane == 0) dev_error(DEV_ERR_BOUNDS);
+            continue;
+        }
+        for (int64_t k = lo + lane; k < hi; k += kWarp) coords[k] = (int32_t)(i + base);
+    }
+}
+
 }  // namespace conv
 
 // Workspace carving helper: 256-byte aligned sub-buffers.
@@ -605,7 +924,8 @@ static conv::Src csr_src(int dtype, int idx_base, int64_t m, int64_t n, const in
 }
 
 static int finish_count(cudaStream_t st, int64_t mb, int idx_base, int32_t *browptr,
-                        int64_t *nnzb, void *ws, size_t wsb, int *dev_bits) {
+                        int64_t *nnzb, void *ws, size_t wsb, int *dev_bits,
+                        const char *overflow_msg = "block count overflows Int32 positions") {
     // browptr[1..mb] holds the counts: scan in place.
     int r = conv::scan(st, mb, browptr + 1, browptr, idx_base, ws, wsb);
     if (r) return r;
@@ -617,8 +937,7 @@ static int finish_count(cudaStream_t st, int64_t mb, int idx_base, int32_t *brow
     if (bits < 0) return fail(JLB_ERR_CUDA, "reading the device error word failed");
     if (bits & DEV_ERR_BOUNDS)
         return fail(JLB_ERR_NONCANONICAL_STORAGE, "coordinate outside the matrix extents");
-    if (bits & DEV_ERR_OVERFLOW)
-        return fail(JLB_ERR_UNSUPPORTED_INDEX_TYPE, "block count overflows Int32 positions");
+    if (bits & DEV_ERR_OVERFLOW) return fail(JLB_ERR_UNSUPPORTED_INDEX_TYPE, "%s", overflow_msg);
     *nnzb = (int64_t)last - idx_base;
     return ok();
 }
@@ -846,4 +1165,247 @@ extern "C" JLB_API int jlb_exclusive_scan_i32_noalloc(void *stream, int64_t n,
     // so the scratch needs no clearing between calls.
     return conv::scan(as_stream(stream), n, counts, out, idx_base, scratch,
                       (size_t)conv::kNoAllocTiles * sizeof(int64_t));
+}
+
+// ------------------------------------------------- sorted compression
+// Workspace: [buckets (as for COO -> BSR with b1 = 1) | stamp | long-bucket
+// count | long-bucket list].  The count phase leaves the sorted buckets there
+// for the fill phase.
+namespace {
+struct SortedWs {
+    uint64_t *stamp;
+    int32_t *n_long, *long_rows;
+    int64_t long_cap;
+    size_t bytes;
+};
+
+SortedWs sorted_ws(void *ws, int64_t n_outer, int64_t nnz) {
+    SortedWs w{};
+    Carve k{reinterpret_cast<char *>(ws)};
+    k.off = coo_ws(n_outer, nnz, 1, 1, 0, nullptr);
+    w.stamp = k.take<uint64_t>(1);
+    w.n_long = k.take<int32_t>(1);
+    w.long_cap = nnz / (conv::kWarpKeys + 1) + 1;
+    w.long_rows = k.take<int32_t>((size_t)w.long_cap);
+    w.bytes = k.off + 256;
+    return w;
+}
+
+uint64_t sorted_key(int64_t n_outer, int64_t n_inner, int64_t nnz, int base, int dtype,
+                    const void *outer, const void *inner, const void *val) {
+    // b1 = b2 = -1 marks a sorted-compression workspace
+    return carry_key(n_outer, n_inner, nnz, -1, -1, base, dtype, outer, inner, val);
+}
+}  // namespace
+
+extern "C" JLB_API size_t jlb_sorted_compress_workspace_size(int64_t n_outer, int64_t nnz) {
+    if (n_outer < 0 || nnz < 0) return 0;
+    return sorted_ws(nullptr, n_outer, nnz).bytes;
+}
+
+extern "C" JLB_API int jlb_sorted_compress_count(void *stream, int dtype, int idx_base,
+                                                 int64_t n_outer, int64_t n_inner, int64_t nnz,
+                                                 const int32_t *outer, const int32_t *inner,
+                                                 const void *val, int32_t *ptr, int64_t *nnz_out,
+                                                 void *workspace, size_t workspace_bytes) {
+    int r = conv_args(dtype, idx_base, n_outer, n_inner, nnz, 1, 1);
+    if (r) return r;
+    if (n_outer > INT32_MAX - 1) return fail(JLB_ERR_UNSUPPORTED_INDEX_TYPE, "outer extent exceeds Int32");
+    if (!ptr || !nnz_out || (nnz > 0 && (!outer || !inner || !val)))
+        return fail(JLB_ERR_INVALID_ARGUMENT, "null buffer");
+    const SortedWs w = sorted_ws(workspace, n_outer, nnz);
+    if (!workspace || workspace_bytes < w.bytes)
+        return fail(JLB_ERR_WORKSPACE, "workspace too small");
+    cudaStream_t st = as_stream(stream);
+    int32_t *boffs, *bent;
+    r = coo_bucket(st, dtype, idx_base, n_outer, n_inner, nnz, outer, inner, val, 1, workspace,
+                   &boffs, &bent);
+    if (r) return r;
+    JLB_CUDA(cudaMemsetAsync(w.n_long, 0, sizeof(int32_t), st));
+    if (n_outer > 0) {
+        const int64_t g = ceil_div(n_outer, conv::kSortThreads / kWarp);
+        conv::sort_short_rows<<<(unsigned)(g < 148 * 16 ? g : 148 * 16), conv::kSortThreads, 0, st>>>(
+            n_outer, boffs, bent, inner, idx_base, ptr + 1, w.long_rows, w.n_long, w.long_cap);
+        JLB_LAUNCH_CHECK("sort_short_rows");
+        const int smem = conv::kCtaKeys * (int)sizeof(uint64_t);
+        JLB_CUDA(cudaFuncSetAttribute(conv::sort_long_rows,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        conv::sort_long_rows<<<148, conv::kLongThreads, smem, st>>>(
+            boffs, bent, inner, idx_base, ptr + 1, w.long_rows, w.n_long, w.long_cap);
+        JLB_LAUNCH_CHECK("sort_long_rows");
+    }
+    const uint64_t key = sorted_key(n_outer, n_inner, nnz, idx_base, dtype, outer, inner, val);
+    JLB_CUDA(cudaMemcpyAsync(w.stamp, &key, sizeof(key), cudaMemcpyHostToDevice, st));
+    // The bucket scan is done with the scan workspace: reuse it for ptr.
+    Carve k{reinterpret_cast<char *>(workspace)};
+    k.take<int32_t>((size_t)n_outer + 1);
+    k.take<int32_t>((size_t)(n_outer > 0 ? n_outer : 1));
+    k.take<int32_t>((size_t)(nnz > 0 ? nnz : 1));
+    const size_t sws = conv::scan_ws(n_outer > 0 ? n_outer : 1);
+    char *scan_ws = k.take<char>(sws);
+    return finish_count(st, n_outer, idx_base, ptr, nnz_out, scan_ws, sws, nullptr,
+                        "an outer index holds more than 16,777,216 entries, the longest this "
+                        "sort takes");
+}
+
+extern "C" JLB_API int jlb_sorted_compress_fill(void *stream, int dtype, int idx_base,
+                                                int64_t n_outer, int64_t n_inner, int64_t nnz,
+                                                const int32_t *outer, const int32_t *inner,
+                                                const void *val, const int32_t *ptr,
+                                                int64_t nnz_out, int32_t *inner_out,
+                                                void *val_out, void *workspace,
+                                                size_t workspace_bytes) {
+    int r = conv_args(dtype, idx_base, n_outer, n_inner, nnz, 1, 1);
+    if (r) return r;
+    if (!ptr || (nnz > 0 && (!outer || !inner || !val)) || (nnz_out > 0 && (!inner_out || !val_out)))
+        return fail(JLB_ERR_INVALID_ARGUMENT, "null buffer");
+    if (nnz_out < 0 || nnz_out > nnz) return fail(JLB_ERR_INVALID_ARGUMENT, "bad nnz_out");
+    const SortedWs w = sorted_ws(workspace, n_outer, nnz);
+    if (!workspace || workspace_bytes < w.bytes)
+        return fail(JLB_ERR_WORKSPACE, "workspace too small");
+    cudaStream_t st = as_stream(stream);
+    uint64_t stamp = 0;
+    JLB_CUDA(cudaMemcpyAsync(&stamp, w.stamp, sizeof(stamp), cudaMemcpyDeviceToHost, st));
+    JLB_CUDA(cudaStreamSynchronize(st));
+    if (stamp != sorted_key(n_outer, n_inner, nnz, idx_base, dtype, outer, inner, val))
+        return fail(JLB_ERR_WORKSPACE,
+                    "the fill phase needs the workspace its count phase filled, unchanged");
+    if (n_outer == 0) return ok();
+    Carve k{reinterpret_cast<char *>(workspace)};
+    const int32_t *boffs = k.take<int32_t>((size_t)n_outer + 1);
+    k.take<int32_t>((size_t)n_outer);
+    const int32_t *bent = k.take<int32_t>((size_t)(nnz > 0 ? nnz : 1));
+    const int64_t g64 = ceil_div(n_outer, conv::kSortThreads / kWarp);
+    const unsigned g = (unsigned)(g64 < 148 * 16 ? g64 : 148 * 16);
+    const size_t es = dtype_size(dtype);
+    if (es == 8)
+        conv::emit_csr_rows<8><<<g, conv::kSortThreads, 0, st>>>(n_outer, boffs, bent, inner, val,
+                                                                 idx_base, ptr, nnz_out, inner_out, val_out);
+    else if (es == 4)
+        conv::emit_csr_rows<4><<<g, conv::kSortThreads, 0, st>>>(n_outer, boffs, bent, inner, val,
+                                                                 idx_base, ptr, nnz_out, inner_out, val_out);
+    else
+        conv::emit_csr_rows<2><<<g, conv::kSortThreads, 0, st>>>(n_outer, boffs, bent, inner, val,
+                                                                 idx_base, ptr, nnz_out, inner_out, val_out);
+    JLB_LAUNCH_CHECK("emit_csr_rows");
+    return ok();
+}
+
+extern "C" JLB_API int jlb_positions_to_coordinates(void *stream, int idx_base, int64_t n_outer,
+                                                    int64_t nnz, const int32_t *ptr,
+                                                    int32_t *coords) {
+    if (idx_base != 0 && idx_base != 1) return fail(JLB_ERR_INVALID_ARGUMENT, "idx_base must be 0 or 1");
+    if (n_outer < 0 || nnz < 0) return fail(JLB_ERR_INCOMPATIBLE_EXTENTS, "negative extent");
+    if (n_outer > INT32_MAX - 1) return fail(JLB_ERR_UNSUPPORTED_INDEX_TYPE, "outer extent exceeds Int32");
+    if (!ptr || (nnz > 0 && !coords)) return fail(JLB_ERR_INVALID_ARGUMENT, "null buffer");
+    if (n_outer == 0) return ok();
+    cudaStream_t st = as_stream(stream);
+    const int64_t g = ceil_div(n_outer, conv::kThreads / kWarp);
+    conv::expand_positions<<<(unsigned)(g < 148 * 16 ? g : 148 * 16), conv::kThreads, 0, st>>>(
+        n_outer, nnz, ptr, idx_base, coords);
+    JLB_LAUNCH_CHECK("expand_positions");
+    return ok();
+}
+
+// ------------------------------------------------------------- COO -> CSR
+// Workspace: [keep flags (nnz) | slots (nnz + 1) | scan scratch].
+namespace {
+struct CooCsrWs {
+    int32_t *keep, *slot;
+    char *scan;
+    size_t scan_bytes, bytes;
+};
+
+CooCsrWs coo_csr_ws(void *ws, int64_t nnz) {
+    CooCsrWs w{};
+    Carve k{reinterpret_cast<char *>(ws)};
+    w.keep = k.take<int32_t>((size_t)(nnz > 0 ? nnz : 1));
+    w.slot = k.take<int32_t>((size_t)nnz + 1);
+    w.scan_bytes = conv::scan_ws(nnz > 0 ? nnz : 1);
+    w.scan = k.take<char>(w.scan_bytes);
+    w.bytes = k.off + 256;
+    return w;
+}
+
+#define JLB_ES_LAUNCH(kernel, es, grid, threads, st, ...)                                 \
+    do {                                                                                   \
+        if ((es) == 8) conv::kernel<8><<<(grid), (threads), 0, (st)>>>(__VA_ARGS__);      \
+        else if ((es) == 4) conv::kernel<4><<<(grid), (threads), 0, (st)>>>(__VA_ARGS__); \
+        else conv::kernel<2><<<(grid), (threads), 0, (st)>>>(__VA_ARGS__);                \
+    } while (0)
+
+// keep flags and their exclusive scan (slot[nnz] = entries kept).
+int coo_csr_slots(cudaStream_t st, int dtype, int idx_base, int64_t m, int64_t n, int64_t nnz,
+                  const int32_t *rows, const int32_t *cols, const void *val, const CooCsrWs &w) {
+    if (nnz > 0) {
+        JLB_ES_LAUNCH(coo_keep, dtype_size(dtype), conv::grid_for(nnz), conv::kThreads, st, nnz,
+                      rows, cols, val, idx_base, m, n, w.keep);
+        JLB_LAUNCH_CHECK("coo_keep");
+    }
+    return conv::scan(st, nnz, w.keep, w.slot, 0, w.scan, w.scan_bytes);
+}
+}  // namespace
+
+extern "C" JLB_API size_t jlb_coo_to_csr_workspace_size(int64_t m, int64_t n, int64_t nnz) {
+    if (m < 0 || nnz < 0) return 0;
+    return coo_csr_ws(nullptr, nnz).bytes;
+}
+
+extern "C" JLB_API int jlb_coo_to_csr_count(void *stream, int dtype, int idx_base, int64_t m,
+                                            int64_t n, int64_t nnz, const int32_t *rows,
+                                            const int32_t *cols, const void *val, int32_t *rowptr,
+                                            int64_t *nnz_out, void *workspace,
+                                            size_t workspace_bytes) {
+    int r = conv_args(dtype, idx_base, m, n, nnz, 1, 1);
+    if (r) return r;
+    if (m > INT32_MAX - 1) return fail(JLB_ERR_UNSUPPORTED_INDEX_TYPE, "rows exceed Int32");
+    if (!rowptr || !nnz_out || (nnz > 0 && (!rows || !cols || !val)))
+        return fail(JLB_ERR_INVALID_ARGUMENT, "null buffer");
+    const CooCsrWs w = coo_csr_ws(workspace, nnz);
+    if (!workspace || workspace_bytes < w.bytes) return fail(JLB_ERR_WORKSPACE, "workspace too small");
+    cudaStream_t st = as_stream(stream);
+    r = coo_csr_slots(st, dtype, idx_base, m, n, nnz, rows, cols, val, w);
+    if (r) return r;
+    conv::fill_rowptr<<<conv::grid_for(m + 1), conv::kThreads, 0, st>>>(m, w.slot + nnz, idx_base,
+                                                                        rowptr);
+    JLB_LAUNCH_CHECK("fill_rowptr");
+    if (nnz > 0) {
+        JLB_ES_LAUNCH(coo_rowptr, dtype_size(dtype), conv::grid_for(nnz), conv::kThreads, st, nnz,
+                      rows, val, idx_base, m, w.keep, w.slot, rowptr);
+        JLB_LAUNCH_CHECK("coo_rowptr");
+    }
+    int32_t total = 0;
+    JLB_CUDA(cudaMemcpyAsync(&total, w.slot + nnz, sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+    JLB_CUDA(cudaStreamSynchronize(st));
+    const int bits = take_dev_error_convert();
+    if (bits < 0) return fail(JLB_ERR_CUDA, "reading the device error word failed");
+    if (bits & DEV_ERR_BOUNDS)
+        return fail(JLB_ERR_NONCANONICAL_STORAGE, "coordinate outside the matrix extents");
+    if (bits & DEV_ERR_ORDER)
+        return fail(JLB_ERR_NONCANONICAL_STORAGE,
+                    "COO rows must not decrease (the COO format declares its rows ordered)");
+    *nnz_out = total;
+    return ok();
+}
+
+extern "C" JLB_API int jlb_coo_to_csr_fill(void *stream, int dtype, int idx_base, int64_t m,
+                                           int64_t n, int64_t nnz, const int32_t *rows,
+                                           const int32_t *cols, const void *val, int64_t nnz_out,
+                                           int32_t *colind, void *csr_val, void *workspace,
+                                           size_t workspace_bytes) {
+    int r = conv_args(dtype, idx_base, m, n, nnz, 1, 1);
+    if (r) return r;
+    if ((nnz > 0 && (!rows || !cols || !val)) || (nnz_out > 0 && (!colind || !csr_val)))
+        return fail(JLB_ERR_INVALID_ARGUMENT, "null buffer");
+    if (nnz_out < 0 || nnz_out > nnz) return fail(JLB_ERR_INVALID_ARGUMENT, "bad nnz_out");
+    const CooCsrWs w = coo_csr_ws(workspace, nnz);
+    if (!workspace || workspace_bytes < w.bytes) return fail(JLB_ERR_WORKSPACE, "workspace too small");
+    if (nnz == 0) return ok();
+    cudaStream_t st = as_stream(stream);
+    r = coo_csr_slots(st, dtype, idx_base, m, n, nnz, rows, cols, val, w);
+    if (r) return r;
+    JLB_ES_LAUNCH(coo_emit, dtype_size(dtype), conv::grid_for(nnz), conv::kThreads, st, nnz, cols,
+                  val, w.keep, w.slot, nnz_out, colind, csr_val);
+    JLB_LAUNCH_CHECK("coo_emit");
+    return ok();
 }

@@ -342,6 +342,64 @@ def coo_to_bsr(m, n, rows, cols, val, b1, b2, base=0):
     return bp, bc, bv
 
 
+def compose_compressed(n_outer, n_inner, outer, inner, val, base=0, sort=True):
+    """The reference's convert_format for a 2-D target whose first level is
+    dense over `outer` and whose second is compressed (unique) over `inner`
+    (src/convert.jl:302-388), given the source's entries as coordinate pairs in
+    storage order: explicit zeros dropped (:316; bf16 given as uint16 bits);
+    with `sort`, the entries stably lexsorted by (outer, inner) (:343-355,
+    419-424: the level order changes), else kept in storage order, where the
+    outer coordinate must not decrease (the dense level's assertion, :246,
+    raised here as ValueError); then each run of equal (outer, inner) keeps its
+    first value (:222-238).  Returns (ptr, inner, val) with the input's origin."""
+    outer = np.asarray(outer, np.int64) - base
+    inner = np.asarray(inner, np.int64) - base
+    val = np.asarray(val)
+    nz = (val & 0x7FFF) != 0 if val.dtype == np.uint16 else val != 0
+    o, i, v = outer[nz], inner[nz], val[nz]
+    if o.size and (o.min() < 0 or o.max() >= n_outer or i.min() < 0 or i.max() >= n_inner):
+        raise ValueError("coordinate outside the extents")
+    if sort:
+        order = np.lexsort((i, o))
+        o, i, v = o[order], i[order], v[order]
+    elif np.any(np.diff(o) < 0):
+        raise ValueError("outer coordinates decrease in an ordered source")
+    keep = np.ones(o.shape[0], bool)
+    keep[1:] = (o[1:] != o[:-1]) | (i[1:] != i[:-1])
+    o, i, v = o[keep], i[keep], v[keep]
+    ptr = np.zeros(n_outer + 1, np.int64)
+    np.cumsum(np.bincount(o, minlength=n_outer), out=ptr[1:])
+    return (ptr + base).astype(np.int32), (i + base).astype(np.int32), v
+
+
+def expand_positions(ptr, base=0):
+    """The outer coordinate (with origin) of every entry of a compressed level."""
+    ptr = np.asarray(ptr, np.int64) - base
+    return (np.repeat(np.arange(ptr.shape[0] - 1), np.diff(ptr)) + base).astype(np.int32)
+
+
+def coo_to_csr(m, n, rows, cols, val, base=0):
+    """COO -> CSR: the COO's levels are ordered, so no sort (convert.jl:346-355)."""
+    return compose_compressed(m, n, rows, cols, val, base, sort=False)
+
+
+def csr_to_csr(m, n, rowptr, colind, val, base=0):
+    return compose_compressed(m, n, expand_positions(rowptr, base), colind, val, base, sort=False)
+
+
+def coo_to_csc(m, n, rows, cols, val, base=0):
+    """COO -> CSC (colptr, rowind, val): the level order changes, so sorted."""
+    return compose_compressed(n, m, cols, rows, val, base, sort=True)
+
+
+def csr_to_csc(m, n, rowptr, colind, val, base=0):
+    return compose_compressed(n, m, colind, expand_positions(rowptr, base), val, base, sort=True)
+
+
+def csc_to_csr(m, n, colptr, rowind, val, base=0):
+    return compose_compressed(m, n, rowind, expand_positions(colptr, base), val, base, sort=True)
+
+
 # ------------------------------------------------------ block sparse matrix --
 def bsm_assemble(row_sizes, col_sizes, blocks):
     """The one CSR the reference compiles a BlockSparseMatrix of CSR blocks to

@@ -155,3 +155,47 @@ def test_dcsr_rows_not_stored_keep_y():
     y = O.dcsr_spmv(3, [0, 2, 4], [0, 2], [0, 2, 0, 2], [1.0, 2.0, 4.0, 5.0], [1.0, 2.0, 3.0],
                     y0, 1.0, 0.5)
     assert y.tolist() == [12.0, 20.0, 34.0]
+
+
+def test_csr_csc_conversion_kats(golden):
+    """The reference's CSR/CSC conversion tests on its 3x4 fixture
+    (test_convert.jl:34-40 CSR -> CSR identity, :44-58 CSR -> CSC buffers,
+    :97-106 CSR -> CSC -> CSR round trip, :110-116 the round trip through
+    COO), restated by the oracle's composer."""
+    g = golden["convert_fixture_3x4"]
+    rp, ci, v, base = _csr(g["A"], np.float32)
+    p2, i2, v2 = O.csr_to_csr(3, 4, rp, ci, v, base)
+    assert p2.tolist() == rp.tolist() and i2.tolist() == ci.tolist() and v2.tolist() == v.tolist()
+    cp, ri, cv = O.csr_to_csc(3, 4, rp, ci, v, base)
+    assert cp.tolist() == g["csc"]["colptr"]
+    assert ri.tolist() == g["csc"]["rowind"]
+    assert cv.tolist() == g["csc"]["val"]
+    p3, i3, v3 = O.csc_to_csr(3, 4, cp, ri, cv, base)
+    assert p3.tolist() == rp.tolist() and i3.tolist() == ci.tolist() and v3.tolist() == v.tolist()
+    rows = O.expand_positions(rp, base)
+    p4, i4, v4 = O.coo_to_csr(3, 4, rows, ci, v, base)
+    assert p4.tolist() == rp.tolist() and i4.tolist() == ci.tolist() and v4.tolist() == v.tolist()
+    # origin preserved (test_convert.jl:161-168)
+    p5, i5, _ = O.csr_to_csc(3, 4, rp + 1, ci + 1, v, 1)
+    assert p5.tolist() == [x + 1 for x in g["csc"]["colptr"]]
+    assert i5.tolist() == [x + 1 for x in g["csc"]["rowind"]]
+
+
+def test_coo_to_csr_composer_semantics():
+    """COO's levels are ordered, so COO -> CSR keeps storage order: columns
+    stay unsorted within a row, adjacent equal coordinates (after dropping
+    zeros) keep the first value, non-adjacent ones stay separate, and rows
+    that decrease are refused (convert.jl:222-246, 316, 346-355)."""
+    rows = np.array([0, 0, 0, 0, 0, 2, 2, 2], np.int32)
+    cols = np.array([3, 1, 1, 1, 3, 0, 0, 2], np.int32)
+    val = np.array([1.0, 2.0, 0.0, 5.0, 6.0, 7.0, 8.0, -0.0])
+    rp, ci, v = O.coo_to_csr(3, 4, rows, cols, val)
+    assert rp.tolist() == [0, 3, 3, 4]
+    assert ci.tolist() == [3, 1, 3, 0]
+    assert v.tolist() == [1.0, 2.0, 6.0, 7.0]
+    with pytest.raises(ValueError):
+        O.coo_to_csr(3, 4, np.array([1, 0], np.int32), np.array([0, 0], np.int32), np.ones(2))
+    # the same entries to CSC are lexsorted by (column, row, storage index)
+    cp, ri, cv = O.coo_to_csc(3, 4, rows, cols, val)
+    assert cp.tolist() == [0, 1, 2, 2, 3]
+    assert ri.tolist() == [2, 0, 0] and cv.tolist() == [7.0, 2.0, 1.0]
