@@ -69,6 +69,7 @@ enum jlb_sddmm_mode {
 
 typedef struct jlb_spmv_plan_s *jlb_spmv_plan;
 typedef struct jlb_spmm_plan_s *jlb_spmm_plan;
+typedef struct jlb_spgemm_plan_s *jlb_spgemm_plan;
 
 /* ---------------------------------------------------------------- runtime */
 
@@ -316,6 +317,37 @@ JLB_API int jlb_coo_to_bsr_fill(void *stream, int dtype, int idx_base, int64_t m
                                 int64_t nnzb, int32_t *bcolind, void *bval, void *workspace,
                                 size_t workspace_bytes);
 
+/* ----------------------------------------------------------------- SpGEMM */
+
+/* Prepared sparse x sparse product C = alpha * A * B, A m x k and B k x n CSR
+ * (Int32 indices, one origin), C m x n CSR with that origin: the reference's
+ * prepare(EmitterBackend, SpGEMMOp, u_A, u_B) / EmitterSpGEMMHandle
+ * (ext/KernelAbstractionsExt/ops/spgemm.jl:313-438; one-shot execute at
+ * :493-506 is create + execute).  Create runs the symbolic pass on the index
+ * buffers (synchronises `stream`, allocates the plan's device memory): C's
+ * row i holds one entry per distinct column among the products of row i's A
+ * entries with their B rows (explicit zeros included, as in the reference);
+ * it returns nnz(C) and the product count (more than 2^31 - 2 products, or a
+ * row of C with more than 2^24 products, is refused with
+ * JLB_ERR_UNSUPPORTED_INDEX_TYPE).  Structure copies C's row pointer (m + 1)
+ * and columns (ascending per row) into caller buffers.  Execute computes C's
+ * values for value buffers a_val, b_val of the planned structures (the
+ * handle's execute(h, u_A, u_B; alpha), :453-491): each entry is the sum from
+ * zero of its products (A value * B value, times alpha unless alpha = 1) in
+ * the order of A's entries then B's entries -- deterministic, where the
+ * reference adds them by atomics.  F32 and F64; beta = 0 only, as in the
+ * reference. */
+JLB_API int jlb_spgemm_plan_create(jlb_spgemm_plan *plan, void *stream, int dtype, int idx_base,
+                                   int64_t m, int64_t k, int64_t n, int64_t nnz_a,
+                                   const int32_t *a_rowptr, const int32_t *a_colind, int64_t nnz_b,
+                                   const int32_t *b_rowptr, const int32_t *b_colind,
+                                   int64_t *nnz_c, int64_t *products);
+JLB_API int jlb_spgemm_plan_structure(jlb_spgemm_plan plan, void *stream, int32_t *c_rowptr,
+                                      int32_t *c_colind);
+JLB_API int jlb_spgemm_plan_execute(jlb_spgemm_plan plan, void *stream, const void *a_val,
+                                    const void *b_val, void *c_val, double alpha);
+JLB_API int jlb_spgemm_plan_destroy(jlb_spgemm_plan plan);
+
 /* COO -> CSR (convert_format(u, Formats.CSR) for a COO u, src/convert.jl:
  * 302-388).  JLUST's COO declares its rows ordered, so the reference composes
  * the entries in storage order without sorting: rows must not decrease
@@ -325,7 +357,10 @@ JLB_API int jlb_coo_to_bsr_fill(void *stream, int dtype, int idx_base, int64_t m
  * nonzero entry before it is merged into it, keeping the first value.  Count
  * fills rowptr (m + 1, origin idx_base) and *nnz_out (synchronises `stream`);
  * the caller allocates colind and csr_val (nnz_out each); fill writes them
- * (columns keep the origin).  A CSR source converts the same way after
+ * (columns keep the origin), reusing the flags count left in the workspace
+ * when it gets the same workspace for the same buffers (any other workspace
+ * of the queried size is also correct: fill then recomputes them; fill
+ * synchronises `stream` to tell).  A CSR source converts the same way after
  * jlb_positions_to_coordinates expands its rows. */
 JLB_API size_t jlb_coo_to_csr_workspace_size(int64_t m, int64_t n, int64_t nnz);
 JLB_API int jlb_coo_to_csr_count(void *stream, int dtype, int idx_base, int64_t m, int64_t n,

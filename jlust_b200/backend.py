@@ -21,7 +21,8 @@ from .errors import (DeviceMismatch, IncompatibleExtents, UnsupportedFormat,
                      UnsupportedValueType)
 from .formats import TensorFormat
 from .ops import Op, OpType
-from .tensor import (USTensor, coordinates, dense_layout, nonzeros, positions, ust)
+from .tensor import (USTensor, coordinates, csr_tensor, dense_layout, nonzeros, positions,
+                     ust)
 
 
 class AbstractUSTBackend:
@@ -66,6 +67,8 @@ def supports_backend(backend, op: Op) -> bool:
         return _dense_n(f[0], 2) and _dense_n(f[1], 2) and f[2].family == "CSR"
     if op.tag == "BlockSpMM" and len(f) == 3:
         return f[0].family == "BSR" and _dense_n(f[1], 2) and _dense_n(f[2], 2)
+    if op.tag == "SpGEMM" and len(f) in (2, 3):
+        return all(x.family == "CSR" for x in f)
     return False
 
 
@@ -273,7 +276,15 @@ def bsr_spmm(A: USTensor, B, Cm, alpha=1.0, beta=0.0):
     return Cm
 
 
-_EXEC = {"SpMV": spmv, "SpMM": spmm, "SDDMM": sddmm, "BlockSpMM": bsr_spmm}
+def spgemm(A: USTensor, B: USTensor, C0=None, alpha=1.0, beta=0.0, transa="N", transb="N"):
+    """C = alpha*A*B for CSR A and B, a new CSR tensor (execute(SpGEMMOp,
+    u_A, u_B, u_C0), KA spgemm.jl:493-506): a plan's symbolic pass, then its
+    numeric pass."""
+    h = B200SpGEMMHandle(A, B, transa=transa, transb=transb, beta=beta)
+    return h.execute(A, B, alpha=alpha, beta=beta)
+
+
+_EXEC = {"SpMV": spmv, "SpMM": spmm, "SDDMM": sddmm, "BlockSpMM": bsr_spmm, "SpGEMM": spgemm}
 
 
 def backend_execute(backend, op: Op, *tensors, **kw):
@@ -385,12 +396,77 @@ class B200SpMVHandle(AbstractKernelHandle):
             pass
 
 
-def prepare(backend, op_type: OpType, A: USTensor, **kw) -> AbstractKernelHandle:
-    """prepare(backend, OpType, u_A) (src/ops.jl:187-202)."""
+class B200SpGEMMHandle(AbstractKernelHandle):
+    """Prepared SpGEMM (the reference's EmitterSpGEMMHandle, KA
+    spgemm.jl:298-438): the plan keeps C's structure and the sorted product
+    list; execute(h, u_A, u_B; alpha) recomputes C's values for new values of
+    the same structures without sorting or allocating on the device."""
+
+    def __init__(self, A: USTensor, B: USTensor, transa="N", transb="N", beta=0.0, **_):
+        if transa != "N" or transb != "N":
+            raise UnsupportedFormat("SpGEMM: transposed operands are not supported")
+        if beta != 0:
+            raise UnsupportedFormat("SpGEMM: beta != 0 is not supported")
+        if A.format.family != "CSR" or B.format.family != "CSR":
+            raise UnsupportedFormat("SpGEMM: only CSR x CSR is supported")
+        m, k, a_rp, a_ci, a_v = _csr_parts(A)
+        k2, n, b_rp, b_ci, b_v = _csr_parts(B)
+        if k != k2:
+            raise IncompatibleExtents(f"SpGEMM: A is {m}x{k}, B is {k2}x{n}")
+        if A.origin.offset != B.origin.offset:
+            from .errors import IndexOriginMismatch
+            raise IndexOriginMismatch("SpGEMM: A and B have different index origins")
+        self.dtype = _value_type(a_v, (torch.float32, torch.float64), "SpGEMM")
+        if b_v.dtype != a_v.dtype:
+            raise UnsupportedValueType("SpGEMM: A and B must share one value type")
+        self.device = _same_device(a_rp, a_ci, a_v, b_rp, b_ci, b_v)
+        self.m, self.k, self.n = m, k, n
+        self.origin = A.origin
+        self.vdtype = a_v.dtype
+        self.nnz_a, self.nnz_b = a_v.numel(), b_v.numel()
+        plan, nnz_c, prods = C.c_void_p(), C.c_int64(), C.c_int64()
+        _lib.call("jlb_spgemm_plan_create", C.byref(plan), _stream(self.device), self.dtype,
+                  A.origin.offset, m, k, n, self.nnz_a, _ptr(a_rp), _ptr(a_ci), self.nnz_b,
+                  _ptr(b_rp), _ptr(b_ci), C.byref(nnz_c), C.byref(prods))
+        self._plan = plan
+        self.nnz_c, self.products = nnz_c.value, prods.value
+        self.c_rowptr = torch.empty(m + 1, dtype=torch.int32, device=self.device)
+        self.c_colind = torch.empty(self.nnz_c, dtype=torch.int32, device=self.device)
+        _lib.call("jlb_spgemm_plan_structure", self._plan, _stream(self.device),
+                  _ptr(self.c_rowptr), _ptr(self.c_colind))
+
+    def execute(self, A: USTensor, B: USTensor, alpha=1.0, beta=0.0, out=None):
+        if beta != 0:
+            raise UnsupportedFormat("SpGEMM: beta != 0 is not supported")
+        a_v, b_v = nonzeros(A), nonzeros(B)
+        if a_v.numel() != self.nnz_a or b_v.numel() != self.nnz_b:
+            raise IncompatibleExtents("SpGEMM handle: A or B does not have the planned structure")
+        if a_v.dtype != self.vdtype or b_v.dtype != self.vdtype:
+            raise UnsupportedValueType("SpGEMM handle: value type differs from the plan's")
+        c_v = out if out is not None else torch.empty(self.nnz_c, dtype=self.vdtype,
+                                                      device=self.device)
+        _same_device(a_v, b_v, c_v)
+        _lib.call("jlb_spgemm_plan_execute", self._plan, _stream(self.device), _ptr(a_v),
+                  _ptr(b_v), _ptr(c_v), float(alpha))
+        return csr_tensor(self.c_rowptr, self.c_colind, c_v, (self.m, self.n), origin=self.origin)
+
+    def __del__(self):
+        try:
+            if getattr(self, "_plan", None) and self._plan.value:
+                _lib.load().jlb_spgemm_plan_destroy(self._plan)
+                self._plan = C.c_void_p()
+        except Exception:
+            pass
+
+
+def prepare(backend, op_type: OpType, A: USTensor, *more, **kw) -> AbstractKernelHandle:
+    """prepare(backend, OpType, u_A[, u_B]) (src/ops.jl:187-202)."""
     if not isinstance(backend, B200Backend):
         raise UnsupportedFormat(f"prepare: {backend!r} is not B200Backend")
     if op_type.tag == "SpMV":
         return B200SpMVHandle(A)
+    if op_type.tag == "SpGEMM":
+        return B200SpGEMMHandle(A, *more, **kw)
     raise UnsupportedFormat(f"prepare: {op_type!r} has no prepared form on B200Backend")
 
 

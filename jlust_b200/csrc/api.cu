@@ -81,9 +81,10 @@ extern "C" JLB_API int jlb_init(int device) {
 extern "C" JLB_API int jlb_device_status(void *stream) {
     JLB_CUDA(cudaStreamSynchronize(as_stream(stream)));
     int bits = 0;
-    const int parts[8] = {take_dev_error_spmv(), take_dev_error_spmm(), take_dev_error_sddmm(),
+    const int parts[9] = {take_dev_error_spmv(), take_dev_error_spmm(), take_dev_error_sddmm(),
                           take_dev_error_bsr(), take_dev_error_convert(), take_dev_error_halo(),
-                          take_dev_error_spmvfmt(), take_dev_error_bbm()};
+                          take_dev_error_spmvfmt(), take_dev_error_bbm(),
+                          take_dev_error_spgemm()};
     for (int v : parts) {
         if (v < 0) return fail(JLB_ERR_CUDA, "reading the device error word failed");
         bits |= v;

@@ -61,6 +61,7 @@ int take_dev_error_convert();
 int take_dev_error_halo();
 int take_dev_error_spmvfmt();
 int take_dev_error_bbm();
+int take_dev_error_spgemm();
 
 #define JLB_DEFINE_DEV_ERROR(unit)                                           \
     static __device__ int g_dev_error;                                       \
@@ -107,6 +108,14 @@ __device__ __forceinline__ T warp_sum(T v) {
 constexpr int kWarp = 32;
 
 __host__ __device__ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+namespace conv {
+// Exclusive scan of n int32 counts into out[0..n] (out[0] = base), with a
+// workspace of scan_ws(n) bytes (convert.cu).
+size_t scan_ws(int64_t n);
+int scan(cudaStream_t st, int64_t n, const int32_t *counts, int32_t *out, int base, void *ws,
+         size_t ws_bytes);
+}  // namespace conv
 
 // Sum over selector patches of row r in patch order, from zero: patch p
 // covers rows rows[2p] .. rows[2p+1] (inclusive) and adds

@@ -22,9 +22,16 @@
 
 #include <mutex>
 
+
 namespace jlb {
 
 JLB_DEFINE_DEV_ERROR(convert)
+
+}  // namespace jlb
+
+#include "sort.cuh"
+
+namespace jlb {
 
 namespace conv {
 
@@ -505,183 +512,23 @@ inline unsigned grid_rows(int64_t mb) { return (unsigned)(mb < 148 * 64 ? (mb > 
 // coordinate, the composer's path when the target's level order differs from
 // the source's (CSC targets, CSC -> CSR): the nonzero entries are bucketed by
 // outer coordinate (coo_bucket with one bucket per outer index), each bucket
-// is sorted by (inner coordinate, storage index) -- the order of the
-// composer's stable lexsort (src/convert.jl:334-345, 419-424) -- and the first
-// entry of every run of equal inner coordinates is kept, as the composer keeps
-// the first value of a run (src/convert.jl:222-238).  Sorting is an ascending
-// bitonic network over 64-bit keys column << 32 | storage index (unique, so
-// the network's instability does not matter), run on positions [0, len) of a
-// power-of-two network; positions past len act as +infinity and are never
-// touched.  Buckets ("rows") of up to kWarpKeys entries are sorted by one warp
-// in shared memory, up to kCtaKeys by one CTA in shared memory, longer ones by
-// one CTA in place in global memory (gathering the inner coordinate per
-// comparison).
-constexpr int kSortThreads = 256;
-constexpr int kWarpKeys = 256;
-constexpr int kLongThreads = 1024;
-constexpr int kCtaKeys = 16384;   // 128 KB of keys
-constexpr int64_t kMaxSortKeys = (int64_t)1 << 24;   // longest row the global-memory sort takes
-
-__device__ __forceinline__ uint64_t entry_key(const int32_t *__restrict__ cols, int base,
-                                              int32_t e) {
-    return ((uint64_t)(uint32_t)(ldg(cols + e) - base) << 32) | (uint32_t)e;
-}
-
-// One step pair of the network: the partner of i in step (k, j), or -1.
-template <typename I>
-__device__ __forceinline__ I bitonic_partner(I i, I k, I j, I len) {
-    const I l = j == (k >> 1) ? (i ^ (k - 1)) : (i ^ j);
-    return (l > i && l < len) ? l : I(-1);
-}
-
-struct WarpSync {
-    __device__ __forceinline__ void operator()() const { __syncwarp(); }
-};
-struct BlockSync {
-    __device__ __forceinline__ void operator()() const { __syncthreads(); }
-};
-
-// Ascending sort of s[0, len) by the threads tid, tid + nthr, ...; sync()
-// separates the steps and must be reached by all of them.
-template <typename Sync>
-__device__ void bitonic_smem(uint64_t *s, int len, int tid, int nthr, Sync sync) {
-    int P = 1;
-    while (P < len) P <<= 1;
-    for (int k = 2; k <= P; k <<= 1)
-        for (int j = k >> 1; j > 0; j >>= 1) {
-            for (int i = tid; i < P; i += nthr) {
-                const int l = bitonic_partner<int>(i, k, j, len);
-                if (l < 0) continue;
-                const uint64_t a = s[i], b = s[l];
-                if (a > b) {
-                    s[i] = b;
-                    s[l] = a;
-                }
-            }
-            sync();
-        }
-}
-
-__device__ __forceinline__ int warp_isum(int v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
-}
-
-// Sorts every bucket of up to kWarpKeys entries (one warp per row) and counts
-// its distinct columns into cnt[r]; longer rows are appended to `long_rows`.
-__global__ void __launch_bounds__(kSortThreads)
-sort_short_rows(int64_t m, const int32_t *__restrict__ offs, int32_t *__restrict__ ent,
-                const int32_t *__restrict__ cols, int base, int32_t *__restrict__ cnt,
-                int32_t *__restrict__ long_rows, int32_t *__restrict__ n_long, int64_t long_cap) {
-    __shared__ uint64_t s_keys[kSortThreads / kWarp][kWarpKeys];
-    const int lane = threadIdx.x % kWarp, warp = threadIdx.x / kWarp;
-    uint64_t *s = s_keys[warp];
-    const int64_t nwarps = (int64_t)gridDim.x * (kSortThreads / kWarp);
-    for (int64_t r = (int64_t)blockIdx.x * (kSortThreads / kWarp) + warp; r < m; r += nwarps) {
-        const int lo = ldg(offs + r), len = ldg(offs + r + 1) - lo;
-        if (len > kWarpKeys) {
-            if (lane == 0) {
-                const int q = atomicAdd(n_long, 1);
-                if (q < long_cap) long_rows[q] = (int32_t)r;
-                else dev_error(DEV_ERR_OVERFLOW);
-            }
-            continue;
-        }
-        for (int i = lane; i < len; i += kWarp) s[i] = entry_key(cols, base, ent[lo + i]);
-        __syncwarp();
-        bitonic_smem(s, len, lane, kWarp, WarpSync{});
-        int u = 0;
-        for (int i = lane; i < len; i += kWarp) {
-            ent[lo + i] = (int32_t)(uint32_t)s[i];
-            u += (i == 0 || (s[i] >> 32) != (s[i - 1] >> 32));
-        }
-        u = warp_isum(u);
-        if (lane == 0) cnt[r] = u;
-        __syncwarp();
-    }
-}
-
-__device__ __forceinline__ int block_isum(int v, int *s_red) {
-    const int lane = threadIdx.x % kWarp, warp = threadIdx.x / kWarp;
-    v = warp_isum(v);
-    if (lane == 0) s_red[warp] = v;
-    __syncthreads();
-    int t = 0;
-    for (int w = 0; w < (int)(blockDim.x / kWarp); ++w) t += s_red[w];
-    __syncthreads();
-    return t;
-}
-
-// Sorts the buckets listed in long_rows, one CTA per row.
-__global__ void __launch_bounds__(kLongThreads)
-sort_long_rows(const int32_t *__restrict__ offs, int32_t *ent, const int32_t *__restrict__ cols,
-               int base, int32_t *__restrict__ cnt, const int32_t *__restrict__ long_rows,
-               const int32_t *__restrict__ n_long, int64_t long_cap) {
-    extern __shared__ uint64_t s_dyn[];
-    __shared__ int s_red[kLongThreads / kWarp];
-    const int tid = threadIdx.x;
-    int nl = *n_long;
-    if (nl > long_cap) nl = (int)long_cap;
-    for (int b = blockIdx.x; b < nl; b += gridDim.x) {
-        const int32_t r = long_rows[b];
-        const int lo = ldg(offs + r), len = ldg(offs + r + 1) - lo;
-        int u = 0;
-        if (len > kMaxSortKeys) {
-            if (tid == 0) {
-                dev_error(DEV_ERR_OVERFLOW);
-                cnt[r] = 0;
-            }
-            continue;
-        }
-        if (len <= kCtaKeys) {
-            for (int i = tid; i < len; i += kLongThreads) s_dyn[i] = entry_key(cols, base, ent[lo + i]);
-            __syncthreads();
-            bitonic_smem(s_dyn, len, tid, kLongThreads, BlockSync{});
-            for (int i = tid; i < len; i += kLongThreads) {
-                ent[lo + i] = (int32_t)(uint32_t)s_dyn[i];
-                u += (i == 0 || (s_dyn[i] >> 32) != (s_dyn[i - 1] >> 32));
-            }
-        } else {
-            // In place in global memory: the same network on entry indices,
-            // each comparison gathering both columns.
-            int32_t *e = ent + lo;
-            const int64_t n64 = len;
-            int64_t P = 1;
-            while (P < n64) P <<= 1;
-            for (int64_t k = 2; k <= P; k <<= 1)
-                for (int64_t j = k >> 1; j > 0; j >>= 1) {
-                    for (int64_t i = tid; i < P; i += kLongThreads) {
-                        const int64_t l = bitonic_partner<int64_t>(i, k, j, n64);
-                        if (l < 0) continue;
-                        const int32_t ea = e[i], eb = e[l];
-                        if (entry_key(cols, base, ea) > entry_key(cols, base, eb)) {
-                            e[i] = eb;
-                            e[l] = ea;
-                        }
-                    }
-                    __syncthreads();
-                }
-            for (int i = tid; i < len; i += kLongThreads)
-                u += (i == 0 || ldg(cols + e[i]) != ldg(cols + e[i - 1]));
-        }
-        u = block_isum(u, s_red);
-        if (tid == 0) cnt[r] = u;
-        __syncthreads();
-    }
-}
+// is sorted by (inner coordinate, storage index) with the sorts of sort.cuh --
+// the order of the composer's stable lexsort (src/convert.jl:334-345,
+// 419-424) -- and the first entry of every run of equal inner coordinates is
+// kept, as the composer keeps the first value of a run (src/convert.jl:
+// 222-238).
 
 // Writes the first entry of every run of equal columns of each sorted bucket
 // to the CSR (one warp per row): its column (origin kept) and value.
 template <int ES>
-__global__ void __launch_bounds__(kSortThreads)
+__global__ void __launch_bounds__(seg::kSortThreads)
 emit_csr_rows(int64_t m, const int32_t *__restrict__ offs, const int32_t *__restrict__ ent,
               const int32_t *__restrict__ cols, const void *__restrict__ val, int base,
               const int32_t *__restrict__ rowptr, int64_t nnz_out, int32_t *__restrict__ colind,
               void *__restrict__ out_val) {
     const int lane = threadIdx.x % kWarp, warp = threadIdx.x / kWarp;
-    const int64_t nwarps = (int64_t)gridDim.x * (kSortThreads / kWarp);
-    for (int64_t r = (int64_t)blockIdx.x * (kSortThreads / kWarp) + warp; r < m; r += nwarps) {
+    const int64_t nwarps = (int64_t)gridDim.x * (seg::kSortThreads / kWarp);
+    for (int64_t r = (int64_t)blockIdx.x * (seg::kSortThreads / kWarp) + warp; r < m; r += nwarps) {
         const int lo = ldg(offs + r), hi = ldg(offs + r + 1);
         const int64_t out = (int64_t)ldg(rowptr + r) - base, end = (int64_t)ldg(rowptr + r + 1) - base;
         int64_t run = 0;
@@ -1185,7 +1032,7 @@ SortedWs sorted_ws(void *ws, int64_t n_outer, int64_t nnz) {
     k.off = coo_ws(n_outer, nnz, 1, 1, 0, nullptr);
     w.stamp = k.take<uint64_t>(1);
     w.n_long = k.take<int32_t>(1);
-    w.long_cap = nnz / (conv::kWarpKeys + 1) + 1;
+    w.long_cap = nnz / (seg::kWarpKeys + 1) + 1;
     w.long_rows = k.take<int32_t>((size_t)w.long_cap);
     w.bytes = k.off + 256;
     return w;
@@ -1223,14 +1070,14 @@ extern "C" JLB_API int jlb_sorted_compress_count(void *stream, int dtype, int id
     if (r) return r;
     JLB_CUDA(cudaMemsetAsync(w.n_long, 0, sizeof(int32_t), st));
     if (n_outer > 0) {
-        const int64_t g = ceil_div(n_outer, conv::kSortThreads / kWarp);
-        conv::sort_short_rows<<<(unsigned)(g < 148 * 16 ? g : 148 * 16), conv::kSortThreads, 0, st>>>(
+        const int64_t g = ceil_div(n_outer, seg::kSortThreads / kWarp);
+        seg::sort_short_rows<<<(unsigned)(g < 148 * 16 ? g : 148 * 16), seg::kSortThreads, 0, st>>>(
             n_outer, boffs, bent, inner, idx_base, ptr + 1, w.long_rows, w.n_long, w.long_cap);
         JLB_LAUNCH_CHECK("sort_short_rows");
-        const int smem = conv::kCtaKeys * (int)sizeof(uint64_t);
-        JLB_CUDA(cudaFuncSetAttribute(conv::sort_long_rows,
+        const int smem = seg::kCtaKeys * (int)sizeof(uint64_t);
+        JLB_CUDA(cudaFuncSetAttribute(seg::sort_long_rows,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-        conv::sort_long_rows<<<148, conv::kLongThreads, smem, st>>>(
+        seg::sort_long_rows<<<148, seg::kLongThreads, smem, st>>>(
             boffs, bent, inner, idx_base, ptr + 1, w.long_rows, w.n_long, w.long_cap);
         JLB_LAUNCH_CHECK("sort_long_rows");
     }
@@ -1275,17 +1122,17 @@ extern "C" JLB_API int jlb_sorted_compress_fill(void *stream, int dtype, int idx
     const int32_t *boffs = k.take<int32_t>((size_t)n_outer + 1);
     k.take<int32_t>((size_t)n_outer);
     const int32_t *bent = k.take<int32_t>((size_t)(nnz > 0 ? nnz : 1));
-    const int64_t g64 = ceil_div(n_outer, conv::kSortThreads / kWarp);
+    const int64_t g64 = ceil_div(n_outer, seg::kSortThreads / kWarp);
     const unsigned g = (unsigned)(g64 < 148 * 16 ? g64 : 148 * 16);
     const size_t es = dtype_size(dtype);
     if (es == 8)
-        conv::emit_csr_rows<8><<<g, conv::kSortThreads, 0, st>>>(n_outer, boffs, bent, inner, val,
+        conv::emit_csr_rows<8><<<g, seg::kSortThreads, 0, st>>>(n_outer, boffs, bent, inner, val,
                                                                  idx_base, ptr, nnz_out, inner_out, val_out);
     else if (es == 4)
-        conv::emit_csr_rows<4><<<g, conv::kSortThreads, 0, st>>>(n_outer, boffs, bent, inner, val,
+        conv::emit_csr_rows<4><<<g, seg::kSortThreads, 0, st>>>(n_outer, boffs, bent, inner, val,
                                                                  idx_base, ptr, nnz_out, inner_out, val_out);
     else
-        conv::emit_csr_rows<2><<<g, conv::kSortThreads, 0, st>>>(n_outer, boffs, bent, inner, val,
+        conv::emit_csr_rows<2><<<g, seg::kSortThreads, 0, st>>>(n_outer, boffs, bent, inner, val,
                                                                  idx_base, ptr, nnz_out, inner_out, val_out);
     JLB_LAUNCH_CHECK("emit_csr_rows");
     return ok();
@@ -1308,9 +1155,12 @@ extern "C" JLB_API int jlb_positions_to_coordinates(void *stream, int idx_base, 
 }
 
 // ------------------------------------------------------------- COO -> CSR
-// Workspace: [keep flags (nnz) | slots (nnz + 1) | scan scratch].
+// Workspace: [stamp | keep flags (nnz) | slots (nnz + 1) | scan scratch].  The
+// count phase stamps the flags and slots it leaves; a fill phase given the
+// same workspace for the same inputs uses them instead of recomputing.
 namespace {
 struct CooCsrWs {
+    uint64_t *stamp;
     int32_t *keep, *slot;
     char *scan;
     size_t scan_bytes, bytes;
@@ -1319,6 +1169,7 @@ struct CooCsrWs {
 CooCsrWs coo_csr_ws(void *ws, int64_t nnz) {
     CooCsrWs w{};
     Carve k{reinterpret_cast<char *>(ws)};
+    w.stamp = k.take<uint64_t>(1);
     w.keep = k.take<int32_t>((size_t)(nnz > 0 ? nnz : 1));
     w.slot = k.take<int32_t>((size_t)nnz + 1);
     w.scan_bytes = conv::scan_ws(nnz > 0 ? nnz : 1);
@@ -1374,6 +1225,9 @@ extern "C" JLB_API int jlb_coo_to_csr_count(void *stream, int dtype, int idx_bas
                       rows, val, idx_base, m, w.keep, w.slot, rowptr);
         JLB_LAUNCH_CHECK("coo_rowptr");
     }
+    // b1 = b2 = -2 marks a COO -> CSR workspace
+    const uint64_t key = carry_key(m, n, nnz, -2, -2, idx_base, dtype, rows, cols, val);
+    JLB_CUDA(cudaMemcpyAsync(w.stamp, &key, sizeof(key), cudaMemcpyHostToDevice, st));
     int32_t total = 0;
     JLB_CUDA(cudaMemcpyAsync(&total, w.slot + nnz, sizeof(int32_t), cudaMemcpyDeviceToHost, st));
     JLB_CUDA(cudaStreamSynchronize(st));
@@ -1402,8 +1256,13 @@ extern "C" JLB_API int jlb_coo_to_csr_fill(void *stream, int dtype, int idx_base
     if (!workspace || workspace_bytes < w.bytes) return fail(JLB_ERR_WORKSPACE, "workspace too small");
     if (nnz == 0) return ok();
     cudaStream_t st = as_stream(stream);
-    r = coo_csr_slots(st, dtype, idx_base, m, n, nnz, rows, cols, val, w);
-    if (r) return r;
+    uint64_t stamp = 0;
+    JLB_CUDA(cudaMemcpyAsync(&stamp, w.stamp, sizeof(stamp), cudaMemcpyDeviceToHost, st));
+    JLB_CUDA(cudaStreamSynchronize(st));
+    if (stamp != carry_key(m, n, nnz, -2, -2, idx_base, dtype, rows, cols, val)) {
+        r = coo_csr_slots(st, dtype, idx_base, m, n, nnz, rows, cols, val, w);
+        if (r) return r;
+    }
     JLB_ES_LAUNCH(coo_emit, dtype_size(dtype), conv::grid_for(nnz), conv::kThreads, st, nnz, cols,
                   val, w.keep, w.slot, nnz_out, colind, csr_val);
     JLB_LAUNCH_CHECK("coo_emit");

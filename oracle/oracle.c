@@ -202,6 +202,69 @@ OR_EXPORT void NAME(int64_t Tp, int64_t n_diag, int64_t n_off, int64_t n_cols,  
 DEFINE_BBM_PERIODIC(or_bbm_periodic_spmv_f64, double)
 DEFINE_BBM_PERIODIC(or_bbm_periodic_spmv_f32, float)
 
+/* SpGEMM C = alpha*A*B (A m x k, B k x n CSR, one origin): JLUST's
+ * scatter-sort-reduce order (ext/KernelAbstractionsExt/ops/spgemm.jl:40-80,
+ * 330-400).  Row i's products A[i,j]*B[j,c] in the order of its A entries,
+ * then of B row j's entries, each times alpha unless alpha == 1; sorted by
+ * (column, product order) -- the reference's stable sort of (row, column)
+ * keys; every run of equal columns is one entry of C, its products summed
+ * from zero left to right (the reference adds them by atomics, in an order
+ * this fixes).  With crp == NULL only nnz(C) is returned. */
+typedef struct { int32_t col; int64_t ord; } or_prod_key;
+static int or_prod_cmp(const void *a, const void *b) {
+    const or_prod_key *x = (const or_prod_key *)a, *y = (const or_prod_key *)b;
+    if (x->col != y->col) return x->col < y->col ? -1 : 1;
+    return x->ord < y->ord ? -1 : (x->ord > y->ord);
+}
+
+#define DEFINE_SPGEMM(NAME, T)                                                  \
+OR_EXPORT int64_t NAME(int64_t m, const int32_t *arp, const int32_t *aci,       \
+                       const T *av, const int32_t *brp, const int32_t *bci,     \
+                       const T *bv, double alpha_d, int base, int32_t *crp,     \
+                       int32_t *cci, T *cv) {                                   \
+    const T alpha = (T)alpha_d;                                                 \
+    int64_t maxp = 0;                                                           \
+    for (int64_t i = 0; i < m; ++i) {                                           \
+        int64_t c = 0;                                                          \
+        for (int64_t p = arp[i] - base; p < arp[i + 1] - base; ++p) {           \
+            const int64_t j = aci[p] - base;                                    \
+            c += brp[j + 1] - brp[j];                                           \
+        }                                                                       \
+        if (c > maxp) maxp = c;                                                 \
+    }                                                                           \
+    or_prod_key *key = (or_prod_key *)malloc(sizeof(or_prod_key) * (maxp ? maxp : 1)); \
+    T *pv = (T *)malloc(sizeof(T) * (maxp ? maxp : 1));                         \
+    int64_t nnz = 0;                                                            \
+    if (crp) crp[0] = base;                                                     \
+    for (int64_t i = 0; i < m; ++i) {                                           \
+        int64_t np = 0;                                                         \
+        for (int64_t p = arp[i] - base; p < arp[i + 1] - base; ++p) {           \
+            const int64_t j = aci[p] - base;                                    \
+            for (int64_t q = brp[j] - base; q < brp[j + 1] - base; ++q) {       \
+                T t = av[p] * bv[q];                                            \
+                if (alpha != (T)1) t = t * alpha;                               \
+                key[np].col = bci[q] - base; key[np].ord = np; pv[np] = t; ++np; \
+            }                                                                   \
+        }                                                                       \
+        qsort(key, (size_t)np, sizeof(or_prod_key), or_prod_cmp);               \
+        for (int64_t s = 0; s < np;) {                                          \
+            int64_t e = s;                                                      \
+            T acc = (T)0;                                                       \
+            while (e < np && key[e].col == key[s].col) { acc = acc + pv[key[e].ord]; ++e; } \
+            if (crp) { cci[nnz] = key[s].col + base; cv[nnz] = acc; }           \
+            ++nnz;                                                              \
+            s = e;                                                              \
+        }                                                                       \
+        if (crp) crp[i + 1] = (int32_t)(nnz + base);                            \
+    }                                                                           \
+    free(key);                                                                  \
+    free(pv);                                                                   \
+    return nnz;                                                                 \
+}
+
+DEFINE_SPGEMM(or_spgemm_f64, double)
+DEFINE_SPGEMM(or_spgemm_f32, float)
+
 /* fp64 reference of the same product plus the per-row magnitude bound
  * sum_k |v_k * x_k|, used for tolerance checks of any value type. */
 OR_EXPORT void or_csr_spmv_ref64(int dtype, int64_t m, const int32_t *rowptr,

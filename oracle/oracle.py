@@ -61,6 +61,9 @@ def _declare(L):
     for n in ("or_bbm_periodic_spmv_f64", "or_bbm_periodic_spmv_f32"):
         getattr(L, n).argtypes = ([_i64, _i64, _i64, _i64, _p, _p, _p, _i64, _p, _p, _p]
                                   + [_p, _p, _p, _i64, _d] * 2 + [_p, _p, _d, _d, _i])
+    for n in ("or_spgemm_f64", "or_spgemm_f32"):
+        getattr(L, n).argtypes = [_i64, _p, _p, _p, _p, _p, _p, _d, _i, _p, _p, _p]
+        getattr(L, n).restype = _i64
     for n in ("or_csr_spmm_f32", "or_csr_spmm_f64"):
         getattr(L, n).argtypes = [_i64, _i64, _p, _p, _p, _p, _i64, _i, _p, _i64, _i, _d, _d, _i]
     L.or_csr_spmm_ref64_f32.argtypes = [_i64, _i64, _p, _p, _p, _p, _i64, _i, _p, _i64, _i,
@@ -340,6 +343,25 @@ def coo_to_bsr(m, n, rows, cols, val, b1, b2, base=0):
     lib().or_coo_to_bsr(m, n, nnz, b1, b2, _ptr(rows), _ptr(cols), _ptr(val), dt, base,
                         _ptr(bp), _ptr(bc), _ptr(bv))
     return bp, bc, bv
+
+
+def spgemm(m, n, a_rp, a_ci, a_v, b_rp, b_ci, b_v, alpha=1.0, base=0):
+    """C = alpha*A*B as CSR (rowptr, colind, val) with the input's origin, in
+    the order of JLUST's scatter-sort-reduce SpGEMM (ext/KernelAbstractionsExt/
+    ops/spgemm.jl:40-80, 330-400): row i's products in A-entry then B-entry
+    order, scaled by alpha unless it is 1, sorted stably by column, each run
+    summed from zero left to right in the value type."""
+    a_rp, a_ci, b_rp, b_ci = (_c(x, np.int32) for x in (a_rp, a_ci, b_rp, b_ci))
+    a_v = _c(a_v)
+    b_v = _c(b_v, a_v.dtype)
+    fn = {np.dtype(np.float64): lib().or_spgemm_f64, np.dtype(np.float32): lib().or_spgemm_f32}[a_v.dtype]
+    args = [m, _ptr(a_rp), _ptr(a_ci), _ptr(a_v), _ptr(b_rp), _ptr(b_ci), _ptr(b_v), alpha, base]
+    nnz = fn(*args, None, None, None)
+    rp = np.empty(m + 1, np.int32)
+    ci = np.empty(max(nnz, 1), np.int32)
+    v = np.empty(max(nnz, 1), a_v.dtype)
+    fn(*args, _ptr(rp), _ptr(ci), _ptr(v))
+    return rp, ci[:nnz], v[:nnz]
 
 
 def compose_compressed(n_outer, n_inner, outer, inner, val, base=0, sort=True):

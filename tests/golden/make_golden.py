@@ -45,6 +45,9 @@ KATS = {
         "C": {"m": 3, "n": 3, "rowptr": [1, 3, 4, 6], "colind": [1, 3, 2, 1, 3],
               "val": [1.0, 1.0, 1.0, 1.0, 1.0], "base": 1},
         "alpha": 1.0, "beta": 0.0, "out": [1.0, 1.0, 1.0, 1.0, 2.0]},
+    "spgemm_csr": {
+        "source": "test/test_cuda.jl:436-451 (C = A*A, Float32)",
+        "A": A_ONE, "C_dense": [[9.0, 0.0, 12.0], [0.0, 9.0, 0.0], [24.0, 0.0, 33.0]]},
     "convert_fixture_3x4": {
         "source": "test/test_convert.jl:3-9 (fixture), :44-58 (CSR->CSC buffers)",
         "A": {"m": 3, "n": 4, "rowptr": [0, 2, 3, 5], "colind": [0, 2, 1, 0, 2],

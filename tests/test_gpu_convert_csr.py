@@ -176,3 +176,41 @@ def test_sorted_fill_needs_count_workspace():
         _lib.call("jlb_sorted_compress_fill", _stream(torch.device(DEV)), _DTYPE[torch.float64],
                   0, 2, 2, 2, p(cols),
                   p(rows), p(val), p(ptr), 2, p(out_i), p(out_v), p(ws), wsb)
+
+
+@pytest.mark.parametrize("same_ws", [True, False])
+def test_coo_to_csr_fill_workspace(same_ws):
+    """Fill reuses the flags count stamped into its workspace; a fresh
+    workspace makes it recompute them, with the same result."""
+    import ctypes as C
+
+    from jlust_b200 import _lib
+    from jlust_b200.backend import _DTYPE, _stream
+    rng = np.random.default_rng(205)
+    m, n = 4000, 3000
+    rows = np.sort(rng.integers(0, m, 60000))
+    cols = rng.integers(0, 40, rows.shape[0])
+    val = _vals(rng, rows.shape[0], np.float64, 0.1)
+    r_d, c_d, v_d = to_dev(rows.astype(np.int32)), to_dev(cols.astype(np.int32)), to_dev(val)
+    L = _lib.load()
+    wsb = L.jlb_coo_to_csr_workspace_size(m, n, rows.shape[0])
+    ws = torch.empty(wsb, dtype=torch.uint8, device=DEV)
+    rowptr = torch.empty(m + 1, dtype=torch.int32, device=DEV)
+    st = _stream(torch.device(DEV))
+
+    def p(t):
+        return C.c_void_p(t.data_ptr())
+    nout = C.c_int64()
+    dt = _DTYPE[torch.float64]
+    _lib.call("jlb_coo_to_csr_count", st, dt, 0, m, n, rows.shape[0], p(r_d), p(c_d), p(v_d),
+              p(rowptr), C.byref(nout), p(ws), wsb)
+    ws2 = ws if same_ws else torch.zeros(wsb, dtype=torch.uint8, device=DEV)
+    ci = torch.empty(nout.value, dtype=torch.int32, device=DEV)
+    vo = torch.empty(nout.value, dtype=torch.float64, device=DEV)
+    _lib.call("jlb_coo_to_csr_fill", st, dt, 0, m, n, rows.shape[0], p(r_d), p(c_d), p(v_d),
+              nout.value, p(ci), p(vo), p(ws2), wsb)
+    J.device_status()
+    ref = O.coo_to_csr(m, n, rows, cols, val, 0)
+    assert np.array_equal(rowptr.cpu().numpy(), ref[0])
+    assert np.array_equal(ci.cpu().numpy(), ref[1])
+    assert np.array_equal(vo.cpu().numpy(), ref[2])

@@ -52,7 +52,9 @@ def test_supports_backend_table():
     assert not J.supports_backend(be, J.SDDMMOp(F.CSR, d2, F.CSR))
     assert J.supports_backend(be, J.BlockSpMMOp(F.BSRRight((64, 64)), d2, d2))
     assert not J.supports_backend(be, J.SpSVOp(F.CSR, d1, d1))
-    assert not J.supports_backend(be, J.SpGEMMOp(F.CSR, F.CSR, F.CSR))
+    assert J.supports_backend(be, J.SpGEMMOp(F.CSR, F.CSR, F.CSR))
+    assert not J.supports_backend(be, J.SpGEMMOp(F.CSC, F.CSC, F.CSC))
+    assert not J.supports_backend(be, J.SpGEMMOp(F.CSR, F.CSC, F.CSR))
 
 
 def test_constructors_validate_shapes():

@@ -199,3 +199,16 @@ def test_coo_to_csr_composer_semantics():
     cp, ri, cv = O.coo_to_csc(3, 4, rows, cols, val)
     assert cp.tolist() == [0, 1, 2, 2, 3]
     assert ri.tolist() == [2, 0, 0] and cv.tolist() == [7.0, 2.0, 1.0]
+
+
+def test_spgemm_kat(golden):
+    """C = A*A for the reference's 3x3 matrix (test_cuda.jl:436-451)."""
+    g = golden["spgemm_csr"]
+    rp, ci, v, base = _csr(g["A"], np.float32)
+    crp, cci, cv = O.spgemm(3, 3, rp, ci, v, rp, ci, v, base=base)
+    D = np.zeros((3, 3), np.float32)
+    for r in range(3):
+        for p in range(crp[r] - base, crp[r + 1] - base):
+            D[r, cci[p] - base] = cv[p]
+    assert D.tolist() == g["C_dense"]
+    assert crp.tolist() == [1, 3, 4, 6]
