@@ -372,6 +372,22 @@ JLB_API int jlb_coo_to_csr_fill(void *stream, int dtype, int idx_base, int64_t m
                                 const void *val, int64_t nnz_out, int32_t *colind, void *csr_val,
                                 void *workspace, size_t workspace_bytes);
 
+/* COO -> COO and, after jlb_positions_to_coordinates, CSR -> COO: a COO
+ * target's levels are not unique and an ordered source is not sorted
+ * (src/convert.jl:346-355), so only the explicit zeros go; the other entries
+ * keep their storage order.  Count returns the number kept (synchronises
+ * `stream`); fill writes rows_out, cols_out and val_out (nnz_out each). */
+JLB_API size_t jlb_coo_drop_zeros_workspace_size(int64_t nnz);
+JLB_API int jlb_coo_drop_zeros_count(void *stream, int dtype, int idx_base, int64_t m, int64_t n,
+                                     int64_t nnz, const int32_t *rows, const int32_t *cols,
+                                     const void *val, int64_t *nnz_out, void *workspace,
+                                     size_t workspace_bytes);
+JLB_API int jlb_coo_drop_zeros_fill(void *stream, int dtype, int idx_base, int64_t m, int64_t n,
+                                    int64_t nnz, const int32_t *rows, const int32_t *cols,
+                                    const void *val, int64_t nnz_out, int32_t *rows_out,
+                                    int32_t *cols_out, void *val_out, void *workspace,
+                                    size_t workspace_bytes);
+
 /* Sorted compression: nnz (outer, inner) coordinate pairs compressed along the
  * outer coordinate with the entries lexsorted by (outer, inner, storage
  * index), explicit zeros dropped and the first of each run of equal

@@ -67,6 +67,10 @@ SIGNATURES = {
     "jlb_spgemm_plan_structure": (_i, [_p, _p, _p, _p]),
     "jlb_spgemm_plan_execute": (_i, [_p, _p, _p, _p, _p, _d]),
     "jlb_spgemm_plan_destroy": (_i, [_p]),
+    "jlb_coo_drop_zeros_workspace_size": (_sz, [_i64]),
+    "jlb_coo_drop_zeros_count": (_i, [_p, _i, _i, _i64, _i64, _i64, _p, _p, _p, _pi64, _p, _sz]),
+    "jlb_coo_drop_zeros_fill": (_i, [_p, _i, _i, _i64, _i64, _i64, _p, _p, _p, _i64, _p, _p, _p,
+                                     _p, _sz]),
     "jlb_coo_to_csr_workspace_size": (_sz, [_i64, _i64, _i64]),
     "jlb_coo_to_csr_count": (_i, [_p, _i, _i, _i64, _i64, _i64, _p, _p, _p, _p, _pi64, _p, _sz]),
     "jlb_coo_to_csr_fill": (_i, [_p, _i, _i, _i64, _i64, _i64, _p, _p, _p, _i64, _p, _p, _p,

@@ -17,7 +17,8 @@ from .backend import _DTYPE, _ptr, _same_device, _stream
 from .errors import UnsupportedFormat, UnsupportedValueType
 from .formats import TensorFormat
 from .formats import Formats
-from .tensor import USTensor, bsr_tensor, coordinates, csr_tensor, nonzeros, positions
+from .tensor import (USTensor, bsr_tensor, coo_tensor, coordinates, csr_tensor, nonzeros,
+                     positions)
 
 
 def exclusive_scan(counts: torch.Tensor, base: int = 0) -> torch.Tensor:
@@ -88,6 +89,8 @@ def convert_format(u: USTensor, fmt: TensorFormat) -> USTensor:
         return _to_csr(u)
     if fmt == Formats.CSC and u.format.family in ("COO", "CSR", "CSC"):
         return _to_csc(u)
+    if fmt == Formats.COO and u.format.family in ("COO", "CSR"):
+        return _to_coo(u)
     if fmt == u.format:
         return u
     raise UnsupportedFormat(f"convert_format: {u.format.name} -> {fmt.name} is not on B200Backend")
@@ -179,3 +182,24 @@ def _to_csc(u: USTensor) -> USTensor:
     rows, cols, val, dev = _entries(u)
     colptr, rowind, out = _sorted_compress(n, m, cols, rows, val, u.origin.offset, dev)
     return USTensor((m, n), Formats.CSC, (None, colptr), (None, rowind), out, u.origin)
+
+
+def _to_coo(u: USTensor) -> USTensor:
+    """COO from an ordered source (COO, CSR): the explicit zeros dropped, the
+    other entries in storage order."""
+    m, n = u.extents
+    rows, cols, val, dev = _entries(u)
+    dt = _DTYPE[val.dtype]
+    st = _stream(dev)
+    nnz, base = val.numel(), u.origin.offset
+    ws_bytes = _lib.load().jlb_coo_drop_zeros_workspace_size(nnz)
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
+    nout = C.c_int64()
+    _lib.call("jlb_coo_drop_zeros_count", st, dt, base, m, n, nnz, _ptr(rows), _ptr(cols),
+              _ptr(val), C.byref(nout), _ptr(ws), ws_bytes)
+    r = torch.empty(nout.value, dtype=torch.int32, device=dev)
+    c = torch.empty(nout.value, dtype=torch.int32, device=dev)
+    v = torch.empty(nout.value, dtype=val.dtype, device=dev)
+    _lib.call("jlb_coo_drop_zeros_fill", st, dt, base, m, n, nnz, _ptr(rows), _ptr(cols),
+              _ptr(val), nout.value, _ptr(r), _ptr(c), _ptr(v), _ptr(ws), ws_bytes)
+    return coo_tensor(r, c, v, (m, n), origin=u.origin)

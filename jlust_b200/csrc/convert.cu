@@ -581,7 +581,8 @@ __device__ __forceinline__ int64_t prev_nonzero(const void *__restrict__ val, in
 template <int ES>
 __global__ void __launch_bounds__(kThreads)
 coo_keep(int64_t nnz, const int32_t *__restrict__ rows, const int32_t *__restrict__ cols,
-         const void *__restrict__ val, int base, int64_t m, int64_t n, int32_t *__restrict__ keep) {
+         const void *__restrict__ val, int base, int64_t m, int64_t n, bool merge,
+         int32_t *__restrict__ keep) {
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < nnz; p += stride) {
         int k = 0;
@@ -591,7 +592,7 @@ coo_keep(int64_t nnz, const int32_t *__restrict__ rows, const int32_t *__restric
                 (int64_t)c - base >= n) {
                 dev_error(DEV_ERR_BOUNDS);
             } else {
-                const int64_t q = prev_nonzero<ES>(val, p);
+                const int64_t q = merge ? prev_nonzero<ES>(val, p) : -1;
                 k = 1;
                 if (q >= 0) {
                     const int32_t rq = ldg(rows + q);
@@ -632,8 +633,9 @@ coo_rowptr(int64_t nnz, const int32_t *__restrict__ rows, const void *__restrict
 
 template <int ES>
 __global__ void __launch_bounds__(kThreads)
-coo_emit(int64_t nnz, const int32_t *__restrict__ cols, const void *__restrict__ val,
-         const int32_t *__restrict__ keep, const int32_t *__restrict__ slot, int64_t nnz_out,
+coo_emit(int64_t nnz, const int32_t *__restrict__ rows, const int32_t *__restrict__ cols,
+         const void *__restrict__ val, const int32_t *__restrict__ keep,
+         const int32_t *__restrict__ slot, int64_t nnz_out, int32_t *__restrict__ rows_out,
          int32_t *__restrict__ colind, void *__restrict__ out_val) {
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < nnz; p += stride) {
@@ -643,6 +645,7 @@ coo_emit(int64_t nnz, const int32_t *__restrict__ cols, const void *__restrict__
             dev_error(DEV_ERR_OVERFLOW);
             continue;
         }
+        if (rows_out) rows_out[q] = ldg(rows + p);
         colind[q] = ldg(cols + p);
         copy_val<ES>(out_val, q, val, p);
     }
@@ -1185,12 +1188,15 @@ CooCsrWs coo_csr_ws(void *ws, int64_t nnz) {
         else conv::kernel<2><<<(grid), (threads), 0, (st)>>>(__VA_ARGS__);                \
     } while (0)
 
-// keep flags and their exclusive scan (slot[nnz] = entries kept).
+// keep flags and their exclusive scan (slot[nnz] = entries kept); merge:
+// adjacent equal coordinates keep their first value (CSR targets), else only
+// zeros go (COO targets).
 int coo_csr_slots(cudaStream_t st, int dtype, int idx_base, int64_t m, int64_t n, int64_t nnz,
-                  const int32_t *rows, const int32_t *cols, const void *val, const CooCsrWs &w) {
+                  const int32_t *rows, const int32_t *cols, const void *val, const CooCsrWs &w,
+                  bool merge = true) {
     if (nnz > 0) {
         JLB_ES_LAUNCH(coo_keep, dtype_size(dtype), conv::grid_for(nnz), conv::kThreads, st, nnz,
-                      rows, cols, val, idx_base, m, n, w.keep);
+                      rows, cols, val, idx_base, m, n, merge, w.keep);
         JLB_LAUNCH_CHECK("coo_keep");
     }
     return conv::scan(st, nnz, w.keep, w.slot, 0, w.scan, w.scan_bytes);
@@ -1263,8 +1269,67 @@ extern "C" JLB_API int jlb_coo_to_csr_fill(void *stream, int dtype, int idx_base
         r = coo_csr_slots(st, dtype, idx_base, m, n, nnz, rows, cols, val, w);
         if (r) return r;
     }
-    JLB_ES_LAUNCH(coo_emit, dtype_size(dtype), conv::grid_for(nnz), conv::kThreads, st, nnz, cols,
-                  val, w.keep, w.slot, nnz_out, colind, csr_val);
+    JLB_ES_LAUNCH(coo_emit, dtype_size(dtype), conv::grid_for(nnz), conv::kThreads, st, nnz, rows,
+                  cols, val, w.keep, w.slot, nnz_out, nullptr, colind, csr_val);
+    JLB_LAUNCH_CHECK("coo_emit");
+    return ok();
+}
+
+// ------------------------------------------------------------- COO -> COO
+// A COO target's levels are not unique and the source is not sorted
+// (src/convert.jl:346-355), so the composer only loses the explicit zeros:
+// a stable compaction without merging (CSR -> COO after the rows are
+// expanded, COO -> COO).  Workspace as for COO -> CSR; fill recomputes.
+extern "C" JLB_API size_t jlb_coo_drop_zeros_workspace_size(int64_t nnz) {
+    if (nnz < 0) return 0;
+    return coo_csr_ws(nullptr, nnz).bytes;
+}
+
+extern "C" JLB_API int jlb_coo_drop_zeros_count(void *stream, int dtype, int idx_base, int64_t m,
+                                                int64_t n, int64_t nnz, const int32_t *rows,
+                                                const int32_t *cols, const void *val,
+                                                int64_t *nnz_out, void *workspace,
+                                                size_t workspace_bytes) {
+    int r = conv_args(dtype, idx_base, m, n, nnz, 1, 1);
+    if (r) return r;
+    if (!nnz_out || (nnz > 0 && (!rows || !cols || !val)))
+        return fail(JLB_ERR_INVALID_ARGUMENT, "null buffer");
+    const CooCsrWs w = coo_csr_ws(workspace, nnz);
+    if (!workspace || workspace_bytes < w.bytes) return fail(JLB_ERR_WORKSPACE, "workspace too small");
+    cudaStream_t st = as_stream(stream);
+    r = coo_csr_slots(st, dtype, idx_base, m, n, nnz, rows, cols, val, w, false);
+    if (r) return r;
+    int32_t total = 0;
+    JLB_CUDA(cudaMemcpyAsync(&total, w.slot + nnz, sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+    JLB_CUDA(cudaStreamSynchronize(st));
+    const int bits = take_dev_error_convert();
+    if (bits < 0) return fail(JLB_ERR_CUDA, "reading the device error word failed");
+    if (bits & DEV_ERR_BOUNDS)
+        return fail(JLB_ERR_NONCANONICAL_STORAGE, "coordinate outside the matrix extents");
+    *nnz_out = total;
+    return ok();
+}
+
+extern "C" JLB_API int jlb_coo_drop_zeros_fill(void *stream, int dtype, int idx_base, int64_t m,
+                                               int64_t n, int64_t nnz, const int32_t *rows,
+                                               const int32_t *cols, const void *val,
+                                               int64_t nnz_out, int32_t *rows_out,
+                                               int32_t *cols_out, void *val_out, void *workspace,
+                                               size_t workspace_bytes) {
+    int r = conv_args(dtype, idx_base, m, n, nnz, 1, 1);
+    if (r) return r;
+    if ((nnz > 0 && (!rows || !cols || !val)) ||
+        (nnz_out > 0 && (!rows_out || !cols_out || !val_out)))
+        return fail(JLB_ERR_INVALID_ARGUMENT, "null buffer");
+    if (nnz_out < 0 || nnz_out > nnz) return fail(JLB_ERR_INVALID_ARGUMENT, "bad nnz_out");
+    const CooCsrWs w = coo_csr_ws(workspace, nnz);
+    if (!workspace || workspace_bytes < w.bytes) return fail(JLB_ERR_WORKSPACE, "workspace too small");
+    if (nnz == 0) return ok();
+    cudaStream_t st = as_stream(stream);
+    r = coo_csr_slots(st, dtype, idx_base, m, n, nnz, rows, cols, val, w, false);
+    if (r) return r;
+    JLB_ES_LAUNCH(coo_emit, dtype_size(dtype), conv::grid_for(nnz), conv::kThreads, st, nnz, rows,
+                  cols, val, w.keep, w.slot, nnz_out, rows_out, cols_out, val_out);
     JLB_LAUNCH_CHECK("coo_emit");
     return ok();
 }

@@ -409,6 +409,15 @@ def csr_to_csr(m, n, rowptr, colind, val, base=0):
     return compose_compressed(m, n, expand_positions(rowptr, base), colind, val, base, sort=False)
 
 
+def to_coo(rows, cols, val):
+    """COO target from an ordered source (convert.jl:316, 346-355): the
+    explicit zeros dropped, nothing sorted or merged (COO's row level is not
+    unique).  Coordinates keep their origin."""
+    rows, cols, val = np.asarray(rows, np.int32), np.asarray(cols, np.int32), np.asarray(val)
+    nz = (val & 0x7FFF) != 0 if val.dtype == np.uint16 else val != 0
+    return rows[nz], cols[nz], val[nz]
+
+
 def coo_to_csc(m, n, rows, cols, val, base=0):
     """COO -> CSC (colptr, rowind, val): the level order changes, so sorted."""
     return compose_compressed(n, m, cols, rows, val, base, sort=True)

@@ -214,3 +214,42 @@ def test_coo_to_csr_fill_workspace(same_ws):
     assert np.array_equal(rowptr.cpu().numpy(), ref[0])
     assert np.array_equal(ci.cpu().numpy(), ref[1])
     assert np.array_equal(vo.cpu().numpy(), ref[2])
+
+
+def test_csr_to_coo_kat_and_round_trip(golden):
+    g = golden["convert_fixture_3x4"]
+    a = g["A"]
+    rp, ci = np.array(a["rowptr"], np.int32), np.array(a["colind"], np.int32)
+    v = np.array(a["val"], np.float32)
+    A = J.csr_tensor(to_dev(rp), to_dev(ci), to_dev(v), (3, 4), origin=0)
+    U = J.convert_format(A, J.Formats.COO)
+    J.device_status()
+    assert U.format == J.Formats.COO
+    assert _host(J.coordinates(U, 1)).tolist() == [0, 0, 1, 2, 2]
+    assert _host(J.coordinates(U, 2)).tolist() == [0, 2, 1, 0, 2]
+    assert _host(J.nonzeros(U)).tolist() == [1, 2, 3, 4, 5]
+    _same(J.convert_format(U, J.Formats.CSR), (rp, ci, v))
+
+
+@pytest.mark.parametrize("dtype", [np.float64, np.uint16])
+def test_to_coo_drops_zeros(dtype):
+    rng = np.random.default_rng(206)
+    m, n = 3000, 2000
+    rp, ci, _ = random_csr(m, n, rng.integers(0, 25, m), seed=207, base=1)
+    val = _vals(rng, ci.shape[0], dtype, 0.3)
+    A = J.csr_tensor(to_dev(rp), to_dev(ci), _dev_vals(val), (m, n), origin=1)
+    U = J.convert_format(A, J.Formats.COO)
+    J.device_status()
+    r, c, vv = O.to_coo(O.expand_positions(rp, 1), ci, val)
+    assert np.array_equal(_host(J.coordinates(U, 1)), r)
+    assert np.array_equal(_host(J.coordinates(U, 2)), c)
+    assert np.array_equal(_host(J.nonzeros(U)).view(np.uint8), vv.view(np.uint8))
+    # COO -> COO of an unordered COO only drops zeros too
+    p = rng.permutation(r.shape[0])
+    vz = vv[p].copy()
+    vz[::7] = 0
+    U2 = J.convert_format(J.coo_tensor(to_dev(r[p]), to_dev(c[p]), _dev_vals(vz), (m, n), origin=1),
+                          J.Formats.COO)
+    r2, c2, v2 = O.to_coo(r[p], c[p], vz)
+    assert np.array_equal(_host(J.coordinates(U2, 1)), r2)
+    assert np.array_equal(_host(J.nonzeros(U2)).view(np.uint8), v2.view(np.uint8))

@@ -133,3 +133,19 @@ def test_block_banded_pattern():
         js = bc[bp[I]:bp[I + 1]]
         assert np.all(np.diff(js) > 0)
         assert set(range(max(0, I - 8), min(64, I + 9))) <= set(js.tolist())
+
+
+def test_spgemm_handle_validation():
+    """The SpGEMM handle's checks run before any device work: transposed
+    operands and beta != 0 are refused as in the reference's prepare
+    (KA spgemm.jl:313-323), and inner extents must agree."""
+    z = torch.zeros(0, dtype=torch.int32)
+    A = J.csr_tensor(torch.zeros(5, dtype=torch.int32), z, torch.zeros(0, dtype=torch.float64),
+                     (4, 3), origin=0)
+    be = J.B200Backend()
+    with pytest.raises(J.UnsupportedFormat):
+        J.prepare(be, J.SpGEMMOp, A, A, transa="T")
+    with pytest.raises(J.UnsupportedFormat):
+        J.prepare(be, J.SpGEMMOp, A, A, beta=1.0)
+    with pytest.raises(J.IncompatibleExtents):
+        J.prepare(be, J.SpGEMMOp, A, A)

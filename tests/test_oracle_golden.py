@@ -212,3 +212,15 @@ def test_spgemm_kat(golden):
             D[r, cci[p] - base] = cv[p]
     assert D.tolist() == g["C_dense"]
     assert crp.tolist() == [1, 3, 4, 6]
+
+
+def test_csr_to_coo_kat(golden):
+    """CSR -> COO of the 3x4 fixture (test_convert.jl:62-79) and the round
+    trip CSR -> COO -> CSR (:110-116)."""
+    g = golden["convert_fixture_3x4"]
+    rp, ci, v, base = _csr(g["A"], np.float32)
+    r, c, vv = O.to_coo(O.expand_positions(rp, base), ci, v)
+    assert r.tolist() == [0, 0, 1, 2, 2] and c.tolist() == [0, 2, 1, 0, 2]
+    assert vv.tolist() == [1, 2, 3, 4, 5]
+    p2, i2, v2 = O.coo_to_csr(3, 4, r, c, vv, base)
+    assert p2.tolist() == rp.tolist() and i2.tolist() == ci.tolist() and v2.tolist() == v.tolist()
