@@ -46,7 +46,7 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--workload", default="laplacian",
-                   choices=["laplacian", "spmv1", "spmm", "sddmm", "bsr", "convert"])
+                   choices=["laplacian", "spmv1", "spmm", "sddmm", "bsr", "convert", "scan"])
     p.add_argument("--exchange", choices=["p2p", "halo", "allgather"], default="p2p",
                    help="p2p: halo fused into the SpMV kernel over NVLink (default); "
                         "halo: NCCL send/recv; allgather: NCCL all-gather of x")
@@ -770,12 +770,75 @@ class Convert(Single):
         return "the first 1/64 of the rows per step (single-threaded composer)"
 
 
+class Scan(Single):
+    """The cfg2 row-pointer scan: exclusive scan of the Laplacian's 16.8 M
+    row lengths (int32) into its row pointer, through the C-ABI with buffers
+    allocated once."""
+
+    kernel, dtype, flush_l2 = "scan_tiles_final", "int32", True
+    launches_per_step = 3
+
+    def setup(self):
+        import ctypes as C
+
+        from jlust_b200 import _lib
+        from jlust_b200.backend import _stream
+        rp, _, _ = self.synth.laplacian_2d(4096)
+        self.h = np.diff(rp).astype(np.int32)
+        self.n = self.h.shape[0]
+        self.counts = self.d(self.h)
+        self.out = self.torch.empty(self.n + 1, dtype=self.torch.int32, device=self.dev)
+        self.wsb = _lib.load().jlb_scan_workspace_size(self.n)
+        self.ws = self.torch.empty(self.wsb, dtype=self.torch.uint8, device=self.dev)
+        self._lib, self._st = _lib, _stream(self.torch.device(self.dev))
+        self._p = lambda t: C.c_void_p(t.data_ptr())
+
+    def api_call(self):
+        p = self._p
+        self._lib.call("jlb_exclusive_scan_i32", self._st, self.n, p(self.counts), p(self.out), 0,
+                       p(self.ws), self.wsb)
+
+    def e2e_setup(self):
+        self.hc = self.counts.cpu().pin_memory()
+        self.hout = self.torch.empty(self.n + 1, dtype=self.torch.int32).pin_memory()
+        self.h2d, self.d2h = 4 * self.n, 4 * (self.n + 1)
+
+    def e2e_step(self):
+        self.counts.copy_(self.hc, non_blocking=True)
+        out = self.J.exclusive_scan(self.counts)          # the public call (allocates)
+        self.hout.copy_(out, non_blocking=True)
+
+    def flops(self):  # reported as counts scanned per second
+        return float(self.n)
+
+    def bytes(self):
+        return 4.0 * self.n + 4.0 * (self.n + 1)
+
+    def config(self):
+        return {"workload": f"cfg2 row-pointer scan: exclusive scan of {self.n} int32 row "
+                            "lengths of the 4096^2 Laplacian",
+                "l2": "256 MB buffer written between timed launches (67 MB of counts < L2)",
+                "value_unit_note": "value = G counts scanned per second"}
+
+    def cpu_setup(self):
+        pass
+
+    def cpu_step(self):
+        from oracle import oracle as O
+        O.exclusive_scan(self.h)
+
+    def cpu_sample(self):
+        return "full scan (single-threaded C loop)"
+
+
 WORKLOADS = {"laplacian": Laplacian, "spmv1": SpMV1, "spmm": SpMM, "sddmm": SDDMM, "bsr": BSR,
-             "convert": Convert}
+             "convert": Convert, "scan": Scan}
 
 
 # ------------------------------------------------------------------- arms --
 def unit_of(W):
+    if isinstance(W, Scan):
+        return "Gcounts/s"
     return "Gentries/s" if isinstance(W, Convert) else "GFLOP/s"
 
 

@@ -266,7 +266,7 @@ JLB_API int jlb_exclusive_scan_i32(void *stream, int64_t n, const int32_t *count
  * example code that must not re-enter a memory pool (Julia finalizers and
  * callbacks run while CUDA.jl's allocator may be busy) or that runs on a
  * device whose memory is entirely handed to another allocator.  Its scratch
- * is a static 128 KB device array inside the library (present on every GPU
+ * is a static 64 KB device array inside the library (present on every GPU
  * that loads it, until the process exits), so n is limited to 33,554,432
  * counts; larger n fails with JLB_ERR_INVALID_ARGUMENT.  The first call on a
  * device looks up that array's device address (cudaGetSymbolAddress), so

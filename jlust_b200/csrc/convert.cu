@@ -37,8 +37,8 @@ namespace conv {
 
 constexpr int kThreads = 256;
 constexpr int kConvThreads = 1024;   // threads of the CSR/COO -> BSR kernels (one CTA per block row)
-constexpr int kScanItems = 8;
-constexpr int kScanTile = kThreads * kScanItems;
+constexpr int kScanItems = 16;
+constexpr int kScanTile = kThreads * kScanItems;   // 4096 counts per tile
 constexpr int64_t kWinBits = 163840;  // block columns per bitmap window (bitmap + prefix = 40 KB)
 constexpr int kWinWords = (int)(kWinBits / 32);
 
@@ -70,32 +70,50 @@ __device__ __forceinline__ int64_t block_exclusive_scan(int64_t v, int64_t *s_wa
     return before + x - v;
 }
 
+// Reduce-then-scan over tiles of kScanTile counts, three launches and no
+// waits between CTAs.  Counts are read in striped order (coalesced); the final
+// pass stages its tile in shared memory so that each thread scans kScanItems
+// consecutive counts, and stores the tile back striped.
+constexpr int kScanSumThreads = 1024;
+
+__device__ __forceinline__ int scan_pad(int i) { return i + (i >> 5); }   // one word per 32: no bank conflicts
+
 __global__ void __launch_bounds__(kThreads)
 scan_tile_sums(int64_t n, const int32_t *__restrict__ counts, int64_t *__restrict__ sums) {
     __shared__ int64_t s_warp[kThreads / kWarp];
     const int64_t t0 = (int64_t)blockIdx.x * kScanTile;
     int64_t v = 0;
+    if (t0 + kScanTile <= n) {
 #pragma unroll
-    for (int j = 0; j < kScanItems; ++j) {
-        const int64_t i = t0 + (int64_t)threadIdx.x * kScanItems + j;
-        if (i < n) v += counts[i];
+        for (int j = 0; j < kScanItems; ++j) v += ldg(counts + t0 + j * kThreads + threadIdx.x);
+    } else {
+#pragma unroll
+        for (int j = 0; j < kScanItems; ++j) {
+            const int64_t i = t0 + j * kThreads + threadIdx.x;
+            if (i < n) v += ldg(counts + i);
+        }
     }
     int64_t total;
     block_exclusive_scan(v, s_warp, total);
     if (threadIdx.x == 0) sums[blockIdx.x] = total;
 }
 
-__global__ void __launch_bounds__(kThreads)
+// Exclusive scan of the tile sums in place by one CTA: each thread adds a
+// contiguous chunk, one block scan of the chunk totals, then each thread
+// rewrites its chunk.
+__global__ void __launch_bounds__(kScanSumThreads)
 scan_sums_single(int64_t ntiles, int64_t *__restrict__ sums) {
-    __shared__ int64_t s_warp[kThreads / kWarp];
-    int64_t carry = 0;
-    for (int64_t c0 = 0; c0 < ntiles; c0 += kThreads) {
-        const int64_t i = c0 + threadIdx.x;
-        const int64_t v = i < ntiles ? sums[i] : 0;
-        int64_t total;
-        const int64_t ex = block_exclusive_scan(v, s_warp, total);
-        if (i < ntiles) sums[i] = carry + ex;
-        carry += total;
+    __shared__ int64_t s_warp[kScanSumThreads / kWarp];
+    const int64_t per = (ntiles + kScanSumThreads - 1) / kScanSumThreads;
+    const int64_t c0 = threadIdx.x * per, c1 = c0 + per < ntiles ? c0 + per : ntiles;
+    int64_t v = 0;
+    for (int64_t i = c0; i < c1; ++i) v += sums[i];
+    int64_t total;
+    int64_t run = block_exclusive_scan<kScanSumThreads>(v, s_warp, total);
+    for (int64_t i = c0; i < c1; ++i) {
+        const int64_t x = sums[i];
+        sums[i] = run;
+        run += x;
     }
 }
 
@@ -103,27 +121,39 @@ __global__ void __launch_bounds__(kThreads)
 scan_tiles_final(int64_t n, const int32_t *counts, int32_t *out, const int64_t *__restrict__ sums,
                  int base) {
     __shared__ int64_t s_warp[kThreads / kWarp];
+    __shared__ int32_t s_tile[kScanTile + kScanTile / 32];
     const int64_t t0 = (int64_t)blockIdx.x * kScanTile;
+    const bool full = t0 + kScanTile <= n;
+    // `out` may alias `counts + 1`: this CTA reads exactly the counts whose
+    // outputs it writes, all before the barrier below.
+#pragma unroll
+    for (int j = 0; j < kScanItems; ++j) {
+        const int k = j * kThreads + threadIdx.x;
+        s_tile[scan_pad(k)] = (full || t0 + k < n) ? counts[t0 + k] : 0;
+    }
+    __syncthreads();
     int32_t items[kScanItems];
     int64_t v = 0;
 #pragma unroll
     for (int j = 0; j < kScanItems; ++j) {
-        const int64_t i = t0 + (int64_t)threadIdx.x * kScanItems + j;
-        items[j] = i < n ? counts[i] : 0;
+        items[j] = s_tile[scan_pad(threadIdx.x * kScanItems + j)];
         v += items[j];
     }
     int64_t total;
     int64_t run = block_exclusive_scan(v, s_warp, total) + sums[blockIdx.x] + base;
-    // `out` may alias `counts + 1`: every element is read above and written
-    // below by the same thread.
+    bool over = false;
 #pragma unroll
     for (int j = 0; j < kScanItems; ++j) {
-        const int64_t i = t0 + (int64_t)threadIdx.x * kScanItems + j;
         run += items[j];
-        if (i < n) {
-            if (run > INT32_MAX) dev_error(DEV_ERR_OVERFLOW);
-            out[i + 1] = (int32_t)run;
-        }
+        over |= run > INT32_MAX;
+        s_tile[scan_pad(threadIdx.x * kScanItems + j)] = (int32_t)run;   // inclusive: out[i + 1]
+    }
+    if (over) dev_error(DEV_ERR_OVERFLOW);
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < kScanItems; ++j) {
+        const int k = j * kThreads + threadIdx.x;
+        if (full || t0 + k < n) out[t0 + k + 1] = s_tile[scan_pad(k)];
     }
     if (blockIdx.x == 0 && threadIdx.x == 0) out[0] = base;
 }
@@ -143,7 +173,7 @@ int scan(cudaStream_t st, int64_t n, const int32_t *counts, int32_t *out, int ba
     const int64_t ntiles = ceil_div(n, kScanTile);
     int64_t *sums = (int64_t *)ws;
     scan_tile_sums<<<(unsigned)ntiles, kThreads, 0, st>>>(n, counts, sums);
-    scan_sums_single<<<1, kThreads, 0, st>>>(ntiles, sums);
+    scan_sums_single<<<1, kScanSumThreads, 0, st>>>(ntiles, sums);
     scan_tiles_final<<<(unsigned)ntiles, kThreads, 0, st>>>(n, counts, out, sums, base);
     JLB_LAUNCH_CHECK("exclusive_scan");
     return ok();
@@ -652,20 +682,49 @@ coo_emit(int64_t nnz, const int32_t *__restrict__ rows, const int32_t *__restric
 }
 
 // coordinates[k] = i + base for k in [ptr[i], ptr[i+1]) - base: the outer
-// coordinate of every entry of a compressed level (one warp per outer index).
+// coordinate of every entry of a compressed level.  Each thread takes 16
+// consecutive entries, finds the row of the first by binary search over ptr
+// and walks on (balanced whatever the row lengths); it stores them as four
+// 16-byte vectors when it can.  The same threads check every row's range.
+constexpr int kExpandItems = 16;
+
 __global__ void __launch_bounds__(kThreads)
 expand_positions(int64_t n_outer, int64_t nnz, const int32_t *__restrict__ ptr, int base,
                  int32_t *__restrict__ coords) {
-    const int lane = threadIdx.x % kWarp;
-    const int64_t nwarps = (int64_t)gridDim.x * (kThreads / kWarp);
-    for (int64_t i = (int64_t)blockIdx.x * (kThreads / kWarp) + threadIdx.x / kWarp; i < n_outer;
-         i += nwarps) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    for (int64_t i = tid; i < n_outer; i += stride) {
         const int64_t lo = (int64_t)ldg(ptr + i) - base, hi = (int64_t)ldg(ptr + i + 1) - base;
-        if (lo < 0 || hi > nnz || lo > hi) {
-            if (lane == 0) dev_error(DEV_ERR_BOUNDS);
-            continue;
+        if (lo < 0 || hi > nnz || lo > hi) dev_error(DEV_ERR_BOUNDS);
+    }
+    const int64_t nchunks = (nnz + kExpandItems - 1) / kExpandItems;
+    const bool vec = (reinterpret_cast<uintptr_t>(coords) & 15) == 0;
+    for (int64_t c = tid; c < nchunks; c += stride) {
+        const int64_t k0 = c * kExpandItems;
+        const int64_t k1 = k0 + kExpandItems < nnz ? k0 + kExpandItems : nnz;
+        // the last row r with ptr[r] - base <= k0
+        int64_t a = 0, b = n_outer - 1;
+        while (a < b) {
+            const int64_t mid = (a + b + 1) >> 1;
+            if ((int64_t)ldg(ptr + mid) - base <= k0) a = mid;
+            else b = mid - 1;
         }
-        for (int64_t k = lo + lane; k < hi; k += kWarp) coords[k] = (int32_t)(i + base);
+        int64_t r = a;
+        int32_t v[kExpandItems];
+#pragma unroll
+        for (int u = 0; u < kExpandItems; ++u) {
+            const int64_t k = k0 + u;
+            while (r + 1 < n_outer && (int64_t)ldg(ptr + r + 1) - base <= k) ++r;
+            v[u] = (int32_t)(r + base);
+        }
+        if (vec && k1 - k0 == kExpandItems) {
+            int4 *dst = reinterpret_cast<int4 *>(coords + k0);
+#pragma unroll
+            for (int q = 0; q < kExpandItems / 4; ++q)
+                dst[q] = make_int4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        } else {
+            for (int64_t k = k0; k < k1; ++k) coords[k] = v[k - k0];
+        }
     }
 }
 
@@ -969,7 +1028,7 @@ extern "C" JLB_API int jlb_coo_to_bsr_fill(void *stream, int dtype, int idx_base
 namespace jlb {
 namespace conv {
 
-constexpr int64_t kNoAllocTiles = 16384;                    // 128 KB of scratch
+constexpr int64_t kNoAllocTiles = 8192;                     // 64 KB of scratch
 constexpr int64_t kNoAllocMaxN = kNoAllocTiles * kScanTile; // 33,554,432 counts
 
 static __device__ __align__(256) int64_t g_scan_noalloc_sums[kNoAllocTiles];
@@ -1150,8 +1209,10 @@ extern "C" JLB_API int jlb_positions_to_coordinates(void *stream, int idx_base, 
     if (!ptr || (nnz > 0 && !coords)) return fail(JLB_ERR_INVALID_ARGUMENT, "null buffer");
     if (n_outer == 0) return ok();
     cudaStream_t st = as_stream(stream);
-    const int64_t g = ceil_div(n_outer, conv::kThreads / kWarp);
-    conv::expand_positions<<<(unsigned)(g < 148 * 16 ? g : 148 * 16), conv::kThreads, 0, st>>>(
+    const int64_t work = n_outer > ceil_div(nnz, conv::kExpandItems) ? n_outer
+                                                                       : ceil_div(nnz, conv::kExpandItems);
+    const int64_t g = ceil_div(work, conv::kThreads);
+    conv::expand_positions<<<(unsigned)(g < 148 * 32 ? g : 148 * 32), conv::kThreads, 0, st>>>(
         n_outer, nnz, ptr, idx_base, coords);
     JLB_LAUNCH_CHECK("expand_positions");
     return ok();

@@ -100,10 +100,11 @@ def test_coo_bounds_error():
     J.device_status()
 
 
-@pytest.mark.parametrize("n", [0, 1, 2047, 2048, 2049, 3_000_001])
+@pytest.mark.parametrize("n", [0, 1, 2047, 2048, 2049, 4095, 4096, 4097, 3_000_001,
+                               16_777_217])
 def test_scan(n):
     rng = np.random.default_rng(66)
-    c = rng.integers(0, 300, size=n).astype(np.int32)
+    c = rng.integers(0, 300 if n < 5_000_000 else 100, size=n).astype(np.int32)
     out = J.exclusive_scan(to_dev(c), base=1)
     J.device_status()
     assert np.array_equal(out.cpu().numpy(), O.exclusive_scan(c, base=1))
@@ -164,3 +165,37 @@ def test_csr_fill_workspace_handover(fill_ws):
     assert np.array_equal(browptr.cpu().numpy(), bp)
     assert np.array_equal(bcol.cpu().numpy(), bc)
     assert np.array_equal(bval.cpu().numpy().view(np.uint8), bv.view(np.uint8))
+
+
+def test_scan_in_place_shifted():
+    """counts given as out + 1 (the row-pointer layout the conversions use):
+    each tile reads only the counts whose outputs it writes."""
+    import ctypes as C
+
+    from jlust_b200 import _lib
+    from jlust_b200.backend import _stream
+    rng = np.random.default_rng(67)
+    n = 1_000_003
+    c = rng.integers(0, 50, size=n).astype(np.int32)
+    buf = torch.zeros(n + 1, dtype=torch.int32, device=DEV)
+    buf[1:] = to_dev(c)
+    L = _lib.load()
+    wsb = L.jlb_scan_workspace_size(n)
+    ws = torch.empty(wsb, dtype=torch.uint8, device=DEV)
+    _lib.call("jlb_exclusive_scan_i32", _stream(torch.device(DEV)), n,
+              C.c_void_p(buf.data_ptr() + 4), C.c_void_p(buf.data_ptr()), 0,
+              C.c_void_p(ws.data_ptr()), wsb)
+    J.device_status()
+    assert np.array_equal(buf.cpu().numpy(), O.exclusive_scan(c))
+
+
+def test_scan_total_past_int32_reported():
+    """A running total past Int32 cannot be a position: the scan flags it and
+    jlb_device_status reports it; the context stays usable."""
+    c = np.full(3_000_000, 1000, np.int32)          # 3e9 in all
+    J.exclusive_scan(to_dev(c))
+    with pytest.raises(J.NonCanonicalStorage):
+        J.device_status()
+    out = J.exclusive_scan(to_dev(np.ones(10, np.int32)))
+    J.device_status()
+    assert out.cpu().tolist() == list(range(11))
