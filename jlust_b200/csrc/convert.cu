@@ -117,7 +117,7 @@ scan_sums_single(int64_t ntiles, int64_t *__restrict__ sums) {
     }
 }
 
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 8)
 scan_tiles_final(int64_t n, const int32_t *counts, int32_t *out, const int64_t *__restrict__ sums,
                  int base) {
     __shared__ int64_t s_warp[kThreads / kWarp];
@@ -132,21 +132,20 @@ scan_tiles_final(int64_t n, const int32_t *counts, int32_t *out, const int64_t *
         s_tile[scan_pad(k)] = (full || t0 + k < n) ? counts[t0 + k] : 0;
     }
     __syncthreads();
-    int32_t items[kScanItems];
+    // the thread's counts are read from shared memory twice rather than held
+    // in registers: 32 registers a thread, eight CTAs an SM
     int64_t v = 0;
 #pragma unroll
-    for (int j = 0; j < kScanItems; ++j) {
-        items[j] = s_tile[scan_pad(threadIdx.x * kScanItems + j)];
-        v += items[j];
-    }
+    for (int j = 0; j < kScanItems; ++j) v += s_tile[scan_pad(threadIdx.x * kScanItems + j)];
     int64_t total;
     int64_t run = block_exclusive_scan(v, s_warp, total) + sums[blockIdx.x] + base;
     bool over = false;
 #pragma unroll
     for (int j = 0; j < kScanItems; ++j) {
-        run += items[j];
+        const int q = scan_pad(threadIdx.x * kScanItems + j);
+        run += s_tile[q];
         over |= run > INT32_MAX;
-        s_tile[scan_pad(threadIdx.x * kScanItems + j)] = (int32_t)run;   // inclusive: out[i + 1]
+        s_tile[q] = (int32_t)run;   // inclusive: out[i + 1]
     }
     if (over) dev_error(DEV_ERR_OVERFLOW);
     __syncthreads();
