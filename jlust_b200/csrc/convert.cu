@@ -117,13 +117,14 @@ scan_sums_single(int64_t ntiles, int64_t *__restrict__ sums) {
     }
 }
 
-__global__ void __launch_bounds__(kThreads, 8)
+__global__ void __launch_bounds__(kThreads, 6)
 scan_tiles_final(int64_t n, const int32_t *counts, int32_t *out, const int64_t *__restrict__ sums,
                  int base) {
     __shared__ int64_t s_warp[kThreads / kWarp];
     __shared__ int32_t s_tile[kScanTile + kScanTile / 32];
     const int64_t t0 = (int64_t)blockIdx.x * kScanTile;
     const bool full = t0 + kScanTile <= n;
+    const int64_t offset = sums[blockIdx.x] + base;   // issued before the tile loads
     // `out` may alias `counts + 1`: this CTA reads exactly the counts whose
     // outputs it writes, all before the barrier below.
 #pragma unroll
@@ -133,12 +134,12 @@ scan_tiles_final(int64_t n, const int32_t *counts, int32_t *out, const int64_t *
     }
     __syncthreads();
     // the thread's counts are read from shared memory twice rather than held
-    // in registers: 32 registers a thread, eight CTAs an SM
+    // in registers: at most 40 registers a thread, six CTAs an SM
     int64_t v = 0;
 #pragma unroll
     for (int j = 0; j < kScanItems; ++j) v += s_tile[scan_pad(threadIdx.x * kScanItems + j)];
     int64_t total;
-    int64_t run = block_exclusive_scan(v, s_warp, total) + sums[blockIdx.x] + base;
+    int64_t run = block_exclusive_scan(v, s_warp, total) + offset;
     bool over = false;
 #pragma unroll
     for (int j = 0; j < kScanItems; ++j) {
