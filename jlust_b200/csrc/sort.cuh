@@ -3,13 +3,14 @@
 // translation unit's JLB_DEFINE_DEV_ERROR: the kernels report through its
 // dev_error.  Everything here has internal linkage, one copy per unit.
 //
-// Sorting is an ascending bitonic network over 64-bit keys
-// coordinate << 32 | storage index (unique, so the network's instability does
-// not matter), run on positions [0, len) of a power-of-two network; positions
-// past len act as +infinity and are never touched.  Buckets of up to
-// kWarpKeys entries are sorted by one warp in shared memory, up to kCtaKeys by
-// one CTA in shared memory, longer ones (up to kMaxSortKeys) by one CTA in
-// place in global memory, gathering the coordinate per comparison.
+// Keys are 64-bit, coordinate << 32 | storage index, so they are unique and
+// any correct sort gives the same order.  Buckets of up to kThreadKeys
+// entries are insertion-sorted by one thread.  Larger ones go through an
+// ascending bitonic network run on positions [0, len) of a power-of-two
+// network (positions past len act as +infinity and are never touched): up to
+// kWarpKeys entries by one warp in shared memory, up to kCtaKeys by one CTA
+// in shared memory, longer ones (up to kMaxSortKeys) by one CTA in place in
+// global memory, gathering the coordinate per comparison.
 #pragma once
 #include "common.cuh"
 
@@ -69,8 +70,14 @@ __device__ __forceinline__ int warp_isum(int v) {
     return v;
 }
 
-// Sorts every bucket of up to kWarpKeys entries (one warp per row) and counts
-// its distinct columns into cnt[r]; longer rows are appended to `long_rows`.
+constexpr int kThreadKeys = 16;
+
+// Sorts every bucket of up to kWarpKeys entries and counts its distinct
+// columns into cnt[r]; longer rows are appended to `long_rows`.  A warp takes
+// 32 rows at a time: each lane sorts its own row when it has at most
+// kThreadKeys entries (insertion sort in registers and local memory), then the
+// warp sorts the others one after another in shared memory.  The keys are
+// unique, so both sorts give the same order.
 __global__ void __launch_bounds__(kSortThreads)
 sort_short_rows(int64_t m, const int32_t *__restrict__ offs, int32_t *__restrict__ ent,
                 const int32_t *__restrict__ cols, int base, int32_t *__restrict__ cnt,
@@ -79,27 +86,59 @@ sort_short_rows(int64_t m, const int32_t *__restrict__ offs, int32_t *__restrict
     const int lane = threadIdx.x % kWarp, warp = threadIdx.x / kWarp;
     uint64_t *s = s_keys[warp];
     const int64_t nwarps = (int64_t)gridDim.x * (kSortThreads / kWarp);
-    for (int64_t r = (int64_t)blockIdx.x * (kSortThreads / kWarp) + warp; r < m; r += nwarps) {
-        const int lo = ldg(offs + r), len = ldg(offs + r + 1) - lo;
-        if (len > kWarpKeys) {
-            if (lane == 0) {
-                const int q = atomicAdd(n_long, 1);
-                if (q < long_cap) long_rows[q] = (int32_t)r;
-                else dev_error(DEV_ERR_OVERFLOW);
+    for (int64_t rb = ((int64_t)blockIdx.x * (kSortThreads / kWarp) + warp) * kWarp; rb < m;
+         rb += nwarps * kWarp) {
+        const int64_t r = rb + lane;
+        int lo = 0, len = 0;
+        if (r < m) {
+            lo = ldg(offs + r);
+            len = ldg(offs + r + 1) - lo;
+        }
+        if (r < m && len <= kThreadKeys) {
+            uint64_t k[kThreadKeys];
+            for (int i = 0; i < len; ++i) {
+                const uint64_t key = entry_key(cols, base, ent[lo + i]);
+                int j = i;
+                while (j > 0 && k[j - 1] > key) {
+                    k[j] = k[j - 1];
+                    --j;
+                }
+                k[j] = key;
             }
-            continue;
+            int u = 0;
+            for (int i = 0; i < len; ++i) {
+                ent[lo + i] = (int32_t)(uint32_t)k[i];
+                u += (i == 0 || (k[i] >> 32) != (k[i - 1] >> 32));
+            }
+            cnt[r] = u;
         }
-        for (int i = lane; i < len; i += kWarp) s[i] = entry_key(cols, base, ent[lo + i]);
-        __syncwarp();
-        bitonic_smem(s, len, lane, kWarp, WarpSync{});
-        int u = 0;
-        for (int i = lane; i < len; i += kWarp) {
-            ent[lo + i] = (int32_t)(uint32_t)s[i];
-            u += (i == 0 || (s[i] >> 32) != (s[i - 1] >> 32));
+        unsigned rest = __ballot_sync(0xffffffffu, r < m && len > kThreadKeys);
+        while (rest) {
+            const int src = __ffs(rest) - 1;
+            rest &= rest - 1;
+            const int64_t rr = rb + src;
+            const int rlo = __shfl_sync(0xffffffffu, lo, src);
+            const int rlen = __shfl_sync(0xffffffffu, len, src);
+            if (rlen > kWarpKeys) {
+                if (lane == 0) {
+                    const int q = atomicAdd(n_long, 1);
+                    if (q < long_cap) long_rows[q] = (int32_t)rr;
+                    else dev_error(DEV_ERR_OVERFLOW);
+                }
+                continue;
+            }
+            for (int i = lane; i < rlen; i += kWarp) s[i] = entry_key(cols, base, ent[rlo + i]);
+            __syncwarp();
+            bitonic_smem(s, rlen, lane, kWarp, WarpSync{});
+            int u = 0;
+            for (int i = lane; i < rlen; i += kWarp) {
+                ent[rlo + i] = (int32_t)(uint32_t)s[i];
+                u += (i == 0 || (s[i] >> 32) != (s[i - 1] >> 32));
+            }
+            u = warp_isum(u);
+            if (lane == 0) cnt[rr] = u;
+            __syncwarp();
         }
-        u = warp_isum(u);
-        if (lane == 0) cnt[r] = u;
-        __syncwarp();
     }
 }
 
