@@ -11,9 +11,9 @@
 // run of consecutive lanes add their terms with a fixed shuffle tree, and the
 // first lane of each run adds the run's sum to y with one atomic (sorted COO,
 // the composer's output, has long runs; unsorted input has runs of one).
-// CSC: one warp per column, lanes over the column's entries, one atomic per
-// entry.  Out-of-range coordinates raise the device bounds flag and are
-// skipped.
+// CSC: one lane per column of up to 16 entries, the warp for longer ones,
+// one atomic per entry.  Out-of-range coordinates raise the device bounds
+// flag and are skipped.
 #include "common.cuh"
 
 namespace jlb {
@@ -68,23 +68,58 @@ coo_entries(int64_t nnz, int64_t m, int64_t n, const int32_t *__restrict__ rows,
     }
 }
 
+// CSC: a warp takes 32 columns at a time.  Each lane scatters its own column
+// when it has at most kLaneEntries entries (one lane per column keeps the
+// lanes busy on short columns); the warp then scatters the longer ones one
+// after another, lanes over entries.  Every term is alpha*v*x[j], added to
+// its row atomically.
+constexpr int kLaneEntries = 16;
+
 template <typename T>
 __global__ void __launch_bounds__(kThreads)
-csc_columns(int64_t n, int64_t m, const int32_t *__restrict__ colptr,
+csc_columns(int64_t n, int64_t m, int64_t nnz, const int32_t *__restrict__ colptr,
             const int32_t *__restrict__ rowind, const T *__restrict__ val,
             const T *__restrict__ x, T *__restrict__ y, T alpha, int base) {
     const int lane = threadIdx.x % kWarp;
     const int64_t warps = (int64_t)gridDim.x * (kThreads / kWarp);
-    for (int64_t j = ((int64_t)blockIdx.x * kThreads + threadIdx.x) / kWarp; j < n; j += warps) {
-        const int lo = ldg(colptr + j) - base, hi = ldg(colptr + j + 1) - base;
-        const T xj = ldg(x + j);
-        for (int p = lo + lane; p < hi; p += kWarp) {
-            const int64_t r = (int64_t)ldg(rowind + p) - base;
-            if (r < 0 || r >= m) {
+    for (int64_t jb = ((int64_t)blockIdx.x * kThreads + threadIdx.x) / kWarp * kWarp; jb < n;
+         jb += warps * kWarp) {
+        const int64_t j = jb + lane;
+        int lo = 0, hi = 0;
+        bool valid = j < n;
+        if (valid) {
+            lo = ldg(colptr + j) - base;
+            hi = ldg(colptr + j + 1) - base;
+            if (lo < 0 || hi > nnz || lo > hi) {
                 dev_error(DEV_ERR_BOUNDS);
-                continue;
+                valid = false;
             }
-            atomicAdd(y + r, mul_rn(mul_rn(alpha, ldg(val + p)), xj));
+        }
+        if (valid && hi - lo <= kLaneEntries) {
+            const T xj = ldg(x + j);
+            for (int p = lo; p < hi; ++p) {
+                const int64_t r = (int64_t)ldg(rowind + p) - base;
+                if (r < 0 || r >= m) {
+                    dev_error(DEV_ERR_BOUNDS);
+                    continue;
+                }
+                atomicAdd(y + r, mul_rn(mul_rn(alpha, ldg(val + p)), xj));
+            }
+        }
+        unsigned rest = __ballot_sync(0xffffffffu, valid && hi - lo > kLaneEntries);
+        while (rest) {
+            const int src = __ffs(rest) - 1;
+            rest &= rest - 1;
+            const int clo = __shfl_sync(0xffffffffu, lo, src), chi = __shfl_sync(0xffffffffu, hi, src);
+            const T xj = ldg(x + jb + src);
+            for (int p = clo + lane; p < chi; p += kWarp) {
+                const int64_t r = (int64_t)ldg(rowind + p) - base;
+                if (r < 0 || r >= m) {
+                    dev_error(DEV_ERR_BOUNDS);
+                    continue;
+                }
+                atomicAdd(y + r, mul_rn(mul_rn(alpha, ldg(val + p)), xj));
+            }
         }
     }
 }
@@ -104,8 +139,8 @@ int launch(cudaStream_t st, bool csc, int base, int64_t m, int64_t n, int64_t nn
     }
     if (csc) {
         if (n > 0) {
-            csc_columns<T><<<grid_for(n * kWarp), kThreads, 0, st>>>(
-                n, m, a, b, (const T *)val, (const T *)x, (T *)y, (T)alpha, base);
+            csc_columns<T><<<grid_for(n), kThreads, 0, st>>>(
+                n, m, nnz, a, b, (const T *)val, (const T *)x, (T *)y, (T)alpha, base);
             JLB_LAUNCH_CHECK("csc_columns");
         }
     } else if (nnz > 0) {
