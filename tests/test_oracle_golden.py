@@ -224,3 +224,63 @@ def test_csr_to_coo_kat(golden):
     assert vv.tolist() == [1, 2, 3, 4, 5]
     p2, i2, v2 = O.coo_to_csr(3, 4, r, c, vv, base)
     assert p2.tolist() == rp.tolist() and i2.tolist() == ci.tolist() and v2.tolist() == v.tolist()
+
+
+def _dense_csr(m, n, rp, ci, v, base=0):
+    D = np.zeros((m, n))
+    for r in range(m):
+        for k in range(rp[r] - base, rp[r + 1] - base):
+            D[r, ci[k] - base] += float(v[k])
+    return D
+
+
+def test_oracle_spgemm_against_dense():
+    """The oracle's SpGEMM against a dense product: C's structure is every
+    column reached by a product (explicit zeros included) and its values agree
+    to fp64 rounding."""
+    from _helpers import random_csr
+    rng = np.random.default_rng(400)
+    m, k, n = 120, 90, 150
+    arp, aci, av = random_csr(m, k, rng.integers(0, 8, m), seed=401, zero_frac=0.1)
+    brp, bci, bv = random_csr(k, n, rng.integers(0, 10, k), seed=402)
+    crp, cci, cv = O.spgemm(m, n, arp, aci, av, brp, bci, bv, alpha=-0.5)
+    A, B = _dense_csr(m, k, arp, aci, av), _dense_csr(k, n, brp, bci, bv)
+    assert np.allclose(_dense_csr(m, n, crp, cci, cv), -0.5 * A @ B, rtol=1e-13, atol=1e-13)
+    pattern = (np.abs(_dense_csr(m, k, arp, aci, np.ones_like(av))) @
+               np.abs(_dense_csr(k, n, brp, bci, np.ones_like(bv)))) > 0
+    got = np.zeros((m, n), bool)
+    for r in range(m):
+        got[r, cci[crp[r]:crp[r + 1]]] = True
+        assert np.all(np.diff(cci[crp[r]:crp[r + 1]]) > 0)
+    assert np.array_equal(got, pattern)
+
+
+def test_oracle_periodic_bbm_with_selectors_against_dense():
+    """The oracle's periodic block-banded product with diagonal patches and a
+    ShiftedDiag coupling block against the dense T-period matrix."""
+    from _helpers import random_csr
+    rng = np.random.default_rng(410)
+    T, nd, no, nc = 5, 40, 15, 50
+    drp, dci, dv = random_csr(nd, nc, rng.integers(0, 6, nd), seed=411)
+    prp, pci, pv = random_csr(no, nc, rng.integers(0, 4, no), seed=412)
+    patches = [(0, 9, 20, 1.5), (10, 39, 3, -2.0)]
+    x = rng.uniform(-1, 1, T * nc)
+    y = O.bbm_periodic_spmv(T, nd, no, nc, (drp, dci, dv), ("shifted", 7, 0.25), (prp, pci, pv), x,
+                            patches=patches)
+    D = _dense_csr(nd, nc, drp, dci, dv)
+    for r0, r1, c0, val in patches:
+        D[np.arange(r0, r1 + 1), c0 + np.arange(r1 - r0 + 1)] += val
+    N = np.zeros((no, nc))
+    N[np.arange(no), 7 + np.arange(no)] = 0.25
+    P = _dense_csr(no, nc, prp, pci, pv)
+    rows = T * nd + (T - 1) * no
+    M = np.zeros((rows, T * nc))
+    r = 0
+    for t in range(T):
+        M[r:r + nd, t * nc:(t + 1) * nc] = D
+        r += nd
+        if t < T - 1:
+            M[r:r + no, t * nc:(t + 1) * nc] = N
+            M[r:r + no, (t + 1) * nc:(t + 2) * nc] = P
+            r += no
+    assert np.allclose(y, M @ x, rtol=1e-13, atol=1e-13)
