@@ -46,7 +46,8 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--workload", default="laplacian",
-                   choices=["laplacian", "spmv1", "spmm", "sddmm", "bsr", "convert", "scan"])
+                   choices=["laplacian", "spmv1", "spmm", "sddmm", "bsr", "convert", "scan",
+                            "coo2csr"])
     p.add_argument("--exchange", choices=["p2p", "halo", "allgather"], default="p2p",
                    help="p2p: halo fused into the SpMV kernel over NVLink (default); "
                         "halo: NCCL send/recv; allgather: NCCL all-gather of x")
@@ -831,15 +832,73 @@ class Scan(Single):
         return "full scan (single-threaded C loop)"
 
 
+class CooToCsr(Single):
+    """COO -> CSR of the cfg2 Laplacian (its 83.9 M fp64 entries given as
+    row-ordered COO) through convert_format: count, host read of nnz, fill."""
+
+    kernel, dtype = "coo_keep", "f64 values, int32 indices"
+    launches_per_step = 7          # keep, scan (3), row pointer fill and write, emit
+
+    def setup(self):
+        J = self.J
+        rp, ci, val, _ = self.synth.config2(g=4096)
+        self.m = rp.shape[0] - 1
+        self.nnz = int(rp[-1])
+        rows = np.repeat(np.arange(self.m, dtype=np.int32), np.diff(rp))
+        self.h = (rows, ci, val)
+        self.A = J.coo_tensor(self.d(rows), self.d(ci), self.d(val), (self.m, self.m), origin=0)
+
+    def api_call(self):
+        self.out = self.J.convert_format(self.A, self.J.Formats.CSR)
+
+    def e2e_setup(self):
+        torch = self.torch
+        self.hv = self.A.val.cpu().pin_memory()
+        self.hout = torch.empty(self.nnz, dtype=torch.float64).pin_memory()
+        self.h2d = self.hv.numel() * 8
+        self.d2h = self.hout.numel() * 8
+
+    def e2e_step(self):
+        self.A.val.copy_(self.hv, non_blocking=True)
+        self.api_call()
+        self.hout.copy_(self.out.val, non_blocking=True)
+
+    def flops(self):  # reported as entries converted per second
+        return float(self.nnz)
+
+    def bytes(self):  # read rows, cols, values; write colind, values, row pointer
+        return 16.0 * self.nnz + 12.0 * self.nnz + 4.0 * (self.m + 1)
+
+    def config(self):
+        return {"workload": f"COO -> CSR of the cfg2 Laplacian ({self.m} rows, nnz={self.nnz}, "
+                            "fp64), count + host read + fill",
+                "value_unit_note": "value = G entries converted per second"}
+
+    def cpu_setup(self):
+        pass
+
+    def cpu_step(self):
+        from oracle import oracle as O
+        rows, ci, val = self.h
+        k = self.nnz // 16
+        O.coo_to_csr(self.m, self.m, rows[:k], ci[:k], val[:k])
+
+    def cpu_flops(self):
+        return float(self.nnz // 16)
+
+    def cpu_sample(self):
+        return "the first 1/16 of the entries per step (vectorised numpy composer)"
+
+
 WORKLOADS = {"laplacian": Laplacian, "spmv1": SpMV1, "spmm": SpMM, "sddmm": SDDMM, "bsr": BSR,
-             "convert": Convert, "scan": Scan}
+             "convert": Convert, "scan": Scan, "coo2csr": CooToCsr}
 
 
 # ------------------------------------------------------------------- arms --
 def unit_of(W):
     if isinstance(W, Scan):
         return "Gcounts/s"
-    return "Gentries/s" if isinstance(W, Convert) else "GFLOP/s"
+    return "Gentries/s" if isinstance(W, (Convert, CooToCsr)) else "GFLOP/s"
 
 
 def timed_flushed(ctx, fn, steps, stream):

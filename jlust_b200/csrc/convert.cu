@@ -608,6 +608,9 @@ __device__ __forceinline__ int64_t prev_nonzero(const void *__restrict__ val, in
     return q;
 }
 
+// The loads of an entry and of the entry before it are issued together (the
+// entry before is almost always the nonzero predecessor); only when that one
+// is an explicit zero does a thread walk further back.
 template <int ES>
 __global__ void __launch_bounds__(kThreads)
 coo_keep(int64_t nnz, const int32_t *__restrict__ rows, const int32_t *__restrict__ cols,
@@ -615,19 +618,36 @@ coo_keep(int64_t nnz, const int32_t *__restrict__ rows, const int32_t *__restric
          int32_t *__restrict__ keep) {
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < nnz; p += stride) {
+        const bool has_prev = p > 0;
+        const int32_t r = ldg(rows + p), c = ldg(cols + p);
+        const int32_t r1 = has_prev ? ldg(rows + p - 1) : 0, c1 = has_prev ? ldg(cols + p - 1) : 0;
+        const bool zero = is_zero<ES>(val, p);
+        const bool zero1 = !has_prev || is_zero<ES>(val, p - 1);
         int k = 0;
-        if (!is_zero<ES>(val, p)) {
-            const int32_t r = ldg(rows + p), c = ldg(cols + p);
+        if (!zero) {
             if ((int64_t)r - base < 0 || (int64_t)r - base >= m || (int64_t)c - base < 0 ||
                 (int64_t)c - base >= n) {
                 dev_error(DEV_ERR_BOUNDS);
             } else {
-                const int64_t q = merge ? prev_nonzero<ES>(val, p) : -1;
                 k = 1;
-                if (q >= 0) {
-                    const int32_t rq = ldg(rows + q);
-                    if (rq > r) dev_error(DEV_ERR_ORDER);
-                    k = (rq != r || ldg(cols + q) != c);
+                if (merge) {
+                    int64_t q = -1;
+                    int32_t rq = 0, cq = 0;
+                    if (!zero1) {
+                        q = p - 1;
+                        rq = r1;
+                        cq = c1;
+                    } else if (has_prev) {
+                        q = prev_nonzero<ES>(val, p - 1);
+                        if (q >= 0) {
+                            rq = ldg(rows + q);
+                            cq = ldg(cols + q);
+                        }
+                    }
+                    if (q >= 0) {
+                        if (rq > r) dev_error(DEV_ERR_ORDER);
+                        k = (rq != r || cq != c);
+                    }
                 }
             }
         }
@@ -652,12 +672,22 @@ coo_rowptr(int64_t nnz, const int32_t *__restrict__ rows, const void *__restrict
            int32_t *__restrict__ rowptr) {
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < nnz; p += stride) {
-        if (!keep[p]) continue;
-        const int64_t r = (int64_t)ldg(rows + p) - base;
-        const int64_t q = prev_nonzero<ES>(val, p);
-        int64_t rp = q < 0 ? -1 : (int64_t)ldg(rows + q) - base;
+        const bool has_prev = p > 0;
+        const int kp = keep[p];
+        const int32_t r0 = ldg(rows + p), sp = slot[p];
+        const int32_t r1 = has_prev ? ldg(rows + p - 1) : 0;
+        const bool zero1 = !has_prev || is_zero<ES>(val, p - 1);
+        if (!kp) continue;
+        const int64_t r = (int64_t)r0 - base;
+        int64_t rp = -1;
+        if (!zero1) {
+            rp = (int64_t)r1 - base;
+        } else if (has_prev) {
+            const int64_t q = prev_nonzero<ES>(val, p - 1);
+            if (q >= 0) rp = (int64_t)ldg(rows + q) - base;
+        }
         if (rp < -1) rp = -1;
-        for (int64_t i = rp + 1; i <= r && i < m; ++i) rowptr[i] = slot[p] + base;
+        for (int64_t i = rp + 1; i <= r && i < m; ++i) rowptr[i] = sp + base;
     }
 }
 
@@ -669,14 +699,16 @@ coo_emit(int64_t nnz, const int32_t *__restrict__ rows, const int32_t *__restric
          int32_t *__restrict__ colind, void *__restrict__ out_val) {
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < nnz; p += stride) {
-        if (!keep[p]) continue;
+        const int kp = keep[p];
         const int64_t q = slot[p];
+        const int32_t c = ldg(cols + p);
+        if (!kp) continue;
         if (q < 0 || q >= nnz_out) {
             dev_error(DEV_ERR_OVERFLOW);
             continue;
         }
         if (rows_out) rows_out[q] = ldg(rows + p);
-        colind[q] = ldg(cols + p);
+        colind[q] = c;
         copy_val<ES>(out_val, q, val, p);
     }
 }
