@@ -149,3 +149,23 @@ def test_spgemm_handle_validation():
         J.prepare(be, J.SpGEMMOp, A, A, beta=1.0)
     with pytest.raises(J.IncompatibleExtents):
         J.prepare(be, J.SpGEMMOp, A, A)
+
+
+def test_conversion_and_selector_host_checks():
+    """Host-side refusals that come before any device work: conversions the
+    backend does not run, and a ShiftedDiag tensor whose shifted diagonal
+    leaves its columns."""
+    bsr = J.bsr_tensor(torch.zeros(3, dtype=torch.int32), torch.zeros(0, dtype=torch.int32),
+                       torch.zeros(0, dtype=torch.float32), (4, 4), (2, 2), origin=0)
+    with pytest.raises(J.UnsupportedFormat):
+        J.convert_format(bsr, J.Formats.CSC)
+    csr = J.csr_tensor(torch.zeros(4, dtype=torch.int32), torch.zeros(0, dtype=torch.int32),
+                       torch.zeros(0, dtype=torch.float64), (3, 3), origin=0)
+    with pytest.raises(J.UnsupportedFormat):
+        J.convert_format(csr, J.Formats.DCSR)
+    S = J.shifted_diag_tensor(torch.float64, 4, 5, shift=2)
+    with pytest.raises(J.IncompatibleExtents):
+        J.execute(J.SpMVOp, S, torch.zeros(5, dtype=torch.float64), torch.zeros(4, dtype=torch.float64),
+                  backend=J.B200Backend())
+    d1 = J.Formats.DensedRight(1)
+    assert J.supports_backend(J.B200Backend(), J.SpMVOp(S.format, d1, d1))
