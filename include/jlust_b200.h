@@ -273,7 +273,9 @@ JLB_API int jlb_exclusive_scan_i32(void *stream, int64_t n, const int32_t *count
  * make the first call on each device before any stream capture.  All calls
  * share the one array: calls that may run concurrently on the GPU (other
  * streams, other host threads) race and must be serialised by the caller.
- * Same result and semantics as jlb_exclusive_scan_i32; allocates nothing. */
+ * Same result and semantics as jlb_exclusive_scan_i32; allocates nothing.
+ * n = 0 only writes out[0] = idx_base, by a kernel on the stream. */
+#define JLB_SCAN_NOALLOC_MAX_N 33554432 /* 8192 tiles of 4096 counts */
 JLB_API int jlb_exclusive_scan_i32_noalloc(void *stream, int64_t n, const int32_t *counts,
                                            int32_t *out, int idx_base);
 

@@ -172,8 +172,6 @@ def _patch_buffers(dev, patches):
     if buf is None:
         if len(_PATCHES) >= 256:      # bounded: distinct selector shapes are few
             _PATCHES.clear()
-        if len(_PATCHES) >= 256:      # bounded: distinct selector shapes are few
-            _PATCHES.clear()
         rows = torch.tensor([v for p in patches for v in (p[0], p[1])], dtype=torch.int64)
         cols = torch.tensor([p[2] for p in patches], dtype=torch.int64)
         vals = torch.tensor([p[3] for p in patches], dtype=torch.float64)

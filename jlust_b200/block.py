@@ -26,7 +26,7 @@ from __future__ import annotations
 import numpy as np
 import torch
 
-from .errors import IncompatibleExtents, UnsupportedFormat
+from .errors import IncompatibleExtents, UnsupportedFormat, UnsupportedValueType
 from .tensor import USTensor, coordinates, csr_tensor, nonzeros, positions, ust
 
 
@@ -112,7 +112,8 @@ class _Graphed:
         if torch.cuda.is_current_stream_capturing():
             self.spmv(x, y)          # a capture the caller started records the launch
             return
-        key = (y.data_ptr(), x.data_ptr())
+        # a graph bakes in the buffers' addresses, element type and strides
+        key = (y.data_ptr(), x.data_ptr(), x.dtype, y.dtype, x.stride(), y.stride())
         g = self.graphs.get(key)
         if g is None:
             self.spmv(x, y)          # first use outside the graph, then capture
@@ -238,10 +239,14 @@ def _Compiled(A: "BlockSparseMatrix") -> _Assembled:
     return _Assembled(m, n, parts, A.dtype, dev, patches)
 
 
-def _vec(t, what):
+def _vec(t, what, dtype, op="BlockSpMV"):
+    """x or y of a block product: a contiguous vector of the matrix's value
+    type (the kernels read and write dtype-sized elements at unit stride)."""
     t = ust(t).val
-    if t.dim() != 1:
-        raise IncompatibleExtents(f"BlockSpMV: {what} must be a vector")
+    if t.dim() != 1 or (t.numel() > 1 and t.stride(0) != 1):
+        raise IncompatibleExtents(f"{op}: {what} must be a contiguous vector")
+    if t.dtype != dtype:
+        raise UnsupportedValueType(f"{op}: {what} has value type {t.dtype}, the matrix {dtype}")
     return t
 
 
@@ -250,7 +255,7 @@ def block_spmv(A: BlockSparseMatrix, x, y, backend=None):
     ext/CUDAExt/ops/block_mul.jl:231-306)."""
     from .backend import B200Backend, backend_execute
     from .ops import SpMVOp
-    x, y = _vec(x, "x"), _vec(y, "y")
+    x, y = _vec(x, "x", A.dtype), _vec(y, "y", A.dtype)
     m, n = A.shape
     if x.numel() != n or y.numel() != m:
         raise IncompatibleExtents(f"BlockSpMV: A is {m}x{n}, x has {x.numel()}, y has {y.numel()}")
@@ -333,9 +338,22 @@ class BlockBandedMatrix:
     (neg, pos) pair of n_off_rows[k-1] x n_cols CSR blocks shared by every
     transition or a list of T-k pairs.  Rows run period by period: period t's
     n_diag_rows diagonal rows, then for each k <= min(bw, T-t) its coupling
-    rows, which compute neg x_t + pos x_{t+k} (block_banded.jl:79-122)."""
+    rows, which compute neg x_t + pos x_{t+k} (block_banded.jl:79-122).
+
+    The reference's bw = 1 form `BlockBandedMatrix(diag, neg_off, pos_off, T,
+    n_diag_rows, n_off_rows, n_cols)` (src/block_banded.jl:56-62: one shared
+    coupling pair, n_off_rows an Int) is accepted too: it is recognised, as
+    Julia's dispatch does, by a coupling block in the second position."""
 
     def __init__(self, diags, off_diags, T, bw, n_diag_rows, n_off_rows, n_cols):
+        if isinstance(off_diags, USTensor):
+            # (diag, neg_off, pos_off, T, n_diag_rows, n_off_rows, n_cols)
+            neg, pos, T, n_diag_rows, n_off, n_cols = off_diags, T, bw, n_diag_rows, n_off_rows, n_cols
+            if not isinstance(pos, USTensor) or not isinstance(n_off, (int, np.integer)):
+                raise ValueError("BlockBandedMatrix(diag, neg_off, pos_off, T, n_diag_rows, "
+                                 "n_off_rows, n_cols): neg_off and pos_off must be USTensors "
+                                 "and n_off_rows an Int")
+            off_diags, bw, n_off_rows = [(neg, pos)], 1, [int(n_off)]
         if T < 1 or bw < 0 or len(off_diags) != bw or len(n_off_rows) != bw:
             raise ValueError("BlockBandedMatrix: need T >= 1 and bw levels of (neg, pos) blocks "
                              "and row counts")
@@ -366,6 +384,14 @@ class BlockBandedMatrix:
         for t in range(1, T):
             starts.append(starts[-1] + n_diag_rows + int(cum[min(bw, T - t)]))
         self.starts, self.cum_off = starts, cum
+        # one value type for every block (Base.eltype(M) is the diagonal's,
+        # src/block_banded.jl:72-75; the fused products read all blocks as it)
+        ts = {_values_dtype(d) for d in self.diags}
+        ts |= {nonzeros(b).dtype for pairs in self.off for pr in pairs for b in pr
+               if b.format.family != "ShiftedDiag"}
+        if len(ts) != 1:
+            raise ValueError(f"BlockBandedMatrix: mixed element types {sorted(map(str, ts))}")
+        self.dtype = ts.pop()
         self._compiled = None
 
     @property
@@ -396,6 +422,10 @@ class BlockBandedMatrix:
         return parts
 
 
+def _values_dtype(d):
+    return d.dtype if isinstance(d, BlockSparseMatrix) else nonzeros(d).dtype
+
+
 def _split_patches(parts):
     """Parts (key, row offset, column offset, block) split into CSR parts and
     selector patches, one per ShiftedDiag block (first row, last row, column
@@ -418,7 +448,7 @@ def bbm_spmv(M: BlockBandedMatrix, x, y):
     periodic kernel when one diagonal block and one coupling pair are shared
     (bw = 1), otherwise one assembled CSR; either replayed from a CUDA graph
     per buffer pair."""
-    x, y = _vec(x, "x"), _vec(y, "y")
+    x, y = _vec(x, "x", M.dtype, "BBMSpMV"), _vec(y, "y", M.dtype, "BBMSpMV")
     m, n = M.shape
     if x.numel() != n or y.numel() != m:
         raise IncompatibleExtents(f"BBMSpMV: M is {m}x{n}, x has {x.numel()}, y has {y.numel()}")

@@ -158,6 +158,8 @@ scan_tiles_final(int64_t n, const int32_t *counts, int32_t *out, const int64_t *
     if (blockIdx.x == 0 && threadIdx.x == 0) out[0] = base;
 }
 
+__global__ void scan_write_base(int32_t *out, int base) { out[0] = base; }
+
 size_t scan_ws(int64_t n) { return (size_t)(ceil_div(n > 0 ? n : 1, kScanTile) * sizeof(int64_t)); }
 
 int scan(cudaStream_t st, int64_t n, const int32_t *counts, int32_t *out, int base, void *ws,
@@ -165,9 +167,10 @@ int scan(cudaStream_t st, int64_t n, const int32_t *counts, int32_t *out, int ba
     if (ws_bytes < scan_ws(n) || (!ws && n > 0))
         return fail(JLB_ERR_WORKSPACE, "scan workspace %zu < %zu bytes", ws_bytes, scan_ws(n));
     if (n == 0) {
-        JLB_CUDA(cudaMemcpyAsync(out, &base, sizeof(int32_t), cudaMemcpyHostToDevice, st));
-        // The host value must outlive the async copy.
-        JLB_CUDA(cudaStreamSynchronize(st));
+        // out[0] = base by a kernel on the stream: no host buffer to outlive
+        // an async copy, no synchronisation, and capturable in a graph.
+        scan_write_base<<<1, 1, 0, st>>>(out, base);
+        JLB_LAUNCH_CHECK("exclusive_scan (empty)");
         return ok();
     }
     const int64_t ntiles = ceil_div(n, kScanTile);
@@ -1054,7 +1057,8 @@ extern "C" JLB_API int jlb_coo_to_bsr_fill(void *stream, int dtype, int idx_base
 
 // ------------------------------------------------- allocation-free scan
 // A variant of jlb_exclusive_scan_i32 for callers that cannot allocate device
-// memory: its scratch (one int64 partial sum per 2048 counts) lives in this
+// memory: its scratch (one int64 partial sum per tile of kScanTile = 4096
+// counts) lives in this
 // file-scope device array instead of a caller workspace.  The array exists on
 // every GPU that loads the library, for the life of the process.
 namespace jlb {
@@ -1062,6 +1066,7 @@ namespace conv {
 
 constexpr int64_t kNoAllocTiles = 8192;                     // 64 KB of scratch
 constexpr int64_t kNoAllocMaxN = kNoAllocTiles * kScanTile; // 33,554,432 counts
+static_assert(kNoAllocMaxN == JLB_SCAN_NOALLOC_MAX_N, "header limit out of date");
 
 static __device__ __align__(256) int64_t g_scan_noalloc_sums[kNoAllocTiles];
 

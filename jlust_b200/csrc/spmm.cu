@@ -33,6 +33,8 @@
 // same storage-order sum.
 #include "common.cuh"
 
+#include <mutex>
+
 namespace jlb {
 
 JLB_DEFINE_DEV_ERROR(spmm)
@@ -478,19 +480,23 @@ constexpr int kLongSmem = kSlotBytes + kGroups * kChunkBytes + 2 * kScanRows * 4
 // returns the stream kernel's resident CTAs per SM times the SM count.
 template <typename T, bool kBeta>
 int prepare_kernels(int *grid_full) {
-    static int per_sm[64] = {0}, sms[64] = {0};
+    // one grid size per device, filled under a lock: two host threads making
+    // their first call at once both see either nothing or the whole entry
+    static int grid[64] = {0};
+    static std::mutex mu;
     int dev = 0;
     JLB_CUDA(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64) return fail(JLB_ERR_DEVICE_MISMATCH, "device ordinal %d", dev);
-    if (!per_sm[dev]) {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!grid[dev]) {
         JLB_CUDA(cudaFuncSetAttribute(spmm_stream<T, kBeta>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmem));
         JLB_CUDA(cudaFuncSetAttribute(spmm_long_rows<T, kBeta>, cudaFuncAttributeMaxDynamicSharedMemorySize, kLongSmem));
-        JLB_CUDA(cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev));
-        int p = 0;
+        int sms = 0, p = 0;
+        JLB_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
         JLB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&p, spmm_stream<T, kBeta>, kThreads, kStreamSmem));
-        per_sm[dev] = p < 1 ? 1 : p;
+        grid[dev] = (p < 1 ? 1 : p) * sms;
     }
-    *grid_full = per_sm[dev] * sms[dev];
+    *grid_full = grid[dev];
     return JLB_OK;
 }
 

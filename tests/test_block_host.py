@@ -113,3 +113,45 @@ def test_selector_patches_compile():
     for r0, r1, c0, pv in patches:
         D[np.arange(r0, r1 + 1), c0 + np.arange(r1 - r0 + 1)] += pv
     assert np.allclose(O.csr_patched_spmv(rp, ci, v, patches, x), D @ x, rtol=1e-14, atol=1e-14)
+
+
+def test_block_products_refuse_mismatched_vectors():
+    """x and y of the compiled block products must be contiguous vectors of
+    the matrix's value type: the kernels read and write value-sized elements
+    at unit stride, so a float32 x with a float64 matrix, or a strided view,
+    is refused before any device work."""
+    _, a = _blk(6, 5, 31)
+    _, b = _blk(6, 4, 32)
+    A = J.BlockSparseMatrix([[a, b]])
+    x64, y64 = torch.zeros(9, dtype=torch.float64), torch.zeros(6, dtype=torch.float64)
+    with pytest.raises(J.UnsupportedValueType):
+        J.mul(y64, A, torch.zeros(9, dtype=torch.float32))
+    with pytest.raises(J.UnsupportedValueType):
+        J.mul(torch.zeros(6, dtype=torch.float32), A, x64)
+    with pytest.raises(J.IncompatibleExtents, match="contiguous"):
+        J.mul(y64, A, torch.zeros(18, dtype=torch.float64)[::2])
+    M, *_ = _bbm_case()
+    m, n = M.shape
+    with pytest.raises(J.UnsupportedValueType):
+        J.mul(torch.zeros(m, dtype=torch.float64), M, torch.zeros(n, dtype=torch.float32))
+    with pytest.raises(J.IncompatibleExtents, match="contiguous"):
+        J.mul(torch.zeros(2 * m, dtype=torch.float64)[::2], M, torch.zeros(n, dtype=torch.float64))
+
+
+def test_bbm_bw1_constructor():
+    """The reference's bw = 1 form BlockBandedMatrix(diag, neg_off, pos_off,
+    T, n_diag_rows, n_off_rows, n_cols) (src/block_banded.jl:56-62) builds
+    the same matrix as the general form with one shared coupling pair."""
+    _, d = _blk(8, 6, 41)
+    _, neg = _blk(3, 6, 42)
+    _, pos = _blk(3, 6, 43)
+    M1 = J.BlockBandedMatrix(d, neg, pos, 4, 8, 3, 6)
+    M2 = J.BlockBandedMatrix(d, [(neg, pos)], 4, 1, 8, [3], 6)
+    assert M1.shape == M2.shape == (4 * 8 + 3 * 3, 24)
+    assert (M1.bw, M1.n_off_rows, M1.starts) == (M2.bw, M2.n_off_rows, M2.starts)
+    assert [(k, r, c) for k, r, c, _ in M1.parts()] == [(k, r, c) for k, r, c, _ in M2.parts()]
+    with pytest.raises(ValueError, match="n_off_rows an Int"):
+        J.BlockBandedMatrix(d, neg, pos, 4, 8, [3], 6)
+    _, f32 = _blk(3, 6, 44, dtype=np.float32)
+    with pytest.raises(ValueError, match="mixed element types"):
+        J.BlockBandedMatrix(d, neg, f32, 4, 8, 3, 6)

@@ -21,7 +21,18 @@ from jlust_b200 import _lib, errors
 
 pytestmark = pytest.mark.gpu
 
-MAX_N = 16384 * 2048
+
+
+def _header_limit() -> int:
+    """JLB_SCAN_NOALLOC_MAX_N as the public header states it."""
+    import os
+    import re
+    h = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include",
+                     "jlust_b200.h")
+    return int(re.search(r"#define JLB_SCAN_NOALLOC_MAX_N (\d+)", open(h).read()).group(1))
+
+
+MAX_N = _header_limit()
 
 
 def _stream():
@@ -77,3 +88,19 @@ def test_noalloc_scan_limits():
     # n = 0 writes just the origin
     got = _scan_noalloc(torch.empty(0, dtype=torch.int32, device="cuda:0"), 1)
     assert got.cpu().tolist() == [1]
+
+
+def test_noalloc_scan_empty_inside_capture():
+    """n = 0 writes out[0] with a kernel on the caller's stream (no host copy,
+    no synchronisation), so a call made while a stream is being captured
+    records into the graph; the replay writes the origin."""
+    _scan_noalloc(torch.empty(0, dtype=torch.int32, device="cuda:0"), 0)   # per-device set-up
+    out = torch.full((1,), -1, dtype=torch.int32, device="cuda:0")
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        _lib.check(_lib.load().jlb_exclusive_scan_i32_noalloc(
+            _stream(), 0, C.c_void_p(0), C.c_void_p(out.data_ptr()), 1))
+    assert out.cpu().tolist() == [-1]       # captured, not run
+    g.replay()
+    torch.cuda.synchronize()
+    assert out.cpu().tolist() == [1]
