@@ -1,8 +1,10 @@
 #!/usr/bin/env python
 """Benchmark of the JLUST hot path on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload laplacian|spmv1|spmm|sddmm|bsr|convert]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference|cusparse]
+                    [--workload laplacian|spmv1|spmm|sddmm|bsr|convert|scan|coo2csr|
+                                spmv_powerlaw|spmv_medium]
+                    [--extra auto|none]
 
 Default workload (the configuration the headline metric is quoted on): CSR
 SpMV fp64 on the 5-point Laplacian of a 4096 x 4096 grid, x <- A x, one step
@@ -16,13 +18,26 @@ the same metric through the public API with the step's input copied from
 pinned host memory and its result copied back inside the timed region;
 `roofline` relates the dominant kernel's algorithmic bytes per launch to the
 measured HBM copy bandwidth; `cpu_baseline` times the CPU restatement of the
-reference's path on this host's cores.  `--impl reference` times only that
-CPU path (rank 0; other ranks exit).
+reference's path on this host's cores (all of them, and one); `parity` checks
+the last timed step's output against that restatement.
+
+With the default workload the line also carries `workloads`: the other
+configurations measured the same way in the same process (cfg3 SpMM, cfg4
+SDDMM, cfg5 BSR SpMM, the CSR -> BSR conversion of the cfg5 matrix and the
+cfg2 row-pointer scan on one GPU; the sharded cfg3/cfg4/cfg5 on N GPUs).
+`--extra none` leaves them out.
+
+`--impl reference` times the CPU restatement of the reference's path (the
+reference is Julia; no Julia toolchain exists here) on the same workloads
+with every host thread (rank 0; other ranks exit).  `--impl cusparse` times
+cuSPARSE (the reference's default GPU library for SpMM and SDDMM) through
+torch.sparse on cfg2, cfg3 and cfg4, as a comparison point only.
 """
 from __future__ import annotations
 
 import argparse
 import datetime
+import gc
 import json
 import os
 import re
@@ -37,17 +52,21 @@ sys.path.insert(0, ROOT)
 import numpy as np  # noqa: E402
 
 METRIC = "SpMV/SpMM GFLOP/s and effective HBM GB/s (% roofline) at 1/2/4/8 B200"
+DATA = "synthetic (numpy PCG64, seeds of the configs)"
 
 
-def parse_args():
+def parse_args(argv=None):
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=200)
     p.add_argument("--warmup", type=int, default=5)
-    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--workload", default="laplacian",
-                   choices=["laplacian", "spmv1", "spmm", "sddmm", "bsr", "convert", "scan",
-                            "coo2csr"])
+    p.add_argument("--impl", choices=["ours", "reference", "cusparse"], default="ours")
+    p.add_argument("--workload", default="laplacian", choices=sorted(WORKLOADS))
+    p.add_argument("--extra", choices=["auto", "none"], default="auto",
+                   help="auto: with the default workload, also measure the other configurations "
+                        "(the `workloads` object); none: the headline workload only")
+    p.add_argument("--extra-steps", type=int, default=20,
+                   help="timed steps of each extra workload (at most --steps)")
     p.add_argument("--exchange", choices=["p2p", "halo", "allgather"], default="p2p",
                    help="p2p: halo fused into the SpMV kernel over NVLink (default); "
                         "halo: NCCL send/recv; allgather: NCCL all-gather of x")
@@ -55,9 +74,12 @@ def parse_args():
     p.add_argument("--l2-persist", type=int, default=1,
                    help="Laplacian: persisting L2 window over the local CSR: 1 = where the "
                         "set-aside holds half of it, 2 = always, 0 = never")
+    p.add_argument("--cpu-budget", type=float, default=5.0,
+                   help="seconds of CPU work per CPU-baseline leg (all cores, one core)")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
-    return p.parse_args()
+    p.add_argument("--no-parity", action="store_true")
+    return p.parse_args(argv)
 
 
 def env_int(name, default):
@@ -167,7 +189,7 @@ class Ctx:
         self.local = env_int("LOCAL_RANK", 0)
         self.args = args
         self.dist = None
-        if args.impl == "ours":
+        if args.impl in ("ours", "cusparse"):
             torch.cuda.set_device(self.local)
             self.device = torch.device("cuda", self.local)
             if self.world > 1:
@@ -225,31 +247,75 @@ def timed(ctx, fn, steps, stream, finish=None):
     return ctx.max_over_ranks(secs), clk.summary()
 
 
+# ----------------------------------------------------------------- parity --
+def tol_check(got, ref, bound, tol):
+    """Per element |got - ref| / bound (bound = sum of |terms|, from the fp64
+    restatement) and the normwise relative error (bench_suitesparse.jl:
+    263-264 form); both must be <= tol."""
+    got = np.asarray(got, dtype=np.float64).reshape(-1)
+    ref = np.asarray(ref, dtype=np.float64).reshape(-1)
+    bound = np.asarray(bound, dtype=np.float64).reshape(-1)
+    if got.size == 0:
+        return 0.0, 0.0
+    per = float(np.max(np.abs(got - ref) / (bound + 1e-300)))
+    nr = float(np.linalg.norm(ref))
+    norm = float(np.linalg.norm(got - ref) / nr) if nr > 0 else 0.0
+    return per, norm
+
+
+def exact_check(got, ref):
+    """Mismatching elements, comparing bits (NaNs match NaNs)."""
+    got, ref = np.asarray(got).reshape(-1), np.asarray(ref).reshape(-1)
+    if got.shape != ref.shape:
+        return max(got.size, ref.size)
+    if got.dtype.kind == "f":
+        bad = (got != ref) & ~(np.isnan(got) & np.isnan(ref))
+        return int(np.count_nonzero(bad))
+    return int(np.count_nonzero(got != ref))
+
+
+def exact_result(mismatches, checked):
+    return {"kind": "bit-exact", "mismatches": int(mismatches), "max_rel": 0.0 if not mismatches
+            else None, "pass": mismatches == 0, "checked": checked}
+
+
+def tol_result(per, norm, tol, checked, **extra):
+    return {"kind": "tol", "tol": tol, "max_rel": per, "normwise": norm,
+            "pass": bool(per <= tol and norm <= tol), "checked": checked, **extra}
+
+
 # ------------------------------------------------------------- workloads --
 class Laplacian:
     """Config 2: x <- A x on the 5-point Laplacian of a g x g grid, fp64."""
 
-    kernel = "spmv_rows"
-    dtype = "f64"
+    key, kernel, dtype, unit = "cfg2_laplacian", "spmv_rows", "f64", "GFLOP/s"
+    profile = "laplacian"
+    bound = "hbm"
 
-    def __init__(self, ctx):
+    def __init__(self, ctx, host_only=False):
+        from jlust_b200 import synth
+        self.ctx = ctx
+        g = ctx.args.grid
+        self.g, self.n = g, g * g
+        self.nnz_total = 5 * self.n - 4 * g
+        self.x0 = np.random.default_rng(1).uniform(-1.0, 1.0, size=self.n)
+        self.synth = synth
+        if host_only:
+            return
         import ctypes as C
 
         import torch
 
         import jlust_b200 as J
-        from jlust_b200 import _lib, synth
+        from jlust_b200 import _lib
         from jlust_b200 import dist as D
 
-        self.ctx, self.J, self.C, self._lib = ctx, J, C, _lib
-        g = ctx.args.grid
-        self.g, self.n = g, g * g
+        self.J, self.C, self._lib = J, C, _lib
         r0, r1 = D.partition_rows(self.n, ctx.world, ctx.rank, align=g)
         self.r0, self.r1, self.R = r0, r1, r1 - r0
         rp, ci, val = synth.laplacian_rows(g, r0, r1)
         lci = (ci.astype(np.int64) - (r0 - g)).astype(np.int32)
         self.nnz_local = int(rp[-1])
-        self.nnz_total = 5 * self.n - 4 * g
         dev = ctx.device
         # the local CSR in one allocation (row pointer | columns | values, 256-byte
         # aligned parts) so that one L2 access-policy window covers it
@@ -274,7 +340,6 @@ class Laplacian:
                 self.persisted = J.l2_persist(0, 0, device=dev)
         self.csr_bytes = tot
         self.A = J.csr_tensor(self.rowptr, self.colind, self.val, (self.R, self.R + 2 * g), origin=0)
-        self.x0 = np.random.default_rng(1).uniform(-1.0, 1.0, size=self.n)
         interior = D.interior_rows(rp, lci, self.R, g) if ctx.world > 1 else (0, self.R)
         self.p2p = ctx.world > 1 and ctx.args.exchange == "p2p"
         if self.p2p:
@@ -340,15 +405,35 @@ class Laplacian:
         return 12.0 * self.nnz_total + 4.0 * (self.n + 1) + 8.0 * (2 * self.n)
 
     def config(self):
-        return {"workload": f"cfg2: CSR SpMV fp64, 2D 5-point Laplacian {self.g}x{self.g} "
-                            f"(n={self.n}, nnz={self.nnz_total}), x <- A x per step",
-                "n": self.n, "nnz": self.nnz_total, "partition": f"rows/{self.ctx.world}",
-                "exchange": "none" if self.ctx.world == 1 else
-                ("halo fused into the SpMV kernel over NVLink peer memory" if self.p2p
-                 else self.ctx.args.exchange),
-                "l2": (f"per-rank CSR {self.csr_bytes} B under a persisting L2 window "
-                       f"({self.persisted} B set-aside), x and y not; no flush"
-                       if self.persisted else "inputs larger than L2, no flush")}
+        c = {"workload": f"cfg2: CSR SpMV fp64, 2D 5-point Laplacian {self.g}x{self.g} "
+                         f"(n={self.n}, nnz={self.nnz_total}), x <- A x per step",
+             "n": self.n, "nnz": self.nnz_total}
+        if not hasattr(self, "halo"):
+            return c
+        c.update({"partition": f"rows/{self.ctx.world}",
+                  "exchange": "none" if self.ctx.world == 1 else
+                  ("halo fused into the SpMV kernel over NVLink peer memory" if self.p2p
+                   else self.ctx.args.exchange),
+                  "l2": (f"per-rank CSR {self.csr_bytes} B under a persisting L2 window "
+                         f"({self.persisted} B set-aside), x and y not; no flush"
+                         if self.persisted else "inputs larger than L2, no flush")})
+        return c
+
+    # parity: after K steps from reset() the own rows hold A^K x0
+    def snapshot(self, k):
+        self.snap = (k, self.halo.own().cpu().numpy().copy())
+
+    def parity(self):
+        from oracle import oracle as O
+        k, got = self.snap
+        rp, ci, val = self.synth.laplacian_2d(self.g)
+        x = self.x0.copy()
+        for _ in range(k):
+            x = O.spmv(rp, ci, val, x)
+        bad = exact_check(got, x[self.r0:self.r1])
+        bad = int(self.ctx.sum_over_ranks(bad))
+        return exact_result(bad, f"x after the {k} timed steps (A^{k} x0, all {self.n} rows over "
+                                 f"{self.ctx.world} rank(s)) against the oracle's {k} iterations")
 
     # end to end through the public API: x from pinned host memory, y back to it
     def e2e_setup(self):
@@ -371,7 +456,7 @@ class Laplacian:
                           for lo, hi in self.chunks]
             self.s_in = torch.cuda.Stream(self.ctx.device)
             self.s_out = torch.cuda.Stream(self.ctx.device)
-            ev = lambda: [torch.cuda.Event() for _ in range(nch)]
+            ev = lambda: [torch.cuda.Event() for _ in range(nch)]  # noqa: E731
             self.ev_in, self.ev_done, self.ev_out = ev(), ev(), ev()
             for e in self.ev_out:
                 e.record(self.s_out)
@@ -428,39 +513,52 @@ class Laplacian:
         h.cur = 1 - h.cur
         self.hcur = 1 - self.hcur
 
-    # CPU restatement of the reference's path on this host's cores
-    def cpu_setup(self):
-        from jlust_b200 import synth
-        self.crp, self.cci, self.cval = synth.laplacian_2d(self.g)
-        self.cx = self.x0.copy()
-
-    def cpu_step(self):
+    # CPU restatement of the reference's path: whole iterations x <- A x while
+    # they fit the sample, else a prefix of the rows of one iteration
+    def cpu_work(self, frac):
         from oracle import oracle as O
-        self.cx = O.spmv(self.crp, self.cci, self.cval, self.cx)
+        if not hasattr(self, "crp"):
+            self.crp, self.cci, self.cval = self.synth.laplacian_2d(self.g)
+        if frac >= 1.0:
+            state = {"x": self.x0.copy()}
 
-    def cpu_sample(self):
-        return f"full iterations x <- A x of the {self.g}^2 Laplacian (fp64, oracle row order)"
+            def fn():
+                state["x"] = O.spmv(self.crp, self.cci, self.cval, state["x"])
+            return fn, 2.0 * self.nnz_total, (f"full iterations x <- A x of the {self.g}^2 "
+                                              "Laplacian (fp64, oracle row order)")
+        rows = max(self.g, int(self.n * frac) // self.g * self.g)
+        rp = self.crp[:rows + 1]
+
+        def fn():  # noqa: F811
+            O.spmv(rp, self.cci, self.cval, self.x0)
+        return fn, 2.0 * int(rp[-1]), f"rows [0, {rows}) of one iteration ({rows / self.n:.4f})"
 
 
 class Single:
-    """Base of the single-GPU workloads (configs 1, 3, 4, 5 and conversion)."""
+    """Base of the workloads other than the Laplacian.  Subclasses set
+    `host()` (the seeded host inputs), `setup()` (this rank's device data) and
+    the work model."""
 
     flush_l2 = False
     launches_per_step = 1
     bound = "hbm"
-
+    unit = "GFLOP/s"
     shardable = False
 
-    def __init__(self, ctx):
+    def __init__(self, ctx, host_only=False):
+        from jlust_b200 import synth
+        self.ctx, self.synth = ctx, synth
+        self.rank, self.world = ctx.rank, ctx.world
+        if not host_only and ctx.world > 1 and not self.shardable:
+            raise SystemExit(f"workload {self.profile} runs on one GPU")
+        self.host()
+        if host_only:
+            return
         import torch
 
         import jlust_b200 as J
-        from jlust_b200 import synth
-        if ctx.world > 1 and not self.shardable:
-            raise SystemExit(f"workload {ctx.args.workload} runs on one GPU")
-        self.ctx, self.J, self.synth, self.torch = ctx, J, synth, torch
+        self.J, self.torch = J, torch
         self.dev = ctx.device
-        self.rank, self.world = ctx.rank, ctx.world
         self.setup()
 
     def shard(self, rowptr):
@@ -479,6 +577,13 @@ class Single:
 
     def reset(self):
         pass
+
+    def close(self):
+        pass
+
+    def snapshot(self, k):
+        """Host copy of the last timed step's output (checked by parity())."""
+        self.snap = [t.cpu().numpy().copy() for t in self.e2e_out()]
 
     def e2e_setup(self):
         self.e2e_inputs = [t.cpu().pin_memory() for t in self.e2e_in()]
@@ -500,14 +605,16 @@ class Single:
 class SpMV1(Single):
     """Config 1: CSR SpMV fp64, n = 100,000, 10 uniform columns per row."""
 
-    kernel, dtype, flush_l2 = "spmv_rows", "f64", True
+    key, kernel, dtype, flush_l2, profile = "cfg1_spmv", "spmv_rows", "f64", True, "spmv1"
+
+    def host(self):
+        self.h = self.synth.config1()
+        rp = self.h[0]
+        self.nnz, self.m = int(rp[-1]), rp.shape[0] - 1
 
     def setup(self):
-        J = self.J
-        rp, ci, val, x = self.synth.config1()
-        self.h = (rp, ci, val, x)
-        self.nnz, self.m = int(rp[-1]), rp.shape[0] - 1
-        self.A = J.csr_tensor(self.d(rp), self.d(ci), self.d(val), (self.m, self.m), origin=0)
+        rp, ci, val, x = self.h
+        self.A = self.J.csr_tensor(self.d(rp), self.d(ci), self.d(val), (self.m, self.m), origin=0)
         self.x, self.y = self.d(x), self.torch.zeros(self.m, dtype=self.torch.float64, device=self.dev)
 
     def api_call(self):
@@ -529,35 +636,80 @@ class SpMV1(Single):
         return {"workload": f"cfg1: CSR SpMV fp64, n={self.m}, 10 nnz/row (nnz={self.nnz}), y = A x",
                 "l2": "256 MB buffer written between timed launches (inputs 14 MB < L2)"}
 
-    def cpu_setup(self):
-        pass
-
-    def cpu_step(self):
+    def parity(self):
         from oracle import oracle as O
         rp, ci, val, x = self.h
-        O.spmv(rp, ci, val, x)
+        return exact_result(exact_check(self.snap[0], O.spmv(rp, ci, val, x)), "all rows of y")
 
-    def cpu_sample(self):
-        return "full y = A x (fp64, oracle row order)"
+    def cpu_work(self, frac):
+        from oracle import oracle as O
+        rp, ci, val, x = self.h
+        rows = max(1, min(self.m, int(self.m * frac)))
+        rps = rp[:rows + 1]
+        return (lambda: O.spmv(rps, ci, val, x)), 2.0 * int(rps[-1]), \
+            f"rows [0, {rows}) of y = A x (fp64, oracle row order)"
+
+
+class SpMVRows(SpMV1):
+    """CSR SpMV fp64 on other row-length distributions (the choice of the
+    vector-per-row variants): `powerlaw` is the cfg3 pattern (Zipf(2) on
+    [1, 4096], 4M rows) with fp64 values; `medium` has 4M/8 rows of 40-200
+    uniform entries."""
+
+    flush_l2 = False
+
+    def host(self):
+        rng_seed = 12
+        if self.profile == "spmv_powerlaw":
+            rp, ci, _ = self.synth.power_law(4_194_304, 4_194_304, 2.0, 4096, seed=2)
+        else:
+            m = 524_288
+            rng = np.random.default_rng(rng_seed)
+            lens = rng.integers(40, 201, size=m)
+            rows = np.repeat(np.arange(m, dtype=np.int64), lens)
+            cols = rng.integers(0, m, size=rows.shape[0], dtype=np.int64)
+            rp, ci = self.synth.csr_from_rows_cols(m, m, rows, cols)
+        rng = np.random.default_rng(rng_seed + 1)
+        m = rp.shape[0] - 1
+        val = rng.uniform(-1.0, 1.0, size=ci.shape[0])
+        x = rng.uniform(-1.0, 1.0, size=m)
+        self.h = (rp, ci, val, x)
+        self.nnz, self.m = int(rp[-1]), m
+
+    def config(self):
+        what = ("power-law (the cfg3 pattern, Zipf 2.0 on [1,4096])" if self.profile == "spmv_powerlaw"
+                else "medium rows (40-200 uniform entries)")
+        return {"workload": f"CSR SpMV fp64, {what}, n={self.m}, nnz={self.nnz}, y = A x",
+                "l2": "inputs larger than L2"}
+
+
+class SpMVPowerLaw(SpMVRows):
+    key, profile = "spmv_powerlaw", "spmv_powerlaw"
+
+
+class SpMVMedium(SpMVRows):
+    key, profile = "spmv_medium", "spmv_medium"
 
 
 class SpMM(Single):
     """Config 3: CSR SpMM fp32, power-law A (4M x 4M), B 4M x 64 row-major."""
 
-    kernel, dtype, shardable = "spmm_stream", "f32", True
+    key, kernel, dtype, shardable, profile = "cfg3_spmm", "spmm_stream", "f32", True, "spmm"
     launches_per_step = 2   # spmm_stream + spmm_long_rows
 
+    def host(self):
+        self.h = self.synth.config3()
+        rp, _, _, B = self.h
+        self.nnz, self.m, self.k = int(rp[-1]), rp.shape[0] - 1, B.shape[1]
+
     def setup(self):
-        J = self.J
-        rp, ci, val, B = self.synth.config3()
-        self.h = (rp, ci, val, B)
-        self.nnz, self.m = int(rp[-1]), rp.shape[0] - 1
-        self.k = B.shape[1]
+        rp, ci, val, B = self.h
         # rows sharded by rows + entries; B replicated on every rank (copied once, untimed)
         r0, r1, lrp = self.shard(rp)
+        self.rows = (r0, r1)
         p0, p1 = int(rp[r0]), int(rp[r1])
-        self.A = J.csr_tensor(self.d(lrp), self.d(ci[p0:p1]), self.d(val[p0:p1]), (r1 - r0, self.m),
-                              origin=0)
+        self.A = self.J.csr_tensor(self.d(lrp), self.d(ci[p0:p1]), self.d(val[p0:p1]),
+                                   (r1 - r0, self.m), origin=0)
         self.B = self.d(B)
         self.C = self.torch.zeros(r1 - r0, self.k, dtype=self.torch.float32, device=self.dev)
 
@@ -585,34 +737,60 @@ class SpMM(Single):
                 "partition": f"rows/{self.world} (balanced by rows + entries), B replicated",
                 "l2": "inputs larger than L2"}
 
-    def cpu_setup(self):
-        pass
-
-    def cpu_step(self):
+    def parity(self):
+        """Rows of at most 256 entries bit-exact against the fp32 restatement;
+        longer rows (summed in segments) within 1e-5 of the fp64 one."""
         from oracle import oracle as O
         rp, ci, val, B = self.h
-        O.spmm(rp, ci, val, B)
+        r0, r1 = self.rows
+        p0, p1 = int(rp[r0]), int(rp[r1])
+        lrp = (rp[r0:r1 + 1].astype(np.int64) - p0).astype(np.int32)
+        got = self.snap[0]
+        lens = np.diff(lrp)
+        short = lens <= 256
+        want = O.spmm(lrp, ci[p0:p1], val[p0:p1], B)
+        bad = exact_check(got[short], want[short])
+        longr = np.nonzero(~short)[0]
+        sub_rp = np.concatenate([[0], np.cumsum(lens[longr])]).astype(np.int32)
+        idx = np.concatenate([np.arange(lrp[r], lrp[r + 1]) for r in longr]) + p0 \
+            if longr.size else np.zeros(0, np.int64)
+        ref, bound = O.spmm_ref64(sub_rp, ci[idx], val[idx], B)
+        per, norm = tol_check(got[longr], ref, bound, 1e-5)
+        per = self.ctx.max_over_ranks(per)
+        norm = self.ctx.max_over_ranks(norm)
+        bad = int(self.ctx.sum_over_ranks(bad))
+        r = tol_result(per, norm, 1e-5, f"all {self.m} rows of C")
+        r["bit_exact_rows_le_256"] = {"mismatches": bad, "pass": bad == 0}
+        r["pass"] = r["pass"] and bad == 0
+        return r
 
-    def cpu_sample(self):
-        return "full C = A B (fp32, Tiled per-(row,col) order)"
+    def cpu_work(self, frac):
+        from oracle import oracle as O
+        rp, ci, val, B = self.h
+        rows = max(1, min(self.m, int(self.m * frac)))
+        rps = rp[:rows + 1]
+        return (lambda: O.spmm(rps, ci, val, B)), 2.0 * int(rps[-1]) * self.k, \
+            f"rows [0, {rows}) of C = A B (fp32, Tiled per-(row,col) order)"
 
 
 class SDDMM(Single):
     """Config 4: SDDMM fp32, 1M x 1M pattern with 32 entries per row, K = 128."""
 
-    kernel, dtype, shardable = "sddmm_fast", "f32", True
+    key, kernel, dtype, shardable, profile = "cfg4_sddmm", "sddmm_fast", "f32", True, "sddmm"
+
+    def host(self):
+        self.h = self.synth.config4()
+        rp, _, A, _, _ = self.h
+        self.nnz, self.m, self.K = int(rp[-1]), rp.shape[0] - 1, A.shape[1]
 
     def setup(self):
-        J = self.J
-        rp, ci, A, B, S = self.synth.config4()
-        self.h = (rp, ci, A, B, S)
-        self.nnz, self.m = int(rp[-1]), rp.shape[0] - 1
-        self.K = A.shape[1]
+        rp, ci, A, B, S = self.h
         r0, r1, lrp = self.shard(rp)
+        self.rows = (r0, r1)
         p0, p1 = int(rp[r0]), int(rp[r1])
         self.S = self.d(S[p0:p1])
-        self.Cs = J.csr_tensor(self.d(lrp), self.d(ci[p0:p1]), self.S.clone(), (r1 - r0, self.m),
-                               origin=0)
+        self.Cs = self.J.csr_tensor(self.d(lrp), self.d(ci[p0:p1]), self.S.clone(),
+                                    (r1 - r0, self.m), origin=0)
         self.A, self.Bt = self.d(A[r0:r1]), self.d(B)
 
     def api_call(self):
@@ -628,49 +806,64 @@ class SDDMM(Single):
     def flops(self):
         return 2.0 * self.nnz * self.K
 
-    def bytes(self):  # gather model: A rows once, one B row per entry
+    def gather_bytes(self):  # A rows once, one B row per entry
         return 4.0 * self.K * (self.m + self.nnz) + 4.0 * self.nnz + 4.0 * (self.m + 1) + 8.0 * self.nnz
+
+    def bytes(self):
+        # the bytes that bound the kernel: its DRAM traffic (ncu); a fifth of
+        # the gathered B rows hit L2, so the gather model overstates the bytes
+        t = profile_traffic("sddmm_fast_sddmm")
+        return t if t is not None else self.gather_bytes()
 
     def config(self):
         return {"workload": f"cfg4: SDDMM fp32, pattern {self.m}x{self.m} with 32 uniform "
                             f"entries/row (nnz={self.nnz}), A, B {self.m}x{self.K} N(0,1), "
                             "out = dot(A_i, B_j) * S_ij",
-                "bytes_model": "gather (512 m + 512 nnz + 12 nnz + 4 (m+1))",
+                "bytes_model": "DRAM bytes per launch measured by ncu (profiles/sddmm_fast_sddmm.md)",
+                "gather_bytes": self.gather_bytes(),
                 "partition": f"pattern rows/{self.world}, A rows sharded, B replicated",
                 "l2": "inputs larger than L2"}
 
-    def cpu_setup(self):
-        pass
-
-    def cpu_step(self):
+    def parity(self):
         from oracle import oracle as O
         rp, ci, A, B, S = self.h
-        rows = self.m // 16
-        O.sddmm(rp[:rows + 1], ci, A, B.T, S, S=S, mode=1)
+        r0, r1 = self.rows
+        p0, p1 = int(rp[r0]), int(rp[r1])
+        lrp = (rp[r0:r1 + 1].astype(np.int64) - p0).astype(np.int32)
+        ref, bound = O.sddmm_ref64(lrp, ci[p0:p1], A[r0:r1], B.T, S=S[p0:p1], mode=1)
+        per, norm = tol_check(self.snap[0], ref, bound, 1e-5)
+        return tol_result(self.ctx.max_over_ranks(per), self.ctx.max_over_ranks(norm), 1e-5,
+                          f"all {self.nnz} sampled entries")
 
-    def cpu_flops(self):
-        return 2.0 * int(self.h[0][self.m // 16]) * self.K
-
-    def cpu_sample(self):
-        return "the first 1/16 of the pattern rows per step (fp32, sequential K loop)"
+    def cpu_work(self, frac):
+        from oracle import oracle as O
+        rp, ci, A, B, S = self.h
+        rows = max(1, min(self.m, int(self.m * frac)))
+        rps = rp[:rows + 1]
+        Ss = S[:int(rps[-1])]
+        return (lambda: O.sddmm(rps, ci, A, B.T, Ss, S=Ss, mode=1)), 2.0 * int(rps[-1]) * self.K, \
+            f"pattern rows [0, {rows}) (fp32, sequential K loop)"
 
 
 class BSR(Single):
     """Config 5: BSR SpMM bf16 -> fp32, 65,536^2 with 64x64 blocks, band +-8 + 2%."""
 
-    kernel, dtype, bound, shardable = "bsr_spmm_tc", "bf16 in, f32 accumulate", "tensor", True
+    key, kernel, dtype, bound, shardable, profile = ("cfg5_bsr", "bsr_spmm_tc",
+                                                     "bf16 in, f32 accumulate", "tensor", True, "bsr")
+
+    def host(self):
+        self.h = self.synth.config5()
+        bp, bc, _, B = self.h
+        self.nnzb, self.mb, self.N = bc.shape[0], bp.shape[0] - 1, B.shape[1]
 
     def setup(self):
-        J = self.J
-        bp, bc, bv, B = self.synth.config5()
-        self.h = (bp, bc, bv, B)
-        self.nnzb, self.mb = bc.shape[0], bp.shape[0] - 1
-        self.N = B.shape[1]
+        bp, bc, bv, B = self.h
         n = self.mb * 64
         I0, I1, lbp = self.shard(bp)
+        self.brows = (I0, I1)
         q0, q1 = int(bp[I0]), int(bp[I1])
-        self.A = J.bsr_tensor(self.d(lbp), self.d(bc[q0:q1]), self.bf(bv[q0 * 4096:q1 * 4096]),
-                              ((I1 - I0) * 64, n), (64, 64), origin=0)
+        self.A = self.J.bsr_tensor(self.d(lbp), self.d(bc[q0:q1]), self.bf(bv[q0 * 4096:q1 * 4096]),
+                                   ((I1 - I0) * 64, n), (64, 64), origin=0)
         self.B = self.bf(B)
         self.C = self.torch.zeros((I1 - I0) * 64, self.N, dtype=self.torch.float32, device=self.dev)
 
@@ -695,38 +888,51 @@ class BSR(Single):
                             f"blocks, band +-8 + 2% off-band (nnzb={self.nnzb}), B "
                             f"{self.mb * 64}x{self.N} bf16 row-major",
                 "partition": f"block rows/{self.world} (balanced by rows + blocks), B replicated",
-                "l2": "A values (311 MB) larger than L2; B (33.5 MB) L2-resident by design"}
+                "l2": "A values (311 MB) larger than L2; B (33.5 MB) L2-resident by design",
+                "parity_note": "BSR values are pinned by no reference vector (the reference has "
+                               "no working BSR SpMM); the check is against the fp64 restatement "
+                               "of its block-SpMM loop"}
 
-    def cpu_setup(self):
-        pass
-
-    def cpu_step(self):
+    def parity(self):
         from oracle import oracle as O
         bp, bc, bv, B = self.h
-        rows = self.mb // 16
-        O.bsr_spmm(bp[:rows + 1], bc, bv, B)
+        I0, I1 = self.brows
+        q0 = int(bp[I0])
+        lbp = (bp[I0:I1 + 1].astype(np.int64) - q0).astype(np.int32)
+        ref, bound = O.bsr_spmm_ref64(lbp, bc[q0:], bv[q0 * 4096:], B)
+        per, norm = tol_check(self.snap[0], ref, bound, 1e-5)
+        return tol_result(self.ctx.max_over_ranks(per), self.ctx.max_over_ranks(norm), 1e-5,
+                          f"all {self.mb * 64} x {self.N} entries of C against the fp64 "
+                          "restatement (no reference vector pins BSR values)")
 
-    def cpu_flops(self):
-        return 2.0 * int(self.h[0][self.mb // 16]) * 64 * 64 * self.N
-
-    def cpu_sample(self):
-        return "the first 1/16 of the block rows per step (fp32, fused-loop order)"
+    def cpu_work(self, frac):
+        from oracle import oracle as O
+        bp, bc, bv, B = self.h
+        rows = max(1, min(self.mb, int(self.mb * frac)))
+        bps = bp[:rows + 1]
+        return (lambda: O.bsr_spmm(bps, bc, bv, B)), 2.0 * int(bps[-1]) * 64 * 64 * self.N, \
+            f"block rows [0, {rows}) (fp32, fused-loop order)"
 
 
 class Convert(Single):
     """CSR -> BSRRight((64, 64)) of the config-5 matrix (bf16 values)."""
 
-    kernel, dtype = "fill_blocks", "bf16 values, int32 indices"
+    key, kernel, dtype, profile, unit = ("csr2bsr", "fill_blocks", "bf16 values, int32 indices",
+                                         "convert", "Gentries/s")
+    launches_per_step = 2
 
-    def setup(self):
-        J = self.J
+    def host(self):
         bp, bc, bv, _ = self.synth.config5(N=64)
+        self.src = (bp, bc, bv)
         rp, ci, vals = self.synth.bsr_to_csr(bp, bc, bv, 64, bp.shape[0] - 1)
         self.h = (rp, ci, vals)
         self.m = rp.shape[0] - 1
         self.nnz = int(rp[-1])
         self.nnzb, self.mb = bc.shape[0], bp.shape[0] - 1
-        self.A = J.csr_tensor(self.d(rp), self.d(ci), self.bf(vals), (self.m, self.m), origin=0)
+
+    def setup(self):
+        rp, ci, vals = self.h
+        self.A = self.J.csr_tensor(self.d(rp), self.d(ci), self.bf(vals), (self.m, self.m), origin=0)
 
     def api_call(self):
         self.out = self.J.convert_format(self.A, self.J.Formats.BSRRight((64, 64)))
@@ -743,7 +949,12 @@ class Convert(Single):
         self.api_call()
         self.hout.copy_(self.out.val, non_blocking=True)
 
-    def flops(self):  # reported as entries converted per second (GFLOP/s field = Gentries/s)
+    def snapshot(self, k):
+        J = self.J
+        self.snap = (J.positions(self.out, 2).cpu().numpy(), J.coordinates(self.out, 2).cpu().numpy(),
+                     self.out.val.view(self.torch.int16).cpu().numpy().view(np.uint16))
+
+    def flops(self):  # reported as entries converted per second
         return float(self.nnz)
 
     def bytes(self):
@@ -755,20 +966,31 @@ class Convert(Single):
                             f"nnzb={self.nnzb}), count + fill (host sync between)",
                 "value_unit_note": "value = G stored entries converted per second"}
 
-    def cpu_setup(self):
-        pass
+    def parity(self):
+        """Byte-exact twice: the whole output against the BSR the CSR was
+        expanded from (an explicit zero comes back as +0 padding), and the
+        first 1/32 of the block rows against the oracle's composer."""
+        from oracle import oracle as O
+        bp, bc, bv = self.src
+        gp, gc, gv = self.snap
+        want_v = np.where((bv & 0x7FFF) == 0, np.uint16(0), bv)
+        bad = exact_check(gp, bp) + exact_check(gc, bc) + exact_check(gv, want_v)
+        rp, ci, vals = self.h
+        rows = (self.mb // 32) * 64
+        op, oc, ov = O.csr_to_bsr(rows, self.m, rp[:rows + 1], ci, vals, 64, 64)
+        nb = int(op[-1])
+        bad_o = exact_check(gp[:rows // 64 + 1], op) + exact_check(gc[:nb], oc) + \
+            exact_check(gv[:nb * 4096], ov)
+        return exact_result(bad + bad_o, f"block row pointer, block columns and all {self.nnzb} "
+                                         "tiles against the source BSR; block rows [0, "
+                                         f"{rows // 64}) also against the oracle composer")
 
-    def cpu_step(self):
+    def cpu_work(self, frac):
         from oracle import oracle as O
         rp, ci, vals = self.h
-        rows = self.m // 64
-        O.csr_to_bsr(rows, self.m, rp[:rows + 1], ci, vals, 64, 64)
-
-    def cpu_flops(self):
-        return float(self.h[0][self.m // 64])
-
-    def cpu_sample(self):
-        return "the first 1/64 of the rows per step (single-threaded composer)"
+        rows = max(64, int(self.m * frac) // 64 * 64)
+        return (lambda: O.csr_to_bsr(rows, self.m, rp[:rows + 1], ci, vals, 64, 64)), \
+            float(rp[rows]), f"rows [0, {rows}) (the composer is single-threaded)"
 
 
 class Scan(Single):
@@ -776,17 +998,20 @@ class Scan(Single):
     row lengths (int32) into its row pointer, through the C-ABI with buffers
     allocated once."""
 
-    kernel, dtype, flush_l2 = "scan_tiles_final", "int32", True
+    key, kernel, dtype, flush_l2, profile, unit = ("scan", "scan_tiles_final", "int32", True,
+                                                   "scan", "Gcounts/s")
     launches_per_step = 3
+
+    def host(self):
+        rp, _, _ = self.synth.laplacian_2d(4096)
+        self.h = np.diff(rp).astype(np.int32)
+        self.n = self.h.shape[0]
 
     def setup(self):
         import ctypes as C
 
         from jlust_b200 import _lib
         from jlust_b200.backend import _stream
-        rp, _, _ = self.synth.laplacian_2d(4096)
-        self.h = np.diff(rp).astype(np.int32)
-        self.n = self.h.shape[0]
         self.counts = self.d(self.h)
         self.out = self.torch.empty(self.n + 1, dtype=self.torch.int32, device=self.dev)
         self.wsb = _lib.load().jlb_scan_workspace_size(self.n)
@@ -809,6 +1034,9 @@ class Scan(Single):
         out = self.J.exclusive_scan(self.counts)          # the public call (allocates)
         self.hout.copy_(out, non_blocking=True)
 
+    def snapshot(self, k):
+        self.snap = [self.out.cpu().numpy()]
+
     def flops(self):  # reported as counts scanned per second
         return float(self.n)
 
@@ -821,32 +1049,37 @@ class Scan(Single):
                 "l2": "256 MB buffer written between timed launches (67 MB of counts < L2)",
                 "value_unit_note": "value = G counts scanned per second"}
 
-    def cpu_setup(self):
-        pass
+    def parity(self):
+        want = np.concatenate([[0], np.cumsum(self.h, dtype=np.int64)]).astype(np.int32)
+        return exact_result(exact_check(self.snap[0], want), f"all {self.n + 1} row pointers")
 
-    def cpu_step(self):
+    def cpu_work(self, frac):
         from oracle import oracle as O
-        O.exclusive_scan(self.h)
-
-    def cpu_sample(self):
-        return "full scan (single-threaded C loop)"
+        k = max(1, min(self.n, int(self.n * frac)))
+        c = self.h[:k]
+        return (lambda: O.exclusive_scan(c)), float(k), \
+            f"counts [0, {k}) (single-threaded C loop)"
 
 
 class CooToCsr(Single):
     """COO -> CSR of the cfg2 Laplacian (its 83.9 M fp64 entries given as
     row-ordered COO) through convert_format: count, host read of nnz, fill."""
 
-    kernel, dtype = "coo_keep", "f64 values, int32 indices"
+    key, kernel, dtype, profile, unit = ("coo2csr", "coo_keep", "f64 values, int32 indices",
+                                         "coo2csr", "Gentries/s")
     launches_per_step = 7          # keep, scan (3), row pointer fill and write, emit
 
-    def setup(self):
-        J = self.J
+    def host(self):
         rp, ci, val, _ = self.synth.config2(g=4096)
         self.m = rp.shape[0] - 1
         self.nnz = int(rp[-1])
         rows = np.repeat(np.arange(self.m, dtype=np.int32), np.diff(rp))
         self.h = (rows, ci, val)
-        self.A = J.coo_tensor(self.d(rows), self.d(ci), self.d(val), (self.m, self.m), origin=0)
+        self.csr = (rp, ci, val)
+
+    def setup(self):
+        rows, ci, val = self.h
+        self.A = self.J.coo_tensor(self.d(rows), self.d(ci), self.d(val), (self.m, self.m), origin=0)
 
     def api_call(self):
         self.out = self.J.convert_format(self.A, self.J.Formats.CSR)
@@ -863,6 +1096,11 @@ class CooToCsr(Single):
         self.api_call()
         self.hout.copy_(self.out.val, non_blocking=True)
 
+    def snapshot(self, k):
+        J = self.J
+        self.snap = (J.positions(self.out, 2).cpu().numpy(), J.coordinates(self.out, 2).cpu().numpy(),
+                     self.out.val.cpu().numpy())
+
     def flops(self):  # reported as entries converted per second
         return float(self.nnz)
 
@@ -874,33 +1112,29 @@ class CooToCsr(Single):
                             "fp64), count + host read + fill",
                 "value_unit_note": "value = G entries converted per second"}
 
-    def cpu_setup(self):
-        pass
+    def parity(self):
+        rp, ci, val = self.csr
+        bad = sum(exact_check(g, w) for g, w in zip(self.snap, (rp, ci, val)))
+        return exact_result(bad, "row pointer, columns and values against the CSR the COO was "
+                                 "expanded from (the composer keeps a row-ordered source's order)")
 
-    def cpu_step(self):
+    def cpu_work(self, frac):
         from oracle import oracle as O
         rows, ci, val = self.h
-        k = self.nnz // 16
-        O.coo_to_csr(self.m, self.m, rows[:k], ci[:k], val[:k])
-
-    def cpu_flops(self):
-        return float(self.nnz // 16)
-
-    def cpu_sample(self):
-        return "the first 1/16 of the entries per step (vectorised numpy composer)"
+        k = max(1, min(self.nnz, int(self.nnz * frac)))
+        return (lambda: O.coo_to_csr(self.m, self.m, rows[:k], ci[:k], val[:k])), float(k), \
+            f"entries [0, {k}) (vectorised numpy composer)"
 
 
 WORKLOADS = {"laplacian": Laplacian, "spmv1": SpMV1, "spmm": SpMM, "sddmm": SDDMM, "bsr": BSR,
-             "convert": Convert, "scan": Scan, "coo2csr": CooToCsr}
+             "convert": Convert, "scan": Scan, "coo2csr": CooToCsr,
+             "spmv_powerlaw": SpMVPowerLaw, "spmv_medium": SpMVMedium}
+
+# measured beside the headline (one GPU: all; N GPUs: the sharded ones)
+EXTRA = ["spmm", "sddmm", "bsr", "convert", "scan"]
 
 
 # ------------------------------------------------------------------- arms --
-def unit_of(W):
-    if isinstance(W, Scan):
-        return "Gcounts/s"
-    return "Gentries/s" if isinstance(W, (Convert, CooToCsr)) else "GFLOP/s"
-
-
 def timed_flushed(ctx, fn, steps, stream):
     """Like timed(), for inputs smaller than L2: a 256 MB buffer is written
     before every launch and only the launches are timed (CUDA events around
@@ -923,9 +1157,9 @@ def timed_flushed(ctx, fn, steps, stream):
     return ctx.max_over_ranks(secs), clk.summary()
 
 
-def cpu_time(step, flops_per_step, min_steps=2, max_steps=20, budget_s=20.0):
+def cpu_time(step, work_per_step, min_steps=2, max_steps=20, budget_s=20.0):
     """Times `step` on the host: one untimed call, then up to max_steps calls
-    or budget_s seconds.  Returns (GFLOP/s, steps timed)."""
+    or budget_s seconds.  Returns (G units/s, steps timed)."""
     step()
     t0 = time.perf_counter()
     k = 0
@@ -933,20 +1167,65 @@ def cpu_time(step, flops_per_step, min_steps=2, max_steps=20, budget_s=20.0):
         step()
         k += 1
     dt = time.perf_counter() - t0
-    return flops_per_step * k / dt / 1e9, k
+    return work_per_step * k / dt / 1e9, k
 
 
-def run_ours(args):
-    ctx = Ctx(args)
+def sample_frac(W, step_s, frac0=1.0 / 256):
+    """The fraction of the workload whose CPU step takes about step_s seconds
+    (a power of two, at most 1): one calibration call at frac0."""
+    fn, _, _ = W.cpu_work(frac0)
+    t0 = time.perf_counter()
+    fn()
+    t = max(time.perf_counter() - t0, 1e-4)
+    frac = frac0 * step_s / t
+    if frac >= 1.0:
+        return 1.0
+    return max(frac0, 2.0 ** np.floor(np.log2(frac)))
+
+
+def cpu_leg(W, threads, budget_s):
+    """The CPU restatement of the reference's path on `threads` host threads,
+    over a sample of W sized to the budget."""
+    from oracle import oracle as O
+    O.set_threads(threads)
+    try:
+        frac = sample_frac(W, budget_s / 4)
+        fn, work, desc = W.cpu_work(frac)
+        v, k = cpu_time(fn, work, min_steps=2, max_steps=20, budget_s=budget_s)
+    finally:
+        O.set_threads(O.max_threads())
+    return round(v, 4), k, desc
+
+
+def cpu_baseline(W, budget_s):
+    from oracle import oracle as O
+    cores = O.max_threads()
+    v, k, desc = cpu_leg(W, cores, budget_s)
+    v1, k1, desc1 = cpu_leg(W, 1, budget_s) if cores > 1 else (v, k, desc)
+    single = getattr(W, "profile", "") in ("convert", "scan")
+    return {"value": v, "unit": W.unit, "cores": 1 if single else cores, "kind": "port",
+            "sample": f"{k} steps, {desc}",
+            "single_thread": {"value": v1, "cores": 1, "sample": f"{k1} steps, {desc1}"},
+            "impl": "C restatement of JLUST's CPU path (oracle/oracle.c)"
+                    + (", sequential by construction" if single else ", OpenMP over rows")}
+
+
+def free_gpu(ctx):
+    gc.collect()
+    ctx.torch.cuda.synchronize(ctx.device)
+    ctx.torch.cuda.empty_cache()
+
+
+def measure(ctx, W, K, warmup, args):
+    """Times W on the GPU(s) and returns its record: value, roofline, e2e,
+    cpu_baseline (rank 0, one GPU), parity, launches and clocks."""
     torch = ctx.torch
     import jlust_b200 as J
-    W = WORKLOADS[args.workload](ctx)
     stream = torch.cuda.current_stream(ctx.device)
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         W.step()
     J.device_status()
     W.reset()
-    K = args.steps
     if getattr(W, "flush_l2", False):
         secs, clocks = timed_flushed(ctx, W.step, K, stream)
     elif hasattr(W, "run_steps"):
@@ -955,12 +1234,13 @@ def run_ours(args):
     else:
         secs, clocks = timed(ctx, W.step, K, stream)
     J.device_status()
+    W.snapshot(K)
     value = W.flops() * K / secs / 1e9
     eff_gbs = W.bytes() * K / secs / 1e9
     pk = peaks()
     per_launch_s = secs / K
-    traffic = profile_traffic(f"spmv_rows_{args.workload}" if W.kernel == "halo_step"
-                              else f"{W.kernel}_{args.workload}")
+    prof = f"spmv_rows_{W.profile}" if W.kernel == "halo_step" else f"{W.kernel}_{W.profile}"
+    traffic = profile_traffic(prof)
     if traffic is not None and ctx.world > 1:
         traffic /= ctx.world        # the capture is of the 1-GPU launch; rows split evenly
     if getattr(W, "bound", "hbm") == "tensor":
@@ -978,9 +1258,22 @@ def run_ours(args):
                 "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
                 "traffic": traffic, "peak_source": pk["source"] + " (hbm_gbs, copy burst)",
                 "algorithmic_bytes_per_launch": W.bytes() / ctx.world}
+        if hasattr(W, "gather_bytes"):
+            g = (W.gather_bytes() / ctx.world) / per_launch_s / 1e9
+            roof["gather_model"] = {"achieved": round(g, 1), "frac": round(g / pk["hbm_gbs"], 4),
+                                    "note": "gather model (every B row fetched from DRAM); "
+                                            "overstates the bytes, an aside only"}
     if ctx.world > 1:
         roof["note"] = ("per GPU: the job's work / N over the step time (max over ranks)"
-                        + (", halo exchange included" if args.workload == "laplacian" else ""))
+                        + (", halo exchange included" if W.profile == "laplacian" else ""))
+
+    parity = None
+    if not args.no_parity:
+        from oracle import oracle as O
+        if ctx.world > 1:
+            O.set_threads(max(1, O.max_threads() // ctx.world))
+        parity = W.parity()
+        O.set_threads(O.max_threads())
 
     e2e = None
     if not args.no_e2e:
@@ -991,102 +1284,176 @@ def run_ours(args):
         if hasattr(W, "e2e_finish"):
             W.e2e_finish()
         J.device_status()
-        ctx.torch.cuda.synchronize(ctx.device)
+        torch.cuda.synchronize(ctx.device)
         e_secs, _ = timed(ctx, W.e2e_step, K, stream, getattr(W, "e2e_finish", None))
         J.device_status()
-        e2e = {"value": round(W.flops() * K / e_secs / 1e9, 3), "unit": unit_of(W),
+        e2e = {"value": round(W.flops() * K / e_secs / 1e9, 3), "unit": W.unit,
                "h2d_bytes_per_step": W.h2d, "d2h_bytes_per_step": W.d2h,
                "ms_per_step": round(e_secs * 1e3 / K, 4), "api": "jlust_b200.execute / convert_format"}
 
     cpu = None
     if ctx.rank == 0 and ctx.world == 1 and not args.no_cpu:
-        from oracle import oracle as O
-        W.cpu_setup()
-        cf = W.cpu_flops() if hasattr(W, "cpu_flops") else W.flops()
-        v, k = cpu_time(W.cpu_step, cf)
-        cpu = {"value": round(v, 3), "unit": unit_of(W), "cores": O.max_threads(), "kind": "port",
-               "sample": f"{k} steps, {W.cpu_sample()}"}
+        cpu = cpu_baseline(W, args.cpu_budget)
 
     launches = int(ctx.sum_over_ranks(W.launches_per_step * K))
-    line = {"metric": METRIC, "value": round(value, 3), "unit": unit_of(W), "n_gpus": ctx.world,
-            "steps": K, "warmup": args.warmup, "ms_per_step": round(secs * 1e3 / K, 5),
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": W.dtype, "data": "synthetic (numpy PCG64, seeds of the configs)",
-            "config": W.config(), "effective_gbs": round(eff_gbs, 1), "roofline": roof,
+    return {"value": round(value, 3), "unit": W.unit, "ms_per_step": round(secs * 1e3 / K, 5),
+            "steps": K, "warmup": warmup, "dtype": W.dtype, "config": W.config(),
+            "effective_gbs": round(eff_gbs, 1), "roofline": roof, "parity": parity,
             "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches, "clocks": clocks}
+
+
+def run_ours(args):
+    ctx = Ctx(args)
+    W = WORKLOADS[args.workload](ctx)
+    r = measure(ctx, W, args.steps, args.warmup, args)
+    W.close()
+    del W
+    line = {"metric": METRIC, "value": r["value"], "unit": r["unit"], "n_gpus": ctx.world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms_per_step"],
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": r["dtype"], "data": DATA}
+    line.update({k: r[k] for k in ("config", "effective_gbs", "roofline", "cpu_baseline", "e2e",
+                                   "parity", "gpu_launches", "clocks")})
+    if args.workload == "laplacian" and args.extra == "auto":
+        free_gpu(ctx)
+        K2, W2 = max(1, min(args.steps, args.extra_steps)), max(3, min(args.warmup, 5))
+        extra = {}
+        for name in EXTRA:
+            cls = WORKLOADS[name]
+            if ctx.world > 1 and not cls.shardable:
+                continue
+            w = cls(ctx)
+            extra[cls.key] = measure(ctx, w, K2, W2, args)
+            w.close()
+            del w
+            free_gpu(ctx)
+        line["workloads"] = extra
     if ctx.rank == 0:
         print(json.dumps(line), flush=True)
-    if hasattr(W, "close"):
-        W.close()
     ctx.close()
 
 
 def run_reference(args):
     """The reference's path on the host cores: the CPU restatement (the
-    reference is Julia; no Julia toolchain exists on this box)."""
+    reference is Julia; no Julia toolchain exists on this box), every host
+    thread, each step a bounded sample of the workload, on the same
+    workloads as run_ours with the same metric and units."""
     if env_int("RANK", 0) != 0:
         return
-    from jlust_b200 import synth
     from oracle import oracle as O
-    if args.workload != "laplacian":
-        print(json.dumps({"impl": "reference", "unavailable":
-                          "reference arm implemented for the default workload only"}))
-        return
-    g = args.grid
-    n = g * g
-    rp, ci, val = synth.laplacian_2d(g)
-    nnz = int(rp[-1])
-    x = np.random.default_rng(1).uniform(-1.0, 1.0, size=n)
+    ctx = Ctx(args)
     threads = O.max_threads()
-    state = {"x": x}
+    K, warm = args.steps, args.warmup
 
-    def step():
-        state["x"] = O.spmv(rp, ci, val, state["x"])
+    def one(W, step_s):
+        frac = sample_frac(W, step_s)
+        fn, work, desc = W.cpu_work(frac)
+        for _ in range(warm):
+            fn()
+        t0 = time.perf_counter()
+        for _ in range(K):
+            fn()
+        dt = time.perf_counter() - t0
+        v = work * K / dt / 1e9
+        single = getattr(W, "profile", "") in ("convert", "scan")
+        return {"value": round(v, 4), "unit": W.unit, "ms_per_step": round(dt * 1e3 / K, 4),
+                "steps": K, "warmup": warm, "dtype": W.dtype, "config": W.config(),
+                "cpu_baseline": {"value": round(v, 4), "unit": W.unit,
+                                 "cores": 1 if single else threads, "kind": "port",
+                                 "sample": f"{K} steps, {desc}; C restatement of JLUST's CPU "
+                                           "path (oracle/oracle.c)"},
+                "e2e": {"value": round(v, 4), "unit": W.unit, "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
 
-    t0 = time.perf_counter()
-    step()
-    one = time.perf_counter() - t0
-    for _ in range(max(args.warmup - 1, 0)):
-        step()
-    # bounded sample: full iterations while K of them fit in ~3 minutes
-    K = args.steps
-    frac = min(1.0, 180.0 / max(one * K, 1e-9))
-    if frac < 1.0:
-        rows = max(g, int(n * frac) // g * g)
-        rp_s = rp[:rows + 1]
-
-        def step():  # noqa: F811 - row-subset sample
-            O.spmv(rp_s, ci, val, state["x"])
-        flops = 2.0 * int(rp_s[-1])
-        sample = f"rows [0, {rows}) of each iteration ({frac:.3f} of the matrix)"
-    else:
-        flops = 2.0 * nnz
-        sample = "full iterations x <- A x"
-    t0 = time.perf_counter()
-    for _ in range(K):
-        step()
-    dt = time.perf_counter() - t0
-    value = flops * K / dt / 1e9
-    line = {"metric": METRIC, "value": round(value, 3), "unit": "GFLOP/s", "n_gpus": args.gpus,
-            "steps": K, "warmup": args.warmup, "ms_per_step": round(dt * 1e3 / K, 4),
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64",
-            "data": "synthetic (numpy PCG64, seeds of the configs)", "impl": "reference",
-            "config": {"workload": f"cfg2: CSR SpMV fp64, 2D 5-point Laplacian {g}x{g} "
-                                   f"(n={n}, nnz={nnz}), x <- A x per step",
-                       "n": n, "nnz": nnz},
-            "cpu_baseline": {"value": round(value, 3), "unit": "GFLOP/s", "cores": threads,
-                             "kind": "port",
-                             "sample": f"{K} steps, {sample}; C restatement of JLUST's CPU "
-                                       "walker (oracle/oracle.c), OpenMP over rows"},
-            "e2e": {"value": round(value, 3), "unit": "GFLOP/s", "h2d_bytes_per_step": 0,
-                    "d2h_bytes_per_step": 0}}
+    W = WORKLOADS[args.workload](ctx, host_only=True)
+    # the headline: full iterations while K of them fit in ~3 minutes
+    r = one(W, 180.0 / max(K, 1))
+    line = {"metric": METRIC, "value": r["value"], "unit": r["unit"], "n_gpus": args.gpus,
+            "steps": K, "warmup": warm, "ms_per_step": r["ms_per_step"],
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": r["dtype"], "data": DATA, "impl": "reference", "config": r["config"],
+            "cpu_baseline": r["cpu_baseline"], "e2e": r["e2e"]}
+    if args.workload == "laplacian" and args.extra == "auto":
+        K2 = max(1, min(args.steps, args.extra_steps))
+        K, warm = K2, max(3, min(args.warmup, 5))
+        extra = {}
+        for name in EXTRA:
+            cls = WORKLOADS[name]
+            if args.gpus > 1 and not cls.shardable:
+                continue
+            w = cls(ctx, host_only=True)
+            extra[cls.key] = one(w, 0.5)
+            del w
+            gc.collect()
+        line["workloads"] = extra
     print(json.dumps(line), flush=True)
 
 
-def main():
-    args = parse_args()
+def run_cusparse(args):
+    """cuSPARSE through torch.sparse (CSR, int32 indices) on cfg2 (SpMV),
+    cfg3 (SpMM) and cfg4 (SDDMM, the additive form with beta = 0: cuSPARSE
+    has no sampled-times-S mode): the reference's default GPU library for
+    SpMM and SDDMM (ext/CUDAExt/CUDAExt.jl:234-239), timed as a comparison
+    point.  Not part of the product."""
+    if env_int("RANK", 0) != 0:
+        return
+    ctx = Ctx(args)
+    torch = ctx.torch
+    dev = ctx.device
+    stream = torch.cuda.current_stream(dev)
+    K, warm = args.steps, args.warmup
+
+    def d(a):
+        return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+    def time_it(fn, flops):
+        for _ in range(warm):
+            fn()
+        torch.cuda.synchronize(dev)
+        secs, clocks = timed(ctx, lambda: [fn() for _ in range(K)], 1, stream)
+        return {"value": round(flops * K / secs / 1e9, 3), "unit": "GFLOP/s",
+                "ms_per_step": round(secs * 1e3 / K, 5), "clocks": clocks}
+
+    from jlust_b200 import synth
+    out = {}
+    rp, ci, val, x = synth.config2(g=args.grid)
+    n = rp.shape[0] - 1
+    A = torch.sparse_csr_tensor(d(rp), d(ci), d(val), (n, n))
+    xv = d(x)
+    r = time_it(lambda: torch.mv(A, xv), 2.0 * int(rp[-1]))
+    r["config"] = f"cfg2 Laplacian {args.grid}^2 fp64, y = A x (torch.mv -> cusparseSpMV)"
+    out["cfg2_laplacian"] = r
+    del A, xv
+    free_gpu(ctx)
+    rp, ci, val, B = synth.config3()
+    m = rp.shape[0] - 1
+    A = torch.sparse_csr_tensor(d(rp), d(ci), d(val), (m, m))
+    Bd = d(B)
+    r = time_it(lambda: torch.mm(A, Bd), 2.0 * int(rp[-1]) * B.shape[1])
+    r["config"] = "cfg3 power-law 4M^2 fp32, C = A B, B 4M x 64 row-major (torch.mm -> cusparseSpMM)"
+    out["cfg3_spmm"] = r
+    del A, Bd, B
+    free_gpu(ctx)
+    rp, ci, Am, Bm, S = synth.config4()
+    m = rp.shape[0] - 1
+    P = torch.sparse_csr_tensor(d(rp), d(ci), d(S), (m, m))
+    Ad, Bt = d(Am), d(Bm).t()
+    r = time_it(lambda: torch.sparse.sampled_addmm(P, Ad, Bt, beta=0.0, alpha=1.0),
+                2.0 * int(rp[-1]) * Am.shape[1])
+    r["config"] = ("cfg4 pattern 1M^2 32/row fp32, K = 128, out = A B^T at the pattern "
+                   "(torch.sparse.sampled_addmm -> cusparseSDDMM, beta = 0)")
+    out["cfg4_sddmm"] = r
+    print(json.dumps({"impl": "cusparse", "metric": METRIC, "n_gpus": 1, "steps": K,
+                      "warmup": warm, "data": DATA, "torch": torch.__version__,
+                      "workloads": out}), flush=True)
+
+
+def main(argv=None):
+    args = parse_args(argv)
     if args.impl == "reference":
         run_reference(args)
+    elif args.impl == "cusparse":
+        run_cusparse(args)
     else:
         run_ours(args)
 

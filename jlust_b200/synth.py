@@ -14,9 +14,14 @@ import numpy as np
 def f32_to_bf16_bits(a: np.ndarray) -> np.ndarray:
     """Round float32 to bfloat16 (round to nearest even) and return the bits as
     uint16.  NaN inputs become a quiet NaN."""
-    u = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32)
-    rounded = ((u + np.uint32(0x7FFF) + ((u >> np.uint32(16)) & np.uint32(1))) >> np.uint32(16))
-    out = rounded.astype(np.uint16)
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    u = a.view(np.uint32)
+    t = u >> np.uint32(16)              # in-place steps: no full-size temporaries
+    t &= np.uint32(1)
+    t += np.uint32(0x7FFF)
+    t += u
+    t >>= np.uint32(16)
+    out = t.astype(np.uint16)
     nan = np.isnan(a)
     if nan.any():
         out[nan] = np.uint16(0x7FC0)
@@ -37,8 +42,11 @@ def _rowptr_from_counts(counts: np.ndarray) -> np.ndarray:
 
 def csr_from_rows_cols(m: int, n: int, rows: np.ndarray, cols: np.ndarray):
     """Canonical CSR pattern (rowptr, colind) of (row, col) pairs, duplicates removed."""
-    key = rows.astype(np.int64) * np.int64(n) + cols.astype(np.int64)
-    key = np.unique(key)
+    key = np.sort(rows.astype(np.int64) * np.int64(n) + cols.astype(np.int64))
+    # sorted unique keys (np.unique's result; a sort and a mask are faster)
+    keep = np.ones(key.shape[0], dtype=bool)
+    np.not_equal(key[1:], key[:-1], out=keep[1:])
+    key = key[keep]
     r = (key // n).astype(np.int64)
     colind = (key % n).astype(np.int32)
     counts = np.bincount(r, minlength=m)
@@ -128,7 +136,10 @@ def config3(seed: int = 2, m: int = 4_194_304, k: int = 64, alpha: float = 2.0, 
     """CSR SpMM fp32: power-law A (values U[0,1]) and row-major B m x k U[-1,1]."""
     rowptr, colind, rng = power_law(m, m, alpha, kmax, seed)
     val = rng.random(colind.shape[0], dtype=np.float32)
-    B = rng.uniform(-1.0, 1.0, size=(m, k)).astype(np.float32)
+    # U[-1, 1) generated in fp32 directly (no fp64 temporary of m x k)
+    B = rng.random(size=(m, k), dtype=np.float32)
+    B *= np.float32(2.0)
+    B -= np.float32(1.0)
     return rowptr, colind, val, B
 
 
@@ -164,18 +175,35 @@ def config5(seed: int = 4, nbr: int = 1024, bs: int = 64, band: int = 8, p_off: 
 
 
 def bsr_to_csr(browptr, bcolind, bval, bs: int, nbr_rows: int, drop_zeros: bool = True):
-    """Expand a BSRRight matrix (row-major tiles) to CSR with the same values,
-    the CSR input of the conversion benchmark."""
+    """Expand a BSRRight matrix (row-major tiles, block columns ascending in
+    each block row) to CSR with the same values, the CSR input of the
+    conversion benchmark.  Row r of block row I holds row r of each of I's
+    tiles in block-column order, so the CSR comes out canonical with no sort.
+    Explicit zeros (either sign) are dropped when drop_zeros."""
+    browptr = np.asarray(browptr, np.int64)
     nnzb = bcolind.shape[0]
-    tiles = bval.reshape(nnzb, bs, bs)
-    brow = np.repeat(np.arange(nbr_rows), np.diff(browptr))
-    rows = (brow[:, None, None] * bs + np.arange(bs)[None, :, None]) + np.zeros((1, 1, bs), np.int64)
-    cols = (bcolind[:, None, None].astype(np.int64) * bs + np.arange(bs)[None, None, :]) + np.zeros((1, bs, 1), np.int64)
-    rows, cols, vals = rows.reshape(-1), cols.reshape(-1), tiles.reshape(-1)
-    if drop_zeros:
-        keep = (vals.view(np.uint16) & 0x7FFF) != 0 if vals.dtype == np.uint16 else vals != 0
-        rows, cols, vals = rows[keep], cols[keep], vals[keep]
-    order = np.lexsort((cols, rows))
-    rows, cols, vals = rows[order], cols[order], vals[order]
-    counts = np.bincount(rows, minlength=nbr_rows * bs)
+    tiles = np.asarray(bval).reshape(nnzb, bs, bs)
+    cols_all = bcolind.astype(np.int64)[:, None] * bs + np.arange(bs)[None, :]   # nnzb x bs
+    val_parts, col_parts, counts = [], [], np.zeros(nbr_rows * bs, np.int64)
+    for I in range(nbr_rows):
+        q0, q1 = int(browptr[I]), int(browptr[I + 1])
+        if q1 == q0:
+            continue
+        v = tiles[q0:q1].transpose(1, 0, 2).reshape(bs, -1)          # rows x (blocks * bs)
+        c = np.broadcast_to(cols_all[q0:q1].reshape(1, -1), v.shape)
+        keep = None
+        if drop_zeros:
+            keep = ((v.view(np.uint16) & 0x7FFF) != 0) if v.dtype == np.uint16 else v != 0
+            if keep.all():
+                keep = None
+        if keep is not None:
+            counts[I * bs:(I + 1) * bs] = keep.sum(axis=1)
+            val_parts.append(v[keep])
+            col_parts.append(c[keep])
+        else:
+            counts[I * bs:(I + 1) * bs] = v.shape[1]
+            val_parts.append(v.reshape(-1))
+            col_parts.append(c.reshape(-1))
+    vals = np.concatenate(val_parts) if val_parts else np.zeros(0, tiles.dtype)
+    cols = np.concatenate(col_parts) if col_parts else np.zeros(0, np.int64)
     return _rowptr_from_counts(counts), cols.astype(np.int32), vals
