@@ -697,8 +697,11 @@ class SpMM(Single):
     key, kernel, dtype, shardable, profile = "cfg3_spmm", "spmm_stream", "f32", True, "spmm"
     launches_per_step = 2   # spmm_stream + spmm_long_rows
 
+    col_major = False
+
     def host(self):
-        self.h = self.synth.config3()
+        self.h = _HOST.pop("cfg3", None) or self.synth.config3()
+        _HOST["cfg3"] = self.h          # kept for the column-major run that follows
         rp, _, _, B = self.h
         self.nnz, self.m, self.k = int(rp[-1]), rp.shape[0] - 1, B.shape[1]
 
@@ -710,8 +713,15 @@ class SpMM(Single):
         p0, p1 = int(rp[r0]), int(rp[r1])
         self.A = self.J.csr_tensor(self.d(lrp), self.d(ci[p0:p1]), self.d(val[p0:p1]),
                                    (r1 - r0, self.m), origin=0)
-        self.B = self.d(B)
-        self.C = self.torch.zeros(r1 - r0, self.k, dtype=self.torch.float32, device=self.dev)
+        if self.col_major:
+            # Julia's native layout: B and C column-major (transposed views
+            # of row-major k x n and k x m device arrays)
+            self.B = self.d(B).t().contiguous().t()
+            self.C = self.torch.zeros(self.k, r1 - r0, dtype=self.torch.float32,
+                                      device=self.dev).t()
+        else:
+            self.B = self.d(B)
+            self.C = self.torch.zeros(r1 - r0, self.k, dtype=self.torch.float32, device=self.dev)
 
     def api_call(self):
         self.J.execute(self.J.SpMMOp, self.A, self.B, self.C)
@@ -767,10 +777,33 @@ class SpMM(Single):
     def cpu_work(self, frac):
         from oracle import oracle as O
         rp, ci, val, B = self.h
+        if self.col_major and not hasattr(self, "hBf"):
+            self.hBf = np.asfortranarray(B)
+        Bx = self.hBf if self.col_major else B
         rows = max(1, min(self.m, int(self.m * frac)))
         rps = rp[:rows + 1]
-        return (lambda: O.spmm(rps, ci, val, B)), 2.0 * int(rps[-1]) * self.k, \
+        return (lambda: O.spmm(rps, ci, val, Bx, c_order=1 if self.col_major else 0)), \
+            2.0 * int(rps[-1]) * self.k, \
             f"rows [0, {rows}) of C = A B (fp32, Tiled per-(row,col) order)"
+
+
+class SpMMCol(SpMM):
+    """Config 3 with JLUST's native column-major B and C (the layout the
+    Julia binding passes): B is transposed into a workspace inside the call."""
+
+    key, profile, col_major = "cfg3_spmm_colmajor", "spmm_col", True
+    launches_per_step = 3   # transpose_tiles + spmm_stream + spmm_long_rows
+
+    def host(self):
+        self.h = _HOST.pop("cfg3", None) or self.synth.config3()
+        rp, _, _, B = self.h
+        self.nnz, self.m, self.k = int(rp[-1]), rp.shape[0] - 1, B.shape[1]
+
+    def config(self):
+        c = super().config()
+        c["workload"] = c["workload"].replace("row-major", "column-major, C column-major "
+                                              "(Julia's layout; B transposed in the call)")
+        return c
 
 
 class SDDMM(Single):
@@ -778,8 +811,12 @@ class SDDMM(Single):
 
     key, kernel, dtype, shardable, profile = "cfg4_sddmm", "sddmm_fast", "f32", True, "sddmm"
 
+    col_major = False
+
     def host(self):
-        self.h = self.synth.config4()
+        self.h = _HOST.pop("cfg4", None) or self.synth.config4()
+        if not self.col_major:
+            _HOST["cfg4"] = self.h      # kept for the column-major run that follows
         rp, _, A, _, _ = self.h
         self.nnz, self.m, self.K = int(rp[-1]), rp.shape[0] - 1, A.shape[1]
 
@@ -792,6 +829,10 @@ class SDDMM(Single):
         self.Cs = self.J.csr_tensor(self.d(lrp), self.d(ci[p0:p1]), self.S.clone(),
                                     (r1 - r0, self.m), origin=0)
         self.A, self.Bt = self.d(A[r0:r1]), self.d(B)
+        if self.col_major:
+            # Julia's native layout: A column-major m x K (B's K x n operand
+            # is column-major already: each B(:, j) contiguous)
+            self.A = self.A.t().contiguous().t()
 
     def api_call(self):
         J = self.J
@@ -841,8 +882,20 @@ class SDDMM(Single):
         rows = max(1, min(self.m, int(self.m * frac)))
         rps = rp[:rows + 1]
         Ss = S[:int(rps[-1])]
-        return (lambda: O.sddmm(rps, ci, A, B.T, Ss, S=Ss, mode=1)), 2.0 * int(rps[-1]) * self.K, \
+        Ax = np.asfortranarray(A[:rows]) if self.col_major else A
+        return (lambda: O.sddmm(rps, ci, Ax, B.T, Ss, S=Ss, mode=1)), 2.0 * int(rps[-1]) * self.K, \
             f"pattern rows [0, {rows}) (fp32, sequential K loop)"
+
+
+class SDDMMCol(SDDMM):
+    """Config 4 with JLUST's native column-major A (m x K) and K x n B."""
+
+    key, profile, col_major = "cfg4_sddmm_colmajor", "sddmm_col", True
+
+    def config(self):
+        c = super().config()
+        c["workload"] += "; A column-major (Julia's layout), B the column-major K x n operand"
+        return c
 
 
 class BSR(Single):
@@ -1128,10 +1181,14 @@ class CooToCsr(Single):
 
 WORKLOADS = {"laplacian": Laplacian, "spmv1": SpMV1, "spmm": SpMM, "sddmm": SDDMM, "bsr": BSR,
              "convert": Convert, "scan": Scan, "coo2csr": CooToCsr,
-             "spmv_powerlaw": SpMVPowerLaw, "spmv_medium": SpMVMedium}
+             "spmv_powerlaw": SpMVPowerLaw, "spmv_medium": SpMVMedium, "spmm_col": SpMMCol,
+             "sddmm_col": SDDMMCol}
 
 # measured beside the headline (one GPU: all; N GPUs: the sharded ones)
-EXTRA = ["spmm", "sddmm", "bsr", "convert", "scan"]
+EXTRA = ["spmm", "spmm_col", "sddmm", "sddmm_col", "bsr", "convert", "scan"]
+
+# host inputs shared by consecutive workloads of one configuration
+_HOST = {}
 
 
 # ------------------------------------------------------------------- arms --
@@ -1183,23 +1240,35 @@ def sample_frac(W, step_s, frac0=1.0 / 256):
     return max(frac0, 2.0 ** np.floor(np.log2(frac)))
 
 
+_THREADS = []
+
+
+def host_threads():
+    """The oracle's thread count at start-up (every host thread OpenMP may
+    use), read once: set_threads changes what max_threads reports."""
+    if not _THREADS:
+        from oracle import oracle as O
+        _THREADS.append(O.max_threads())
+    return _THREADS[0]
+
+
 def cpu_leg(W, threads, budget_s):
     """The CPU restatement of the reference's path on `threads` host threads,
     over a sample of W sized to the budget."""
     from oracle import oracle as O
+    all_threads = host_threads()
     O.set_threads(threads)
     try:
         frac = sample_frac(W, budget_s / 4)
         fn, work, desc = W.cpu_work(frac)
         v, k = cpu_time(fn, work, min_steps=2, max_steps=20, budget_s=budget_s)
     finally:
-        O.set_threads(O.max_threads())
+        O.set_threads(all_threads)
     return round(v, 4), k, desc
 
 
 def cpu_baseline(W, budget_s):
-    from oracle import oracle as O
-    cores = O.max_threads()
+    cores = host_threads()
     v, k, desc = cpu_leg(W, cores, budget_s)
     v1, k1, desc1 = cpu_leg(W, 1, budget_s) if cores > 1 else (v, k, desc)
     single = getattr(W, "profile", "") in ("convert", "scan")
@@ -1270,10 +1339,11 @@ def measure(ctx, W, K, warmup, args):
     parity = None
     if not args.no_parity:
         from oracle import oracle as O
+        all_threads = host_threads()
         if ctx.world > 1:
-            O.set_threads(max(1, O.max_threads() // ctx.world))
+            O.set_threads(max(1, all_threads // ctx.world))
         parity = W.parity()
-        O.set_threads(O.max_threads())
+        O.set_threads(all_threads)
 
     e2e = None
     if not args.no_e2e:
@@ -1340,9 +1410,8 @@ def run_reference(args):
     workloads as run_ours with the same metric and units."""
     if env_int("RANK", 0) != 0:
         return
-    from oracle import oracle as O
     ctx = Ctx(args)
-    threads = O.max_threads()
+    threads = host_threads()
     K, warm = args.steps, args.warmup
 
     def one(W, step_s):

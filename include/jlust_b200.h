@@ -216,6 +216,22 @@ JLB_API int jlb_csr_spmm(void *stream, int dtype, int idx_base, int64_t m, int64
                          const void *val, int64_t k, const void *B, int64_t ldb, int b_order,
                          void *C, int64_t ldc, int c_order, double alpha, double beta);
 
+/* jlb_csr_spmm with a caller workspace, for JLUST's native column-major B
+ * (KA spmm.jl:31-38, ext/CUDAExt/ops/spmm.jl:1-4): a column-major B is
+ * transposed on the stream into the workspace (n*k values) and its rows are
+ * gathered from there by the streaming kernels, whose order of operations --
+ * hence whose results -- are those of the row-major case.  Column-major C
+ * needs no workspace.  Without a large enough workspace the call behaves as
+ * jlb_csr_spmm.  jlb_csr_spmm_workspace_size returns 0 when no workspace is
+ * used.  Same contract as execute(::EmitterBackend, ::Op{:SpMM})
+ * (KA spmm.jl:397-423). */
+JLB_API size_t jlb_csr_spmm_workspace_size(int dtype, int64_t n, int64_t k, int b_order);
+JLB_API int jlb_csr_spmm_ws(void *stream, int dtype, int idx_base, int64_t m, int64_t n,
+                            int64_t nnz, const int32_t *rowptr, const int32_t *colind,
+                            const void *val, int64_t k, const void *B, int64_t ldb, int b_order,
+                            void *C, int64_t ldc, int c_order, double alpha, double beta,
+                            void *workspace, size_t workspace_bytes);
+
 /* ------------------------------------------------------------------ SDDMM */
 
 /* Sampled dense-dense product over the sparsity pattern of the m x n CSR

@@ -45,6 +45,9 @@ SIGNATURES = {
     "jlb_spmv_plan_destroy": (_i, [_p]),
     "jlb_csr_spmm": (_i, [_p, _i, _i, _i64, _i64, _i64, _p, _p, _p, _i64, _p, _i64, _i, _p,
                           _i64, _i, _d, _d]),
+    "jlb_csr_spmm_workspace_size": (_sz, [_i, _i64, _i64, _i]),
+    "jlb_csr_spmm_ws": (_i, [_p, _i, _i, _i64, _i64, _i64, _p, _p, _p, _i64, _p, _i64, _i, _p,
+                             _i64, _i, _d, _d, _p, _sz]),
     "jlb_sddmm": (_i, [_p, _i, _i, _i64, _i64, _i64, _p, _p, _i64, _p, _i64, _i, _p, _i64, _i,
                        _p, _p, _i, _d, _d]),
     "jlb_bsr_spmm": (_i, [_p, _i, _i64, _i64, _i64, _i, _p, _p, _p, _i64, _p, _i64, _p, _i64,

@@ -217,9 +217,13 @@ def spmm(A: USTensor, B, Cm, alpha=1.0, beta=0.0):
         raise IncompatibleExtents("SpMM: B and C must be row- or column-major strided")
     dev = _same_device(rowptr, colind, val, B, Cm)
     k = B.shape[1]
-    _lib.call("jlb_csr_spmm", _stream(dev), dt, A.origin.offset, m, n, val.numel(), _ptr(rowptr),
-              _ptr(colind), _ptr(val), k, _ptr(B), lb[1], lb[0], _ptr(Cm), lc[1], lc[0],
-              float(alpha), float(beta))
+    # a column-major B (JLUST's native layout) is transposed into a workspace
+    # and gathered by rows from there
+    wsb = _lib.load().jlb_csr_spmm_workspace_size(dt, n, k, lb[0]) if val.numel() else 0
+    ws = torch.empty(wsb, dtype=torch.uint8, device=dev) if wsb else None
+    _lib.call("jlb_csr_spmm_ws", _stream(dev), dt, A.origin.offset, m, n, val.numel(),
+              _ptr(rowptr), _ptr(colind), _ptr(val), k, _ptr(B), lb[1], lb[0], _ptr(Cm), lc[1],
+              lc[0], float(alpha), float(beta), _ptr(ws), wsb)
     return Cm
 
 

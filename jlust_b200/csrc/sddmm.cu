@@ -1,8 +1,9 @@
 // sddmm.cu -- sampled dense-dense product over a CSR pattern, sm_100a.
 //
-// Fast path (A row-major, the K x n operand B stored with each column j
-// contiguous -- i.e. a row-major n x K array -- both with 16-byte aligned
-// rows): one warp per pattern row i keeps A(i, :) in registers (16 bytes per
+// Fast path (A row-major with 16-byte aligned rows, or column-major as
+// Julia stores it; the K x n operand B stored with each column j contiguous
+// -- Julia's column-major K x n, or a row-major n x K array -- with 16-byte
+// aligned columns): one warp per pattern row i keeps A(i, :) in registers (16 bytes per
 // lane per 32*16-byte chunk of K); every stored position (i, j) costs one
 // coalesced read of B(:, j) and a fixed-order warp reduction.  Positions are
 // processed four at a time so four B columns are in flight per warp.  Results
@@ -51,7 +52,23 @@ __device__ __forceinline__ T finish(T dot, T s, T old, T alpha, T beta, int mode
     return o;
 }
 
-template <typename T, int NC>
+// A(i, kk .. kk+E-1) as one vector: a 16-byte load of a row-major A, or E
+// scalar loads of a column-major A (Julia's layout, element (i, kk) at
+// i + kk*lda).  Consecutive rows go to the warps of one CTA, so the 32-byte
+// sectors of a column-major A are shared by eight neighbouring rows in L1.
+template <typename T, bool kColA>
+__device__ __forceinline__ typename V16<T>::type load_a(const T *__restrict__ A, int64_t lda,
+                                                        int64_t i, int64_t kk) {
+    using VT = typename V16<T>::type;
+    if (!kColA) return __ldcs(reinterpret_cast<const VT *>(A + i * lda + kk));
+    T e[V16<T>::E];
+#pragma unroll
+    for (int u = 0; u < V16<T>::E; ++u) e[u] = __ldg(A + i + (kk + u) * lda);
+    if constexpr (V16<T>::E == 4) return make_float4(e[0], e[1], e[2], e[3]);
+    else return make_double2(e[0], e[1]);
+}
+
+template <typename T, int NC, bool kColA>
 __global__ void __launch_bounds__(kThreads)
 sddmm_fast(int64_t m, int64_t K, const int32_t *__restrict__ rowptr,
            const int32_t *__restrict__ colind, const T *__restrict__ A, int64_t lda,
@@ -67,7 +84,7 @@ sddmm_fast(int64_t m, int64_t K, const int32_t *__restrict__ rowptr,
 #pragma unroll
         for (int c = 0; c < NC; ++c) {
             const int64_t kk = (int64_t)c * CW + (int64_t)lane * E;
-            if (kk < K) a[c] = __ldcs(reinterpret_cast<const VT *>(A + i * lda + kk));
+            if (kk < K) a[c] = load_a<T, kColA>(A, lda, i, kk);
         }
         const int lo = rowptr[i] - base, hi = rowptr[i + 1] - base;
         for (int pb = lo; pb < hi; pb += kWarp) {
@@ -162,21 +179,32 @@ int launch(cudaStream_t st, int base, int64_t m, int64_t K, const int32_t *rowpt
                                          ? ceil_div(warps_needed, kThreads / kWarp)
                                          : 148 * 64);
     const int nc = (int)ceil_div(K, CW);
-    const bool fast = a_order == JLB_ROW_MAJOR && b_order == JLB_COL_MAJOR && K % E == 0 &&
-                      lda % E == 0 && ldb % E == 0 && aligned16(A) && aligned16(B) && nc >= 1 &&
-                      nc <= 4;
-#define JLB_SDDMM_FAST(NC)                                                                     \
-    sddmm_fast<T, NC><<<grid, kThreads, 0, st>>>(m, K, rowptr, colind, (const T *)A, lda,      \
-                                                 (const T *)B, ldb, (const T *)S, (T *)out,    \
-                                                 mode, a, b, has_beta, base)
-    if (fast) {
+    // B(:, j) contiguous (the K x n operand column-major: JLUST's native
+    // layout, or a row-major n x K array); A row-major or column-major
+    const bool a_fast = (a_order == JLB_ROW_MAJOR && lda % E == 0 && aligned16(A)) ||
+                        a_order == JLB_COL_MAJOR;
+    const bool fast = a_fast && b_order == JLB_COL_MAJOR && K % E == 0 && ldb % E == 0 &&
+                      aligned16(B) && nc >= 1 && nc <= 4;
+#define JLB_SDDMM_FAST(NC, CA)                                                                 \
+    sddmm_fast<T, NC, CA><<<grid, kThreads, 0, st>>>(m, K, rowptr, colind, (const T *)A, lda,  \
+                                                     (const T *)B, ldb, (const T *)S,          \
+                                                     (T *)out, mode, a, b, has_beta, base)
+    if (fast && a_order == JLB_ROW_MAJOR) {
         switch (nc) {
-            case 1: JLB_SDDMM_FAST(1); break;
-            case 2: JLB_SDDMM_FAST(2); break;
-            case 3: JLB_SDDMM_FAST(3); break;
-            default: JLB_SDDMM_FAST(4); break;
+            case 1: JLB_SDDMM_FAST(1, false); break;
+            case 2: JLB_SDDMM_FAST(2, false); break;
+            case 3: JLB_SDDMM_FAST(3, false); break;
+            default: JLB_SDDMM_FAST(4, false); break;
         }
         JLB_LAUNCH_CHECK("sddmm_fast");
+    } else if (fast) {
+        switch (nc) {
+            case 1: JLB_SDDMM_FAST(1, true); break;
+            case 2: JLB_SDDMM_FAST(2, true); break;
+            case 3: JLB_SDDMM_FAST(3, true); break;
+            default: JLB_SDDMM_FAST(4, true); break;
+        }
+        JLB_LAUNCH_CHECK("sddmm_fast (column-major A)");
     } else {
         sddmm_generic<T><<<grid, kThreads, 0, st>>>(m, K, rowptr, colind, (const T *)A, lda,
                                                     a_order, (const T *)B, ldb, b_order,

@@ -137,7 +137,11 @@ __device__ __forceinline__ void set_chunk(Slots<T> &s, int64_t c0, int64_t k) {
     for (int w = 0; w < kVec; ++w) s.ok[w] = Lanes<T>::col(c0, s.lane, w) < k;
 }
 
-template <typename T, bool kBeta>
+// Stores a row's chunk of C: 16-byte vectors into a row-major C, or scalars
+// into a column-major C (element (row, col) at row + col*ldc, Julia's layout).
+// A group walks consecutive rows, so the 32-byte sectors of a column-major C
+// fill up in L2 before they are written back.
+template <typename T, bool kBeta, bool kColC>
 __device__ __forceinline__ void store_chunk(T *C, int64_t ldc, int64_t row, int64_t c0, int64_t k,
                                             const T (&acc)[kVec][V16<T>::E], T alpha, T beta,
                                             int lane) {
@@ -147,6 +151,16 @@ __device__ __forceinline__ void store_chunk(T *C, int64_t ldc, int64_t row, int6
     for (int w = 0; w < kVec; ++w) {
         const int64_t col = Lanes<T>::col(c0, lane, w);
         if (col >= k) continue;
+        if (kColC) {
+#pragma unroll
+            for (int e = 0; e < E; ++e) {
+                T *d = C + row + (col + e) * ldc;
+                T o = mul_rn(alpha, acc[w][e]);
+                if (kBeta) o = add_rn(o, mul_rn(beta, *d));
+                *d = o;
+            }
+            continue;
+        }
         VT *dst = reinterpret_cast<VT *>(C + row * ldc + col);
         VT out;
         VT old;
@@ -232,7 +246,7 @@ __device__ __forceinline__ void issue_seek(int &r, int &p, int &e, int re,
 // longer than kLong excluded) with kDepth B-row chunks in flight, storing each
 // row's chunk of C when its last entry is in, and the chunk of every empty row
 // as alpha * 0 (+ beta * C).
-template <typename T, bool kBeta>
+template <typename T, bool kBeta, bool kColC>
 __global__ void __launch_bounds__(kThreads, 4)
 spmm_stream(int64_t m, int64_t k, const int32_t *__restrict__ rowptr,
             const int32_t *__restrict__ colind, const T *__restrict__ val,
@@ -272,7 +286,7 @@ spmm_stream(int64_t m, int64_t k, const int32_t *__restrict__ rowptr,
             ce = ldg(rowptr + rc + 1) - base;
             if (ce - lo > kLong || ce < lo) continue;
             if (ce == lo) {
-                store_chunk<T, kBeta>(C, ldc, rc, c0, k, acc, alpha, beta, lane);
+                store_chunk<T, kBeta, kColC>(C, ldc, rc, c0, k, acc, alpha, beta, lane);
                 continue;
             }
             cp = lo;
@@ -300,7 +314,7 @@ spmm_stream(int64_t m, int64_t k, const int32_t *__restrict__ rowptr,
                 if (!(live >> u & 1u)) continue;
                 sl.add(u, v[u], acc);
                 if (++cp >= ce) {
-                    store_chunk<T, kBeta>(C, ldc, rc, c0, k, acc, alpha, beta, lane);
+                    store_chunk<T, kBeta, kColC>(C, ldc, rc, c0, k, acc, alpha, beta, lane);
                     zero(acc);
                     for (;;) {
                         if (++rc >= re) break;
@@ -308,7 +322,7 @@ spmm_stream(int64_t m, int64_t k, const int32_t *__restrict__ rowptr,
                         ce = ldg(rowptr + rc + 1) - base;
                         if (ce - lo > kLong || ce < lo) continue;
                         if (ce == lo) {
-                            store_chunk<T, kBeta>(C, ldc, rc, c0, k, acc, alpha, beta, lane);
+                            store_chunk<T, kBeta, kColC>(C, ldc, rc, c0, k, acc, alpha, beta, lane);
                             continue;
                         }
                         cp = lo;
@@ -370,7 +384,7 @@ __device__ __forceinline__ void range_accumulate(const Slots<T> &sl, T (&acc)[kV
 // each taking one contiguous segment of ceil(L_i / g_i) entries; the first
 // group of the row adds the g_i partial sums in segment order and stores the
 // chunk.  Allocation and order depend only on the matrix: deterministic.
-template <typename T, bool kBeta>
+template <typename T, bool kBeta, bool kColC>
 __global__ void __launch_bounds__(kThreads, 4)
 spmm_long_rows(int64_t m, int64_t k, const int32_t *__restrict__ rowptr,
                const int32_t *__restrict__ colind, const T *__restrict__ val,
@@ -466,7 +480,7 @@ spmm_long_rows(int64_t m, int64_t k, const int32_t *__restrict__ rowptr,
                         sum[w][e] = s_part[first][idx];
                         for (int q = 1; q < cnt_g; ++q) sum[w][e] = add_rn(sum[w][e], s_part[first + q][idx]);
                     }
-                store_chunk<T, kBeta>(C, ldc, r, c0, k, sum, alpha, beta, lane);
+                store_chunk<T, kBeta, kColC>(C, ldc, r, c0, k, sum, alpha, beta, lane);
             }
             __syncthreads();
         }
@@ -478,7 +492,7 @@ constexpr int kLongSmem = kSlotBytes + kGroups * kChunkBytes + 2 * kScanRows * 4
 
 // Opts the kernels into their dynamic shared memory once per device and
 // returns the stream kernel's resident CTAs per SM times the SM count.
-template <typename T, bool kBeta>
+template <typename T, bool kBeta, bool kColC>
 int prepare_kernels(int *grid_full) {
     // one grid size per device, filled under a lock: two host threads making
     // their first call at once both see either nothing or the whole entry
@@ -489,11 +503,11 @@ int prepare_kernels(int *grid_full) {
     if (dev < 0 || dev >= 64) return fail(JLB_ERR_DEVICE_MISMATCH, "device ordinal %d", dev);
     std::lock_guard<std::mutex> lock(mu);
     if (!grid[dev]) {
-        JLB_CUDA(cudaFuncSetAttribute(spmm_stream<T, kBeta>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmem));
-        JLB_CUDA(cudaFuncSetAttribute(spmm_long_rows<T, kBeta>, cudaFuncAttributeMaxDynamicSharedMemorySize, kLongSmem));
+        JLB_CUDA(cudaFuncSetAttribute(spmm_stream<T, kBeta, kColC>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmem));
+        JLB_CUDA(cudaFuncSetAttribute(spmm_long_rows<T, kBeta, kColC>, cudaFuncAttributeMaxDynamicSharedMemorySize, kLongSmem));
         int sms = 0, p = 0;
         JLB_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-        JLB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&p, spmm_stream<T, kBeta>, kThreads, kStreamSmem));
+        JLB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&p, spmm_stream<T, kBeta, kColC>, kThreads, kStreamSmem));
         grid[dev] = (p < 1 ? 1 : p) * sms;
     }
     *grid_full = grid[dev];
@@ -527,38 +541,89 @@ __global__ void spmm_generic(int64_t m, int64_t k, const int32_t *__restrict__ r
     }
 }
 
-template <typename T, bool kBeta>
+template <typename T, bool kBeta, bool kColC>
 int launch_fast(cudaStream_t st, int base, int64_t m, int64_t nnz, int64_t k,
                 const int32_t *rowptr, const int32_t *colind, const T *val, const T *B,
                 int64_t ldb, T *C, int64_t ldc, T a, T b) {
     int full = 0;
-    const int rc = prepare_kernels<T, kBeta>(&full);
+    const int rc = prepare_kernels<T, kBeta, kColC>(&full);
     if (rc != JLB_OK) return rc;
     const int64_t need = ceil_div(m + nnz, (int64_t)kGroups * kMinWork);
     const unsigned grid = (unsigned)(need < full ? need : full);
-    spmm_stream<T, kBeta><<<grid, kThreads, kStreamSmem, st>>>(m, k, rowptr, colind, val, B, ldb,
-                                                               C, ldc, a, b, base);
-    spmm_long_rows<T, kBeta><<<(unsigned)ceil_div(m, kScanRows), kThreads, kLongSmem, st>>>(
+    spmm_stream<T, kBeta, kColC><<<grid, kThreads, kStreamSmem, st>>>(m, k, rowptr, colind, val, B,
+                                                                      ldb, C, ldc, a, b, base);
+    spmm_long_rows<T, kBeta, kColC><<<(unsigned)ceil_div(m, kScanRows), kThreads, kLongSmem, st>>>(
         m, k, rowptr, colind, val, B, ldb, C, ldc, a, b, base);
     JLB_LAUNCH_CHECK("spmm_stream");
     return ok();
 }
 
 template <typename T>
-int launch(cudaStream_t st, int base, int64_t m, int64_t nnz, int64_t k, const int32_t *rowptr,
-           const int32_t *colind, const void *val, const void *B, int64_t ldb, int b_order,
-           void *C, int64_t ldc, int c_order, double alpha, double beta) {
+int launch_fast_any(cudaStream_t st, int base, int64_t m, int64_t nnz, int64_t k,
+                    const int32_t *rowptr, const int32_t *colind, const T *val, const T *B,
+                    int64_t ldb, T *C, int64_t ldc, bool col_c, T a, T b) {
+    if (b == T(0))
+        return col_c ? launch_fast<T, false, true>(st, base, m, nnz, k, rowptr, colind, val, B, ldb, C, ldc, a, b)
+                     : launch_fast<T, false, false>(st, base, m, nnz, k, rowptr, colind, val, B, ldb, C, ldc, a, b);
+    return col_c ? launch_fast<T, true, true>(st, base, m, nnz, k, rowptr, colind, val, B, ldb, C, ldc, a, b)
+                 : launch_fast<T, true, false>(st, base, m, nnz, k, rowptr, colind, val, B, ldb, C, ldc, a, b);
+}
+
+// out (cols x rows, row-major, leading dim ldo) = in^T for in rows x cols
+// row-major (leading dim ldi): 32 x 32 tiles through shared memory, both
+// sides coalesced.  Turns a column-major n x k B (a row-major k x n array)
+// into the row-major n x k copy the stream kernels gather rows from.
+template <typename T>
+__global__ void __launch_bounds__(256)
+transpose_tiles(int64_t rows, int64_t cols, const T *__restrict__ in, int64_t ldi,
+                T *__restrict__ out, int64_t ldo) {
+    __shared__ T tile[32][33];
+    const int64_t c0 = (int64_t)blockIdx.x * 32;
+    for (int64_t r0 = (int64_t)blockIdx.y * 32; r0 < rows; r0 += (int64_t)gridDim.y * 32) {
+#pragma unroll
+        for (int i = threadIdx.y; i < 32; i += 8) {
+            const int64_t r = r0 + i, c = c0 + threadIdx.x;
+            if (r < rows && c < cols) tile[i][threadIdx.x] = in[r * ldi + c];
+        }
+        __syncthreads();
+#pragma unroll
+        for (int i = threadIdx.y; i < 32; i += 8) {
+            const int64_t orow = c0 + i, ocol = r0 + threadIdx.x;
+            if (orow < cols && ocol < rows) out[orow * ldo + ocol] = tile[threadIdx.x][i];
+        }
+        __syncthreads();
+    }
+}
+
+inline size_t bt_bytes(int64_t n, int64_t k, size_t es) { return (size_t)n * (size_t)k * es + 256; }
+
+template <typename T>
+int launch(cudaStream_t st, int base, int64_t m, int64_t n, int64_t nnz, int64_t k,
+           const int32_t *rowptr, const int32_t *colind, const void *val, const void *B,
+           int64_t ldb, int b_order, void *C, int64_t ldc, int c_order, double alpha,
+           double beta, void *ws, size_t ws_bytes) {
     if (m == 0 || k == 0) return ok();
     constexpr int E = V16<T>::E;
     const T a = (T)alpha, b = (T)beta;
-    const bool fast = m < INT32_MAX && b_order == JLB_ROW_MAJOR && c_order == JLB_ROW_MAJOR && k % E == 0 &&
-                      ldb % E == 0 && ldc % E == 0 && aligned16(B) && aligned16(C);
-    if (fast) {
-        if (b == T(0))
-            return launch_fast<T, false>(st, base, m, nnz, k, rowptr, colind, (const T *)val,
-                                         (const T *)B, ldb, (T *)C, ldc, a, b);
-        return launch_fast<T, true>(st, base, m, nnz, k, rowptr, colind, (const T *)val,
-                                    (const T *)B, ldb, (T *)C, ldc, a, b);
+    // C: row-major with 16-byte aligned rows, or column-major (scalar stores)
+    const bool c_fast = (c_order == JLB_ROW_MAJOR && ldc % E == 0 && aligned16(C)) ||
+                        c_order == JLB_COL_MAJOR;
+    const bool shape_fast = m < INT32_MAX && k % E == 0 && c_fast;
+    const bool col_c = c_order == JLB_COL_MAJOR;
+    if (shape_fast && b_order == JLB_ROW_MAJOR && ldb % E == 0 && aligned16(B))
+        return launch_fast_any<T>(st, base, m, nnz, k, rowptr, colind, (const T *)val,
+                                  (const T *)B, ldb, (T *)C, ldc, col_c, a, b);
+    // column-major B (Julia's layout): a B row is k strided elements, each
+    // in its own sector; with a workspace it is transposed once into a
+    // row-major copy and the rows are gathered from that
+    if (shape_fast && b_order == JLB_COL_MAJOR && ws && ws_bytes >= bt_bytes(n, k, sizeof(T)) && n > 0) {
+        T *bt = reinterpret_cast<T *>((reinterpret_cast<uintptr_t>(ws) + 255) & ~(uintptr_t)255);
+        const int64_t gy = ceil_div(k, 32) < 65535 ? ceil_div(k, 32) : 65535;
+        transpose_tiles<T><<<dim3((unsigned)ceil_div(n, 32), (unsigned)gy), dim3(32, 8), 0, st>>>(
+            k, n, (const T *)B, ldb, bt, k);
+        JLB_LAUNCH_CHECK("transpose_tiles");
+        return launch_fast_any<T>(st, base, m, nnz, k, rowptr, colind, (const T *)val, bt, k,
+                                  (T *)C, ldc, col_c, a, b);
     }
     const int64_t total = m * k;
     const unsigned grid = (unsigned)(ceil_div(total, 256) < 148 * 32 ? ceil_div(total, 256) : 148 * 32);
@@ -574,11 +639,10 @@ int launch(cudaStream_t st, int base, int64_t m, int64_t nnz, int64_t k, const i
 
 using namespace jlb;
 
-extern "C" JLB_API int jlb_csr_spmm(void *stream, int dtype, int idx_base, int64_t m, int64_t n,
-                                    int64_t nnz, const int32_t *rowptr, const int32_t *colind,
-                                    const void *val, int64_t k, const void *B, int64_t ldb,
-                                    int b_order, void *C, int64_t ldc, int c_order, double alpha,
-                                    double beta) {
+static int csr_spmm(void *stream, int dtype, int idx_base, int64_t m, int64_t n, int64_t nnz,
+                    const int32_t *rowptr, const int32_t *colind, const void *val, int64_t k,
+                    const void *B, int64_t ldb, int b_order, void *C, int64_t ldc, int c_order,
+                    double alpha, double beta, void *ws, size_t ws_bytes) {
     if (dtype != JLB_F32 && dtype != JLB_F64)
         return fail(JLB_ERR_UNSUPPORTED_VALUE_TYPE, "SpMM supports Float32 and Float64 (dtype %d)", dtype);
     if (idx_base != 0 && idx_base != 1) return fail(JLB_ERR_INVALID_ARGUMENT, "idx_base must be 0 or 1");
@@ -592,8 +656,32 @@ extern "C" JLB_API int jlb_csr_spmm(void *stream, int dtype, int idx_base, int64
     if (m > 0 && k > 0 && (!rowptr || !C)) return fail(JLB_ERR_INVALID_ARGUMENT, "null rowptr or C");
     if (nnz > 0 && k > 0 && (!colind || !val || !B)) return fail(JLB_ERR_INVALID_ARGUMENT, "null colind, val or B");
     if (dtype == JLB_F64)
-        return spmm::launch<double>(as_stream(stream), idx_base, m, nnz, k, rowptr, colind, val, B, ldb,
-                                    b_order, C, ldc, c_order, alpha, beta);
-    return spmm::launch<float>(as_stream(stream), idx_base, m, nnz, k, rowptr, colind, val, B, ldb,
-                               b_order, C, ldc, c_order, alpha, beta);
+        return spmm::launch<double>(as_stream(stream), idx_base, m, n, nnz, k, rowptr, colind, val, B,
+                                    ldb, b_order, C, ldc, c_order, alpha, beta, ws, ws_bytes);
+    return spmm::launch<float>(as_stream(stream), idx_base, m, n, nnz, k, rowptr, colind, val, B,
+                               ldb, b_order, C, ldc, c_order, alpha, beta, ws, ws_bytes);
+}
+
+extern "C" JLB_API int jlb_csr_spmm(void *stream, int dtype, int idx_base, int64_t m, int64_t n,
+                                    int64_t nnz, const int32_t *rowptr, const int32_t *colind,
+                                    const void *val, int64_t k, const void *B, int64_t ldb,
+                                    int b_order, void *C, int64_t ldc, int c_order, double alpha,
+                                    double beta) {
+    return csr_spmm(stream, dtype, idx_base, m, n, nnz, rowptr, colind, val, k, B, ldb, b_order, C,
+                    ldc, c_order, alpha, beta, nullptr, 0);
+}
+
+extern "C" JLB_API size_t jlb_csr_spmm_workspace_size(int dtype, int64_t n, int64_t k, int b_order) {
+    if (b_order != JLB_COL_MAJOR || n <= 0 || k <= 0) return 0;
+    return spmm::bt_bytes(n, k, dtype == JLB_F64 ? 8 : 4);
+}
+
+extern "C" JLB_API int jlb_csr_spmm_ws(void *stream, int dtype, int idx_base, int64_t m, int64_t n,
+                                       int64_t nnz, const int32_t *rowptr, const int32_t *colind,
+                                       const void *val, int64_t k, const void *B, int64_t ldb,
+                                       int b_order, void *C, int64_t ldc, int c_order,
+                                       double alpha, double beta, void *workspace,
+                                       size_t workspace_bytes) {
+    return csr_spmm(stream, dtype, idx_base, m, n, nnz, rowptr, colind, val, k, B, ldb, b_order, C,
+                    ldc, c_order, alpha, beta, workspace, workspace_bytes);
 }

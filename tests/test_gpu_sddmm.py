@@ -80,3 +80,40 @@ def test_reduced_config4():
     J.device_status()
     ref, bound = O.sddmm_ref64(rp, ci, A, B.T, S=S, mode=1)
     assert_within(Cs.val.cpu().numpy(), ref, bound, 1e-5)
+
+
+@pytest.mark.parametrize("K", [128, 64, 20])
+@pytest.mark.parametrize("dtype", [np.float32, np.float64])
+def test_column_major_a_fast_path(K, dtype):
+    """JLUST's native layouts: A column-major m x K and B the column-major
+    K x n operand; the warp-per-row kernel reads A(i, :) with strided scalar
+    loads.  Within tolerance of the fp64 restatement, both modes, beta != 0."""
+    rng = np.random.default_rng(47)
+    m, n = 3000, 2000
+    rp, ci, _ = random_csr(m, n, rng.integers(0, 45, size=m), seed=48, dtype=dtype)
+    A = np.asfortranarray(rng.standard_normal((m, K)).astype(dtype))
+    Bkn = np.asfortranarray(rng.standard_normal((K, n)).astype(dtype))
+    v0 = rng.random(ci.shape[0]).astype(dtype)
+    Ad = torch.from_numpy(np.ascontiguousarray(A.T)).to(DEV).t()
+    Bd = torch.from_numpy(np.ascontiguousarray(Bkn.T)).to(DEV).t()
+    tol = 1e-5 if dtype == np.float32 else 1e-12
+    for mode in ("add", "mul"):
+        Cs = J.csr_tensor(to_dev(rp), to_dev(ci), to_dev(v0.copy()), (m, n), origin=0)
+        J.execute(J.SDDMMOp, Ad, Bd, Cs, alpha=0.5, beta=0.25, mode=mode)
+        J.device_status()
+        got = Cs.val.cpu().numpy()
+        if dtype == np.float64:
+            # the fp64 restatement in the reference's order; the warp's sum
+            # differs from it by rounding only: per entry within 1e-12 of
+            # the sum of the absolute terms
+            ref = O.sddmm(rp, ci, A, Bkn, v0, S=v0, mode=0 if mode == "add" else 1, alpha=0.5,
+                          beta=0.25)
+            rows = np.repeat(np.arange(m), np.diff(rp))
+            terms = np.einsum("pk,pk->p", np.abs(A[rows]), np.abs(Bkn[:, ci].T)) * 0.5
+            if mode == "mul":
+                terms = terms * np.abs(v0)
+            assert_within(got, ref, terms + 0.25 * np.abs(v0), tol)
+        else:
+            ref, bound = O.sddmm_ref64(rp, ci, A, Bkn, out_in=v0, S=v0,
+                                       mode=0 if mode == "add" else 1, alpha=0.5, beta=0.25)
+            assert_within(got, ref, bound, tol)

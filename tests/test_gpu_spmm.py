@@ -70,10 +70,15 @@ def test_long_rows_tolerance():
     assert np.array_equal(got[short], O.spmm(rp, ci, val, B)[short])
 
 
+@pytest.mark.parametrize("k", [24, 7])
 @pytest.mark.parametrize("b_f,c_f", [(True, True), (True, False), (False, True)])
-def test_generic_layouts_bit_exact(b_f, c_f):
+def test_column_major_layouts_bit_exact(b_f, c_f, k):
+    """JLUST's native column-major B and C: B transposed into a workspace and
+    gathered by the streaming kernels, C stored column-major by them (k = 24);
+    k = 7 (not a whole number of vectors) takes the generic kernel.  Both
+    sum each row in storage order: bit-exact."""
     rng = np.random.default_rng(35)
-    m, n, k = 700, 500, 24
+    m, n = 700, 500
     rp, ci, val = random_csr(m, n, rng.integers(0, 30, size=m), seed=36)
     B = rng.uniform(-1, 1, size=(n, k))
     if b_f:
@@ -81,6 +86,45 @@ def test_generic_layouts_bit_exact(b_f, c_f):
     C0 = rng.uniform(-1, 1, size=(m, k))
     got = run(rp, ci, val, B, m, n, 0, C0, 1.5, 0.5, c_col_major=c_f)
     assert np.array_equal(got, O.spmm(rp, ci, val, B, C0, 1.5, 0.5))
+
+
+@pytest.mark.parametrize("beta", [0.0, 0.5])
+def test_column_major_long_rows(beta):
+    """Column-major B and C (fp32, k = 64) with rows past the long-row
+    threshold and 1-based storage: short rows bit-exact, long rows within
+    1e-5."""
+    rng = np.random.default_rng(37)
+    m, n, k = 3000, 9000, 64
+    lengths = rng.integers(0, 12, size=m)
+    lengths[::53] = rng.integers(257, 3000, size=lengths[::53].shape[0])
+    rp, ci, val = random_csr(m, n, lengths, seed=38, base=1, dtype=np.float32)
+    B = np.asfortranarray(rng.uniform(-1, 1, size=(n, k)).astype(np.float32))
+    C0 = rng.uniform(-1, 1, size=(m, k)).astype(np.float32)
+    got = run(rp, ci, val, B, m, n, 1, C0, 1.0, beta, c_col_major=True)
+    short = np.diff(rp) <= 256
+    assert np.array_equal(got[short], O.spmm(rp, ci, val, B, C0, 1.0, beta, 1)[short])
+    ref, bound = O.spmm_ref64(rp - 1, ci - 1, val, B, C0 if beta else None, 1.0, beta)
+    assert_within(got[~short], ref[~short], bound[~short], 1e-5)
+
+
+def test_column_major_b_without_workspace():
+    """jlb_csr_spmm (no workspace) with a column-major B runs the generic
+    kernel: bit-exact, no allocation."""
+    import ctypes as C
+    from jlust_b200 import _lib
+    rng = np.random.default_rng(39)
+    m, n, k = 400, 300, 16
+    rp, ci, val = random_csr(m, n, rng.integers(0, 20, size=m), seed=40, dtype=np.float32)
+    B = np.asfortranarray(rng.uniform(-1, 1, size=(n, k)).astype(np.float32))
+    rpd, cid, vd = to_dev(rp), to_dev(ci), to_dev(val)
+    Bd = torch.from_numpy(np.ascontiguousarray(B.T)).to(DEV)          # k x n row-major = B col-major
+    Cd = torch.zeros(m, k, dtype=torch.float32, device=DEV)
+    p = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+    st = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    _lib.call("jlb_csr_spmm", st, _lib.F32, 0, m, n, ci.shape[0], p(rpd), p(cid), p(vd), k, p(Bd),
+              n, 1, p(Cd), k, 0, 1.0, 0.0)
+    J.device_status()
+    assert np.array_equal(Cd.cpu().numpy(), O.spmm(rp, ci, val, B))
 
 
 def test_power_law_reduced_config3():
