@@ -792,7 +792,7 @@ class SpMMCol(SpMM):
     Julia binding passes): B is transposed into a workspace inside the call."""
 
     key, profile, col_major = "cfg3_spmm_colmajor", "spmm_col", True
-    launches_per_step = 3   # transpose_tiles + spmm_stream + spmm_long_rows
+    launches_per_step = 4   # transpose B, spmm_stream, spmm_long_rows, transpose C
 
     def host(self):
         self.h = _HOST.pop("cfg3", None) or self.synth.config3()
@@ -1458,62 +1458,152 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+class _CuSparse:
+    """The cuSPARSE generic API through ctypes (libcusparse of the CUDA
+    toolkit), for the comparison arm only."""
+
+    INDEX_32I, BASE_ZERO, NON_TRANSPOSE, ORDER_COL, ORDER_ROW = 2, 0, 0, 1, 2
+    R_32F, R_64F = 0, 1
+
+    def __init__(self, stream):
+        import ctypes as C
+        self.C = C
+        for name in ("libcusparse.so.12", "/usr/local/cuda/lib64/libcusparse.so.12"):
+            try:
+                self.L = C.CDLL(name)
+                break
+            except OSError:
+                continue
+        self.h = C.c_void_p()
+        self.ok(self.L.cusparseCreate(C.byref(self.h)), "cusparseCreate")
+        self.ok(self.L.cusparseSetStream(self.h, C.c_void_p(stream)), "cusparseSetStream")
+
+    def ok(self, st, what):
+        if st != 0:
+            raise RuntimeError(f"{what} failed with cuSPARSE status {st}")
+
+    def csr(self, m, n, nnz, rp, ci, val, dt):
+        C = self.C
+        d = C.c_void_p()
+        self.ok(self.L.cusparseCreateCsr(C.byref(d), C.c_int64(m), C.c_int64(n), C.c_int64(nnz),
+                                         C.c_void_p(rp), C.c_void_p(ci), C.c_void_p(val),
+                                         self.INDEX_32I, self.INDEX_32I, self.BASE_ZERO, dt),
+                "cusparseCreateCsr")
+        return d
+
+    def vec(self, size, ptr, dt):
+        C = self.C
+        d = C.c_void_p()
+        self.ok(self.L.cusparseCreateDnVec(C.byref(d), C.c_int64(size), C.c_void_p(ptr), dt),
+                "cusparseCreateDnVec")
+        return d
+
+    def mat(self, rows, cols, ld, ptr, dt, order):
+        C = self.C
+        d = C.c_void_p()
+        self.ok(self.L.cusparseCreateDnMat(C.byref(d), C.c_int64(rows), C.c_int64(cols),
+                                           C.c_int64(ld), C.c_void_p(ptr), dt, order),
+                "cusparseCreateDnMat")
+        return d
+
+    def scalars(self, dt):
+        C = self.C
+        t = C.c_double if dt == self.R_64F else C.c_float
+        self._one, self._zero = t(1.0), t(0.0)
+        return C.byref(self._one), C.byref(self._zero)
+
+
 def run_cusparse(args):
-    """cuSPARSE through torch.sparse (CSR, int32 indices) on cfg2 (SpMV),
-    cfg3 (SpMM) and cfg4 (SDDMM, the additive form with beta = 0: cuSPARSE
-    has no sampled-times-S mode): the reference's default GPU library for
-    SpMM and SDDMM (ext/CUDAExt/CUDAExt.jl:234-239), timed as a comparison
-    point.  Not part of the product."""
+    """cuSPARSE (the reference's default GPU library for SpMM and SDDMM,
+    ext/CUDAExt/CUDAExt.jl:234-239, and its CUSPARSEBackend SpMV) through its
+    generic API on cfg2 (cusparseSpMV), cfg3 (cusparseSpMM, row-major B and
+    C) and cfg4 (cusparseSDDMM, the additive form with beta = 0: cuSPARSE has
+    no sampled-times-S mode), timed with CUDA events after a warm-up, as a
+    comparison point.  Not part of the product."""
     if env_int("RANK", 0) != 0:
         return
+    import ctypes as C
     ctx = Ctx(args)
     torch = ctx.torch
     dev = ctx.device
     stream = torch.cuda.current_stream(dev)
+    cs = _CuSparse(stream.cuda_stream)
     K, warm = args.steps, args.warmup
 
     def d(a):
         return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
 
-    def time_it(fn, flops):
+    def time_it(fn, flops, byts=None):
         for _ in range(warm):
             fn()
         torch.cuda.synchronize(dev)
         secs, clocks = timed(ctx, lambda: [fn() for _ in range(K)], 1, stream)
-        return {"value": round(flops * K / secs / 1e9, 3), "unit": "GFLOP/s",
-                "ms_per_step": round(secs * 1e3 / K, 5), "clocks": clocks}
+        r = {"value": round(flops * K / secs / 1e9, 3), "unit": "GFLOP/s",
+             "ms_per_step": round(secs * 1e3 / K, 5), "clocks": clocks}
+        if byts:
+            r["effective_gbs"] = round(byts * K / secs / 1e9, 1)
+        return r
+
+    def buffer(size_fn, *a):
+        sz = C.c_size_t(0)
+        cs.ok(size_fn(cs.h, *a, C.byref(sz)), "bufferSize")
+        return torch.empty(max(int(sz.value), 1), dtype=torch.uint8, device=dev)
 
     from jlust_b200 import synth
     out = {}
+    # cfg2: SpMV fp64
     rp, ci, val, x = synth.config2(g=args.grid)
-    n = rp.shape[0] - 1
-    A = torch.sparse_csr_tensor(d(rp), d(ci), d(val), (n, n))
-    xv = d(x)
-    r = time_it(lambda: torch.mv(A, xv), 2.0 * int(rp[-1]))
-    r["config"] = f"cfg2 Laplacian {args.grid}^2 fp64, y = A x (torch.mv -> cusparseSpMV)"
+    n, nnz = rp.shape[0] - 1, int(rp[-1])
+    tr, tc, tv, tx = d(rp), d(ci), d(val), d(x)
+    ty = torch.zeros(n, dtype=torch.float64, device=dev)
+    A = cs.csr(n, n, nnz, tr.data_ptr(), tc.data_ptr(), tv.data_ptr(), cs.R_64F)
+    vx, vy = cs.vec(n, tx.data_ptr(), cs.R_64F), cs.vec(n, ty.data_ptr(), cs.R_64F)
+    one, zero = cs.scalars(cs.R_64F)
+    buf = buffer(cs.L.cusparseSpMV_bufferSize, 0, one, A, vx, zero, vy, cs.R_64F, 0)
+    r = time_it(lambda: cs.ok(cs.L.cusparseSpMV(cs.h, 0, one, A, vx, zero, vy, cs.R_64F, 0,
+                                                C.c_void_p(buf.data_ptr())), "cusparseSpMV"),
+                2.0 * nnz, 12.0 * nnz + 4.0 * (n + 1) + 16.0 * n)
+    r["config"] = f"cfg2 Laplacian {args.grid}^2 fp64, y = A x (cusparseSpMV, CUSPARSE_SPMV_ALG_DEFAULT)"
     out["cfg2_laplacian"] = r
-    del A, xv
+    del tr, tc, tv, tx, ty, buf
     free_gpu(ctx)
+    # cfg3: SpMM fp32, row-major B and C
     rp, ci, val, B = synth.config3()
-    m = rp.shape[0] - 1
-    A = torch.sparse_csr_tensor(d(rp), d(ci), d(val), (m, m))
-    Bd = d(B)
-    r = time_it(lambda: torch.mm(A, Bd), 2.0 * int(rp[-1]) * B.shape[1])
-    r["config"] = "cfg3 power-law 4M^2 fp32, C = A B, B 4M x 64 row-major (torch.mm -> cusparseSpMM)"
+    m, nnz, k = rp.shape[0] - 1, int(rp[-1]), B.shape[1]
+    tr, tc, tv, tB = d(rp), d(ci), d(val), d(B)
+    tC = torch.zeros(m, k, dtype=torch.float32, device=dev)
+    A = cs.csr(m, m, nnz, tr.data_ptr(), tc.data_ptr(), tv.data_ptr(), cs.R_32F)
+    mB = cs.mat(m, k, k, tB.data_ptr(), cs.R_32F, cs.ORDER_ROW)
+    mC = cs.mat(m, k, k, tC.data_ptr(), cs.R_32F, cs.ORDER_ROW)
+    one, zero = cs.scalars(cs.R_32F)
+    buf = buffer(cs.L.cusparseSpMM_bufferSize, 0, 0, one, A, mB, zero, mC, cs.R_32F, 0)
+    r = time_it(lambda: cs.ok(cs.L.cusparseSpMM(cs.h, 0, 0, one, A, mB, zero, mC, cs.R_32F, 0,
+                                                C.c_void_p(buf.data_ptr())), "cusparseSpMM"),
+                2.0 * nnz * k, 8.0 * nnz + 4.0 * (m + 1) + 4.0 * k * (nnz + m))
+    r["config"] = ("cfg3 power-law 4M^2 fp32, C = A B, B 4M x 64 and C row-major "
+                   "(cusparseSpMM, CUSPARSE_SPMM_ALG_DEFAULT)")
     out["cfg3_spmm"] = r
-    del A, Bd, B
+    del tr, tc, tv, tB, tC, buf, B
     free_gpu(ctx)
+    # cfg4: SDDMM fp32; B (n x K row-major) is the column-major K x n operand
     rp, ci, Am, Bm, S = synth.config4()
-    m = rp.shape[0] - 1
-    P = torch.sparse_csr_tensor(d(rp), d(ci), d(S), (m, m))
-    Ad, Bt = d(Am), d(Bm).t()
-    r = time_it(lambda: torch.sparse.sampled_addmm(P, Ad, Bt, beta=0.0, alpha=1.0),
-                2.0 * int(rp[-1]) * Am.shape[1])
+    m, nnz, Kd = rp.shape[0] - 1, int(rp[-1]), Am.shape[1]
+    tr, tc, tS, tA, tB = d(rp), d(ci), d(S), d(Am), d(Bm)
+    P = cs.csr(m, m, nnz, tr.data_ptr(), tc.data_ptr(), tS.data_ptr(), cs.R_32F)
+    mA = cs.mat(m, Kd, Kd, tA.data_ptr(), cs.R_32F, cs.ORDER_ROW)
+    mB = cs.mat(Kd, m, Kd, tB.data_ptr(), cs.R_32F, cs.ORDER_COL)
+    one, zero = cs.scalars(cs.R_32F)
+    buf = buffer(cs.L.cusparseSDDMM_bufferSize, 0, 0, one, mA, mB, zero, P, cs.R_32F, 0)
+    cs.ok(cs.L.cusparseSDDMM_preprocess(cs.h, 0, 0, one, mA, mB, zero, P, cs.R_32F, 0,
+                                        C.c_void_p(buf.data_ptr())), "cusparseSDDMM_preprocess")
+    r = time_it(lambda: cs.ok(cs.L.cusparseSDDMM(cs.h, 0, 0, one, mA, mB, zero, P, cs.R_32F, 0,
+                                                 C.c_void_p(buf.data_ptr())), "cusparseSDDMM"),
+                2.0 * nnz * Kd)
     r["config"] = ("cfg4 pattern 1M^2 32/row fp32, K = 128, out = A B^T at the pattern "
-                   "(torch.sparse.sampled_addmm -> cusparseSDDMM, beta = 0)")
+                   "(cusparseSDDMM, beta = 0, after cusparseSDDMM_preprocess)")
     out["cfg4_sddmm"] = r
     print(json.dumps({"impl": "cusparse", "metric": METRIC, "n_gpus": 1, "steps": K,
-                      "warmup": warm, "data": DATA, "torch": torch.__version__,
+                      "warmup": warm, "data": DATA, "library": "cuSPARSE (CUDA toolkit, generic API)",
                       "workloads": out}), flush=True)
 
 

@@ -111,16 +111,16 @@ function execute(::B200Backend, ::Op{:SpMV,F}, A::USTensor, x::USTensor, y::USTe
 end
 
 # ----------------------------------------------------------------- SpMM
-# replaces the CUSPARSEBackend SpMM default (CUDAExt/ops/spmm.jl:50-58).  A
-# column-major B (JLUST's native layout) is transposed into a workspace by
-# the library and gathered by rows from there.
+# replaces the CUSPARSEBackend SpMM default (CUDAExt/ops/spmm.jl:50-58).
+# Column-major B and C (JLUST's native layout) go through row-major copies in
+# a workspace the library transposes on the stream.
 function execute(::B200Backend, ::Op{:SpMM,F}, A::USTensor, B::USTensor, C::USTensor;
                  alpha=one(eltype(A)), beta=zero(eltype(A))) where {F}
     format_family(A) === :BSR && return _bsr_spmm(A, B, C, alpha, beta)
     m, n = extents(A); k = size(nonzeros(B), 2)
     bo, ldb = _order(nonzeros(B)); co, ldc = _order(nonzeros(C))
-    wsb = ccall((:jlb_csr_spmm_workspace_size, lib), Csize_t, (Cint, Int64, Int64, Cint),
-                _dt(eltype(A)), n, k, bo)
+    wsb = ccall((:jlb_csr_spmm_workspace_size, lib), Csize_t,
+                (Cint, Int64, Int64, Int64, Cint, Cint), _dt(eltype(A)), m, n, k, bo, co)
     ws = CuArray{UInt8}(undef, Int(wsb))
     st = ccall((:jlb_csr_spmm_ws, lib), Cint,
                (Ptr{Cvoid}, Cint, Cint, Int64, Int64, Int64, CuPtr{Int32}, CuPtr{Int32},

@@ -195,11 +195,19 @@ JLB_API int jlb_spmv_plan_create(jlb_spmv_plan *plan, void *stream, int dtype, i
 JLB_API int jlb_spmv_plan_execute(jlb_spmv_plan plan, void *stream, const void *val,
                                   const void *x, void *y, double alpha, double beta);
 /* Row-length profile recorded by the plan: max and mean entries per row and
- * the variant (0: every row summed by one thread in storage order, i.e.
- * bit-exact with the CPU walker; 1: some rows longer than 32 entries are
- * summed by a warp). */
+ * the kernel variant the plan picked from them (the reference's warp-vector
+ * choice, KA spmv.jl:296-323, re-tuned on B200).  Variant 0: a thread per
+ * row, summing in storage order (bit-exact with the CPU walker) for rows of
+ * up to 32 entries, a warp for longer rows.  Variant W (2, 4, 8, 16, 32):
+ * groups of W lanes per row, 16-byte loads of four columns and values per
+ * lane, a fixed-order butterfly across the group (within tolerance).  The
+ * plan takes 4 when the mean row length is 12 to 40 and no row exceeds 128
+ * entries, else 0. */
 JLB_API int jlb_spmv_plan_info(jlb_spmv_plan plan, int64_t *max_row, double *mean_row,
                                int *variant);
+/* Overrides the plan's variant (0, 2, 4, 8, 16 or 32), e.g. to tune it for
+ * a matrix; no counterpart in the reference. */
+JLB_API int jlb_spmv_plan_set_variant(jlb_spmv_plan plan, int variant);
 JLB_API int jlb_spmv_plan_destroy(jlb_spmv_plan plan);
 
 /* ------------------------------------------------------------------- SpMM */
@@ -217,15 +225,17 @@ JLB_API int jlb_csr_spmm(void *stream, int dtype, int idx_base, int64_t m, int64
                          void *C, int64_t ldc, int c_order, double alpha, double beta);
 
 /* jlb_csr_spmm with a caller workspace, for JLUST's native column-major B
- * (KA spmm.jl:31-38, ext/CUDAExt/ops/spmm.jl:1-4): a column-major B is
- * transposed on the stream into the workspace (n*k values) and its rows are
- * gathered from there by the streaming kernels, whose order of operations --
- * hence whose results -- are those of the row-major case.  Column-major C
- * needs no workspace.  Without a large enough workspace the call behaves as
- * jlb_csr_spmm.  jlb_csr_spmm_workspace_size returns 0 when no workspace is
- * used.  Same contract as execute(::EmitterBackend, ::Op{:SpMM})
- * (KA spmm.jl:397-423). */
-JLB_API size_t jlb_csr_spmm_workspace_size(int dtype, int64_t n, int64_t k, int b_order);
+ * and C (KA spmm.jl:31-38, ext/CUDAExt/ops/spmm.jl:1-4): on the stream, a
+ * column-major B is transposed into the workspace (n*k values) and its rows
+ * are gathered from there, and a column-major C is computed row-major in the
+ * workspace (m*k values; transposed in first when beta != 0) and transposed
+ * out.  The streaming kernels' order of operations -- hence the results --
+ * is the row-major case's.  Without a large enough workspace the call
+ * behaves as jlb_csr_spmm.  jlb_csr_spmm_workspace_size returns 0 when no
+ * workspace is used.  Same contract as execute(::EmitterBackend,
+ * ::Op{:SpMM}) (KA spmm.jl:397-423). */
+JLB_API size_t jlb_csr_spmm_workspace_size(int dtype, int64_t m, int64_t n, int64_t k,
+                                           int b_order, int c_order);
 JLB_API int jlb_csr_spmm_ws(void *stream, int dtype, int idx_base, int64_t m, int64_t n,
                             int64_t nnz, const int32_t *rowptr, const int32_t *colind,
                             const void *val, int64_t k, const void *B, int64_t ldb, int b_order,

@@ -43,9 +43,10 @@ SIGNATURES = {
     "jlb_spmv_plan_execute": (_i, [_p, _p, _p, _p, _p, _d, _d]),
     "jlb_spmv_plan_info": (_i, [_p, _pi64, C.POINTER(_d), C.POINTER(_i)]),
     "jlb_spmv_plan_destroy": (_i, [_p]),
+    "jlb_spmv_plan_set_variant": (_i, [_p, _i]),
     "jlb_csr_spmm": (_i, [_p, _i, _i, _i64, _i64, _i64, _p, _p, _p, _i64, _p, _i64, _i, _p,
                           _i64, _i, _d, _d]),
-    "jlb_csr_spmm_workspace_size": (_sz, [_i, _i64, _i64, _i]),
+    "jlb_csr_spmm_workspace_size": (_sz, [_i, _i64, _i64, _i64, _i, _i]),
     "jlb_csr_spmm_ws": (_i, [_p, _i, _i, _i64, _i64, _i64, _p, _p, _p, _i64, _p, _i64, _i, _p,
                              _i64, _i, _d, _d, _p, _sz]),
     "jlb_sddmm": (_i, [_p, _i, _i, _i64, _i64, _i64, _p, _p, _i64, _p, _i64, _i, _p, _i64, _i,

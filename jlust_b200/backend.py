@@ -217,9 +217,9 @@ def spmm(A: USTensor, B, Cm, alpha=1.0, beta=0.0):
         raise IncompatibleExtents("SpMM: B and C must be row- or column-major strided")
     dev = _same_device(rowptr, colind, val, B, Cm)
     k = B.shape[1]
-    # a column-major B (JLUST's native layout) is transposed into a workspace
-    # and gathered by rows from there
-    wsb = _lib.load().jlb_csr_spmm_workspace_size(dt, n, k, lb[0]) if val.numel() else 0
+    # column-major B and C (JLUST's native layout) go through row-major
+    # copies in a workspace
+    wsb = _lib.load().jlb_csr_spmm_workspace_size(dt, m, n, k, lb[0], lc[0])
     ws = torch.empty(wsb, dtype=torch.uint8, device=dev) if wsb else None
     _lib.call("jlb_csr_spmm_ws", _stream(dev), dt, A.origin.offset, m, n, val.numel(),
               _ptr(rowptr), _ptr(colind), _ptr(val), k, _ptr(B), lb[1], lb[0], _ptr(Cm), lc[1],
@@ -367,6 +367,12 @@ class B200SpMVHandle(AbstractKernelHandle):
         mx, mean, var = C.c_int64(), C.c_double(), C.c_int()
         _lib.call("jlb_spmv_plan_info", self._plan, C.byref(mx), C.byref(mean), C.byref(var))
         return {"max_row": mx.value, "mean_row": mean.value, "variant": var.value}
+
+    def set_variant(self, variant: int):
+        """Force the kernel variant: 0 (a thread per row, bit-exact for rows of
+        up to 32 entries) or W in 2, 4, 8, 16, 32 (groups of W lanes per row)."""
+        _lib.call("jlb_spmv_plan_set_variant", self._plan, int(variant))
+        return self
 
     def execute(self, *args, alpha=1.0, beta=0.0):
         # execute(h, x, y) or execute(h, A, x, y) (KA spmv.jl:533-544)

@@ -373,11 +373,17 @@ class BlockBandedMatrix:
             if tuple(d.shape if isinstance(d, BlockSparseMatrix) else d.extents) != (n_diag_rows, n_cols):
                 raise ValueError(f"BlockBandedMatrix: diagonal block of period {t + 1} is not "
                                  f"{n_diag_rows}x{n_cols}")
+        # a coupling block may be narrower than a period: its columns are the
+        # first ones of the period's x slice, as the reference's fused
+        # periodic kernel indexes them (block_periodic.jl:114-163)
         for k, pairs in enumerate(self.off, start=1):
             for neg, pos in pairs:
-                if neg.extents != (self.n_off_rows[k - 1], n_cols) or pos.extents != neg.extents:
-                    raise ValueError(f"BlockBandedMatrix: level-{k} blocks are not "
-                                     f"{self.n_off_rows[k - 1]}x{n_cols}")
+                for b in (neg, pos):
+                    rows, cols = b.extents
+                    if rows != self.n_off_rows[k - 1] or cols > n_cols:
+                        raise ValueError(f"BlockBandedMatrix: level-{k} blocks must have "
+                                         f"{self.n_off_rows[k - 1]} rows and at most {n_cols} "
+                                         f"columns (got {rows}x{cols})")
         # first row of each period (block_banded.jl _bbm_diag_starts)
         cum = np.concatenate([[0], np.cumsum(self.n_off_rows)]).astype(np.int64)
         starts = [0]
@@ -483,7 +489,7 @@ class _Periodic(_Graphed):
         for b in (neg, pos):
             if b.format.family == "ShiftedDiag":
                 shift, _ = b.format.diag
-                if shift < 0 or M.n_off_rows[0] - 1 + shift >= M.n_cols:
+                if shift < 0 or M.n_off_rows[0] - 1 + shift >= b.extents[1]:
                     raise IncompatibleExtents(f"BlockBandedMatrix: ShiftedDiag coupling block "
                                               f"with shift {shift} reaches outside its columns")
         self.blocks = (d, neg, pos)

@@ -1,32 +1,36 @@
 // bsr_spmm.cu -- BSR (64 x 64 bf16 blocks) x dense bf16 -> fp32 on sm_100a
 // tensor cores: TMA-fed shared-memory tiles, tcgen05.mma, TMEM accumulators.
 //
-// Formulation.  For block row I, C[I*64 : I*64+64, :] = sum over stored blocks
-// (I, J) of A_IJ (64 x 64) x B[J*64 : J*64+64, :].  The MMA computes the
-// transpose, D = B_J^T x A_IJ^T, so that the long side of the output (the N
-// columns of C) is the MMA's M = 128 dimension and the 64 rows of the block are
-// its N = 64 dimension:
-//   MMA A operand  (M=128 x K=16)  = B[J*64 + k, t*128 + m]   -- "MN-major":
-//                   m is contiguous in B's rows; a TMA box of 64 B-columns x
-//                   64 B-rows with 128-byte swizzle is exactly the canonical
-//                   MN-major SW128 atom stack (LBO = 8 KB between the two
-//                   64-column boxes of an M-tile, SBO = 1 KB between 8-row
-//                   groups of K).
-//   MMA B operand  (N=64 x K=16)   = A_IJ[n, k]                 -- "K-major":
-//                   the block's rows are 128-byte rows of a TMA box with
-//                   128-byte swizzle (SBO = 1 KB; K advances 32 bytes per
-//                   16-element step inside the swizzle atom).
-//   D (fp32, TMEM) lane m, column n  = C[I*64 + n, t*128 + m].
-// Each CTA accumulates a whole block row (N/128 M-tiles x 64 TMEM columns),
-// double-buffered so the epilogue of one block row overlaps the MMAs of the
-// next.
+// Formulation.  Block rows are taken in pairs (I, I+1).  A pair's blocks are
+// walked as the merge of the two rows' block-column lists (each row's blocks
+// in its storage order): a group is one block column J with the block of row
+// I, of row I+1 or of both.  For a group the MMA computes
+//   D (M = 128 x N) += A_pair (128 x 64) x B_J (64 x N)
+// with
+//   A operand (M=128 x K=16, K-major) = the two 64 x 64 blocks stacked, row
+//       I's in rows 0-63 and row I+1's in rows 64-127: two 128-byte-swizzled
+//       TMA boxes back to back (SBO = 1 KB between 8-row groups, K advancing
+//       32 bytes per 16-element step inside the swizzle atom).  A row with no
+//       block in J gets a box loaded from outside the value array, which TMA
+//       fills with zeros.
+//   B operand (N x K=16, MN-major) = B[J*64 + k, n]: N/64 boxes of 64 B-columns
+//       x 64 B-rows with 128-byte swizzle, the canonical MN-major atom stack
+//       (LBO = 8 KB between 64-column boxes, SBO = 1 KB between 8-row groups
+//       of K); up to 256 columns per MMA.
+//   D (fp32, TMEM) lane m, column n = C[I*64 + m, n].
+// So a block column both rows hold costs one B slab load and one set of MMAs
+// for two blocks (the band of a block-banded matrix), and every MMA is
+// 128 x N x 16: four per group for N <= 256.  Each CTA accumulates a whole
+// pair (N TMEM columns), double-buffered for N <= 256 so that the epilogue of
+// one pair overlaps the MMAs of the next.
 //
-// Warp roles (192 threads): warp 0 = TMA producer, warp 1 = TMEM owner and MMA
-// issuer, warps 2-5 = epilogue (warp w reads TMEM lanes 32*(w%4) .. +31).  No
-// cluster multicast is used anywhere.  Every mbarrier wait is bounded: on
-// expiry the kernel raises the device error word, all roles leave their
-// loops, the producer waits (bounded) for its outstanding copies, the MMA
-// issuer waits (bounded) for its outstanding MMAs and TMEM is freed.
+// Warp roles (224 threads): warps 0 and 6 = TMA producers (alternate groups;
+// each walks the same merge), warp 1 = TMEM owner and MMA issuer, warps 2-5 =
+// epilogue (warp w reads TMEM lanes 32*(w%4) .. +31, i.e. C rows).  No cluster
+// multicast is used anywhere.  Every mbarrier wait is bounded: on expiry the
+// kernel raises the device error word, all roles leave their loops, every
+// copy issued is waited for (bounded) before exit, the MMA issuer waits
+// (bounded) for its outstanding MMAs and TMEM is freed.
 #include "common.cuh"
 
 #include <cuda.h>
@@ -39,7 +43,7 @@ JLB_DEFINE_DEV_ERROR(bsr)
 namespace bsr {
 
 constexpr int kBS = 64;                        // block size on the tensor path
-constexpr int kThreads = 192;
+constexpr int kThreads = 224;                  // 7 warps: see the kernel's role split
 constexpr uint32_t kATileBytes = kBS * kBS * 2;  // 8 KB
 constexpr uint32_t kBoxBytes = 64 * 128;         // one 64-col x 64-row bf16 box
 constexpr long long kTimeoutCycles = 4000000000ll;  // ~2 s at 2 GHz
@@ -110,13 +114,33 @@ __device__ __forceinline__ void tc_commit(uint32_t bar) {
                  : "memory");
 }
 
-__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
-                                       uint32_t idesc, uint32_t accumulate) {
+
+// The four K-steps (K = 64) of one group into one accumulator, from one asm
+// block: the descriptors' low (address) words advance by the K-step's offset
+// in 16-byte units -- 32 bytes of the K-major A operand (2), 2048 bytes of
+// the MN-major B operand (128) -- so that the issuing thread spends a few
+// register moves per MMA.  `first` == 0 makes the first K-step overwrite the
+// accumulator.
+__device__ __forceinline__ void tc_mma_k64(uint32_t d_tmem, uint32_t a_lo, uint32_t a_hi,
+                                           uint32_t b_lo, uint32_t b_hi, uint32_t idesc,
+                                           uint32_t first) {
     asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        "{\n\t.reg .pred p, q;\n\t.reg .b64 a, b;\n\t.reg .b32 t, u;\n\t"
+        "setp.ne.b32 p, %5, 0;\n\t"
+        "setp.eq.b32 q, %5, %5;\n\t"
+        "mov.b64 a, {%1, %2};\n\t"
+        "mov.b64 b, {%3, %4};\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %6, p;\n\t"
+        "add.u32 t, %1, 2;\n\tadd.u32 u, %3, 128;\n\t"
+        "mov.b64 a, {t, %2};\n\tmov.b64 b, {u, %4};\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %6, q;\n\t"
+        "add.u32 t, %1, 4;\n\tadd.u32 u, %3, 256;\n\t"
+        "mov.b64 a, {t, %2};\n\tmov.b64 b, {u, %4};\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %6, q;\n\t"
+        "add.u32 t, %1, 6;\n\tadd.u32 u, %3, 384;\n\t"
+        "mov.b64 a, {t, %2};\n\tmov.b64 b, {u, %4};\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %6, q;\n\t}"
+        ::"r"(d_tmem), "r"(a_lo), "r"(a_hi), "r"(b_lo), "r"(b_hi), "r"(first), "r"(idesc)
         : "memory");
 }
 
@@ -133,9 +157,12 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t addr, uint32_t lbo, uin
     return d;
 }
 
-// Instruction descriptor: bf16 x bf16 -> f32, A MN-major, B K-major, M=128, N=64.
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 15) | (0u << 16) |
-                            ((64u >> 3) << 17) | ((128u >> 4) << 24);
+// Instruction descriptor: bf16 x bf16 -> f32, A K-major, B MN-major, M = 128,
+// N columns (a multiple of 16, at most 256).
+__host__ __device__ constexpr uint32_t idesc_for(uint32_t n) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | (0u << 15) | (1u << 16) | ((n >> 3) << 17) |
+           ((128u >> 4) << 24);
+}
 
 #define JLB_TMEM_LD32(taddr, r)                                                              \
     asm volatile(                                                                            \
@@ -163,6 +190,8 @@ struct Ctl {
     uint64_t tfull[2];
     uint64_t tempty[2];
     uint64_t mma_done;
+    long long last_fill[kMaxStages];   // last group index copied into each stage
+    uint32_t ginfo[kMaxStages];        // the stage's group: bit 0 first of its pair, bit 1 last
     uint32_t tmem_base;
     int abort;
 };
@@ -178,33 +207,81 @@ __device__ __forceinline__ void mbar_drain(uint32_t bar, uint32_t parity) {
     }
 }
 
-__device__ __forceinline__ uint32_t tmem_cols_for(int n_mt) {
-    const uint32_t need = 2u * (uint32_t)n_mt * 64u;
+__host__ __device__ inline uint32_t tmem_cols_for(int n, int nbuf) {
+    const uint32_t need = (uint32_t)(n * nbuf);
     uint32_t c = 32;
     while (c < need) c <<= 1;
     return c;
 }
 
+// Block-column merge of a pair of block rows: rows a = I and b = I+1 (b may
+// not exist).  next() yields the groups in order: the smallest head block
+// column, with each row whose head it is (each row's blocks stay in their
+// storage order, sorted or not).  The heads are loaded one step ahead.
+struct PairMerge {
+    const int32_t *bcolind;
+    int base;
+    int qa, qa1, qb, qb1;
+    int ja, jb;                     // current heads (block columns), valid while q < q1
+
+    __device__ void init(const int32_t *__restrict__ browptr, const int32_t *__restrict__ bc,
+                         int64_t I, int64_t mb, int b0) {
+        bcolind = bc;
+        base = b0;
+        qa = browptr[I] - base;
+        qa1 = browptr[I + 1] - base;
+        if (I + 1 < mb) {
+            qb = qa1;
+            qb1 = browptr[I + 2] - base;
+        } else {
+            qb = qb1 = 0;
+        }
+        ja = qa < qa1 ? bcolind[qa] - base : 0;
+        jb = qb < qb1 ? bcolind[qb] - base : 0;
+    }
+    __device__ bool done() const { return qa >= qa1 && qb >= qb1; }
+    // group: block column J, entries of row a / row b (-1 when absent)
+    __device__ void next(int &J, int &ea, int &eb) {
+        const bool ha = qa < qa1, hb = qb < qb1;
+        J = ha && hb ? (ja < jb ? ja : jb) : ha ? ja : jb;
+        ea = (ha && ja == J) ? qa : -1;
+        eb = (hb && jb == J) ? qb : -1;
+        if (ea >= 0) {
+            ++qa;
+            ja = qa < qa1 ? bcolind[qa] - base : 0;
+        }
+        if (eb >= 0) {
+            ++qb;
+            jb = qb < qb1 ? bcolind[qb] - base : 0;
+        }
+    }
+};
+
+template <int N>
 __global__ void __launch_bounds__(kThreads, 1)
 bsr_spmm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
             int64_t mb, const int32_t *__restrict__ browptr, const int32_t *__restrict__ bcolind,
-            int base, int n_mt, int stages, float *__restrict__ C, int64_t ldc, float alpha,
-            float beta, int has_beta) {
+            int base, int stages, int64_t zero_row, float *__restrict__ C, int64_t ldc,
+            float alpha, float beta, int has_beta) {
+    constexpr int kNBuf = 2 * N <= 512 ? 2 : 1;            // accumulators in TMEM
+    constexpr int kChunks = N <= 256 ? 1 : 2;               // MMAs per K-step
+    constexpr int kN0 = N <= 256 ? N : 256;                 // columns of the first MMA
+    constexpr uint32_t kStageBytes = 2 * kATileBytes + (uint32_t)(N / 64) * kBoxBytes;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t pad = ((raw + 1023u) & ~1023u) - raw;
     uint8_t *tiles = smem_raw + pad;
     const uint32_t tiles_u32 = raw + pad;
-    const uint32_t stage_bytes = kATileBytes + (uint32_t)n_mt * 2u * kBoxBytes;
-    Ctl *ctl = reinterpret_cast<Ctl *>(tiles + (size_t)stages * stage_bytes);
+    Ctl *ctl = reinterpret_cast<Ctl *>(tiles + (size_t)stages * kStageBytes);
     const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
-    const uint32_t ncols = tmem_cols_for(n_mt);
-    const int64_t N = (int64_t)n_mt * 128;
+    const uint32_t ncols = tmem_cols_for(N, kNBuf);
+    const int64_t npairs = (mb + 1) / 2;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < stages; ++s) {
             mbar_init(smem_u32(&ctl->full[s]), 1);
             mbar_init(smem_u32(&ctl->empty[s]), 1);
+            ctl->last_fill[s] = -1;
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(smem_u32(&ctl->tfull[b]), 1);
@@ -227,31 +304,46 @@ bsr_spmm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     const uint32_t tmem = ctl->tmem_base;
     volatile int *abort_flag = &ctl->abort;
 
-    if (warp == 0 && lane == 0) {
-        // ------------------------------------------------------ TMA producer
-        int stage = 0;
-        uint32_t pe = 1;
-        uint32_t fills[kMaxStages];
-        for (int s = 0; s < kMaxStages; ++s) fills[s] = 0;
+    if ((warp == 0 || warp == 6) && lane == 0) {
+        // ------------------------------------------------------ TMA producers
+        // Two producer threads take alternate groups (one thread's loop --
+        // barrier wait, expect-tx, TMA issues -- costs about as much as a
+        // group's MMAs).  Both walk the same merge; group k of the CTA goes to
+        // stage k % stages, its empty-barrier phase parity follows from
+        // k / stages.
+        const int pid = warp == 0 ? 0 : 1;
+        long long k = 0;
         bool ok = true;
-        for (int64_t I = blockIdx.x; I < mb && ok; I += gridDim.x) {
-            const int q0 = browptr[I] - base, q1 = browptr[I + 1] - base;
-            for (int q = q0; q < q1; ++q) {
-                if (!mbar_wait(smem_u32(&ctl->empty[stage]), pe, abort_flag)) { ok = false; break; }
-                const uint32_t full = smem_u32(&ctl->full[stage]);
-                mbar_arrive_expect_tx(full, stage_bytes);
-                const uint32_t sA = tiles_u32 + (uint32_t)stage * stage_bytes;
-                tma_load_2d(sA, &tmA, full, 0, q * kBS);
-                const int J = bcolind[q] - base;
-                for (int c = 0; c < 2 * n_mt; ++c)
-                    tma_load_2d(sA + kATileBytes + (uint32_t)c * kBoxBytes, &tmB, full, c * 64, J * kBS);
-                fills[stage] += 1;
-                if (++stage == stages) { stage = 0; pe ^= 1; }
+        for (int64_t P = blockIdx.x; P < npairs && ok; P += gridDim.x) {
+            PairMerge mg;
+            mg.init(browptr, bcolind, 2 * P, mb, base);
+            while (!mg.done()) {
+                int J, ea, eb;
+                mg.next(J, ea, eb);
+                const bool last = mg.done();
+                if ((int)(k & 1) == pid) {
+                    const int stage = (int)(k % stages);
+                    const uint32_t pe = (uint32_t)(((k / stages) & 1) ^ 1);
+                    if (!mbar_wait(smem_u32(&ctl->empty[stage]), pe, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t sA = tiles_u32 + (uint32_t)stage * kStageBytes;
+                    const uint32_t full = smem_u32(&ctl->full[stage]);
+                    ctl->ginfo[stage] = (last ? 2u : 0u);
+                    mbar_arrive_expect_tx(full, kStageBytes);
+                    // a missing block: a box wholly past the value array, filled with zeros
+                    tma_load_2d(sA, &tmA, full, 0, ea >= 0 ? ea * kBS : (int32_t)zero_row);
+                    tma_load_2d(sA + kATileBytes, &tmA, full, 0, eb >= 0 ? eb * kBS : (int32_t)zero_row);
+#pragma unroll
+                    for (int c = 0; c < N / 64; ++c)
+                        tma_load_2d(sA + 2 * kATileBytes + (uint32_t)c * kBoxBytes, &tmB, full, c * 64,
+                                    J * kBS);
+                    atomicMax(&ctl->last_fill[stage], k);
+                }
+                ++k;
             }
         }
-        // Let every copy this thread issued land before the CTA can exit.
-        for (int s = 0; s < stages; ++s)
-            if (fills[s]) mbar_drain(smem_u32(&ctl->full[s]), (fills[s] - 1u) & 1u);
     } else if (warp == 1 && lane == 0) {
         // ------------------------------------------------------- MMA issuer
         int stage = 0;
@@ -259,79 +351,110 @@ bsr_spmm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         uint32_t te_phase[2] = {1u, 1u};
         int buf = 0;
         bool ok = true;
-        for (int64_t I = blockIdx.x; I < mb && ok; I += gridDim.x) {
-            const int q0 = browptr[I] - base, q1 = browptr[I + 1] - base;
-            if (q1 <= q0) continue;
+        const uint64_t adesc0 = sdesc_sw128(tiles_u32, 16u, 1024u);
+        const uint64_t bdesc0 = sdesc_sw128(tiles_u32 + 2 * kATileBytes, kBoxBytes, 1024u);
+        const uint32_t a_hi = (uint32_t)(adesc0 >> 32), b_hi = (uint32_t)(bdesc0 >> 32);
+        constexpr uint32_t kId0 = idesc_for(kN0);
+        constexpr uint32_t kId1 = idesc_for(N - kN0 > 0 ? N - kN0 : 16);
+        for (int64_t P = blockIdx.x; P < npairs && ok; P += gridDim.x) {
+            const int64_t I = 2 * P;
+            const int q0 = browptr[I] - base;
+            const int q2 = browptr[I + 1 < mb ? I + 2 : I + 1] - base;
+            if (q2 <= q0) continue;                      // no blocks: the epilogue writes it
             if (!mbar_wait(smem_u32(&ctl->tempty[buf]), te_phase[buf], abort_flag)) { ok = false; break; }
             te_phase[buf] ^= 1u;
             tc_fence_after();
-            const uint32_t dbase = tmem + (uint32_t)(buf * n_mt * 64);
-            for (int q = q0; q < q1; ++q) {
+            const uint32_t dbase = tmem + (uint32_t)(buf * N);
+            uint32_t first = 0;
+            for (;;) {
                 if (!mbar_wait(smem_u32(&ctl->full[stage]), pf, abort_flag)) { ok = false; break; }
                 tc_fence_after();
-                const uint32_t sA = tiles_u32 + (uint32_t)stage * stage_bytes;
-                const uint32_t sB = sA + kATileBytes;
-                for (int t = 0; t < n_mt; ++t) {
-#pragma unroll
-                    for (int s = 0; s < 4; ++s) {
-                        const uint64_t adesc = sdesc_sw128(sB + (uint32_t)t * 2u * kBoxBytes + (uint32_t)s * 2048u, kBoxBytes, 1024u);
-                        const uint64_t bdesc = sdesc_sw128(sA + (uint32_t)s * 32u, 16u, 1024u);
-                        tc_mma(dbase + (uint32_t)t * 64u, adesc, bdesc, kIdesc, (q > q0 || s > 0) ? 1u : 0u);
-                    }
-                }
+                const uint32_t last = ctl->ginfo[stage] & 2u;
+                // the stage's descriptors: only the low (address) word moves,
+                // without carry (addresses below 256 KB)
+                const uint32_t soff = (uint32_t)stage * kStageBytes >> 4;
+                const uint32_t a_lo = (uint32_t)adesc0 + soff, b_lo = (uint32_t)bdesc0 + soff;
+                tc_mma_k64(dbase, a_lo, a_hi, b_lo, b_hi, kId0, first);
+                if (kChunks == 2)
+                    tc_mma_k64(dbase + (uint32_t)kN0, a_lo, a_hi, b_lo + (uint32_t)(4 * kBoxBytes >> 4),
+                               b_hi, kId1, first);
                 tc_commit(smem_u32(&ctl->empty[stage]));
                 if (++stage == stages) { stage = 0; pf ^= 1; }
+                first = 1;
+                if (last) break;
             }
             if (!ok) break;
             tc_commit(smem_u32(&ctl->tfull[buf]));
-            buf ^= 1;
+            buf = (buf + 1) % kNBuf;
         }
         // All MMAs of this thread complete before TMEM can be freed.
         tc_commit(smem_u32(&ctl->mma_done));
         mbar_drain(smem_u32(&ctl->mma_done), 0);
-    } else if (warp >= 2) {
+    } else if (warp >= 2 && warp < 6) {
         // --------------------------------------------------------- epilogue
-        const int qd = warp & 3;  // TMEM lane quarter this warp may read
+        // warp q (= warp % 4) owns TMEM lanes 32q .. 32q+31: C rows I*64 + 32q
+        // + lane, N columns in 32-column loads, stored as 16-byte vectors
+        const int qd = warp & 3;
         uint32_t tf_phase[2] = {0u, 0u};
         int buf = 0;
-        for (int64_t I = blockIdx.x; I < mb; I += gridDim.x) {
-            const int q0 = browptr[I] - base, q1 = browptr[I + 1] - base;
-            const int64_t row0 = I * kBS;
-            if (q1 <= q0) {
-                for (int64_t idx = threadIdx.x - 64; idx < (int64_t)kBS * N; idx += 128) {
-                    float *dst = C + (row0 + idx / N) * ldc + idx % N;
-                    *dst = has_beta ? add_rn(mul_rn(alpha, 0.0f), mul_rn(beta, *dst)) : mul_rn(alpha, 0.0f);
-                }
+        const int64_t nrows = mb * kBS;
+        for (int64_t P = blockIdx.x; P < npairs; P += gridDim.x) {
+            const int64_t I = 2 * P;
+            const int q0 = browptr[I] - base;
+            const int q2 = browptr[I + 1 < mb ? I + 2 : I + 1] - base;
+            const int64_t row = I * kBS + qd * 32 + lane;
+            if (q2 <= q0) {
+                if (row < nrows)
+                    for (int64_t c = 0; c < N; ++c) {
+                        float *dst = C + row * ldc + c;
+                        *dst = has_beta ? add_rn(mul_rn(alpha, 0.0f), mul_rn(beta, *dst))
+                                        : mul_rn(alpha, 0.0f);
+                    }
                 continue;
             }
             if (!mbar_wait(smem_u32(&ctl->tfull[buf]), tf_phase[buf], abort_flag)) break;
             tf_phase[buf] ^= 1u;
             tc_fence_after();
-            for (int t = 0; t < n_mt; ++t) {
-                const int64_t col = (int64_t)t * 128 + qd * 32 + lane;
 #pragma unroll 1
-                for (int h = 0; h < 2; ++h) {
-                    uint32_t r[32];
-                    const uint32_t taddr = tmem + ((uint32_t)(qd * 32) << 16) +
-                                           (uint32_t)(buf * n_mt * 64 + t * 64 + h * 32);
-                    JLB_TMEM_LD32(taddr, r);
-                    tmem_wait_ld();
+            for (int c0 = 0; c0 < N; c0 += 32) {
+                uint32_t r[32];
+                const uint32_t taddr = tmem + ((uint32_t)(qd * 32) << 16) + (uint32_t)(buf * N + c0);
+                JLB_TMEM_LD32(taddr, r);
+                tmem_wait_ld();
+                if (row < nrows) {
+                    float4 *dst = reinterpret_cast<float4 *>(C + row * ldc + c0);
 #pragma unroll
-                    for (int n = 0; n < 32; ++n) {
-                        float *dst = C + (row0 + h * 32 + n) * ldc + col;
-                        float v = mul_rn(alpha, __uint_as_float(r[n]));
-                        if (has_beta) v = add_rn(v, mul_rn(beta, *dst));
-                        *dst = v;
+                    for (int v = 0; v < 8; ++v) {
+                        float4 o;
+                        o.x = mul_rn(alpha, __uint_as_float(r[4 * v + 0]));
+                        o.y = mul_rn(alpha, __uint_as_float(r[4 * v + 1]));
+                        o.z = mul_rn(alpha, __uint_as_float(r[4 * v + 2]));
+                        o.w = mul_rn(alpha, __uint_as_float(r[4 * v + 3]));
+                        if (has_beta) {
+                            const float4 old = dst[v];
+                            o.x = add_rn(o.x, mul_rn(beta, old.x));
+                            o.y = add_rn(o.y, mul_rn(beta, old.y));
+                            o.z = add_rn(o.z, mul_rn(beta, old.z));
+                            o.w = add_rn(o.w, mul_rn(beta, old.w));
+                        }
+                        dst[v] = o;
                     }
                 }
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(&ctl->tempty[buf]));
-            buf ^= 1;
+            buf = (buf + 1) % kNBuf;
         }
     }
 
+    __syncthreads();
+    // every copy issued lands before the CTA can exit (they all have when the
+    // MMA issuer consumed every stage; an aborted run may leave some in flight)
+    if (threadIdx.x == 0)
+        for (int st = 0; st < stages; ++st)
+            if (ctl->last_fill[st] >= 0)
+                mbar_drain(smem_u32(&ctl->full[st]), (uint32_t)((ctl->last_fill[st] / stages) & 1));
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
@@ -402,9 +525,11 @@ static int make_map(CUtensorMap *map, const void *base, uint64_t inner, uint64_t
 }
 
 bool tc_eligible(int bs, int64_t N, int64_t ldb, const void *bval, const void *B, int64_t nnzb,
-                 int64_t nb) {
+                 int64_t nb, const float *C, int64_t ldc) {
+    // TMA coordinates are int32: the zero-filled box starts at row nnzb * 64
     return bs == kBS && N % 128 == 0 && N >= 128 && N <= 512 && ldb % 8 == 0 && aligned16(bval) &&
-           aligned16(B) && nnzb > 0 && nnzb * kBS < (int64_t)UINT32_MAX && nb * kBS < (int64_t)INT32_MAX;
+           aligned16(B) && aligned16(C) && ldc % 4 == 0 && nnzb > 0 &&
+           nnzb * kBS + kBS < (int64_t)INT32_MAX && nb * kBS < (int64_t)INT32_MAX;
 }
 
 }  // namespace bsr
@@ -427,14 +552,13 @@ extern "C" JLB_API int jlb_bsr_spmm(void *stream, int idx_base, int64_t mb, int6
         return fail(JLB_ERR_INVALID_ARGUMENT, "null buffer");
     cudaStream_t st = as_stream(stream);
     const float a = (float)alpha, b = (float)beta;
-    if (bsr::tc_eligible(bs, N, ldb, bval, B, nnzb, nb)) {
+    if (bsr::tc_eligible(bs, N, ldb, bval, B, nnzb, nb, C, ldc)) {
         CUtensorMap tmA, tmB;
         int r = bsr::make_map(&tmA, bval, 64, (uint64_t)nnzb * 64, 128);
         if (r) return r;
         r = bsr::make_map(&tmB, B, (uint64_t)N, (uint64_t)nb * 64, (uint64_t)ldb * 2);
         if (r) return r;
-        const int n_mt = (int)(N / 128);
-        const uint32_t stage_bytes = bsr::kATileBytes + (uint32_t)n_mt * 2u * bsr::kBoxBytes;
+        const uint32_t stage_bytes = 2 * bsr::kATileBytes + (uint32_t)(N / 64) * bsr::kBoxBytes;
         const size_t budget = 227 * 1024 - 1024 - sizeof(bsr::Ctl) - 64;
         int stages = (int)(budget / stage_bytes);
         if (stages > bsr::kMaxStages) stages = bsr::kMaxStages;
@@ -443,10 +567,22 @@ extern "C" JLB_API int jlb_bsr_spmm(void *stream, int idx_base, int64_t mb, int6
         int dev = 0, sms = 148;
         JLB_CUDA(cudaGetDevice(&dev));
         JLB_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-        JLB_CUDA(cudaFuncSetAttribute(bsr::bsr_spmm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        const unsigned grid = (unsigned)(mb < sms ? mb : sms);
-        bsr::bsr_spmm_tc<<<grid, bsr::kThreads, smem, st>>>(tmA, tmB, mb, browptr, bcolind, idx_base,
-                                                            n_mt, stages, C, ldc, a, b, b != 0.0f);
+        const int64_t npairs = (mb + 1) / 2;
+        const unsigned grid = (unsigned)(npairs < sms ? npairs : sms);
+        const int64_t zero_row = nnzb * 64;       // a box wholly past the values: zeros
+#define JLB_BSR_TC(NN)                                                                          \
+    JLB_CUDA(cudaFuncSetAttribute(bsr::bsr_spmm_tc<NN>,                                         \
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));    \
+    bsr::bsr_spmm_tc<NN><<<grid, bsr::kThreads, smem, st>>>(tmA, tmB, mb, browptr, bcolind,     \
+                                                            idx_base, stages, zero_row, C, ldc, \
+                                                            a, b, b != 0.0f)
+        switch (N) {
+            case 128: JLB_BSR_TC(128); break;
+            case 256: JLB_BSR_TC(256); break;
+            case 384: JLB_BSR_TC(384); break;
+            default: JLB_BSR_TC(512); break;
+        }
+#undef JLB_BSR_TC
         JLB_LAUNCH_CHECK("bsr_spmm_tc");
         return ok();
     }

@@ -570,32 +570,57 @@ int launch_fast_any(cudaStream_t st, int base, int64_t m, int64_t nnz, int64_t k
 }
 
 // out (cols x rows, row-major, leading dim ldo) = in^T for in rows x cols
-// row-major (leading dim ldi): 32 x 32 tiles through shared memory, both
-// sides coalesced.  Turns a column-major n x k B (a row-major k x n array)
-// into the row-major n x k copy the stream kernels gather rows from.
+// row-major (leading dim ldi): 64 x 64 tiles through shared memory (padded a
+// column, no bank conflicts either way), 16 loads in flight per thread, both
+// sides in 128-byte warp accesses.  Turns a column-major n x k B (a row-major
+// k x n array) into the row-major n x k copy the stream kernels gather rows
+// from, and a row-major C back into a column-major one.
+constexpr int kTile = 64;
 template <typename T>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, 4)
 transpose_tiles(int64_t rows, int64_t cols, const T *__restrict__ in, int64_t ldi,
                 T *__restrict__ out, int64_t ldo) {
-    __shared__ T tile[32][33];
-    const int64_t c0 = (int64_t)blockIdx.x * 32;
-    for (int64_t r0 = (int64_t)blockIdx.y * 32; r0 < rows; r0 += (int64_t)gridDim.y * 32) {
+    __shared__ T tile[kTile][kTile + 1];
+    const int tx = threadIdx.x % kTile, ty = threadIdx.x / kTile;   // 64 x 4 threads
+    const int64_t c0 = (int64_t)blockIdx.x * kTile;
+    for (int64_t r0 = (int64_t)blockIdx.y * kTile; r0 < rows; r0 += (int64_t)gridDim.y * kTile) {
+        const int64_t c = c0 + tx;
 #pragma unroll
-        for (int i = threadIdx.y; i < 32; i += 8) {
-            const int64_t r = r0 + i, c = c0 + threadIdx.x;
-            if (r < rows && c < cols) tile[i][threadIdx.x] = in[r * ldi + c];
+        for (int j = 0; j < kTile / 4; ++j) {
+            const int64_t r = r0 + ty + 4 * j;
+            if (r < rows && c < cols) tile[ty + 4 * j][tx] = __ldcs(in + r * ldi + c);
         }
         __syncthreads();
+        const int64_t ocol = r0 + tx;
 #pragma unroll
-        for (int i = threadIdx.y; i < 32; i += 8) {
-            const int64_t orow = c0 + i, ocol = r0 + threadIdx.x;
-            if (orow < cols && ocol < rows) out[orow * ldo + ocol] = tile[threadIdx.x][i];
+        for (int j = 0; j < kTile / 4; ++j) {
+            const int64_t orow = c0 + ty + 4 * j;
+            if (orow < cols && ocol < rows) __stcs(out + orow * ldo + ocol, tile[tx][ty + 4 * j]);
         }
         __syncthreads();
     }
 }
 
 inline size_t bt_bytes(int64_t n, int64_t k, size_t es) { return (size_t)n * (size_t)k * es + 256; }
+
+// Workspace of a call with column-major operands: [row-major copy of B (n x k)
+// when B is column-major | row-major C (m x k) when C is column-major], each
+// part 256-byte aligned.
+inline size_t ws_bytes_for(int64_t m, int64_t n, int64_t k, int b_order, int c_order, size_t es) {
+    size_t b = 0;
+    if (b_order == JLB_COL_MAJOR && n > 0 && k > 0) b += bt_bytes(n, k, es);
+    if (c_order == JLB_COL_MAJOR && m > 0 && k > 0) b += bt_bytes(m, k, es);
+    return b;
+}
+
+template <typename T>
+void transpose(cudaStream_t st, int64_t rows, int64_t cols, const T *in, int64_t ldi, T *out,
+               int64_t ldo) {
+    const int64_t gx = ceil_div(cols, kTile);
+    const int64_t gy = ceil_div(rows, kTile) < 65535 ? ceil_div(rows, kTile) : 65535;
+    transpose_tiles<T><<<dim3((unsigned)gx, (unsigned)gy), 256, 0, st>>>(rows, cols, in, ldi, out,
+                                                                       ldo);
+}
 
 template <typename T>
 int launch(cudaStream_t st, int base, int64_t m, int64_t n, int64_t nnz, int64_t k,
@@ -610,21 +635,50 @@ int launch(cudaStream_t st, int base, int64_t m, int64_t n, int64_t nnz, int64_t
                         c_order == JLB_COL_MAJOR;
     const bool shape_fast = m < INT32_MAX && k % E == 0 && c_fast;
     const bool col_c = c_order == JLB_COL_MAJOR;
-    if (shape_fast && b_order == JLB_ROW_MAJOR && ldb % E == 0 && aligned16(B))
+    const bool b_fast = b_order == JLB_ROW_MAJOR && ldb % E == 0 && aligned16(B);
+    // Column-major operands (Julia's layout).  A column-major B row is k
+    // strided elements, each in its own sector, and a column-major C row is
+    // k stores 4*m bytes apart (a different page each): with a workspace, B
+    // is transposed once into a row-major copy whose rows are gathered, and
+    // C is computed row-major in the workspace and transposed out (in first
+    // as well when beta != 0).  The arithmetic is the row-major path's.
+    const bool b_col = b_order == JLB_COL_MAJOR;
+    if (m < INT32_MAX && k % E == 0 && (b_col || b_fast) && (b_col || col_c) && ws &&
+        ws_bytes >= ws_bytes_for(m, n, k, b_order, c_order, sizeof(T))) {
+        uintptr_t cur = (reinterpret_cast<uintptr_t>(ws) + 255) & ~(uintptr_t)255;
+        const T *bsrc = (const T *)B;
+        int64_t ldb_use = ldb;
+        if (b_col && n > 0) {
+            T *bt = reinterpret_cast<T *>(cur);
+            cur = (cur + (size_t)n * (size_t)k * sizeof(T) + 255) & ~(uintptr_t)255;
+            transpose<T>(st, k, n, (const T *)B, ldb, bt, k);
+            JLB_LAUNCH_CHECK("transpose_tiles (B)");
+            bsrc = bt;
+            ldb_use = k;
+        }
+        T *cdst = (T *)C;
+        int64_t ldc_use = ldc;
+        if (col_c) {
+            cdst = reinterpret_cast<T *>(cur);
+            ldc_use = k;
+            if (b != T(0)) {
+                transpose<T>(st, k, m, (const T *)C, ldc, cdst, k);
+                JLB_LAUNCH_CHECK("transpose_tiles (C in)");
+            }
+        }
+        int rc = launch_fast_any<T>(st, base, m, nnz, k, rowptr, colind, (const T *)val, bsrc,
+                                    ldb_use, cdst, ldc_use, false, a, b);
+        if (rc != JLB_OK) return rc;
+        if (col_c) {
+            transpose<T>(st, m, k, cdst, k, (T *)C, ldc);
+            JLB_LAUNCH_CHECK("transpose_tiles (C out)");
+        }
+        return ok();
+    }
+    // row-major B; C row-major, or column-major stored by scalars (no workspace)
+    if (shape_fast && b_fast)
         return launch_fast_any<T>(st, base, m, nnz, k, rowptr, colind, (const T *)val,
                                   (const T *)B, ldb, (T *)C, ldc, col_c, a, b);
-    // column-major B (Julia's layout): a B row is k strided elements, each
-    // in its own sector; with a workspace it is transposed once into a
-    // row-major copy and the rows are gathered from that
-    if (shape_fast && b_order == JLB_COL_MAJOR && ws && ws_bytes >= bt_bytes(n, k, sizeof(T)) && n > 0) {
-        T *bt = reinterpret_cast<T *>((reinterpret_cast<uintptr_t>(ws) + 255) & ~(uintptr_t)255);
-        const int64_t gy = ceil_div(k, 32) < 65535 ? ceil_div(k, 32) : 65535;
-        transpose_tiles<T><<<dim3((unsigned)ceil_div(n, 32), (unsigned)gy), dim3(32, 8), 0, st>>>(
-            k, n, (const T *)B, ldb, bt, k);
-        JLB_LAUNCH_CHECK("transpose_tiles");
-        return launch_fast_any<T>(st, base, m, nnz, k, rowptr, colind, (const T *)val, bt, k,
-                                  (T *)C, ldc, col_c, a, b);
-    }
     const int64_t total = m * k;
     const unsigned grid = (unsigned)(ceil_div(total, 256) < 148 * 32 ? ceil_div(total, 256) : 148 * 32);
     spmm_generic<T><<<grid, 256, 0, st>>>(m, k, rowptr, colind, (const T *)val, (const T *)B,
@@ -671,9 +725,9 @@ extern "C" JLB_API int jlb_csr_spmm(void *stream, int dtype, int idx_base, int64
                     ldc, c_order, alpha, beta, nullptr, 0);
 }
 
-extern "C" JLB_API size_t jlb_csr_spmm_workspace_size(int dtype, int64_t n, int64_t k, int b_order) {
-    if (b_order != JLB_COL_MAJOR || n <= 0 || k <= 0) return 0;
-    return spmm::bt_bytes(n, k, dtype == JLB_F64 ? 8 : 4);
+extern "C" JLB_API size_t jlb_csr_spmm_workspace_size(int dtype, int64_t m, int64_t n, int64_t k,
+                                                      int b_order, int c_order) {
+    return spmm::ws_bytes_for(m, n, k, b_order, c_order, dtype == JLB_F64 ? 8 : 4);
 }
 
 extern "C" JLB_API int jlb_csr_spmm_ws(void *stream, int dtype, int idx_base, int64_t m, int64_t n,

@@ -31,6 +31,7 @@ namespace spmv {
 
 constexpr int kThreads = 256;
 constexpr int kShortMax = 32;   // longest row summed by a single thread
+constexpr double kScalarMean = 12.0;   // thread per row up to this mean row length
 
 template <typename T, bool kBeta>
 __device__ __forceinline__ void write_row(T *y, int64_t r, T acc, T alpha, T beta) {
@@ -93,11 +94,125 @@ spmv_rows(int64_t m, const int32_t *__restrict__ rowptr, const int32_t *__restri
         const int src = __ffs(longs) - 1;
         longs &= longs - 1;
         const int l = __shfl_sync(0xffffffffu, lo, src), h = __shfl_sync(0xffffffffu, hi, src);
+        // lane-strided over the row, four entries of each lane in flight:
+        // their columns and values, then their four x gathers, then the sums
         T acc = T(0);
-        for (int k = l + lane; k < h; k += kWarp)
+        int k = l + lane;
+        for (; k + 3 * kWarp < h; k += 4 * kWarp) {
+            int c[4];
+            T v[4], xv[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                c[u] = __ldcs(colind + k + u * kWarp);
+                v[u] = __ldcs(val + k + u * kWarp);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) xv[u] = ldg(x + (c[u] - base));
+#pragma unroll
+            for (int u = 0; u < 4; ++u) acc = add_rn(acc, mul_rn(v[u], xv[u]));
+        }
+        for (; k < h; k += kWarp)
             acc = add_rn(acc, mul_rn(__ldcs(val + k), ldg(x + (__ldcs(colind + k) - base))));
         acc = warp_sum(acc);
         if (lane == src) write_row<T, kBeta>(y, r, acc, alpha, beta);
+    }
+}
+
+// ------------------------------------------------------- vector-per-row
+// Four consecutive entries [q, q+4) of the value and column arrays: one
+// 16-byte load of columns and 16-byte loads of values when the quad lies
+// inside the arrays (q is a multiple of 4 and both arrays are 16-byte
+// aligned), scalar loads of the valid entries otherwise.
+template <typename T>
+struct Quad {
+    int c[4];
+    T v[4];
+};
+
+template <typename T>
+__device__ __forceinline__ void load_quad(Quad<T> &d, int q, int lo, int hi, int nnz,
+                                          const int32_t *__restrict__ colind,
+                                          const T *__restrict__ val) {
+    if (q + 4 <= nnz) {
+        const int4 c = __ldcs(reinterpret_cast<const int4 *>(colind + q));
+        d.c[0] = c.x; d.c[1] = c.y; d.c[2] = c.z; d.c[3] = c.w;
+        if constexpr (sizeof(T) == 8) {
+            const double2 a = __ldcs(reinterpret_cast<const double2 *>(val + q));
+            const double2 b = __ldcs(reinterpret_cast<const double2 *>(val + q + 2));
+            d.v[0] = a.x; d.v[1] = a.y; d.v[2] = b.x; d.v[3] = b.y;
+        } else {
+            const float4 a = __ldcs(reinterpret_cast<const float4 *>(val + q));
+            d.v[0] = a.x; d.v[1] = a.y; d.v[2] = a.z; d.v[3] = a.w;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const bool in = q + i >= lo && q + i < hi;
+            d.c[i] = in ? ldg(colind + q + i) : 0;
+            d.v[i] = in ? ldg(val + q + i) : T(0);
+        }
+    }
+}
+
+// Rows summed by groups of W lanes (W = 2 .. 32, the reference's warp-vector
+// width VS, KA spmv.jl:296-323).  Lane l of a row's group takes the quads
+// q = a0 + 4*l, a0 + 4*(l + W), ... (a0 = the row's first entry rounded down
+// to a multiple of 4), two at a time, adds the products of the quads'
+// entries that belong to the row in storage order, and the group adds its W
+// partial sums with a fixed xor butterfly: deterministic, within tolerance
+// of the sequential sum.  The W lanes of a group read 16*W contiguous bytes of columns and
+// 32*W (fp64) or 16*W (fp32) of values per step.
+template <int W, typename T>
+__device__ __forceinline__ T group_sum(T v) {
+#pragma unroll
+    for (int o = W / 2; o > 0; o >>= 1) v = add_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+template <typename T, int W, bool kBeta>
+__global__ void __launch_bounds__(kThreads)
+spmv_vec(int64_t m, int nnz, const int32_t *__restrict__ rowptr,
+         const int32_t *__restrict__ colind, const T *__restrict__ val,
+         const T *__restrict__ x, T *__restrict__ y, T alpha, T beta, int base) {
+    constexpr int kRowsPerCta = kThreads / W;
+    const int lane = threadIdx.x % W;
+    const int64_t stride = (int64_t)gridDim.x * kRowsPerCta;
+    // every lane of a warp runs the same number of row iterations (the
+    // stride is a whole number of warps' rows), so the butterfly below sees
+    // the whole warp converged
+    const int64_t first = (int64_t)blockIdx.x * kRowsPerCta + threadIdx.x / W;
+    const int64_t warp_first = first - (threadIdx.x % kWarp) / W;
+    for (int64_t r0 = warp_first; r0 < m; r0 += stride) {
+        const int64_t r = r0 + (threadIdx.x % kWarp) / W;
+        const bool live = r < m;
+        int lo = 0, hi = 0;
+        if (live) {
+            lo = ldg(rowptr + r) - base;
+            hi = ldg(rowptr + r + 1) - base;
+        }
+        T acc = T(0);
+        // two quads of the lane in flight per step: both quads' loads, then
+        // their eight x gathers, then the sums in entry order
+        for (int q = (lo & ~3) + 4 * lane; q < hi; q += 8 * W) {
+            Quad<T> d0, d1;
+            const int q1 = q + 4 * W;
+            load_quad<T>(d0, q, lo, hi, nnz, colind, val);
+            if (q1 < hi) load_quad<T>(d1, q1, lo, hi, nnz, colind, val);
+            T xs0[4], xs1[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                xs0[i] = (q + i >= lo && q + i < hi) ? ldg(x + (d0.c[i] - base)) : T(0);
+                xs1[i] = (q1 + i < hi) ? ldg(x + (d1.c[i] - base)) : T(0);
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                if (q + i >= lo && q + i < hi) acc = add_rn(acc, mul_rn(d0.v[i], xs0[i]));
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                if (q1 + i < hi) acc = add_rn(acc, mul_rn(d1.v[i], xs1[i]));
+        }
+        acc = group_sum<W>(acc);
+        if (live && lane == 0) write_row<T, kBeta>(y, r, acc, alpha, beta);
     }
 }
 
@@ -171,6 +286,18 @@ int launch_dcsr(cudaStream_t st, int base, int64_t nrows, int64_t nfib, const in
     return ok();
 }
 
+template <typename T, int W>
+void launch_vec(cudaStream_t st, int base, int64_t m, int64_t nnz, const int32_t *rowptr,
+                const int32_t *colind, const T *val, const T *x, T *y, T a, T b) {
+    constexpr int kRowsPerCta = kThreads / W;
+    const int64_t need = ceil_div(m, kRowsPerCta);
+    const unsigned grid = (unsigned)(need < 148 * 16 ? need : 148 * 16);
+    if (b == T(0))
+        spmv_vec<T, W, false><<<grid, kThreads, 0, st>>>(m, (int)nnz, rowptr, colind, val, x, y, a, b, base);
+    else
+        spmv_vec<T, W, true><<<grid, kThreads, 0, st>>>(m, (int)nnz, rowptr, colind, val, x, y, a, b, base);
+}
+
 template <typename T>
 int launch(cudaStream_t st, int base, int64_t m, int64_t nnz, const int32_t *rowptr,
            const int32_t *colind, const void *val, const void *x, void *y, double alpha,
@@ -188,6 +315,33 @@ int launch(cudaStream_t st, int base, int64_t m, int64_t nnz, const int32_t *row
     return ok();
 }
 
+// Variant 0: a thread per row (bit-exact for rows of up to kShortMax entries),
+// the warp for longer rows.  Variant W in {2, 4, 8, 16, 32}: groups of W
+// lanes per row; they need 16-byte aligned colind and val (else variant 0
+// runs).
+template <typename T>
+int launch_variant(cudaStream_t st, int base, int64_t m, int64_t nnz, const int32_t *rowptr,
+                   const int32_t *colind, const void *val, const void *x, void *y, double alpha,
+                   double beta, int variant) {
+    if (m == 0) return ok();
+    if (variant != 0 && aligned16(colind) && aligned16(val)) {
+        const T a = (T)alpha, b = (T)beta;
+        const T *v = (const T *)val, *xx = (const T *)x;
+        T *yy = (T *)y;
+        switch (variant) {
+            case 2: launch_vec<T, 2>(st, base, m, nnz, rowptr, colind, v, xx, yy, a, b); break;
+            case 4: launch_vec<T, 4>(st, base, m, nnz, rowptr, colind, v, xx, yy, a, b); break;
+            case 8: launch_vec<T, 8>(st, base, m, nnz, rowptr, colind, v, xx, yy, a, b); break;
+            case 16: launch_vec<T, 16>(st, base, m, nnz, rowptr, colind, v, xx, yy, a, b); break;
+            default: launch_vec<T, 32>(st, base, m, nnz, rowptr, colind, v, xx, yy, a, b); break;
+        }
+        JLB_LAUNCH_CHECK("spmv_vec");
+        return ok();
+    }
+    return launch<T>(st, base, m, nnz, rowptr, colind, val, x, y, alpha, beta);
+}
+
+
 // ------------------------------------------------------------- validation
 static __device__ int g_validate_flags;
 
@@ -195,7 +349,8 @@ __global__ void csr_validate_kernel(int64_t m, int64_t n, int64_t nnz,
                                     const int32_t *__restrict__ rowptr,
                                     const int32_t *__restrict__ colind, int base,
                                     int require_sorted, int32_t *__restrict__ stats) {
-    // stats[0] = max row length, stats[1] = rows longer than kShortMax
+    // stats[0] = max row length, stats[1] = rows longer than kShortMax,
+    // stats[2] = entries in those rows
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < m; r += stride) {
         const int64_t lo = (int64_t)rowptr[r] - base, hi = (int64_t)rowptr[r + 1] - base;
@@ -204,7 +359,10 @@ __global__ void csr_validate_kernel(int64_t m, int64_t n, int64_t nnz,
         if (hi < lo || lo < 0 || hi > nnz) { atomicOr(&g_validate_flags, 4); continue; }
         if (stats) {
             atomicMax(&stats[0], (int32_t)(hi - lo));
-            if (hi - lo > kShortMax) atomicAdd(&stats[1], 1);
+            if (hi - lo > kShortMax) {
+                atomicAdd(&stats[1], 1);
+                atomicAdd(&stats[2], (int32_t)(hi - lo));
+            }
         }
         int64_t prev = -1;
         for (int64_t k = lo; k < hi; ++k) {
@@ -219,7 +377,7 @@ __global__ void csr_validate_kernel(int64_t m, int64_t n, int64_t nnz,
 }  // namespace spmv
 
 // Runs the validation kernel; on success optionally returns (max row length,
-// rows longer than kShortMax) through stats_host.
+// rows longer than kShortMax, entries in them) through stats_host.
 int csr_validate_impl(cudaStream_t st, int base, int64_t m, int64_t n, int64_t nnz,
                       const int32_t *rowptr, const int32_t *colind, int require_sorted,
                       int32_t *stats_dev, int32_t *stats_host) {
@@ -230,7 +388,7 @@ int csr_validate_impl(cudaStream_t st, int base, int64_t m, int64_t n, int64_t n
     const int zero = 0;
     JLB_CUDA(cudaMemcpyToSymbolAsync(spmv::g_validate_flags, &zero, sizeof(int), 0,
                                      cudaMemcpyHostToDevice, st));
-    if (stats_dev) JLB_CUDA(cudaMemsetAsync(stats_dev, 0, 2 * sizeof(int32_t), st));
+    if (stats_dev) JLB_CUDA(cudaMemsetAsync(stats_dev, 0, 3 * sizeof(int32_t), st));
     if (m > 0) {
         const unsigned grid = (unsigned)(ceil_div(m, 256) < 148 * 16 ? ceil_div(m, 256) : 148 * 16);
         spmv::csr_validate_kernel<<<grid, 256, 0, st>>>(m, n, nnz, rowptr, colind, base,
@@ -247,7 +405,7 @@ int csr_validate_impl(cudaStream_t st, int base, int64_t m, int64_t n, int64_t n
     JLB_CUDA(cudaMemcpyFromSymbolAsync(&flags, spmv::g_validate_flags, sizeof(int), 0,
                                        cudaMemcpyDeviceToHost, st));
     if (stats_dev && stats_host)
-        JLB_CUDA(cudaMemcpyAsync(stats_host, stats_dev, 2 * sizeof(int32_t),
+        JLB_CUDA(cudaMemcpyAsync(stats_host, stats_dev, 3 * sizeof(int32_t),
                                  cudaMemcpyDeviceToHost, st));
     JLB_CUDA(cudaStreamSynchronize(st));
     if (flags & 1) return fail(JLB_ERR_NONCANONICAL_STORAGE, "rowptr[0] != idx_base");
@@ -339,8 +497,32 @@ struct jlb_spmv_plan_s {
     const int32_t *rowptr, *colind;
     int64_t max_row;
     int64_t long_rows;
+    int64_t long_nnz;
     int variant;
 };
+
+namespace jlb {
+namespace spmv {
+// Kernel variant from the row-length profile: a thread per row while every
+// row is short and rows are short on average (bit-exact with the CPU
+// walker), otherwise groups of W lanes per row with W from the mean row
+// length (the reference's warp-vector table, KA spmv.jl:296-323, scaled by
+// the four entries a lane loads at once).
+int choose_variant(int64_t m, int64_t nnz, int64_t max_row, int64_t long_nnz) {
+    if (m == 0) return 0;
+    const double mean = (double)nnz / (double)m;
+    // measured on B200 (fp64): the thread per row wins on regular short rows
+    // (5-point Laplacian) and on power-law rows (its warp path takes the
+    // long ones); groups of 4 lanes win on uniform rows of 16 to 48 entries;
+    // on longer rows the two are level (both bound by the x gathers' L1
+    // sector throughput), and variant 0 keeps its bit-exact short rows
+    (void)long_nnz;
+    if (max_row <= kShortMax && mean <= kScalarMean) return 0;
+    if (mean >= kScalarMean && mean < 40.0 && max_row <= 4 * kShortMax) return 4;
+    return 0;
+}
+}  // namespace spmv
+}  // namespace jlb
 
 extern "C" JLB_API int jlb_spmv_plan_create(jlb_spmv_plan *plan, void *stream, int dtype,
                                             int idx_base, int64_t m, int64_t n, int64_t nnz,
@@ -351,8 +533,8 @@ extern "C" JLB_API int jlb_spmv_plan_create(jlb_spmv_plan *plan, void *stream, i
                        (const void *)1, (void *)1);
     if (st) return st;
     int32_t *stats_dev = nullptr;
-    JLB_CUDA(cudaMallocAsync((void **)&stats_dev, 2 * sizeof(int32_t), as_stream(stream)));
-    int32_t stats[2] = {0, 0};
+    JLB_CUDA(cudaMallocAsync((void **)&stats_dev, 3 * sizeof(int32_t), as_stream(stream)));
+    int32_t stats[3] = {0, 0, 0};
     st = csr_validate_impl(as_stream(stream), idx_base, m, n, nnz, rowptr, colind, 0, stats_dev,
                            stats);
     cudaFreeAsync(stats_dev, as_stream(stream));
@@ -363,8 +545,18 @@ extern "C" JLB_API int jlb_spmv_plan_create(jlb_spmv_plan *plan, void *stream, i
     p->rowptr = rowptr; p->colind = colind;
     p->max_row = stats[0];
     p->long_rows = stats[1];
-    p->variant = stats[1] == 0 ? 0 : 1;
+    p->long_nnz = stats[2];
+    p->variant = spmv::choose_variant(m, nnz, p->max_row, p->long_nnz);
     *plan = p;
+    return ok();
+}
+
+extern "C" JLB_API int jlb_spmv_plan_set_variant(jlb_spmv_plan p, int variant) {
+    if (!p) return fail(JLB_ERR_INVALID_ARGUMENT, "null plan");
+    if (variant != 0 && variant != 2 && variant != 4 && variant != 8 && variant != 16 && variant != 32)
+        return fail(JLB_ERR_INVALID_ARGUMENT, "SpMV variant must be 0, 2, 4, 8, 16 or 32 (got %d)",
+                    variant);
+    p->variant = variant;
     return ok();
 }
 
@@ -374,10 +566,10 @@ extern "C" JLB_API int jlb_spmv_plan_execute(jlb_spmv_plan p, void *stream, cons
     int st = spmv_args(p->dtype, p->base, p->m, p->n, p->nnz, p->rowptr, p->colind, val, x, y);
     if (st) return st;
     if (p->dtype == JLB_F64)
-        return spmv::launch<double>(as_stream(stream), p->base, p->m, p->nnz, p->rowptr,
-                                    p->colind, val, x, y, alpha, beta);
-    return spmv::launch<float>(as_stream(stream), p->base, p->m, p->nnz, p->rowptr, p->colind,
-                               val, x, y, alpha, beta);
+        return spmv::launch_variant<double>(as_stream(stream), p->base, p->m, p->nnz, p->rowptr,
+                                            p->colind, val, x, y, alpha, beta, p->variant);
+    return spmv::launch_variant<float>(as_stream(stream), p->base, p->m, p->nnz, p->rowptr,
+                                       p->colind, val, x, y, alpha, beta, p->variant);
 }
 
 extern "C" JLB_API int jlb_spmv_plan_info(jlb_spmv_plan p, int64_t *max_row, double *mean_row,

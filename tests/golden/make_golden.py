@@ -56,6 +56,20 @@ KATS = {
                 "val": [1.0, 4.0, 3.0, 2.0, 5.0]},
         "decomposer_visits": [[[0, 0], 1.0], [[0, 2], 2.0], [[1, 1], 3.0], [[2, 0], 4.0],
                               [[2, 2], 5.0]]},
+    "bsm_diagonal": {
+        "source": "test/test_emitter_cuda.jl:297-310 (BlockSparseMatrix([A1 nothing; nothing A2]))",
+        "blocks": {"0,0": {"m": 2, "n": 3, "rowptr": [1, 3, 4], "colind": [1, 3, 2],
+                           "val": [1.0, 2.0, 3.0], "base": 1},
+                   "1,1": {"m": 2, "n": 3, "rowptr": [1, 2, 4], "colind": [2, 1, 3],
+                           "val": [1.0, 1.0, 1.0], "base": 1}},
+        "grid": [2, 2], "x": [1.0, 2.0, 3.0, 4.0, 5.0, 6.0], "y": [7.0, 6.0, 5.0, 10.0]},
+    "bsm_accumulate": {
+        "source": "test/test_emitter_cuda.jl:312-322 (BlockSparseMatrix([A1 A2]))",
+        "blocks": {"0,0": {"m": 2, "n": 3, "rowptr": [1, 3, 4], "colind": [1, 3, 2],
+                           "val": [1.0, 2.0, 3.0], "base": 1},
+                   "0,1": {"m": 2, "n": 3, "rowptr": [1, 2, 4], "colind": [2, 1, 3],
+                           "val": [1.0, 1.0, 1.0], "base": 1}},
+        "grid": [1, 2], "x": [1.0, 2.0, 3.0, 1.0, 2.0, 3.0], "y": [9.0, 10.0]},
     "bsr_level_maps": {
         "source": "test/test_formats.jl:59-60,70,87-88,167-172",
         "dim2lvl": [

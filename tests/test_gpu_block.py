@@ -378,3 +378,108 @@ def test_block_banded_assembled_with_shifted_diag():
             ref.append(Nd @ xs[t] + Pd @ xs[t + 1])
             bound.append(np.abs(Nd) @ np.abs(xs[t]) + np.abs(Pd) @ np.abs(xs[t + 1]))
     assert_within(yd.cpu().numpy(), np.concatenate(ref), np.concatenate(bound), 1e-12)
+
+
+# ---- the reference's own block-path tests (test/test_emitter_cuda.jl) ------
+def _kat_bsm(g):
+    nbr, nbc = g["grid"]
+    grid = [[None] * nbc for _ in range(nbr)]
+    for key, b in g["blocks"].items():
+        i, j = map(int, key.split(","))
+        grid[i][j] = J.csr_tensor(to_dev(np.array(b["rowptr"], np.int32)),
+                                  to_dev(np.array(b["colind"], np.int32)),
+                                  to_dev(np.array(b["val"])), (b["m"], b["n"]), origin=b["base"])
+    return J.BlockSparseMatrix(grid)
+
+
+@pytest.mark.parametrize("name", ["bsm_diagonal", "bsm_accumulate"])
+def test_reference_bsm_kats(golden, name):
+    """BlockSparseMatrix diagonal [7, 6, 5, 10] and accumulate [9, 10]
+    (test/test_emitter_cuda.jl:297-322): mul! and a second product on the
+    same buffers (graph replay) give the reference's vectors exactly."""
+    g = golden[name]
+    A = _kat_bsm(g)
+    x = to_dev(np.array(g["x"]))
+    y = torch.zeros(A.shape[0], dtype=torch.float64, device=DEV)
+    for _ in range(2):
+        J.mul(y, A, x)
+        J.device_status()
+        assert y.cpu().tolist() == g["y"]
+
+
+def test_reference_shifted_diag_standalone():
+    """shifted_diag_tensor SpMV (test/test_emitter_cuda.jl:330-345): shift 0,
+    val 2.5 gives 2.5 x; an n x (n+3) tensor with shift 3, val -1.5 gives
+    -1.5 x[3:]."""
+    n = 1024
+    x = torch.rand(n, dtype=torch.float64, device=DEV)
+    y = torch.zeros(n, dtype=torch.float64, device=DEV)
+    J.execute(J.SpMVOp, J.shifted_diag_tensor(torch.float64, n, n, shift=0, val=2.5, device=DEV),
+              x, y)
+    J.device_status()
+    assert torch.equal(y, 2.5 * x)
+    x2 = torch.rand(n + 3, dtype=torch.float64, device=DEV)
+    y2 = torch.zeros(n, dtype=torch.float64, device=DEV)
+    J.execute(J.SpMVOp, J.shifted_diag_tensor(torch.float64, n, n + 3, shift=3, val=-1.5,
+                                               device=DEV), x2, y2)
+    J.device_status()
+    assert torch.equal(y2, -1.5 * x2[3:])
+
+
+def _eye_csr(n, v):
+    return J.csr_tensor(to_dev(np.arange(1, n + 2, dtype=np.int32)),
+                        to_dev(np.arange(1, n + 1, dtype=np.int32)), to_dev(np.full(n, v)),
+                        (n, n), origin=1)
+
+
+def test_reference_bsm_shifted_diag_equivalence():
+    """A CSR -I block and a ShiftedDiag(-I) block give the same product
+    (test/test_emitter_cuda.jl:348-368), and [3I -I 2I] with two ShiftedDiag
+    blocks gives 3 x1 - x2 + 2 x3 (:370-382)."""
+    n = 16
+    A = _eye_csr(n, 2.0)
+    B_csr = J.BlockSparseMatrix([[A, _eye_csr(n, -1.0)]])
+    B_sh = J.BlockSparseMatrix([[A, J.shifted_diag_tensor(torch.float64, n, n, val=-1.0,
+                                                           device=DEV)]])
+    x = torch.rand(2 * n, dtype=torch.float64, device=DEV)
+    y1 = torch.zeros(n, dtype=torch.float64, device=DEV)
+    y2 = torch.zeros(n, dtype=torch.float64, device=DEV)
+    J.mul(y1, B_csr, x)
+    J.mul(y2, B_sh, x)
+    J.device_status()
+    assert torch.equal(y1, y2)
+    n = 8
+    M = J.BlockSparseMatrix([[_eye_csr(n, 3.0),
+                              J.shifted_diag_tensor(torch.float64, n, n, val=-1.0, device=DEV),
+                              J.shifted_diag_tensor(torch.float64, n, n, val=2.0, device=DEV)]])
+    x = torch.rand(3 * n, dtype=torch.float64, device=DEV)
+    y = torch.zeros(n, dtype=torch.float64, device=DEV)
+    J.mul(y, M, x)
+    J.device_status()
+    xh = x.cpu().numpy()
+    want = 3.0 * xh[:n] - xh[n:2 * n] + 2.0 * xh[2 * n:]
+    assert np.allclose(y.cpu().numpy(), want, rtol=1e-15, atol=1e-15)
+
+
+def test_reference_bbm_periodic_shifted_diag_equivalence():
+    """BlockBandedMatrix (bw = 1 form) whose BlockSparseMatrix diagonal holds
+    a CSR -I block or a ShiftedDiag(-I) block, with a (-R, R) coupling pair
+    (test/test_emitter_cuda.jl:384-418): identical products -- the CSR -I is
+    recognised as a selector and both run as the same patch."""
+    n, T = 16, 4
+    A = _eye_csr(n, 3.0)
+    bsm_csr = J.BlockSparseMatrix([[A, _eye_csr(n, -1.0)]])
+    bsm_sh = J.BlockSparseMatrix([[A, J.shifted_diag_tensor(torch.float64, n, n, val=-1.0,
+                                                             device=DEV)]])
+    negR, R = _eye_csr(n, -1.0), _eye_csr(n, 1.0)
+    M_csr = J.BlockBandedMatrix(bsm_csr, negR, R, T, n, n, 2 * n)
+    M_sh = J.BlockBandedMatrix(bsm_sh, negR, R, T, n, n, 2 * n)
+    n_total = T * n + (T - 1) * n
+    assert M_csr.shape == (n_total, T * 2 * n)
+    x = torch.rand(T * 2 * n, dtype=torch.float64, device=DEV)
+    y1 = torch.zeros(n_total, dtype=torch.float64, device=DEV)
+    y2 = torch.zeros(n_total, dtype=torch.float64, device=DEV)
+    J.mul(y1, M_csr, x)
+    J.mul(y2, M_sh, x)
+    J.device_status()
+    assert torch.equal(y1, y2)

@@ -36,7 +36,7 @@ def test_tensor_path_empty_rows_alpha_beta():
     rng = np.random.default_rng(52)
     nbr = 24
     present = rng.random((nbr, nbr)) < 0.15
-    present[[0, 3, 17, 23]] = False                          # empty block rows
+    present[[0, 3, 6, 7, 17, 23]] = False                    # empty block rows (6, 7: a whole pair)
     bp = np.zeros(nbr + 1, np.int32)
     bp[1:] = np.cumsum(present.sum(axis=1))
     bc = np.nonzero(present)[1].astype(np.int32)

@@ -173,3 +173,66 @@ def test_row_range_views_match_whole():
                   parts[lo:hi])
     J.device_status()
     assert torch.equal(whole, parts)
+
+
+@pytest.mark.parametrize("variant", [2, 4, 8, 16, 32])
+@pytest.mark.parametrize("dtype", [np.float64, np.float32])
+@pytest.mark.parametrize("base", [0, 1])
+def test_vector_variants_within_tolerance(variant, dtype, base):
+    """Groups of W lanes per row (16-byte loads of four columns and values,
+    quads straddling row boundaries masked, the array's last partial quad
+    loaded entry by entry): within tolerance of the fp64 restatement for
+    empty, short, medium and very long rows, alpha and beta != 0."""
+    rng = np.random.default_rng(60 + variant)
+    m, n = 4001, 7000
+    lengths = rng.integers(0, 60, size=m)
+    lengths[::31] = 0
+    lengths[::97] = rng.integers(100, 3000, size=lengths[::97].shape[0])
+    lengths[-1] = 3                     # the last quad ends inside the arrays' tail
+    rp, ci, val = random_csr(m, n, lengths, seed=61, base=base, dtype=dtype)
+    x = rng.uniform(-1, 1, n).astype(dtype)
+    y0 = rng.uniform(-1, 1, m).astype(dtype)
+    A = J.csr_tensor(to_dev(rp), to_dev(ci), to_dev(val), (m, n), origin=base)
+    h = J.prepare(J.B200Backend(), J.SpMVOp, A).set_variant(variant)
+    assert h.info()["variant"] == variant
+    yd = to_dev(y0)
+    J.execute(J.SpMVOp, h, to_dev(x), yd, alpha=1.5, beta=-0.5)
+    J.device_status()
+    ref, bound = O.spmv_ref64(rp - base, ci - base, val, x, y0, 1.5, -0.5)
+    assert_within(yd.cpu().numpy(), ref, bound, TOL[dtype])
+
+
+def test_plan_picks_vector_rows_for_uniform_rows():
+    """Uniform rows of 16-40 entries: the plan takes groups of 4 lanes per row
+    and agrees within tolerance with the restatement; the set_variant
+    override refuses widths other than 0, 2, 4, 8, 16, 32."""
+    rng = np.random.default_rng(70)
+    m, n = 20000, 20000
+    rp, ci, val = random_csr(m, n, rng.integers(16, 41, size=m), seed=71)
+    x = rng.uniform(-1, 1, n)
+    A = J.csr_tensor(to_dev(rp), to_dev(ci), to_dev(val), (m, n), origin=0)
+    h = J.prepare(J.B200Backend(), J.SpMVOp, A)
+    assert h.info()["variant"] == 4
+    y = torch.zeros(m, dtype=torch.float64, device=DEV)
+    J.execute(J.SpMVOp, h, to_dev(x), y)
+    J.device_status()
+    ref, bound = O.spmv_ref64(rp, ci, val, x)
+    assert_within(y.cpu().numpy(), ref, bound, 1e-12)
+    with pytest.raises(J.errors.InvalidArgument):
+        h.set_variant(3)
+
+
+def test_vector_variant_unaligned_values_fall_back():
+    """A value array that is not 16-byte aligned (a view one element in)
+    runs the thread-per-row kernel: bit-exact for short rows."""
+    rng = np.random.default_rng(72)
+    m, n = 3000, 3000
+    rp, ci, val = random_csr(m, n, rng.integers(0, 20, size=m), seed=73)
+    store = to_dev(np.concatenate([[0.0], val]))
+    A = J.csr_tensor(to_dev(rp), to_dev(ci), store[1:], (m, n), origin=0)
+    h = J.prepare(J.B200Backend(), J.SpMVOp, A).set_variant(8)
+    x = rng.uniform(-1, 1, n)
+    y = torch.zeros(m, dtype=torch.float64, device=DEV)
+    J.execute(J.SpMVOp, h, to_dev(x), y)
+    J.device_status()
+    assert np.array_equal(y.cpu().numpy(), O.spmv(rp, ci, val, x))

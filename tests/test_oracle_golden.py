@@ -284,3 +284,28 @@ def test_oracle_periodic_bbm_with_selectors_against_dense():
             M[r:r + no, (t + 1) * nc:(t + 2) * nc] = P
             r += no
     assert np.allclose(y, M @ x, rtol=1e-13, atol=1e-13)
+
+
+def _kat_blocks(g):
+    out = {}
+    for key, b in g["blocks"].items():
+        i, j = map(int, key.split(","))
+        out[(i, j)] = (np.array(b["rowptr"], np.int32), np.array(b["colind"], np.int32),
+                       np.array(b["val"]), b["base"])
+    return out
+
+
+@pytest.mark.parametrize("name", ["bsm_diagonal", "bsm_accumulate"])
+def test_bsm_kats(golden, name):
+    """The reference's BlockSparseMatrix KATs (test/test_emitter_cuda.jl:
+    297-322) through the oracle's restatement of the compiled CSR
+    (block_mul.jl:128-229) and its SpMV."""
+    g = golden[name]
+    blocks = _kat_blocks(g)
+    nbr, nbc = g["grid"]
+    row_sizes = [[g["blocks"][k]["m"] for k in g["blocks"] if int(k.split(",")[0]) == r][0]
+                 for r in range(nbr)]
+    col_sizes = [[g["blocks"][k]["n"] for k in g["blocks"] if int(k.split(",")[1]) == c][0]
+                 for c in range(nbc)]
+    rp, ci, v = O.bsm_assemble(row_sizes, col_sizes, blocks)
+    assert O.spmv(rp, ci, v, np.array(g["x"])).tolist() == g["y"]
