@@ -24,6 +24,13 @@
 // pair (N TMEM columns), double-buffered for N <= 256 so that the epilogue of
 // one pair overlaps the MMAs of the next.
 //
+// Work split.  One CTA per SM (or per block row when there are fewer), each
+// with a contiguous range of block rows holding an equal share of the units
+// (block rows + stored blocks), found by a binary search over browptr in the
+// prologue; the range's rows are paired from its first row.  Cycling pairs
+// over the grid instead left SMs with 4 pairs next to SMs with 3 (1024 block
+// rows on 148 SMs), a 14% tail.
+//
 // Warp roles (224 threads): warps 0 and 6 = TMA producers (alternate groups;
 // each walks the same merge), warp 1 = TMEM owner and MMA issuer, warps 2-5 =
 // epilogue (warp w reads TMEM lanes 32*(w%4) .. +31, i.e. C rows).  No cluster
@@ -190,11 +197,30 @@ struct Ctl {
     uint64_t tfull[2];
     uint64_t tempty[2];
     uint64_t mma_done;
-    long long last_fill[kMaxStages];   // last group index copied into each stage
-    uint32_t ginfo[kMaxStages];        // the stage's group: bit 0 first of its pair, bit 1 last
+    long long last_fill[2][kMaxStages];  // per producer: last group index copied into each stage
+    int64_t row0, row1;                  // this CTA's block rows [row0, row1)
+    uint32_t ginfo[kMaxStages];          // the stage's group: bit 1 last of its pair
     uint32_t tmem_base;
     int abort;
 };
+
+// First block row of CTA c's share when G CTAs split the block rows by work
+// units u(r) = r + (browptr[r] - base) (one unit per block row for its
+// epilogue, one per stored block): the smallest r with u(r) >= c * U / G,
+// U = u(mb) = mb + nnzb.  u is strictly increasing, so CTA 0 starts at row 0,
+// the last CTA ends at row mb, and neighbouring CTAs' ranges meet.
+__device__ int64_t share_start(const int32_t *__restrict__ browptr, int64_t mb, int base,
+                               int64_t c, int64_t G) {
+    const int64_t U = mb + (int64_t)(browptr[mb] - base);
+    const int64_t target = U * c / G;
+    int64_t lo = 0, hi = mb;               // answer in [lo, hi]
+    while (lo < hi) {
+        const int64_t mid = (lo + hi) / 2;
+        if (mid + (int64_t)(browptr[mid] - base) >= target) hi = mid;
+        else lo = mid + 1;
+    }
+    return lo;
+}
 
 // Waits without looking at the abort flag (used while draining on exit).
 __device__ __forceinline__ void mbar_drain(uint32_t bar, uint32_t parity) {
@@ -214,8 +240,8 @@ __host__ __device__ inline uint32_t tmem_cols_for(int n, int nbuf) {
     return c;
 }
 
-// Block-column merge of a pair of block rows: rows a = I and b = I+1 (b may
-// not exist).  next() yields the groups in order: the smallest head block
+// Block-column merge of a pair of block rows: rows a = I and b = I+1 (b
+// absent when has_b is false).  next() yields the groups in order: the smallest head block
 // column, with each row whose head it is (each row's blocks stay in their
 // storage order, sorted or not).  The heads are loaded one step ahead.
 struct PairMerge {
@@ -225,12 +251,12 @@ struct PairMerge {
     int ja, jb;                     // current heads (block columns), valid while q < q1
 
     __device__ void init(const int32_t *__restrict__ browptr, const int32_t *__restrict__ bc,
-                         int64_t I, int64_t mb, int b0) {
+                         int64_t I, bool has_b, int b0) {
         bcolind = bc;
         base = b0;
         qa = browptr[I] - base;
         qa1 = browptr[I + 1] - base;
-        if (I + 1 < mb) {
+        if (has_b) {
             qb = qa1;
             qb1 = browptr[I + 2] - base;
         } else {
@@ -275,14 +301,15 @@ bsr_spmm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     Ctl *ctl = reinterpret_cast<Ctl *>(tiles + (size_t)stages * kStageBytes);
     const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
     const uint32_t ncols = tmem_cols_for(N, kNBuf);
-    const int64_t npairs = (mb + 1) / 2;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < stages; ++s) {
             mbar_init(smem_u32(&ctl->full[s]), 1);
             mbar_init(smem_u32(&ctl->empty[s]), 1);
-            ctl->last_fill[s] = -1;
+            ctl->last_fill[0][s] = ctl->last_fill[1][s] = -1;
         }
+        ctl->row0 = share_start(browptr, mb, base, blockIdx.x, gridDim.x);
+        ctl->row1 = share_start(browptr, mb, base, blockIdx.x + 1, gridDim.x);
         for (int b = 0; b < 2; ++b) {
             mbar_init(smem_u32(&ctl->tfull[b]), 1);
             mbar_init(smem_u32(&ctl->tempty[b]), 4);
@@ -303,27 +330,30 @@ bsr_spmm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     tc_fence_after();
     const uint32_t tmem = ctl->tmem_base;
     volatile int *abort_flag = &ctl->abort;
+    // The CTA's block rows, taken in pairs (I, I+1) from row0; a last row
+    // without a partner inside the range forms a pair of its own.
+    const int64_t row0 = ctl->row0, row1 = ctl->row1;
 
     if ((warp == 0 || warp == 6) && lane == 0) {
         // ------------------------------------------------------ TMA producers
         // Two producer threads take alternate groups (one thread's loop --
         // barrier wait, expect-tx, TMA issues -- costs about as much as a
         // group's MMAs).  Both walk the same merge; group k of the CTA goes to
-        // stage k % stages, its empty-barrier phase parity follows from
-        // k / stages.
+        // stage k % stages with empty-barrier phase parity (k / stages) & 1 ^ 1,
+        // both kept as running counters.
         const int pid = warp == 0 ? 0 : 1;
         long long k = 0;
+        int stage = 0;
+        uint32_t pe = 1u;
         bool ok = true;
-        for (int64_t P = blockIdx.x; P < npairs && ok; P += gridDim.x) {
+        for (int64_t I = row0; I < row1 && ok; I += 2) {
             PairMerge mg;
-            mg.init(browptr, bcolind, 2 * P, mb, base);
+            mg.init(browptr, bcolind, I, I + 1 < row1, base);
             while (!mg.done()) {
                 int J, ea, eb;
                 mg.next(J, ea, eb);
                 const bool last = mg.done();
                 if ((int)(k & 1) == pid) {
-                    const int stage = (int)(k % stages);
-                    const uint32_t pe = (uint32_t)(((k / stages) & 1) ^ 1);
                     if (!mbar_wait(smem_u32(&ctl->empty[stage]), pe, abort_flag)) {
                         ok = false;
                         break;
@@ -339,9 +369,10 @@ bsr_spmm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                     for (int c = 0; c < N / 64; ++c)
                         tma_load_2d(sA + 2 * kATileBytes + (uint32_t)c * kBoxBytes, &tmB, full, c * 64,
                                     J * kBS);
-                    atomicMax(&ctl->last_fill[stage], k);
+                    ctl->last_fill[pid][stage] = k;
                 }
                 ++k;
+                if (++stage == stages) { stage = 0; pe ^= 1u; }
             }
         }
     } else if (warp == 1 && lane == 0) {
@@ -356,10 +387,9 @@ bsr_spmm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         const uint32_t a_hi = (uint32_t)(adesc0 >> 32), b_hi = (uint32_t)(bdesc0 >> 32);
         constexpr uint32_t kId0 = idesc_for(kN0);
         constexpr uint32_t kId1 = idesc_for(N - kN0 > 0 ? N - kN0 : 16);
-        for (int64_t P = blockIdx.x; P < npairs && ok; P += gridDim.x) {
-            const int64_t I = 2 * P;
+        for (int64_t I = row0; I < row1 && ok; I += 2) {
             const int q0 = browptr[I] - base;
-            const int q2 = browptr[I + 1 < mb ? I + 2 : I + 1] - base;
+            const int q2 = browptr[I + 1 < row1 ? I + 2 : I + 1] - base;
             if (q2 <= q0) continue;                      // no blocks: the epilogue writes it
             if (!mbar_wait(smem_u32(&ctl->tempty[buf]), te_phase[buf], abort_flag)) { ok = false; break; }
             te_phase[buf] ^= 1u;
@@ -397,11 +427,11 @@ bsr_spmm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         const int qd = warp & 3;
         uint32_t tf_phase[2] = {0u, 0u};
         int buf = 0;
-        const int64_t nrows = mb * kBS;
-        for (int64_t P = blockIdx.x; P < npairs; P += gridDim.x) {
-            const int64_t I = 2 * P;
+        for (int64_t I = row0; I < row1; I += 2) {
+            const int64_t rlim = I + 1 < row1 ? I + 2 : I + 1;
             const int q0 = browptr[I] - base;
-            const int q2 = browptr[I + 1 < mb ? I + 2 : I + 1] - base;
+            const int q2 = browptr[rlim] - base;
+            const int64_t nrows = rlim * kBS;           // end of this pair's C rows
             const int64_t row = I * kBS + qd * 32 + lane;
             if (q2 <= q0) {
                 if (row < nrows)
@@ -452,9 +482,11 @@ bsr_spmm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     // every copy issued lands before the CTA can exit (they all have when the
     // MMA issuer consumed every stage; an aborted run may leave some in flight)
     if (threadIdx.x == 0)
-        for (int st = 0; st < stages; ++st)
-            if (ctl->last_fill[st] >= 0)
-                mbar_drain(smem_u32(&ctl->full[st]), (uint32_t)((ctl->last_fill[st] / stages) & 1));
+        for (int st = 0; st < stages; ++st) {
+            const long long lf = ctl->last_fill[0][st] > ctl->last_fill[1][st] ? ctl->last_fill[0][st]
+                                                                               : ctl->last_fill[1][st];
+            if (lf >= 0) mbar_drain(smem_u32(&ctl->full[st]), (uint32_t)((lf / stages) & 1));
+        }
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
@@ -567,8 +599,7 @@ extern "C" JLB_API int jlb_bsr_spmm(void *stream, int idx_base, int64_t mb, int6
         int dev = 0, sms = 148;
         JLB_CUDA(cudaGetDevice(&dev));
         JLB_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-        const int64_t npairs = (mb + 1) / 2;
-        const unsigned grid = (unsigned)(npairs < sms ? npairs : sms);
+        const unsigned grid = (unsigned)(mb < sms ? mb : sms);
         const int64_t zero_row = nnzb * 64;       // a box wholly past the values: zeros
 #define JLB_BSR_TC(NN)                                                                          \
     JLB_CUDA(cudaFuncSetAttribute(bsr::bsr_spmm_tc<NN>,                                         \
