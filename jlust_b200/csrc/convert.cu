@@ -203,6 +203,13 @@ __device__ __forceinline__ void copy_val(void *dst, int64_t q, const void *src, 
     else reinterpret_cast<uint16_t *>(dst)[q] = reinterpret_cast<const uint16_t *>(src)[p];
 }
 
+template <int ES>
+__device__ __forceinline__ void store_zero(void *dst, int64_t q) {
+    if (ES == 8) reinterpret_cast<uint64_t *>(dst)[q] = 0;
+    else if (ES == 4) reinterpret_cast<uint32_t *>(dst)[q] = 0;
+    else reinterpret_cast<uint16_t *>(dst)[q] = 0;
+}
+
 // Zero-fills bytes [b0, b1) of `dst` with the CTA, 16-byte stores where aligned.
 __device__ void zero_bytes(char *dst, int64_t b0, int64_t b1) {
     const uintptr_t a0 = reinterpret_cast<uintptr_t>(dst + b0);
@@ -225,8 +232,10 @@ struct Src {
     const int32_t *boffs;    // COO: bucket offsets (mb+1), base 0
     const int32_t *bent;     // COO: bucketed storage indices
     int64_t m, n;
+    int64_t nnz;             // CSR: entries in cols / val
     int b1, b2, base, es;
     int sh1, sh2;            // log2(b1), log2(b2) when a power of two, else -1
+    int vec;                 // CSR: cols 16-byte aligned (four columns per load)
 
     __device__ __forceinline__ int64_t blk_col(int64_t j) const { return sh2 >= 0 ? j >> sh2 : j / b2; }
     __device__ __forceinline__ int64_t in_col(int64_t j) const { return sh2 >= 0 ? j & (b2 - 1) : j % b2; }
@@ -235,6 +244,14 @@ struct Src {
     __device__ __forceinline__ int blk_col32(int j) const { return sh2 >= 0 ? j >> sh2 : j / b2; }
     __device__ __forceinline__ int in_col32(int j) const { return sh2 >= 0 ? j & (b2 - 1) : j % b2; }
 };
+
+// Block column of column j: a shift when the block width is a power of two
+// (P2), else a division.
+template <bool P2>
+__device__ __forceinline__ int blk32(const Src &s, int j) {
+    if constexpr (P2) return j >> s.sh2;
+    else return j / s.b2;
+}
 
 inline int log2_exact(int b) {
     int k = 0;
@@ -311,21 +328,112 @@ __device__ __forceinline__ void for_each_entry(const Src &s, int64_t I, F f) {
     }
 }
 
+// Entries [E0, E1) of a CSR (the rows of one block row, contiguous), marking
+// the block columns of window [w0i, w0i + kWinBits) that hold a nonzero
+// entry.  The CTA's warps take chunks of kWarp * K entries round robin, K (a
+// multiple of 4) consecutive entries a lane (16-byte loads of columns
+// when aligned), so every warp has the same share whatever the row lengths.
+// A lead is an entry whose block column differs from the entry before it in
+// the chunk (the chunk's first entry always leads).  Only leads' values are
+// read: when every lead of a chunk is nonzero, every block column of the
+// chunk holds a nonzero entry and the leads mark them all (one atomic per run
+// of a block column); when some lead is zero the chunk reads all its values
+// and marks per nonzero entry.  With desc non-null, adds the number of
+// entries whose column is not above the previous entry's (first entry
+// excluded) -- row starts included, which the caller accounts for.
+template <int ES, int K>
+__device__ __forceinline__ void mark_csr_flat(const Src &s, int E0, int E1, int w0i,
+                                              uint32_t *bits, int *desc) {
+    constexpr int kChunk = kWarp * K;
+    const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
+    const int nwarps = blockDim.x / kWarp;
+    const unsigned n = (unsigned)(s.n < INT32_MAX ? s.n : INT32_MAX);
+    int d = 0;
+    auto mark = [&](int J) {
+        const int Jw = J - w0i;
+        if (Jw >= 0 && Jw < kWinBits) atomicOr(&bits[Jw >> 5], 1u << (Jw & 31));
+    };
+    for (int g0 = (E0 & ~3) + warp * kChunk; g0 < E1; g0 += nwarps * kChunk) {
+        const int g = g0 + K * lane;
+        int c[K];
+        bool v[K];
+#pragma unroll
+        for (int u = 0; u < K; ++u) v[u] = g + u >= E0 && g + u < E1;
+        if (s.vec && (int64_t)g + K <= s.nnz) {
+#pragma unroll
+            for (int h = 0; h < K; h += 4) {
+                const int4 q = __ldg(reinterpret_cast<const int4 *>(s.cols + g + h));
+                c[h] = q.x; c[h + 1] = q.y; c[h + 2] = q.z; c[h + 3] = q.w;
+            }
+        } else {
+#pragma unroll
+            for (int u = 0; u < K; ++u) c[u] = v[u] ? __ldg(s.cols + g + u) : 0;
+        }
+        // the entry before this lane's first: the previous lane's last, or
+        // (lane 0) a load
+        int prev = __shfl_up_sync(0xffffffffu, c[K - 1], 1);
+        const bool has_prev = g - 1 >= E0 && g - 1 < E1;
+        if (lane == 0) prev = has_prev ? __ldg(s.cols + g - 1) : 0;
+        prev -= s.base;
+        int J[K];
+#pragma unroll
+        for (int u = 0; u < K; ++u) {
+            c[u] -= s.base;
+            if (v[u] && (unsigned)c[u] >= n) {
+                dev_error(DEV_ERR_BOUNDS);
+                v[u] = false;
+            }
+            J[u] = s.blk_col32(c[u]);
+        }
+        if (desc) {
+            if (v[0] && has_prev && c[0] <= prev) ++d;
+#pragma unroll
+            for (int u = 1; u < K; ++u)
+                if (v[u] && v[u - 1] && c[u] <= c[u - 1]) ++d;
+        }
+        bool lead[K], zero_lead = false;
+#pragma unroll
+        for (int u = 0; u < K; ++u) {
+            const int pj = u > 0 ? (v[u - 1] ? J[u - 1] : -1)
+                                 : (lane > 0 && has_prev ? s.blk_col32(prev) : -1);
+            lead[u] = v[u] && J[u] != pj;
+            if (lead[u] && is_zero<ES>(s.val, g + u)) zero_lead = true;
+        }
+        if (__any_sync(0xffffffffu, zero_lead)) {
+            int pj = -1;
+#pragma unroll
+            for (int u = 0; u < K; ++u)
+                if (v[u] && !is_zero<ES>(s.val, g + u)) {
+                    if (J[u] != pj) mark(J[u]);
+                    pj = J[u];
+                }
+        } else {
+#pragma unroll
+            for (int u = 0; u < K; ++u)
+                if (lead[u]) mark(J[u]);
+        }
+    }
+    if (desc) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+        if (lane == 0 && d) atomicAdd(desc, d);
+    }
+}
+
+// Entry range of block row I of a CSR: [E0, E1).
+__device__ __forceinline__ void csr_block_range(const Src &s, int64_t I, int &E0, int &E1) {
+    const int64_t i0 = I * s.b1, i1 = i0 + s.b1 < s.m ? i0 + s.b1 : s.m;
+    E0 = s.rowptr[i0] - s.base;
+    E1 = s.rowptr[i1] - s.base;
+}
+
 // Marks the block columns of window [w0, w0 + kWinBits) hit by block row I.
 template <int ES>
 __device__ __forceinline__ void mark_window(const Src &s, int64_t I, int64_t w0, uint32_t *bits) {
     if (s.rowptr) {
-        // CSR: a row's columns ascend, so one atomic per run of equal block
-        // columns across the lanes (compare with the previous lane; unsorted
-        // rows stay correct, with more atomics)
-        const int w0i = (int)w0;   // block columns fit 32 bits
-        for_each_csr_row_sync<ES>(s, I, [&](int, int64_t, int j, bool ok) {
-            const int J = ok ? s.blk_col32(j) - w0i : -1;
-            const bool in = ok && J >= 0 && J < kWinBits;
-            const int prev = __shfl_up_sync(0xffffffffu, in ? J : -1, 1);
-            const bool lead = (threadIdx.x % kWarp) == 0 || prev != J;
-            if (in && lead) atomicOr(&bits[J >> 5], 1u << (J & 31));
-        });
+        int E0, E1;
+        csr_block_range(s, I, E0, E1);
+        mark_csr_flat<ES, 4>(s, E0, E1, (int)w0, bits, nullptr);   // block columns fit 32 bits
         return;
     }
     for_each_entry<ES>(s, I, [&](int64_t p, int64_t i, int64_t j) {
@@ -339,13 +447,14 @@ __device__ __forceinline__ void mark_window(const Src &s, int64_t I, int64_t w0,
     });
 }
 
+template <int NT = kConvThreads>
 __device__ __forceinline__ int64_t block_sum(int64_t v, int64_t *s_red) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
     if (threadIdx.x % kWarp == 0) s_red[threadIdx.x / kWarp] = v;
     __syncthreads();
     int64_t t = 0;
-    for (int w = 0; w < kConvThreads / kWarp; ++w) t += s_red[w];
+    for (int w = 0; w < NT / kWarp; ++w) t += s_red[w];
     __syncthreads();
     return t;
 }
@@ -357,6 +466,9 @@ __device__ __forceinline__ int64_t block_sum(int64_t v, int64_t *s_red) {
 // its own key matches, and marks them again otherwise.
 struct Carry {
     uint32_t *bits;      // mb x words, or null: no hand-over
+    uint8_t *asc;        // mb flags: every row of the block row strictly ascending
+    uint8_t *row_done;   // mb * b1 flags of the fill's tile-row path
+    int32_t *row_runs;   // mb * b1: the row's runs of block columns, -1 unknown (count pass)
     uint64_t *stamp;
     uint64_t key;
 };
@@ -391,7 +503,494 @@ count_blocks(Src s, int64_t mb, int64_t nb, int32_t *__restrict__ counts, Carry 
     if (carry.bits && blockIdx.x == 0 && threadIdx.x == 0) *carry.stamp = carry.key;
 }
 
+// Nonzero flags of entries g .. g+7 (v: in range), from one, two or four
+// 16-byte loads of values when `vec`.
+template <int ES>
+__device__ __forceinline__ void nonzero8(const Src &s, int g, bool vec, const bool (&v)[8],
+                                         bool (&nz)[8]) {
+    if (vec) {
+        const int4 *q = reinterpret_cast<const int4 *>(static_cast<const char *>(s.val) + (size_t)g * ES);
+        if constexpr (ES == 2) {
+            const int4 a = __ldg(q);
+            const uint32_t w[4] = {(uint32_t)a.x, (uint32_t)a.y, (uint32_t)a.z, (uint32_t)a.w};
+#pragma unroll
+            for (int u = 0; u < 8; ++u) nz[u] = v[u] && ((w[u >> 1] >> ((u & 1) * 16)) & 0x7fffu) != 0;
+        } else if constexpr (ES == 4) {
+            const int4 a = __ldg(q), b = __ldg(q + 1);
+            const uint32_t w[8] = {(uint32_t)a.x, (uint32_t)a.y, (uint32_t)a.z, (uint32_t)a.w,
+                                   (uint32_t)b.x, (uint32_t)b.y, (uint32_t)b.z, (uint32_t)b.w};
+#pragma unroll
+            for (int u = 0; u < 8; ++u) nz[u] = v[u] && (w[u] & 0x7fffffffu) != 0;
+        } else {
+            uint32_t w[16];
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+                const int4 a = __ldg(q + h);
+                w[4 * h] = a.x; w[4 * h + 1] = a.y; w[4 * h + 2] = a.z; w[4 * h + 3] = a.w;
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) nz[u] = v[u] && (w[2 * u] | (w[2 * u + 1] & 0x7fffffffu)) != 0;
+        }
+    } else {
+#pragma unroll
+        for (int u = 0; u < 8; ++u) nz[u] = v[u] && !is_zero<ES>(s.val, g + u);
+    }
+}
+
+// Columns and values of eight consecutive entries g .. g+7 as loaded (16-byte
+// loads when aligned and inside the arrays, else the in-range ones singly).
+template <int ES>
+struct Raw8 {
+    int c[8];
+    uint32_t w[2 * ES];   // the eight values' bits (vector loads)
+    uint32_t nzm;         // nonzero mask (single loads)
+    bool vec;
+
+    __device__ __forceinline__ void load(const Src &s, int g, int E0, int E1) {
+        vec = s.vec && (int64_t)g + 8 <= s.nnz;
+        if (vec) {
+            const int4 p0 = __ldg(reinterpret_cast<const int4 *>(s.cols + g));
+            const int4 p1 = __ldg(reinterpret_cast<const int4 *>(s.cols + g + 4));
+            c[0] = p0.x; c[1] = p0.y; c[2] = p0.z; c[3] = p0.w;
+            c[4] = p1.x; c[5] = p1.y; c[6] = p1.z; c[7] = p1.w;
+            const int4 *q = reinterpret_cast<const int4 *>(static_cast<const char *>(s.val) + (size_t)g * ES);
+#pragma unroll
+            for (int h = 0; h < ES / 2; ++h) {
+                const int4 a = __ldg(q + h);
+                w[4 * h] = a.x; w[4 * h + 1] = a.y; w[4 * h + 2] = a.z; w[4 * h + 3] = a.w;
+            }
+        } else {
+            nzm = 0;
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const bool in = g + u >= E0 && g + u < E1;
+                c[u] = in ? __ldg(s.cols + g + u) : 0;
+                if (in && !is_zero<ES>(s.val, g + u)) nzm |= 1u << u;
+            }
+        }
+    }
+    __device__ __forceinline__ void nonzero(const bool (&v)[8], bool (&nz)[8]) const {
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            bool z;
+            if (!vec) z = !((nzm >> u) & 1u);
+            else if (ES == 2) z = ((w[u >> 1] >> ((u & 1) * 16)) & 0x7fffu) == 0;
+            else if (ES == 4) z = (w[u] & 0x7fffffffu) == 0;
+            else z = (w[2 * u] | (w[2 * u + 1] & 0x7fffffffu)) == 0;
+            nz[u] = v[u] && !z;
+        }
+    }
+};
+
+// Entries [E0, E1) of a CSR (the rows of one block row, contiguous), marking
+// the block columns of window [w0i, w0i + kWinBits) that hold a nonzero
+// entry, for the count pass.  The CTA's warps take chunks of 256 entries
+// round robin (chunks aligned to 8 entries), eight consecutive entries a
+// lane.
+//   Lean chunks -- inside [E0, E1), 16-byte loads, every lane's eight entries
+//   ascending, nonzero and in at most two adjacent block columns -- need only
+//   each lane's first and last entries: a lane marks its first entry's block
+//   column unless the lane before ended in it, and its last entry's when it
+//   differs.
+//   Other chunks go entry by entry: an entry marks its block column when it
+//   is nonzero and the previous nonzero entry (in the lane, or the lane
+//   before) had another one.
+// Adds to *desc the number of entries whose column is not above the previous
+// entry's (first entry excluded) -- row starts included, which the caller
+// accounts for.  With jc non-null, sets bit e - E0 of jc for every entry e
+// whose block column differs from the entry before's, and sets *zero_run when
+// such an entry is zero.
+template <int ES, bool P2>
+__device__ __forceinline__ void mark_csr_count(const Src &s, int E0, int E1, int w0i, uint32_t *bits,
+                                               int *desc, uint32_t *jc, int *zero_run) {
+    const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
+    const int nwarps = blockDim.x / kWarp;
+    const unsigned n = (unsigned)(s.n < INT32_MAX ? s.n : INT32_MAX);
+    int d = 0;
+    auto mark = [&](int J) {
+        const int Jw = J - w0i;
+        if (Jw >= 0 && Jw < kWinBits) atomicOr(&bits[Jw >> 5], 1u << (Jw & 31));
+    };
+    auto change_at = [&](int e) { atomicOr(&jc[(e - E0) >> 5], 1u << ((e - E0) & 31)); };
+    for (int g0 = (E0 & ~7) + warp * 8 * kWarp; g0 < E1; g0 += nwarps * 8 * kWarp) {
+        const int g = g0 + 8 * lane;
+        const bool interior = s.vec && g0 >= E0 && g0 + 8 * kWarp <= E1;   // warp-uniform
+        if (interior) {
+            const int4 p0 = __ldg(reinterpret_cast<const int4 *>(s.cols + g));
+            const int4 p1 = __ldg(reinterpret_cast<const int4 *>(s.cols + g + 4));
+            const int4 *q = reinterpret_cast<const int4 *>(static_cast<const char *>(s.val) + (size_t)g * ES);
+            bool f = p0.y > p0.x && p0.z > p0.y && p0.w > p0.z && p1.x > p0.w && p1.y > p1.x &&
+                     p1.z > p1.y && p1.w > p1.z;
+            if constexpr (ES == 2) {
+                // a 16-bit half that is +-0: (t - 0x00010001) & ~t & 0x80008000 != 0
+                // for t = w & 0x7fff7fff when some half of t is zero (a borrow
+                // may flag its neighbour too, which only sends the chunk to the
+                // entry-by-entry path)
+                const int4 a = __ldg(q);
+                const uint32_t w[4] = {(uint32_t)a.x, (uint32_t)a.y, (uint32_t)a.z, (uint32_t)a.w};
+                uint32_t z = 0;
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                    const uint32_t t = w[h] & 0x7fff7fffu;
+                    z |= (t - 0x00010001u) & ~t & 0x80008000u;
+                }
+                f = f && z == 0;
+            } else if constexpr (ES == 4) {
+                const int4 a = __ldg(q), b = __ldg(q + 1);
+                f = f && (a.x & 0x7fffffff) && (a.y & 0x7fffffff) && (a.z & 0x7fffffff) &&
+                    (a.w & 0x7fffffff) && (b.x & 0x7fffffff) && (b.y & 0x7fffffff) &&
+                    (b.z & 0x7fffffff) && (b.w & 0x7fffffff);
+            } else {
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                    const int4 a = __ldg(q + h);
+                    f = f && (a.x | (a.y & 0x7fffffff)) && (a.z | (a.w & 0x7fffffff));
+                }
+            }
+            const int c0 = p0.x - s.base, c7 = p1.w - s.base;
+            const int J0 = blk32<P2>(s, c0), J7 = blk32<P2>(s, c7);
+            f = f && c0 >= 0 && (unsigned)c7 < n && J7 - J0 <= 1;
+            int prev = __shfl_up_sync(0xffffffffu, p1.w, 1);
+            const int upJ = __shfl_up_sync(0xffffffffu, J7, 1);
+            if (__all_sync(0xffffffffu, f)) {
+                const bool has_prev = g > E0;
+                if (lane == 0 && has_prev) prev = __ldg(s.cols + g - 1);
+                if (has_prev && p0.x <= prev) ++d;   // a descent: not above the entry before
+                if (lane == 0 || J0 != upJ) mark(J0);
+                if (J7 != J0) mark(J7);
+                if (jc) {
+                    if (has_prev && J0 != blk32<P2>(s, prev - s.base)) change_at(g);
+                    if (J7 != J0) {
+                        const int cs[7] = {p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+                        int uc = 7;
+#pragma unroll
+                        for (int u = 6; u >= 0; --u)
+                            if (blk32<P2>(s, cs[u] - s.base) != J0) uc = u + 1;
+                        change_at(g + uc);
+                    }
+                }
+                continue;
+            }
+        }
+        // entry by entry
+        Raw8<ES> cur;
+        cur.load(s, g, E0, E1);
+        bool v[8], nz[8];
+        int c[8], J[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            v[u] = g + u >= E0 && g + u < E1;
+            c[u] = cur.c[u];
+        }
+        cur.nonzero(v, nz);
+        const bool has_prev = g - 1 >= E0 && g - 1 < E1;
+        int prevc = __shfl_up_sync(0xffffffffu, c[7], 1);
+        if (lane == 0) prevc = has_prev ? __ldg(s.cols + g - 1) : 0;
+        prevc -= s.base;
+        int last_nz = -1;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            c[u] -= s.base;
+            if (v[u] && (unsigned)c[u] >= n) {
+                dev_error(DEV_ERR_BOUNDS);
+                v[u] = nz[u] = false;
+            }
+            J[u] = blk32<P2>(s, c[u]);
+            if (nz[u]) last_nz = J[u];
+        }
+        const int up_nz = __shfl_up_sync(0xffffffffu, last_nz, 1);
+        int pnz = lane == 0 ? -1 : up_nz;
+        if (v[0] && has_prev && c[0] <= prevc) ++d;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            if (u > 0 && v[u] && v[u - 1] && c[u] <= c[u - 1]) ++d;
+            if (nz[u] && J[u] != pnz) mark(J[u]);
+            if (nz[u]) pnz = J[u];
+            if (jc && v[u] && (u > 0 ? v[u - 1] && J[u] != J[u - 1] : has_prev && J[0] != blk32<P2>(s, prevc))) {
+                change_at(g + u);
+                if (!nz[u]) *zero_run = 1;
+            }
+        }
+    }
+    if (desc) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+        if (lane == 0 && d) atomicAdd(desc, d);
+    }
+}
+
+// Count pass of a CSR source, one block row per CTA of kCsrThreads threads
+// (two CTAs an SM): the block row's entries are marked as one flat range
+// (mark_csr_count).  With a hand-over it also records what the fill pass's
+// tile-row path relies on:
+//   * per block row, whether every row's columns strictly ascend: the
+//     entries not above their predecessor (counted while marking) must all
+//     be row starts, i.e. their number must equal the number of nonempty rows
+//     whose first column is not above the last column before it;
+//   * per row, its number of runs of block columns -- 1 + the block-column
+//     changes after its first entry (the jc bits) -- or -1 when some run
+//     starts with a zero (or the block row has too many entries to track).
+// Shared memory (dynamic): the block-column bitmap, then the jc bits.
+constexpr int kCsrThreads = 512;
+constexpr int kJcWords = 8192;     // entries of a block row the change bits cover: 262,144
+constexpr size_t kCountSmem = (size_t)(kWinWords + kJcWords) * 4;
+
+template <int ES, bool P2>
+__global__ void __launch_bounds__(kCsrThreads, 2)
+count_csr(Src s, int64_t mb, int64_t nb, int32_t *__restrict__ counts, Carry carry) {
+    extern __shared__ uint32_t dyn_smem[];
+    uint32_t *bits = dyn_smem;
+    uint32_t *jc = dyn_smem + kWinWords;
+    __shared__ int64_t s_red[kCsrThreads / kWarp];
+    __shared__ int s_desc, s_zero;
+    for (int64_t I = blockIdx.x; I < mb; I += gridDim.x) {
+        int E0, E1;
+        csr_block_range(s, I, E0, E1);
+        const int64_t i0 = I * s.b1;
+        const int rows = (int)(s.m - i0 < s.b1 ? s.m - i0 : s.b1);
+        const bool runs = carry.bits && E1 - E0 <= kJcWords * 32;
+        if (threadIdx.x == 0) s_desc = s_zero = 0;
+        if (runs)
+            for (int w = threadIdx.x; w < (int)ceil_div(E1 - E0, 32); w += kCsrThreads) jc[w] = 0;
+        int64_t total = 0;
+        for (int64_t w0 = 0; w0 < nb; w0 += kWinBits) {
+            const int nw = (int)ceil_div((nb - w0) < kWinBits ? (nb - w0) : kWinBits, 32);
+            for (int w = threadIdx.x; w < nw; w += kCsrThreads) bits[w] = 0;
+            __syncthreads();
+            mark_csr_count<ES, P2>(s, E0, E1, (int)w0, bits, w0 == 0 ? &s_desc : nullptr,
+                                   runs && w0 == 0 ? jc : nullptr, &s_zero);
+            __syncthreads();
+            int64_t c = 0;
+            for (int w = threadIdx.x; w < nw; w += kCsrThreads) {
+                c += __popc(bits[w]);
+                if (carry.bits) carry.bits[I * nw + w] = bits[w];
+            }
+            total += block_sum<kCsrThreads>(c, s_red);
+        }
+        // per row: descent at its start; its runs
+        int64_t at_starts = 0;
+        for (int r = threadIdx.x; r < rows; r += kCsrThreads) {
+            const int lo = s.rowptr[i0 + r] - s.base, hi = s.rowptr[i0 + r + 1] - s.base;
+            int nr = 0;
+            bool zr = !runs || s_zero;
+            if (hi > lo) {
+                if (lo > E0 && __ldg(s.cols + lo) <= __ldg(s.cols + lo - 1)) ++at_starts;
+                if (runs) {
+                    zr = zr || is_zero<ES>(s.val, lo);
+                    nr = 1;
+                    for (int b = lo - E0 + 1; b < hi - E0;) {   // change bits in (lo, hi)
+                        const int w = b >> 5, sh = b & 31;
+                        const int take = min(32 - sh, hi - E0 - b);
+                        const uint32_t m = take == 32 ? 0xffffffffu : ((1u << take) - 1u) << sh;
+                        nr += __popc(jc[w] & m);
+                        b += take;
+                    }
+                }
+            }
+            if (carry.bits) carry.row_runs[i0 + r] = zr ? -1 : nr;
+        }
+        at_starts = block_sum<kCsrThreads>(at_starts, s_red);
+        if (threadIdx.x == 0) {
+            if (total > INT32_MAX) dev_error(DEV_ERR_OVERFLOW);
+            counts[I] = (int32_t)total;
+            if (carry.bits) carry.asc[I] = (uint8_t)(s_desc == at_starts);
+        }
+        __syncthreads();
+    }
+    if (carry.bits && blockIdx.x == 0 && threadIdx.x == 0) *carry.stamp = carry.key;
+}
+
+// ---------------------------------------------------------- fill, fast rows
+// Value copy with explicit zeros (either sign) written as +0, as the tiles'
+// zero padding: U-byte units of ES-byte values.
+template <int ES, typename UT>
+__device__ __forceinline__ UT plus_zero(UT w);
+template <>
+__device__ __forceinline__ uint16_t plus_zero<2, uint16_t>(uint16_t w) { return (w & 0x7fffu) ? w : 0; }
+__device__ __forceinline__ uint32_t pz2(uint32_t w) {
+    uint32_t keep = 0;
+    if (w & 0x00007fffu) keep |= 0x0000ffffu;
+    if (w & 0x7fff0000u) keep |= 0xffff0000u;
+    return w & keep;
+}
+__device__ __forceinline__ uint32_t pz4(uint32_t w) { return (w & 0x7fffffffu) ? w : 0u; }
+__device__ __forceinline__ uint2 pz8(uint2 w) {
+    return ((w.x | (w.y & 0x7fffffffu)) != 0) ? w : make_uint2(0u, 0u);
+}
+template <>
+__device__ __forceinline__ uint32_t plus_zero<2, uint32_t>(uint32_t w) { return pz2(w); }
+template <>
+__device__ __forceinline__ uint32_t plus_zero<4, uint32_t>(uint32_t w) { return pz4(w); }
+template <>
+__device__ __forceinline__ uint2 plus_zero<2, uint2>(uint2 w) { return make_uint2(pz2(w.x), pz2(w.y)); }
+template <>
+__device__ __forceinline__ uint2 plus_zero<4, uint2>(uint2 w) { return make_uint2(pz4(w.x), pz4(w.y)); }
+template <>
+__device__ __forceinline__ uint2 plus_zero<8, uint2>(uint2 w) { return pz8(w); }
+template <>
+__device__ __forceinline__ uint4 plus_zero<2, uint4>(uint4 w) {
+    return make_uint4(pz2(w.x), pz2(w.y), pz2(w.z), pz2(w.w));
+}
+template <>
+__device__ __forceinline__ uint4 plus_zero<4, uint4>(uint4 w) {
+    return make_uint4(pz4(w.x), pz4(w.y), pz4(w.z), pz4(w.w));
+}
+template <>
+__device__ __forceinline__ uint4 plus_zero<8, uint4>(uint4 w) {
+    const uint2 a = pz8(make_uint2(w.x, w.y)), b = pz8(make_uint2(w.z, w.w));
+    return make_uint4(a.x, a.y, b.x, b.y);
+}
+
+// Copies `run` consecutive full tile rows: values [p, p + run * b2) of the
+// CSR (contiguous) to tile row r of tiles k .. k + run - 1 (dst = tile k's
+// row r, tiles tile_bytes apart), in UT units spread over the warp's lanes.
+constexpr int kCopyUnroll = 8;   // units a lane loads before storing
+
+template <int ES, typename UT>
+__device__ __forceinline__ void copy_tile_rows(char *dst, int64_t tile_bytes, const char *src,
+                                               int upr, int upr_sh, int run, int lane) {
+    const UT *s = reinterpret_cast<const UT *>(src);
+    const int total = run * upr;
+    for (int x0 = 0; x0 < total; x0 += kCopyUnroll * kWarp) {
+        UT w[kCopyUnroll];
+#pragma unroll
+        for (int j = 0; j < kCopyUnroll; ++j) {
+            const int x = x0 + j * kWarp + lane;
+            if (x < total) w[j] = s[x];
+        }
+#pragma unroll
+        for (int j = 0; j < kCopyUnroll; ++j) {
+            const int x = x0 + j * kWarp + lane;
+            if (x < total) {
+                const int t = upr_sh >= 0 ? x >> upr_sh : x / upr;
+                const int u = x - t * upr;
+                reinterpret_cast<UT *>(dst + (int64_t)t * tile_bytes)[u] = plus_zero<ES, UT>(w[j]);
+            }
+        }
+    }
+}
+
+// Zero-fills `bytes` bytes at dst with the warp (UT-aligned dst and size).
+template <typename UT>
+__device__ __forceinline__ void zero_units(char *dst, int bytes, int lane) {
+    UT z;
+    memset(&z, 0, sizeof(UT));
+    for (int x = lane; x < bytes / (int)sizeof(UT); x += kWarp) reinterpret_cast<UT *>(dst)[x] = z;
+}
+
+__device__ __forceinline__ void zero_row(char *dst, int bytes, int lane) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(dst) | (uintptr_t)bytes;
+    if ((a & 15) == 0) zero_units<uint4>(dst, bytes, lane);
+    else if ((a & 7) == 0) zero_units<uint2>(dst, bytes, lane);
+    else if ((a & 3) == 0) zero_units<uint32_t>(dst, bytes, lane);
+    else if ((a & 1) == 0) zero_units<uint16_t>(dst, bytes, lane);
+    else zero_units<uint8_t>(dst, bytes, lane);
+}
+
+// Copies `run` full runs of a row starting at entry p (values [p, p + run *
+// b2), contiguous) to tile row r of `run` consecutive tiles (dst = the first
+// one's row), in the widest unit the addresses allow.
+template <int ES>
+__device__ __forceinline__ void copy_row_any(const char *src, char *dst, int64_t tile_bytes, int total,
+                                             int upr_sh, int lane);
+
+template <int ES>
+__device__ __forceinline__ void copy_runs(const Src &s, int64_t p, char *dst, int64_t tile_bytes,
+                                          int run, int lane) {
+    const int b2 = s.b2, row_bytes = b2 * ES;
+    const char *src = reinterpret_cast<const char *>(s.val) + p * ES;
+    const uintptr_t dal = reinterpret_cast<uintptr_t>(dst) | (uintptr_t)row_bytes | (uintptr_t)tile_bytes;
+    const uintptr_t al = reinterpret_cast<uintptr_t>(src) | dal;
+    auto sh = [](int upr) { return (upr & (upr - 1)) ? -1 : __ffs(upr) - 1; };
+    if ((dal & 15) == 0 && sh(row_bytes / 16) >= 0) {
+        // 16-byte units on the tile side, any source offset
+        copy_row_any<ES>(src, dst, tile_bytes, run * (row_bytes / 16), sh(row_bytes / 16), lane);
+    } else if ((al & 15) == 0) {
+        copy_tile_rows<ES, uint4>(dst, tile_bytes, src, row_bytes / 16, sh(row_bytes / 16), run, lane);
+    } else if ((al & 7) == 0) {
+        copy_tile_rows<ES, uint2>(dst, tile_bytes, src, row_bytes / 8, sh(row_bytes / 8), run, lane);
+    } else if (ES <= 4 && (al & 3) == 0) {
+        if constexpr (ES <= 4)
+            copy_tile_rows<ES, uint32_t>(dst, tile_bytes, src, row_bytes / 4, sh(row_bytes / 4), run, lane);
+    } else {
+        // 2-byte values at odd positions: one value at a time
+        for (int t = 0; t < run; ++t)
+            for (int c = lane; c < b2; c += kWarp) {
+                const int64_t e = p + (int64_t)t * b2 + c;
+                if (is_zero<ES>(s.val, e)) store_zero<ES>(dst + (int64_t)t * tile_bytes, c);
+                else copy_val<ES>(dst + (int64_t)t * tile_bytes, c, s.val, e);
+            }
+    }
+}
+
+// One row of block row I by runs (the row is ascending): for the block row's
+// blocks k (block columns bcol[k], ascending) a tile row is a full run when
+// the row's entries from the cursor p are exactly the block's b2 columns --
+// with ascending columns that holds iff the first is the block's first
+// column and the entry b2 - 1 further is its last.  The 32 lanes test blocks
+// k .. k+31 at once, assuming each earlier one a full run, and the warp
+// copies the leading full runs as one contiguous stretch of values; a block
+// that is not a full run is zeroed and its entries scattered (entries before
+// it belong to blocks with only explicit zeros and are skipped).
+template <int ES>
+__device__ __noinline__ void fill_row_runs(const Src &s, int64_t i, char *row0, int nblk, const int32_t *bcol,
+                              int64_t tile_bytes, int lane) {
+    const int b2 = s.b2, row_bytes = b2 * ES;
+    if (i >= s.m) {   // rows past the matrix: padding
+        for (int k = 0; k < nblk; ++k) zero_row(row0 + (int64_t)k * tile_bytes, row_bytes, lane);
+        return;
+    }
+    int64_t p = s.rowptr[i] - s.base;
+    const int64_t hi = s.rowptr[i + 1] - s.base;
+    int k = 0;
+    while (k < nblk) {
+        const int kk = k + lane;
+        bool full = false;
+        if (kk < nblk) {
+            const int64_t c0 = (int64_t)(__ldcg(bcol + kk) - s.base) * b2;
+            const int64_t ph = p + (int64_t)lane * b2;
+            if (ph + b2 <= hi)
+                full = (int64_t)(__ldg(s.cols + ph) - s.base) == c0 &&
+                       (int64_t)(__ldg(s.cols + ph + b2 - 1) - s.base) == c0 + b2 - 1;
+        }
+        const unsigned fm = __ballot_sync(0xffffffffu, full);
+        const int run = fm == 0xffffffffu ? kWarp : __ffs(~fm) - 1;
+        if (run > 0) {
+            copy_runs<ES>(s, p, row0 + (int64_t)k * tile_bytes, tile_bytes, run, lane);
+            p += (int64_t)run * b2;
+            k += run;
+        }
+        if (run < kWarp && k < nblk) {
+            // block k is not a full run of this row: zero its tile row, then
+            // scatter the row's entries that fall in it
+            const int64_t c0 = (int64_t)(__ldcg(bcol + k) - s.base) * b2;
+            char *dst = row0 + (int64_t)k * tile_bytes;
+            zero_row(dst, row_bytes, lane);
+            __syncwarp();
+            for (;;) {
+                const int64_t e = p + lane;
+                const int64_t c = e < hi ? (int64_t)(__ldg(s.cols + e) - s.base) : INT64_MAX;
+                const bool in = c < c0 + b2;   // ascending: a prefix of the lanes
+                const int cnt = __popc(__ballot_sync(0xffffffffu, in));
+                if (in && c >= c0 && !is_zero<ES>(s.val, e)) copy_val<ES>(dst, c - c0, s.val, e);
+                p += cnt;
+                if (cnt < kWarp) break;
+            }
+            __syncwarp();
+            ++k;
+        }
+    }
+}
+
+// A CSR block row that the tile-row fill (fill_ascending) takes: the count
+// pass handed its bitmap over and found all its rows ascending.
+__device__ __forceinline__ bool fast_block_row(const Src &s, const Carry &carry, bool handed,
+                                               int64_t I) {
+    return handed && s.rowptr && carry.asc[I];
+}
+
 // Fill pass.  winner == nullptr means the source has unique coordinates.
+// The block rows that fast_block_row() picks are left to fill_ascending.
 template <int ES>
 __global__ void __launch_bounds__(kConvThreads, 2)
 fill_blocks(Src s, int64_t mb, int64_t nb, int64_t nnzb, const int32_t *__restrict__ browptr,
@@ -403,6 +1002,7 @@ fill_blocks(Src s, int64_t mb, int64_t nb, int64_t nnzb, const int32_t *__restri
     __shared__ int64_t s_warp[kConvThreads / kWarp];
     const int64_t bsz = (int64_t)s.b1 * s.b2;
     for (int64_t I = blockIdx.x; I < mb; I += gridDim.x) {
+        if (!winner && fast_block_row(s, carry, handed, I)) continue;
         int64_t q0 = (int64_t)browptr[I] - s.base, q1 = (int64_t)browptr[I + 1] - s.base;
         if (q0 < 0 || q1 < q0 || q1 > nnzb) {
             if (threadIdx.x == 0) dev_error(DEV_ERR_BOUNDS);
@@ -487,6 +1087,262 @@ fill_blocks(Src s, int64_t mb, int64_t nb, int64_t nnzb, const int32_t *__restri
             }
             rank0 += carry;
             __syncthreads();
+        }
+    }
+}
+
+// Fill of the block rows that fast_block_row() picks, in three launches:
+// fill_asc_columns writes their block columns (from the handed-over bitmap:
+// one window, as the hand-over implies), fill_whole_rows copies every row
+// that is whole -- nblk * b2 entries forming a full run in each of the block
+// row's blocks -- and fill_other_rows writes the rest run by run.  Every byte
+// of these tiles is written once (no zero fill).  A per-row flag in the
+// workspace tells the third launch which rows the second did.
+constexpr int kAscThreads = 512;
+
+template <int ES>
+__global__ void __launch_bounds__(kAscThreads)
+fill_asc_columns(Src s, int64_t mb, int64_t nb, int64_t nnzb, const int32_t *__restrict__ browptr,
+                 int32_t *__restrict__ bcolind, Carry carry) {
+    const bool handed = carry.bits && *carry.stamp == carry.key;
+    if (!handed) return;
+    __shared__ uint32_t bits[kWinWords];
+    __shared__ int32_t pref[kWinWords];
+    __shared__ int64_t s_warp[kAscThreads / kWarp];
+    const int nw = (int)ceil_div(nb, 32);
+    for (int64_t I = blockIdx.x; I < mb; I += gridDim.x) {
+        if (!fast_block_row(s, carry, handed, I)) continue;
+        const int64_t q0 = (int64_t)browptr[I] - s.base, q1 = (int64_t)browptr[I + 1] - s.base;
+        if (q0 < 0 || q1 < q0 || q1 > nnzb) {
+            if (threadIdx.x == 0) dev_error(DEV_ERR_BOUNDS);
+            continue;   // write nothing for this block row
+        }
+        for (int w = threadIdx.x; w < nw; w += kAscThreads) bits[w] = carry.bits[I * nw + w];
+        __syncthreads();
+        int64_t run = 0;
+        for (int c0 = 0; c0 < nw; c0 += kAscThreads) {
+            const int w = c0 + threadIdx.x;
+            const int64_t v = w < nw ? __popc(bits[w]) : 0;
+            int64_t tot;
+            const int64_t ex = block_exclusive_scan<kAscThreads>(v, s_warp, tot);
+            if (w < nw) pref[w] = (int32_t)(run + ex);
+            run += tot;
+        }
+        __syncthreads();
+        if (run != q1 - q0) {   // block row pointer and bitmap disagree
+            if (threadIdx.x == 0) dev_error(DEV_ERR_BOUNDS);
+            continue;
+        }
+        for (int w = threadIdx.x; w < nw; w += kAscThreads) {
+            uint32_t word = bits[w];
+            int r = pref[w];
+            while (word) {
+                const int b = __ffs(word) - 1;
+                word &= word - 1;
+                bcolind[q0 + r] = w * 32 + b + s.base;
+                ++r;
+            }
+        }
+        __syncthreads();
+    }
+}
+
+// The block row of row i when fast_block_row() picks it and its block row
+// pointer is sane: q0 and nblk; false otherwise.
+__device__ __forceinline__ bool asc_row(const Src &s, const Carry &carry, bool handed,
+                                        const int32_t *__restrict__ browptr, int64_t nnzb,
+                                        int64_t I, int64_t &q0, int &nblk) {
+    if (!fast_block_row(s, carry, handed, I)) return false;
+    q0 = (int64_t)browptr[I] - s.base;
+    const int64_t q1 = (int64_t)browptr[I + 1] - s.base;
+    if (q0 < 0 || q1 < q0 || q1 > nnzb) return false;   // reported by fill_asc_columns
+    nblk = (int)(q1 - q0);
+    return true;
+}
+
+// One warp per row (rows of all block rows, padding rows included).  A whole
+// row's values are contiguous and its tile rows are nblk * b2 * ES bytes of
+// them in order, so the copy is a stream of 16-, 8- or 4-byte units, four in
+// flight per lane.  Marks row_done[i] for the rows it wrote.
+constexpr int kRowThreads = 256;
+
+template <int ES, typename UT>
+__device__ __forceinline__ void copy_row_units(const char *src, char *dst, int64_t tile_bytes,
+                                               int total, int upr_sh, int lane) {
+    const UT *sp = reinterpret_cast<const UT *>(src);
+    const int mask = (1 << upr_sh) - 1;
+    for (int x0 = 0; x0 < total; x0 += 4 * kWarp) {
+        UT w[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int x = x0 + j * kWarp + lane;
+            if (x < total) w[j] = __ldcs(sp + x);
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int x = x0 + j * kWarp + lane;
+            if (x < total)
+                reinterpret_cast<UT *>(dst + (int64_t)(x >> upr_sh) * tile_bytes)[x & mask] =
+                    plus_zero<ES, UT>(w[j]);
+        }
+    }
+}
+
+// The same stream when the source starts `off` bytes (0 < off < 16, a
+// multiple of ES) past a 16-byte boundary: each lane loads the aligned unit
+// holding its first bytes, takes the next one from the lane after it (lane 31
+// loads it), and funnel-shifts the pair into place.  The aligned units read
+// stay inside the 16-byte blocks that hold the row's own bytes.
+template <int ES, int WS>
+__device__ __forceinline__ uint4 realign(uint4 a, uint4 b, int bs) {
+    const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    return make_uint4(__funnelshift_r(w[WS], w[WS + 1], bs), __funnelshift_r(w[WS + 1], w[WS + 2], bs),
+                      __funnelshift_r(w[WS + 2], w[WS + 3], bs), __funnelshift_r(w[WS + 3], w[WS + 4], bs));
+}
+
+template <int ES, int WS>
+__device__ __forceinline__ void copy_row_shifted(const uint4 *sp, int bs, char *dst, int64_t tile_bytes,
+                                                 int total, int upr_sh, int lane) {
+    // destination units x < total read aligned source units x and x + 1
+    // (unit `total` holds the row's last bytes)
+    const int mask = (1 << upr_sh) - 1;
+    for (int x0 = 0; x0 < total; x0 += 4 * kWarp) {
+        uint4 a[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int x = x0 + j * kWarp + lane;
+            a[j] = x <= total ? __ldcs(sp + x) : make_uint4(0, 0, 0, 0);
+        }
+        const uint4 tail = lane == kWarp - 1 && x0 + 4 * kWarp <= total ? __ldcs(sp + x0 + 4 * kWarp)
+                                                                        : make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            // unit x + 1: the next lane's, for lane 31 lane 0's of the next j
+            const uint4 &up = j < 3 ? a[j + 1] : a[j];
+            uint4 nx, wrap;
+            nx.x = __shfl_down_sync(0xffffffffu, a[j].x, 1);
+            nx.y = __shfl_down_sync(0xffffffffu, a[j].y, 1);
+            nx.z = __shfl_down_sync(0xffffffffu, a[j].z, 1);
+            nx.w = __shfl_down_sync(0xffffffffu, a[j].w, 1);
+            wrap.x = __shfl_sync(0xffffffffu, up.x, 0);
+            wrap.y = __shfl_sync(0xffffffffu, up.y, 0);
+            wrap.z = __shfl_sync(0xffffffffu, up.z, 0);
+            wrap.w = __shfl_sync(0xffffffffu, up.w, 0);
+            if (lane == kWarp - 1) nx = j < 3 ? wrap : tail;
+            const int x = x0 + j * kWarp + lane;
+            if (x < total)
+                reinterpret_cast<uint4 *>(dst + (int64_t)(x >> upr_sh) * tile_bytes)[x & mask] =
+                    plus_zero<ES, uint4>(realign<ES, WS>(a[j], nx, bs));
+        }
+    }
+}
+
+template <int ES>
+__device__ __forceinline__ void copy_row_any(const char *src, char *dst, int64_t tile_bytes, int total,
+                                             int upr_sh, int lane) {
+    const int off = (int)(reinterpret_cast<uintptr_t>(src) & 15);
+    if (off == 0) {
+        copy_row_units<ES, uint4>(src, dst, tile_bytes, total, upr_sh, lane);
+        return;
+    }
+    const uint4 *sp = reinterpret_cast<const uint4 *>(src - off);
+    const int bs = (off & 3) * 8;
+    switch (off >> 2) {
+        case 0: copy_row_shifted<ES, 0>(sp, bs, dst, tile_bytes, total, upr_sh, lane); break;
+        case 1: copy_row_shifted<ES, 1>(sp, bs, dst, tile_bytes, total, upr_sh, lane); break;
+        case 2: copy_row_shifted<ES, 2>(sp, bs, dst, tile_bytes, total, upr_sh, lane); break;
+        default: copy_row_shifted<ES, 3>(sp, bs, dst, tile_bytes, total, upr_sh, lane); break;
+    }
+}
+
+template <int ES>
+__global__ void __launch_bounds__(kRowThreads, 3)
+fill_whole_rows(Src s, int64_t mb, int64_t nnzb, const int32_t *__restrict__ browptr,
+                const int32_t *__restrict__ bcolind, char *__restrict__ bval, Carry carry) {
+    const bool handed = carry.bits && *carry.stamp == carry.key;
+    if (!handed) return;
+    const int lane = threadIdx.x % kWarp;
+    const int b1 = s.b1, b2 = s.b2, row_bytes = b2 * ES;
+    const int64_t tile_bytes = (int64_t)b1 * row_bytes;
+    const int64_t nrows = mb * b1;
+    const int64_t warps = (int64_t)gridDim.x * (kRowThreads / kWarp);
+    for (int64_t i = (int64_t)blockIdx.x * (kRowThreads / kWarp) + threadIdx.x / kWarp; i < nrows;
+         i += warps) {
+        const int64_t I = i / b1;
+        const int r = (int)(i - I * b1);
+        int64_t q0;
+        int nblk;
+        if (!asc_row(s, carry, handed, browptr, nnzb, I, q0, nblk)) continue;
+        char *row0 = bval + q0 * tile_bytes + (int64_t)r * row_bytes;
+        bool done = false;
+        if (i >= s.m) {   // rows past the matrix: padding
+            for (int k = 0; k < nblk; ++k) zero_row(row0 + (int64_t)k * tile_bytes, row_bytes, lane);
+            done = true;
+        } else if (nblk == 0) {
+            done = true;
+        } else {
+            const int64_t lo = s.rowptr[i] - s.base, hi = s.rowptr[i + 1] - s.base;
+            // ascending, nblk runs (block columns) each starting nonzero -- so
+            // each is one of the block row's nblk blocks -- and nblk * b2
+            // entries: at most b2 a block, so exactly b2, every run full
+            const bool whole = carry.row_runs[i] == nblk && hi - lo == (int64_t)nblk * b2;
+            const char *src = reinterpret_cast<const char *>(s.val) + lo * ES;
+            const uintptr_t dal = reinterpret_cast<uintptr_t>(row0) | (uintptr_t)row_bytes |
+                                  (uintptr_t)tile_bytes;
+            const uintptr_t al = reinterpret_cast<uintptr_t>(src) | dal;
+            const int ub = (al & 15) == 0 ? 16 : (al & 7) == 0 ? 8 : (al & 3) == 0 ? 4 : 0;
+            const int upr = ub ? row_bytes / ub : 0;
+            const int upr16 = row_bytes / 16;
+            if (whole && (dal & 15) == 0 && (upr16 & (upr16 - 1)) == 0) {
+                // 16-byte units on the tile side, any source offset
+                copy_row_any<ES>(src, row0, tile_bytes, nblk * upr16, __ffs(upr16) - 1, lane);
+                done = true;
+            } else if (whole && ub && (upr & (upr - 1)) == 0) {
+                const int sh = __ffs(upr) - 1, total = nblk * upr;
+                if (ub == 16) copy_row_units<ES, uint4>(src, row0, tile_bytes, total, sh, lane);
+                else if (ub == 8) copy_row_units<ES, uint2>(src, row0, tile_bytes, total, sh, lane);
+                else if constexpr (ES <= 4)
+                    copy_row_units<ES, uint32_t>(src, row0, tile_bytes, total, sh, lane);
+                done = true;
+            }
+        }
+        if (lane == 0) carry.row_done[i] = done;
+    }
+}
+
+// The rows fill_whole_rows left, run by run: a warp takes 32 rows, finds the
+// ones to do with one flag load a lane, and does them one after another.
+template <int ES>
+__global__ void __launch_bounds__(kRowThreads)
+fill_other_rows(Src s, int64_t mb, int64_t nnzb, const int32_t *__restrict__ browptr,
+                const int32_t *__restrict__ bcolind, char *__restrict__ bval, Carry carry) {
+    const bool handed = carry.bits && *carry.stamp == carry.key;
+    if (!handed) return;
+    const int lane = threadIdx.x % kWarp;
+    const int b1 = s.b1, row_bytes = s.b2 * ES;
+    const int64_t tile_bytes = (int64_t)b1 * row_bytes;
+    const int64_t nrows = mb * b1;
+    const int64_t warps = (int64_t)gridDim.x * (kRowThreads / kWarp);
+    for (int64_t i0 = ((int64_t)blockIdx.x * (kRowThreads / kWarp) + threadIdx.x / kWarp) * kWarp;
+         i0 < nrows; i0 += warps * kWarp) {
+        const int64_t i = i0 + lane;
+        bool todo = false;
+        if (i < nrows) {
+            const int64_t I = i / b1;
+            int64_t q0;
+            int nblk;
+            todo = asc_row(s, carry, handed, browptr, nnzb, I, q0, nblk) && !carry.row_done[i];
+        }
+        unsigned pend = __ballot_sync(0xffffffffu, todo);
+        while (pend) {
+            const int l = __ffs(pend) - 1;
+            pend &= pend - 1;
+            const int64_t ir = i0 + l, I = ir / b1;
+            int64_t q0;
+            int nblk;
+            asc_row(s, carry, handed, browptr, nnzb, I, q0, nblk);
+            fill_row_runs<ES>(s, ir, bval + q0 * tile_bytes + (ir - I * b1) * row_bytes, nblk,
+                              bcolind + q0, tile_bytes, lane);
         }
     }
 }
@@ -808,10 +1664,17 @@ constexpr size_t kMaxCarryBytes = (size_t)256 << 20;
 
 static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
+// bitmaps (mb x words) then one ascending-rows flag per block row
+static size_t carry_bits_bytes(int64_t m, int64_t n, int b1, int b2) {
+    const int64_t mb = ceil_div(m, b1), nb = ceil_div(n, b2);
+    return align256((size_t)mb * (size_t)ceil_div(nb, 32) * 4);
+}
+
 static size_t carry_bytes(int64_t m, int64_t n, int b1, int b2) {
     const int64_t mb = ceil_div(m, b1), nb = ceil_div(n, b2);
     if (nb > conv::kWinBits || mb <= 0) return 0;
-    const size_t bytes = (size_t)mb * (size_t)ceil_div(nb, 32) * 4;
+    const size_t bytes = carry_bits_bytes(m, n, b1, b2) + align256((size_t)mb) +
+                         align256((size_t)mb * (size_t)b1) + align256((size_t)mb * (size_t)b1 * 4);
     return bytes <= kMaxCarryBytes ? bytes : 0;
 }
 
@@ -841,13 +1704,16 @@ static uint64_t carry_key(int64_t m, int64_t n, int64_t nnz, int b1, int b2, int
 static conv::Carry csr_carry(void *ws, size_t wsb, int64_t m, int64_t n, int64_t nnz, int b1,
                              int b2, int base, int dtype, const void *rowptr, const void *colind,
                              const void *val) {
-    conv::Carry c{nullptr, nullptr, 0};
+    conv::Carry c{nullptr, nullptr, nullptr, nullptr, nullptr, 0};
     const size_t cb = carry_bytes(m, n, b1, b2);
     const size_t scan = csr_scan_ws(m, b1);
     if (!cb || !ws || wsb < scan + 256 + cb) return c;
     char *p = reinterpret_cast<char *>(ws);
     c.stamp = reinterpret_cast<uint64_t *>(p + scan);
     c.bits = reinterpret_cast<uint32_t *>(p + scan + 256);
+    c.asc = reinterpret_cast<uint8_t *>(p + scan + 256 + carry_bits_bytes(m, n, b1, b2));
+    c.row_done = c.asc + align256((size_t)ceil_div(m, b1));
+    c.row_runs = reinterpret_cast<int32_t *>(c.row_done + align256((size_t)ceil_div(m, b1) * (size_t)b1));
     c.key = carry_key(m, n, nnz, b1, b2, base, dtype, rowptr, colind, val);
     return c;
 }
@@ -857,13 +1723,15 @@ extern "C" JLB_API size_t jlb_csr_to_bsr_workspace_size(int64_t m, int64_t n, in
     return b1 > 0 && b2 > 0 ? csr_ws(m, n, b1, b2) : 0;
 }
 
-static conv::Src csr_src(int dtype, int idx_base, int64_t m, int64_t n, const int32_t *rowptr,
-                         const int32_t *colind, const void *val, int b1, int b2) {
+static conv::Src csr_src(int dtype, int idx_base, int64_t m, int64_t n, int64_t nnz,
+                         const int32_t *rowptr, const int32_t *colind, const void *val, int b1,
+                         int b2) {
     conv::Src s{};
     s.rowptr = rowptr; s.rows = nullptr; s.cols = colind; s.val = val;
     s.boffs = nullptr; s.bent = nullptr; s.m = m; s.n = n;
     s.b1 = b1; s.b2 = b2; s.base = idx_base; s.es = (int)dtype_size(dtype);
     s.sh1 = conv::log2_exact(b1); s.sh2 = conv::log2_exact(b2);
+    s.nnz = nnz; s.vec = aligned16(colind);
     return s;
 }
 
@@ -899,12 +1767,30 @@ extern "C" JLB_API int jlb_csr_to_bsr_count(void *stream, int dtype, int idx_bas
     cudaStream_t st = as_stream(stream);
     const int64_t mb = ceil_div(m, b1), nb = ceil_div(n, b2);
     if (mb > 0) {
-        JLB_CONV_LAUNCH(count_blocks, dtype_size(dtype), conv::grid_rows(mb), st,
-                        csr_src(dtype, idx_base, m, n, rowptr, colind, val, b1, b2), mb, nb,
-                        browptr + 1,
-                        csr_carry(workspace, workspace_bytes, m, n, nnz, b1, b2, idx_base, dtype,
-                                  rowptr, colind, val));
-        JLB_LAUNCH_CHECK("count_blocks");
+        const conv::Src src = csr_src(dtype, idx_base, m, n, nnz, rowptr, colind, val, b1, b2);
+        const conv::Carry cy = csr_carry(workspace, workspace_bytes, m, n, nnz, b1, b2, idx_base,
+                                         dtype, rowptr, colind, val);
+        const unsigned grid = conv::grid_rows(mb);
+        const int es = (int)dtype_size(dtype);
+#define JLB_COUNT_CSR(E)                                                                         \
+    if (src.sh2 >= 0) {                                                                          \
+        JLB_CUDA(cudaFuncSetAttribute(conv::count_csr<E, true>,                                  \
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,              \
+                                      (int)conv::kCountSmem));                                   \
+        conv::count_csr<E, true><<<grid, conv::kCsrThreads, conv::kCountSmem, st>>>(             \
+            src, mb, nb, browptr + 1, cy);                                                       \
+    } else {                                                                                     \
+        JLB_CUDA(cudaFuncSetAttribute(conv::count_csr<E, false>,                                 \
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,              \
+                                      (int)conv::kCountSmem));                                   \
+        conv::count_csr<E, false><<<grid, conv::kCsrThreads, conv::kCountSmem, st>>>(            \
+            src, mb, nb, browptr + 1, cy);                                                       \
+    }
+        if (es == 8) { JLB_COUNT_CSR(8); }
+        else if (es == 4) { JLB_COUNT_CSR(4); }
+        else { JLB_COUNT_CSR(2); }
+#undef JLB_COUNT_CSR
+        JLB_LAUNCH_CHECK("count_csr");
     }
     return finish_count(st, mb, idx_base, browptr, nnzb, workspace, workspace_bytes, nullptr);
 }
@@ -922,11 +1808,35 @@ extern "C" JLB_API int jlb_csr_to_bsr_fill(void *stream, int dtype, int idx_base
     const int64_t mb = ceil_div(m, b1), nb = ceil_div(n, b2);
     if (mb == 0) return ok();
     cudaStream_t st = as_stream(stream);
-    JLB_CONV_LAUNCH(fill_blocks, dtype_size(dtype), conv::grid_rows(mb), st,
-                    csr_src(dtype, idx_base, m, n, rowptr, colind, val, b1, b2), mb, nb, nnzb,
-                    browptr, bcolind, bval, nullptr,
-                    csr_carry(workspace, workspace_bytes, m, n, nnz, b1, b2, idx_base, dtype,
-                              rowptr, colind, val));
+    const conv::Src src = csr_src(dtype, idx_base, m, n, nnz, rowptr, colind, val, b1, b2);
+    const conv::Carry cy = csr_carry(workspace, workspace_bytes, m, n, nnz, b1, b2, idx_base, dtype,
+                                     rowptr, colind, val);
+    // block rows the count pass found ascending (hand-over present) take the
+    // tile-row kernel; the entry-by-entry kernel does the others
+    if (cy.bits) {
+        const unsigned grid = conv::grid_rows(mb);
+        const int64_t rows = mb * (int64_t)b1;
+        const unsigned rgrid = (unsigned)std::min<int64_t>(ceil_div(rows, conv::kRowThreads / kWarp),
+                                                           148 * 16);
+        const unsigned ogrid = (unsigned)std::min<int64_t>(
+            ceil_div(rows, (int64_t)conv::kRowThreads / kWarp * kWarp), 148 * 4);
+        char *bv = static_cast<char *>(bval);
+#define JLB_ASC_FILL(E)                                                                           \
+    conv::fill_asc_columns<E><<<grid, conv::kAscThreads, 0, st>>>(src, mb, nb, nnzb, browptr,       \
+                                                                  bcolind, cy);                    \
+    conv::fill_whole_rows<E><<<rgrid, conv::kRowThreads, 0, st>>>(src, mb, nnzb, browptr, bcolind,  \
+                                                                  bv, cy);                          \
+    conv::fill_other_rows<E><<<ogrid, conv::kRowThreads, 0, st>>>(src, mb, nnzb, browptr, bcolind,  \
+                                                                  bv, cy)
+        const int es = (int)dtype_size(dtype);
+        if (es == 8) { JLB_ASC_FILL(8); }
+        else if (es == 4) { JLB_ASC_FILL(4); }
+        else { JLB_ASC_FILL(2); }
+#undef JLB_ASC_FILL
+        JLB_LAUNCH_CHECK("fill_ascending");
+    }
+    JLB_CONV_LAUNCH(fill_blocks, dtype_size(dtype), conv::grid_rows(mb), st, src, mb, nb, nnzb,
+                    browptr, bcolind, bval, nullptr, cy);
     JLB_LAUNCH_CHECK("fill_blocks");
     return ok();
 }
@@ -1050,7 +1960,7 @@ extern "C" JLB_API int jlb_coo_to_bsr_fill(void *stream, int dtype, int idx_base
     int32_t *winner = k.take<int32_t>((size_t)nnzb * (size_t)b1 * (size_t)b2);
     JLB_CONV_LAUNCH(fill_blocks, dtype_size(dtype), conv::grid_rows(mb), st,
                     coo_src(dtype, idx_base, m, n, rows, cols, val, b1, b2, boffs, bent), mb, nb,
-                    nnzb, browptr, bcolind, bval, winner, conv::Carry{nullptr, nullptr, 0});
+                    nnzb, browptr, bcolind, bval, winner, conv::Carry{nullptr, nullptr, nullptr, nullptr, nullptr, 0});
     JLB_LAUNCH_CHECK("fill_blocks");
     return ok();
 }

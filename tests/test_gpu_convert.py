@@ -56,6 +56,77 @@ def test_csr_random(dtype, base, b1, b2):
     check_csr(m, n, rp, ci, val, b1, b2, base)
 
 
+def _dense_tile_csr(m, n, b1, b2, dtype, seed, base):
+    """CSR whose rows are mostly whole tile rows of dense blocks (the fill's
+    tile-row path), with the cases that leave it: rows thinned inside a block,
+    blocks missing from single rows, explicit zeros of both signs, a block
+    holding only zeros, rows of odd length (later rows start at odd entries)
+    and a partial last block row."""
+    rng = np.random.default_rng(seed)
+    mb, nb = -(-m // b1), -(-n // b2)
+    rows_cols = []
+    for I in range(mb):
+        blocks = np.sort(rng.choice(nb, size=min(nb, 5), replace=False))
+        for i in range(I * b1, min(m, I * b1 + b1)):
+            cols = []
+            for J_ in blocks:
+                c = np.arange(J_ * b2, min(n, J_ * b2 + b2))
+                u = rng.random()
+                if u < 0.1:
+                    continue                                   # block absent from this row
+                if u < 0.3:
+                    c = np.sort(rng.choice(c, size=rng.integers(1, c.size + 1), replace=False))
+                cols.append(c)
+            if i % 7 == 3:
+                cols.append(np.array([n - 1]))               # odd lengths, ragged starts
+            rows_cols.append(np.unique(np.concatenate(cols)) if cols else np.zeros(0, np.int64))
+    lens = np.array([c.size for c in rows_cols])
+    rp = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    ci = np.concatenate(rows_cols).astype(np.int32)
+    val = rng.uniform(0.5, 2.0, size=ci.size) * rng.choice([-1.0, 1.0], size=ci.size)
+    if dtype == np.uint16:
+        val = synth.f32_to_bf16_bits(val.astype(np.float32))
+        neg0, pos0 = np.uint16(0x8000), np.uint16(0)
+    else:
+        val = val.astype(dtype)
+        neg0, pos0 = dtype(-0.0), dtype(0.0)
+    val[rng.random(val.size) < 0.03] = neg0
+    val[rng.random(val.size) < 0.03] = pos0
+    # block row 1: its first block column holds only zeros
+    if mb > 1:
+        I, J0 = 1, None
+        for i in range(b1, min(m, 2 * b1)):
+            seg = np.arange(rp[i], rp[i + 1])
+            if J0 is None and seg.size:
+                J0 = ci[seg[0]] // b2
+            if J0 is not None:
+                val[seg[ci[seg] // b2 == J0]] = neg0
+    return (rp + base).astype(np.int32), (ci + base).astype(np.int32), val
+
+
+@pytest.mark.parametrize("dtype", [np.float64, np.float32, np.uint16])
+@pytest.mark.parametrize("b1,b2", [(64, 64), (8, 8), (3, 5), (16, 32)])
+@pytest.mark.parametrize("base", [0, 1])
+def test_csr_dense_tile_rows(dtype, b1, b2, base):
+    m, n = 5 * b1 - 1, 11 * b2 - 2
+    rp, ci, val = _dense_tile_csr(m, n, b1, b2, dtype, 70 + b1, base)
+    check_csr(m, n, rp, ci, val, b1, b2, base)
+
+
+@pytest.mark.parametrize("dtype", [np.float32, np.uint16])
+def test_csr_unsorted_rows(dtype):
+    """Rows whose columns are not ascending take the entry-by-entry fill; the
+    result is the composer's (which sorts)."""
+    rng = np.random.default_rng(80)
+    m, n, b1, b2 = 200, 300, 16, 16
+    rp, ci, val = _dense_tile_csr(m, n, b1, b2, dtype, 81, 0)
+    for i in range(0, m, 3):                                # every third row shuffled
+        s = slice(rp[i], rp[i + 1])
+        perm = rng.permutation(rp[i + 1] - rp[i])
+        ci[s], val[s] = ci[s][perm], val[s][perm]
+    check_csr(m, n, rp, ci, val, b1, b2, 0)
+
+
 def test_csr_wide_matrix_windows():
     """More block columns than one shared-memory bitmap window holds."""
     rng = np.random.default_rng(63)
