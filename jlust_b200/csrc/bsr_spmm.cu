@@ -109,6 +109,15 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map
         : "memory");
 }
 
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map, uint32_t bar,
+                                            int32_t x, int32_t y, int32_t z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
+
 __device__ __forceinline__ void tc_fence_after() {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
@@ -241,19 +250,24 @@ __host__ __device__ inline uint32_t tmem_cols_for(int n, int nbuf) {
 }
 
 // Block-column merge of a pair of block rows: rows a = I and b = I+1 (b
-// absent when has_b is false).  next() yields the groups in order: the smallest head block
-// column, with each row whose head it is (each row's blocks stay in their
-// storage order, sorted or not).  The heads are loaded one step ahead.
+// absent when has_b is false).  next() yields the groups in order: the
+// smallest head block column, with each row whose head it is (each row's
+// blocks stay in their storage order, sorted or not).
 struct PairMerge {
     const int32_t *bcolind;
     int base;
     int qa, qa1, qb, qb1;
-    int ja, jb;                     // current heads (block columns), valid while q < q1
+    // block columns of the next four entries of each row (INT_MAX past the
+    // row's end): each load is issued three steps before its value is needed
+    int a0, a1, a2, a3, b0, b1, b2, b3;
 
+    __device__ __forceinline__ int col(int q, int q1) const {
+        return q < q1 ? __ldg(bcolind + q) - base : INT_MAX;
+    }
     __device__ void init(const int32_t *__restrict__ browptr, const int32_t *__restrict__ bc,
-                         int64_t I, bool has_b, int b0) {
+                         int64_t I, bool has_b, int b0_) {
         bcolind = bc;
-        base = b0;
+        base = b0_;
         qa = browptr[I] - base;
         qa1 = browptr[I + 1] - base;
         if (has_b) {
@@ -262,23 +276,22 @@ struct PairMerge {
         } else {
             qb = qb1 = 0;
         }
-        ja = qa < qa1 ? bcolind[qa] - base : 0;
-        jb = qb < qb1 ? bcolind[qb] - base : 0;
+        a0 = col(qa, qa1); a1 = col(qa + 1, qa1); a2 = col(qa + 2, qa1); a3 = col(qa + 3, qa1);
+        b0 = col(qb, qb1); b1 = col(qb + 1, qb1); b2 = col(qb + 2, qb1); b3 = col(qb + 3, qb1);
     }
     __device__ bool done() const { return qa >= qa1 && qb >= qb1; }
     // group: block column J, entries of row a / row b (-1 when absent)
     __device__ void next(int &J, int &ea, int &eb) {
-        const bool ha = qa < qa1, hb = qb < qb1;
-        J = ha && hb ? (ja < jb ? ja : jb) : ha ? ja : jb;
-        ea = (ha && ja == J) ? qa : -1;
-        eb = (hb && jb == J) ? qb : -1;
+        J = a0 < b0 ? a0 : b0;
+        ea = (qa < qa1 && a0 == J) ? qa : -1;
+        eb = (qb < qb1 && b0 == J) ? qb : -1;
         if (ea >= 0) {
             ++qa;
-            ja = qa < qa1 ? bcolind[qa] - base : 0;
+            a0 = a1; a1 = a2; a2 = a3; a3 = col(qa + 3, qa1);
         }
         if (eb >= 0) {
             ++qb;
-            jb = qb < qb1 ? bcolind[qb] - base : 0;
+            b0 = b1; b1 = b2; b2 = b3; b3 = col(qb + 3, qb1);
         }
     }
 };
@@ -288,7 +301,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 bsr_spmm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
             int64_t mb, const int32_t *__restrict__ browptr, const int32_t *__restrict__ bcolind,
             int base, int stages, int64_t zero_row, float *__restrict__ C, int64_t ldc,
-            float alpha, float beta, int has_beta) {
+            float alpha, float beta, int has_beta, int b_slab3d) {
     constexpr int kNBuf = 2 * N <= 512 ? 2 : 1;            // accumulators in TMEM
     constexpr int kChunks = N <= 256 ? 1 : 2;               // MMAs per K-step
     constexpr int kN0 = N <= 256 ? N : 256;                 // columns of the first MMA
@@ -365,10 +378,15 @@ bsr_spmm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                     // a missing block: a box wholly past the value array, filled with zeros
                     tma_load_2d(sA, &tmA, full, 0, ea >= 0 ? ea * kBS : (int32_t)zero_row);
                     tma_load_2d(sA + kATileBytes, &tmA, full, 0, eb >= 0 ? eb * kBS : (int32_t)zero_row);
+                    if (b_slab3d) {
+                        // the whole slab, its N/64 column boxes stacked, in one copy
+                        tma_load_3d(sA + 2 * kATileBytes, &tmB, full, 0, J * kBS, 0);
+                    } else {
 #pragma unroll
-                    for (int c = 0; c < N / 64; ++c)
-                        tma_load_2d(sA + 2 * kATileBytes + (uint32_t)c * kBoxBytes, &tmB, full, c * 64,
-                                    J * kBS);
+                        for (int c = 0; c < N / 64; ++c)
+                            tma_load_2d(sA + 2 * kATileBytes + (uint32_t)c * kBoxBytes, &tmB, full,
+                                        c * 64, J * kBS);
+                    }
                     ctl->last_fill[pid][stage] = k;
                 }
                 ++k;
@@ -556,6 +574,22 @@ static int make_map(CUtensorMap *map, const void *base, uint64_t inner, uint64_t
     return JLB_OK;
 }
 
+// B as a 3-D tensor {64 columns, rows, N/64 column boxes} (strides ldb * 2
+// and 128 bytes), so that one box {64, 64, N/64} is a whole 64-row slab laid
+// out box after box, as the 2-D boxes would put it.  False when the driver
+// refuses the layout.
+static bool make_map_b3(CUtensorMap *map, const void *B, int64_t N, uint64_t rows, uint64_t ldb) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[3] = {64, rows, (cuuint64_t)(N / 64)};
+    cuuint64_t strides[2] = {ldb * 2, 128};
+    cuuint32_t box[3] = {64, 64, (cuuint32_t)(N / 64)};
+    cuuint32_t estr[3] = {1, 1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(B), dims, strides, box,
+              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool tc_eligible(int bs, int64_t N, int64_t ldb, const void *bval, const void *B, int64_t nnzb,
                  int64_t nb, const float *C, int64_t ldc) {
     // TMA coordinates are int32: the zero-filled box starts at row nnzb * 64
@@ -588,8 +622,11 @@ extern "C" JLB_API int jlb_bsr_spmm(void *stream, int idx_base, int64_t mb, int6
         CUtensorMap tmA, tmB;
         int r = bsr::make_map(&tmA, bval, 64, (uint64_t)nnzb * 64, 128);
         if (r) return r;
-        r = bsr::make_map(&tmB, B, (uint64_t)N, (uint64_t)nb * 64, (uint64_t)ldb * 2);
-        if (r) return r;
+        const int b3 = bsr::make_map_b3(&tmB, B, N, (uint64_t)nb * 64, (uint64_t)ldb) ? 1 : 0;
+        if (!b3) {
+            r = bsr::make_map(&tmB, B, (uint64_t)N, (uint64_t)nb * 64, (uint64_t)ldb * 2);
+            if (r) return r;
+        }
         const uint32_t stage_bytes = 2 * bsr::kATileBytes + (uint32_t)(N / 64) * bsr::kBoxBytes;
         const size_t budget = 227 * 1024 - 1024 - sizeof(bsr::Ctl) - 64;
         int stages = (int)(budget / stage_bytes);
@@ -606,7 +643,7 @@ extern "C" JLB_API int jlb_bsr_spmm(void *stream, int idx_base, int64_t mb, int6
                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));    \
     bsr::bsr_spmm_tc<NN><<<grid, bsr::kThreads, smem, st>>>(tmA, tmB, mb, browptr, bcolind,     \
                                                             idx_base, stages, zero_row, C, ldc, \
-                                                            a, b, b != 0.0f)
+                                                            a, b, b != 0.0f, b3)
         switch (N) {
             case 128: JLB_BSR_TC(128); break;
             case 256: JLB_BSR_TC(256); break;
