@@ -970,9 +970,11 @@ class BSR(Single):
 class Convert(Single):
     """CSR -> BSRRight((64, 64)) of the config-5 matrix (bf16 values)."""
 
-    key, kernel, dtype, profile, unit = ("csr2bsr", "fill_blocks", "bf16 values, int32 indices",
+    key, kernel, dtype, profile, unit = ("csr2bsr", "count_csr", "bf16 values, int32 indices",
                                          "convert", "Gentries/s")
-    launches_per_step = 2
+    # count, three scan launches, then the three tile-row fill kernels and the
+    # entry-by-entry one (for block rows that are not ascending)
+    launches_per_step = 8
 
     def host(self):
         bp, bc, bv, _ = self.synth.config5(N=64)
