@@ -78,9 +78,17 @@ constexpr int kScanSumThreads = 1024;
 
 __device__ __forceinline__ int scan_pad(int i) { return i + (i >> 5); }   // one word per 32: no bank conflicts
 
+// Programmatic dependent launch between the three scan kernels: each lets
+// the next grid be scheduled once all its CTAs have started, and the next
+// waits for this grid's completion (griddepcontrol.wait, a no-op when
+// launched normally) before it reads what this one wrote.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __global__ void __launch_bounds__(kThreads)
 scan_tile_sums(int64_t n, const int32_t *__restrict__ counts, int64_t *__restrict__ sums) {
     __shared__ int64_t s_warp[kThreads / kWarp];
+    pdl_trigger();
     const int64_t t0 = (int64_t)blockIdx.x * kScanTile;
     int64_t v = 0;
     if (t0 + kScanTile <= n) {
@@ -104,10 +112,17 @@ scan_tile_sums(int64_t n, const int32_t *__restrict__ counts, int64_t *__restric
 __global__ void __launch_bounds__(kScanSumThreads)
 scan_sums_single(int64_t ntiles, int64_t *__restrict__ sums) {
     __shared__ int64_t s_warp[kScanSumThreads / kWarp];
+    pdl_trigger();
+    pdl_wait();
     const int64_t per = (ntiles + kScanSumThreads - 1) / kScanSumThreads;
     const int64_t c0 = threadIdx.x * per, c1 = c0 + per < ntiles ? c0 + per : ntiles;
     int64_t v = 0;
-    for (int64_t i = c0; i < c1; ++i) v += sums[i];
+    int64_t i = c0;
+    for (; i + 4 <= c1; i += 4) {   // four loads in flight
+        const int64_t a = sums[i], b = sums[i + 1], c = sums[i + 2], d = sums[i + 3];
+        v += a + b + c + d;
+    }
+    for (; i < c1; ++i) v += sums[i];
     int64_t total;
     int64_t run = block_exclusive_scan<kScanSumThreads>(v, s_warp, total);
     for (int64_t i = c0; i < c1; ++i) {
@@ -124,14 +139,16 @@ scan_tiles_final(int64_t n, const int32_t *counts, int32_t *out, const int64_t *
     __shared__ int32_t s_tile[kScanTile + kScanTile / 32];
     const int64_t t0 = (int64_t)blockIdx.x * kScanTile;
     const bool full = t0 + kScanTile <= n;
-    const int64_t offset = sums[blockIdx.x] + base;   // issued before the tile loads
     // `out` may alias `counts + 1`: this CTA reads exactly the counts whose
-    // outputs it writes, all before the barrier below.
+    // outputs it writes, all before the barrier below.  The counts are the
+    // caller's input: they are read before waiting for the tile sums.
 #pragma unroll
     for (int j = 0; j < kScanItems; ++j) {
         const int k = j * kThreads + threadIdx.x;
         s_tile[scan_pad(k)] = (full || t0 + k < n) ? counts[t0 + k] : 0;
     }
+    pdl_wait();
+    const int64_t offset = sums[blockIdx.x] + base;
     __syncthreads();
     // the thread's counts are read from shared memory twice rather than held
     // in registers: at most 40 registers a thread, six CTAs an SM
@@ -176,8 +193,19 @@ int scan(cudaStream_t st, int64_t n, const int32_t *counts, int32_t *out, int ba
     const int64_t ntiles = ceil_div(n, kScanTile);
     int64_t *sums = (int64_t *)ws;
     scan_tile_sums<<<(unsigned)ntiles, kThreads, 0, st>>>(n, counts, sums);
-    scan_sums_single<<<1, kScanSumThreads, 0, st>>>(ntiles, sums);
-    scan_tiles_final<<<(unsigned)ntiles, kThreads, 0, st>>>(n, counts, out, sums, base);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(kScanSumThreads);
+    JLB_CUDA(cudaLaunchKernelEx(&cfg, scan_sums_single, ntiles, sums));
+    cfg.gridDim = dim3((unsigned)ntiles);
+    cfg.blockDim = dim3(kThreads);
+    JLB_CUDA(cudaLaunchKernelEx(&cfg, scan_tiles_final, n, counts, out, (const int64_t *)sums, base));
     JLB_LAUNCH_CHECK("exclusive_scan");
     return ok();
 }
@@ -587,11 +615,11 @@ struct Raw8 {
 // entry, for the count pass.  The CTA's warps take chunks of 256 entries
 // round robin (chunks aligned to 8 entries), eight consecutive entries a
 // lane.
-//   Lean chunks -- inside [E0, E1), 16-byte loads, every lane's eight entries
-//   ascending, nonzero and in at most two adjacent block columns -- need only
-//   each lane's first and last entries: a lane marks its first entry's block
-//   column unless the lane before ended in it, and its last entry's when it
-//   differs.
+//   Lean chunks -- inside [E0, E1), 16-byte loads, every entry nonzero and in
+//   range -- mark only where the block column changes: a lane marks its first
+//   entry's block column unless the lane before ended in it, and each entry
+//   whose block column differs from the entry before it in the lane (a bit
+//   mask; usually empty).
 //   Other chunks go entry by entry: an entry marks its block column when it
 //   is nonzero and the previous nonzero entry (in the lane, or the lane
 //   before) had another one.
@@ -619,8 +647,7 @@ __device__ __forceinline__ void mark_csr_count(const Src &s, int E0, int E1, int
             const int4 p0 = __ldg(reinterpret_cast<const int4 *>(s.cols + g));
             const int4 p1 = __ldg(reinterpret_cast<const int4 *>(s.cols + g + 4));
             const int4 *q = reinterpret_cast<const int4 *>(static_cast<const char *>(s.val) + (size_t)g * ES);
-            bool f = p0.y > p0.x && p0.z > p0.y && p0.w > p0.z && p1.x > p0.w && p1.y > p1.x &&
-                     p1.z > p1.y && p1.w > p1.z;
+            bool f = true;
             if constexpr (ES == 2) {
                 // a 16-bit half that is +-0: (t - 0x00010001) & ~t & 0x80008000 != 0
                 // for t = w & 0x7fff7fff when some half of t is zero (a borrow
@@ -634,10 +661,10 @@ __device__ __forceinline__ void mark_csr_count(const Src &s, int E0, int E1, int
                     const uint32_t t = w[h] & 0x7fff7fffu;
                     z |= (t - 0x00010001u) & ~t & 0x80008000u;
                 }
-                f = f && z == 0;
+                f = z == 0;
             } else if constexpr (ES == 4) {
                 const int4 a = __ldg(q), b = __ldg(q + 1);
-                f = f && (a.x & 0x7fffffff) && (a.y & 0x7fffffff) && (a.z & 0x7fffffff) &&
+                f = (a.x & 0x7fffffff) && (a.y & 0x7fffffff) && (a.z & 0x7fffffff) &&
                     (a.w & 0x7fffffff) && (b.x & 0x7fffffff) && (b.y & 0x7fffffff) &&
                     (b.z & 0x7fffffff) && (b.w & 0x7fffffff);
             } else {
@@ -647,27 +674,36 @@ __device__ __forceinline__ void mark_csr_count(const Src &s, int E0, int E1, int
                     f = f && (a.x | (a.y & 0x7fffffff)) && (a.z | (a.w & 0x7fffffff));
                 }
             }
-            const int c0 = p0.x - s.base, c7 = p1.w - s.base;
-            const int J0 = blk32<P2>(s, c0), J7 = blk32<P2>(s, c7);
-            f = f && c0 >= 0 && (unsigned)c7 < n && J7 - J0 <= 1;
+            const int cr[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+            int c[8], J[8];
+            uint32_t chg = 0;   // bit u: entry u's block column differs from entry u-1's
+            int dsc = 0;        // entries not above the one before, inside the lane
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                c[u] = cr[u] - s.base;
+                f = f && (unsigned)c[u] < n;
+                J[u] = blk32<P2>(s, c[u]);
+            }
+#pragma unroll
+            for (int u = 1; u < 8; ++u) {
+                dsc += c[u] <= c[u - 1];
+                chg |= (uint32_t)(J[u] != J[u - 1]) << u;
+            }
             int prev = __shfl_up_sync(0xffffffffu, p1.w, 1);
-            const int upJ = __shfl_up_sync(0xffffffffu, J7, 1);
+            const int upJ = __shfl_up_sync(0xffffffffu, J[7], 1);
             if (__all_sync(0xffffffffu, f)) {
                 const bool has_prev = g > E0;
                 if (lane == 0 && has_prev) prev = __ldg(s.cols + g - 1);
-                if (has_prev && p0.x <= prev) ++d;   // a descent: not above the entry before
-                if (lane == 0 || J0 != upJ) mark(J0);
-                if (J7 != J0) mark(J7);
-                if (jc) {
-                    if (has_prev && J0 != blk32<P2>(s, prev - s.base)) change_at(g);
-                    if (J7 != J0) {
-                        const int cs[7] = {p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
-                        int uc = 7;
-#pragma unroll
-                        for (int u = 6; u >= 0; --u)
-                            if (blk32<P2>(s, cs[u] - s.base) != J0) uc = u + 1;
-                        change_at(g + uc);
-                    }
+                d += dsc + (has_prev && p0.x <= prev);   // descents: not above the entry before
+                if (lane == 0 || J[0] != upJ) mark(J[0]);
+                if (jc && has_prev && J[0] != blk32<P2>(s, prev - s.base)) change_at(g);
+                while (chg) {   // usually no bit, at most a few
+                    const int u = __ffs(chg) - 1;
+                    chg &= chg - 1;
+                    const int Ju = u == 1 ? J[1] : u == 2 ? J[2] : u == 3 ? J[3] : u == 4 ? J[4]
+                                 : u == 5 ? J[5] : u == 6 ? J[6] : J[7];
+                    mark(Ju);
+                    if (jc) change_at(g + u);
                 }
                 continue;
             }
