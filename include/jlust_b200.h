@@ -201,12 +201,17 @@ JLB_API int jlb_spmv_plan_execute(jlb_spmv_plan plan, void *stream, const void *
  * up to 32 entries, a warp for longer rows.  Variant W (2, 4, 8, 16, 32):
  * groups of W lanes per row, 16-byte loads of four columns and values per
  * lane, a fixed-order butterfly across the group (within tolerance).  The
- * plan takes 4 when the mean row length is 12 to 40 and no row exceeds 128
+ * plan takes 4 when the mean row length is 12 to 96 and no row exceeds 128
  * entries, else 0. */
 JLB_API int jlb_spmv_plan_info(jlb_spmv_plan plan, int64_t *max_row, double *mean_row,
                                int *variant);
-/* Overrides the plan's variant (0, 2, 4, 8, 16 or 32), e.g. to tune it for
- * a matrix; no counterpart in the reference. */
+/* Overrides the plan's variant, e.g. to tune it for a matrix: 0 (a thread
+ * per row, the warp for rows over 32 entries), 1 (the same sums with each
+ * block of 1024 rows' window of x -- columns [row - lower bandwidth, row +
+ * upper bandwidth], from the plan's scan -- staged in shared memory by one
+ * bulk copy: banded structure; variant 0 runs when the window does not fit),
+ * or W = 2, 4, 8, 16, 32 (groups of W lanes per row).  No counterpart in the
+ * reference. */
 JLB_API int jlb_spmv_plan_set_variant(jlb_spmv_plan plan, int variant);
 JLB_API int jlb_spmv_plan_destroy(jlb_spmv_plan plan);
 

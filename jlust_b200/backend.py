@@ -370,7 +370,9 @@ class B200SpMVHandle(AbstractKernelHandle):
 
     def set_variant(self, variant: int):
         """Force the kernel variant: 0 (a thread per row, bit-exact for rows of
-        up to 32 entries) or W in 2, 4, 8, 16, 32 (groups of W lanes per row)."""
+        up to 32 entries), 1 (the same sums with x staged in shared memory per
+        block of rows, for banded structure) or W in 2, 4, 8, 16, 32 (groups of
+        W lanes per row)."""
         _lib.call("jlb_spmv_plan_set_variant", self._plan, int(variant))
         return self
 

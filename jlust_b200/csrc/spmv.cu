@@ -298,6 +298,157 @@ void launch_vec(cudaStream_t st, int base, int64_t m, int64_t nnz, const int32_t
         spmv_vec<T, W, true><<<grid, kThreads, 0, st>>>(m, (int)nnz, rowptr, colind, val, x, y, a, b, base);
 }
 
+// ------------------------------------------------------ banded, staged x
+// Variant 1, for banded structure: a CTA takes kBandRows consecutive rows,
+// whose columns all lie in [r0 - lbw, r1 + ubw) (lbw, ubw: the matrix's
+// lower and upper bandwidths, from the plan), and stages that window of x in
+// shared memory with one bulk copy (cp.async.bulk, completion on an
+// mbarrier) before summing.  Rows are summed as variant 0 sums them (a
+// thread per row of up to kShortMax entries in storage order -- bit-exact --
+// the warp for longer rows), reading x from shared memory; a column outside
+// the window (structure changed since the plan) reads x from global memory.
+// The wait for the copy is bounded: past it the device error word is set and
+// x is read from global memory; the copy is waited for (bounded) again
+// before the CTA exits.
+constexpr int kBandRowsPerThread = 4;
+constexpr int kBandRows = kThreads * kBandRowsPerThread;
+constexpr size_t kBandMaxSmem = 110 * 1024;   // two CTAs an SM
+constexpr long long kBandWaitCycles = 2000000000ll;   // ~1 s
+
+__device__ __forceinline__ bool band_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+__device__ __forceinline__ bool band_wait(uint32_t bar) {
+    const long long t0 = clock64();
+    while (!band_try_wait(bar, 0))
+        if (clock64() - t0 > kBandWaitCycles) return false;
+    return true;
+}
+
+// x window of the CTA's rows: first column (a 16-byte boundary) and bytes (a
+// multiple of 16; the last 16-byte block may extend past x's end inside the
+// block that holds its last element)
+template <typename T>
+__host__ __device__ inline void band_window(int64_t r0, int64_t r1, int64_t n, int64_t lbw,
+                                            int64_t ubw, int64_t &w0, int64_t &bytes) {
+    constexpr int64_t kPer16 = 16 / (int64_t)sizeof(T);
+    int64_t a = r0 - lbw, b = r1 + ubw;
+    if (a < 0) a = 0;
+    if (b > n) b = n;
+    a &= ~(kPer16 - 1);
+    w0 = a;
+    bytes = b > a ? (((b - a) * (int64_t)sizeof(T) + 15) & ~(int64_t)15) : 0;
+}
+
+template <typename T, bool kBeta>
+__global__ void __launch_bounds__(kThreads)
+spmv_band(int64_t m, int64_t n, const int32_t *__restrict__ rowptr,
+          const int32_t *__restrict__ colind, const T *__restrict__ val, const T *__restrict__ x,
+          T *__restrict__ y, T alpha, T beta, int base, int64_t lbw, int64_t ubw) {
+    extern __shared__ __align__(16) unsigned char band_smem[];
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ int s_ok;
+    const int lane = threadIdx.x % kWarp;
+    const int64_t r0 = (int64_t)blockIdx.x * kBandRows;
+    const int64_t r1 = r0 + kBandRows < m ? r0 + kBandRows : m;
+    int64_t w0, bytes;
+    band_window<T>(r0, r1, n, lbw, ubw, w0, bytes);
+    const T *xs = reinterpret_cast<const T *>(band_smem);
+    const uint32_t bar_a = static_cast<uint32_t>(__cvta_generic_to_shared(&bar));
+    if (threadIdx.x == 0) {
+        s_ok = 1;
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar_a) : "memory");
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && bytes > 0) {
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar_a),
+                     "r"((uint32_t)bytes)
+                     : "memory");
+        asm volatile(
+            "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+            ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(band_smem))), "l"(x + w0),
+            "r"((uint32_t)bytes), "r"(bar_a)
+            : "memory");
+    }
+    if (bytes > 0 && !band_wait(bar_a)) {
+        s_ok = 0;
+        dev_error(DEV_ERR_TIMEOUT);
+    }
+    __syncthreads();
+    const bool staged = s_ok != 0;
+    const int64_t wn = bytes / (int64_t)sizeof(T);
+    auto xat = [&](int c) -> T {   // c: 0-based column
+        const int64_t i = (int64_t)c - w0;
+        return staged && i >= 0 && i < wn ? xs[i] : ldg(x + c);
+    };
+#pragma unroll 1
+    for (int j = 0; j < kBandRowsPerThread; ++j) {
+        const int64_t r = r0 + (int64_t)j * kThreads + threadIdx.x;
+        const bool live = r < r1;
+        int lo = 0, hi = 0;
+        if (live) {
+            lo = ldg(rowptr + r) - base;
+            hi = ldg(rowptr + r + 1) - base;
+        }
+        const bool is_long = hi - lo > kShortMax;
+        if (live && !is_long) {
+            T acc = T(0);
+            for (int k = lo; k < hi; ++k) acc = add_rn(acc, mul_rn(ldg(val + k), xat(ldg(colind + k) - base)));
+            write_row<T, kBeta>(y, r, acc, alpha, beta);
+        }
+        unsigned longs = __ballot_sync(0xffffffffu, live && is_long);
+        while (longs) {
+            const int src = __ffs(longs) - 1;
+            longs &= longs - 1;
+            const int l = __shfl_sync(0xffffffffu, lo, src), h = __shfl_sync(0xffffffffu, hi, src);
+            T acc = T(0);
+            for (int k = l + lane; k < h; k += kWarp)
+                acc = add_rn(acc, mul_rn(__ldcs(val + k), xat(__ldcs(colind + k) - base)));
+            acc = warp_sum(acc);
+            if (lane == src) write_row<T, kBeta>(y, r, acc, alpha, beta);   // lane src's own row
+        }
+    }
+    // a copy that outlived the bounded wait lands before the CTA exits
+    if (!staged && threadIdx.x == 0 && !band_wait(bar_a)) dev_error(DEV_ERR_TIMEOUT);
+}
+
+// Launches variant 1 when the window fits; false otherwise (the caller then
+// runs variant 0).
+template <typename T>
+bool launch_band(cudaStream_t st, int base, int64_t m, int64_t n, const int32_t *rowptr,
+                 const int32_t *colind, const T *val, const T *x, T *y, T a, T b, int64_t lbw,
+                 int64_t ubw) {
+    const int64_t span = kBandRows + lbw + ubw + 16;
+    if (lbw < 0 || ubw < 0 || span * (int64_t)sizeof(T) > (int64_t)kBandMaxSmem || !aligned16(x))
+        return false;
+    const size_t smem = (size_t)(((span * (int64_t)sizeof(T)) + 15) & ~(int64_t)15);
+    const unsigned grid = (unsigned)ceil_div(m, kBandRows);
+    if (b == T(0)) {
+        if (cudaFuncSetAttribute(spmv_band<T, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)smem) != cudaSuccess)
+            return false;
+        spmv_band<T, false><<<grid, kThreads, smem, st>>>(m, n, rowptr, colind, val, x, y, a, b, base,
+                                                          lbw, ubw);
+    } else {
+        if (cudaFuncSetAttribute(spmv_band<T, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)smem) != cudaSuccess)
+            return false;
+        spmv_band<T, true><<<grid, kThreads, smem, st>>>(m, n, rowptr, colind, val, x, y, a, b, base,
+                                                         lbw, ubw);
+    }
+    return true;
+}
+
 template <typename T>
 int launch(cudaStream_t st, int base, int64_t m, int64_t nnz, const int32_t *rowptr,
            const int32_t *colind, const void *val, const void *x, void *y, double alpha,
@@ -316,14 +467,24 @@ int launch(cudaStream_t st, int base, int64_t m, int64_t nnz, const int32_t *row
 }
 
 // Variant 0: a thread per row (bit-exact for rows of up to kShortMax entries),
-// the warp for longer rows.  Variant W in {2, 4, 8, 16, 32}: groups of W
-// lanes per row; they need 16-byte aligned colind and val (else variant 0
-// runs).
+// the warp for longer rows.  Variant 1: the same sums with x staged in shared
+// memory per block of rows (banded structure; needs the bandwidths and a
+// window that fits, else variant 0 runs).  Variant W in {2, 4, 8, 16, 32}:
+// groups of W lanes per row; they need 16-byte aligned colind and val (else
+// variant 0 runs).
 template <typename T>
 int launch_variant(cudaStream_t st, int base, int64_t m, int64_t nnz, const int32_t *rowptr,
                    const int32_t *colind, const void *val, const void *x, void *y, double alpha,
-                   double beta, int variant) {
+                   double beta, int variant, int64_t n = 0, int64_t lbw = -1, int64_t ubw = -1) {
     if (m == 0) return ok();
+    if (variant == 1) {
+        if (launch_band<T>(st, base, m, n, rowptr, colind, (const T *)val, (const T *)x, (T *)y,
+                           (T)alpha, (T)beta, lbw, ubw)) {
+            JLB_LAUNCH_CHECK("spmv_band");
+            return ok();
+        }
+        variant = 0;
+    }
     if (variant != 0 && aligned16(colind) && aligned16(val)) {
         const T a = (T)alpha, b = (T)beta;
         const T *v = (const T *)val, *xx = (const T *)x;
@@ -344,13 +505,15 @@ int launch_variant(cudaStream_t st, int base, int64_t m, int64_t nnz, const int3
 
 // ------------------------------------------------------------- validation
 static __device__ int g_validate_flags;
+constexpr int kValidateStats = 5;
 
 __global__ void csr_validate_kernel(int64_t m, int64_t n, int64_t nnz,
                                     const int32_t *__restrict__ rowptr,
                                     const int32_t *__restrict__ colind, int base,
                                     int require_sorted, int32_t *__restrict__ stats) {
     // stats[0] = max row length, stats[1] = rows longer than kShortMax,
-    // stats[2] = entries in those rows
+    // stats[2] = entries in those rows, stats[3] / stats[4] = lower / upper
+    // bandwidth (max of row - column / column - row over the entries)
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < m; r += stride) {
         const int64_t lo = (int64_t)rowptr[r] - base, hi = (int64_t)rowptr[r + 1] - base;
@@ -364,12 +527,18 @@ __global__ void csr_validate_kernel(int64_t m, int64_t n, int64_t nnz,
                 atomicAdd(&stats[2], (int32_t)(hi - lo));
             }
         }
-        int64_t prev = -1;
+        int64_t prev = -1, below = 0, above = 0;
         for (int64_t k = lo; k < hi; ++k) {
             const int64_t c = (int64_t)colind[k] - base;
             if (c < 0 || c >= n) { atomicOr(&g_validate_flags, 8); break; }
             if (require_sorted && c <= prev) { atomicOr(&g_validate_flags, 16); break; }
             prev = c;
+            if (r - c > below) below = r - c;
+            if (c - r > above) above = c - r;
+        }
+        if (stats) {
+            if (below > 0) atomicMax(&stats[3], (int32_t)(below < INT32_MAX ? below : INT32_MAX));
+            if (above > 0) atomicMax(&stats[4], (int32_t)(above < INT32_MAX ? above : INT32_MAX));
         }
     }
 }
@@ -388,7 +557,7 @@ int csr_validate_impl(cudaStream_t st, int base, int64_t m, int64_t n, int64_t n
     const int zero = 0;
     JLB_CUDA(cudaMemcpyToSymbolAsync(spmv::g_validate_flags, &zero, sizeof(int), 0,
                                      cudaMemcpyHostToDevice, st));
-    if (stats_dev) JLB_CUDA(cudaMemsetAsync(stats_dev, 0, 3 * sizeof(int32_t), st));
+    if (stats_dev) JLB_CUDA(cudaMemsetAsync(stats_dev, 0, spmv::kValidateStats * sizeof(int32_t), st));
     if (m > 0) {
         const unsigned grid = (unsigned)(ceil_div(m, 256) < 148 * 16 ? ceil_div(m, 256) : 148 * 16);
         spmv::csr_validate_kernel<<<grid, 256, 0, st>>>(m, n, nnz, rowptr, colind, base,
@@ -405,7 +574,7 @@ int csr_validate_impl(cudaStream_t st, int base, int64_t m, int64_t n, int64_t n
     JLB_CUDA(cudaMemcpyFromSymbolAsync(&flags, spmv::g_validate_flags, sizeof(int), 0,
                                        cudaMemcpyDeviceToHost, st));
     if (stats_dev && stats_host)
-        JLB_CUDA(cudaMemcpyAsync(stats_host, stats_dev, 3 * sizeof(int32_t),
+        JLB_CUDA(cudaMemcpyAsync(stats_host, stats_dev, spmv::kValidateStats * sizeof(int32_t),
                                  cudaMemcpyDeviceToHost, st));
     JLB_CUDA(cudaStreamSynchronize(st));
     if (flags & 1) return fail(JLB_ERR_NONCANONICAL_STORAGE, "rowptr[0] != idx_base");
@@ -498,6 +667,7 @@ struct jlb_spmv_plan_s {
     int64_t max_row;
     int64_t long_rows;
     int64_t long_nnz;
+    int64_t lbw, ubw;   // lower / upper bandwidth
     int variant;
 };
 
@@ -512,13 +682,17 @@ int choose_variant(int64_t m, int64_t nnz, int64_t max_row, int64_t long_nnz) {
     if (m == 0) return 0;
     const double mean = (double)nnz / (double)m;
     // measured on B200 (fp64): the thread per row wins on regular short rows
-    // (5-point Laplacian) and on power-law rows (its warp path takes the
-    // long ones); groups of 4 lanes win on uniform rows of 16 to 48 entries;
-    // on longer rows the two are level (both bound by the x gathers' L1
-    // sector throughput), and variant 0 keeps its bit-exact short rows
+    // (5-point Laplacian, bands of 5 and 17 entries) and on power-law rows
+    // (its warp path takes the long ones); groups of 4 lanes win on rows of
+    // 16 to about 100 entries when no row is long (random columns; bands of
+    // 33 and 65 entries: 2.3x and 1.17x variant 0); with longer rows present
+    // the two are level on random columns (both bound by the x gathers' L1
+    // sector throughput), and variant 0 keeps its bit-exact short rows.
+    // Variant 1 (x staged per block of rows) is never picked: it was slower
+    // than variant 0 on every banded matrix measured.
     (void)long_nnz;
     if (max_row <= kShortMax && mean <= kScalarMean) return 0;
-    if (mean >= kScalarMean && mean < 40.0 && max_row <= 4 * kShortMax) return 4;
+    if (mean >= kScalarMean && mean < 96.0 && max_row <= 4 * kShortMax) return 4;
     return 0;
 }
 }  // namespace spmv
@@ -533,8 +707,9 @@ extern "C" JLB_API int jlb_spmv_plan_create(jlb_spmv_plan *plan, void *stream, i
                        (const void *)1, (void *)1);
     if (st) return st;
     int32_t *stats_dev = nullptr;
-    JLB_CUDA(cudaMallocAsync((void **)&stats_dev, 3 * sizeof(int32_t), as_stream(stream)));
-    int32_t stats[3] = {0, 0, 0};
+    JLB_CUDA(cudaMallocAsync((void **)&stats_dev, spmv::kValidateStats * sizeof(int32_t),
+                             as_stream(stream)));
+    int32_t stats[spmv::kValidateStats] = {0, 0, 0, 0, 0};
     st = csr_validate_impl(as_stream(stream), idx_base, m, n, nnz, rowptr, colind, 0, stats_dev,
                            stats);
     cudaFreeAsync(stats_dev, as_stream(stream));
@@ -546,6 +721,8 @@ extern "C" JLB_API int jlb_spmv_plan_create(jlb_spmv_plan *plan, void *stream, i
     p->max_row = stats[0];
     p->long_rows = stats[1];
     p->long_nnz = stats[2];
+    p->lbw = stats[3];
+    p->ubw = stats[4];
     p->variant = spmv::choose_variant(m, nnz, p->max_row, p->long_nnz);
     *plan = p;
     return ok();
@@ -553,9 +730,10 @@ extern "C" JLB_API int jlb_spmv_plan_create(jlb_spmv_plan *plan, void *stream, i
 
 extern "C" JLB_API int jlb_spmv_plan_set_variant(jlb_spmv_plan p, int variant) {
     if (!p) return fail(JLB_ERR_INVALID_ARGUMENT, "null plan");
-    if (variant != 0 && variant != 2 && variant != 4 && variant != 8 && variant != 16 && variant != 32)
-        return fail(JLB_ERR_INVALID_ARGUMENT, "SpMV variant must be 0, 2, 4, 8, 16 or 32 (got %d)",
-                    variant);
+    if (variant != 0 && variant != 1 && variant != 2 && variant != 4 && variant != 8 &&
+        variant != 16 && variant != 32)
+        return fail(JLB_ERR_INVALID_ARGUMENT,
+                    "SpMV variant must be 0, 1, 2, 4, 8, 16 or 32 (got %d)", variant);
     p->variant = variant;
     return ok();
 }
@@ -567,9 +745,11 @@ extern "C" JLB_API int jlb_spmv_plan_execute(jlb_spmv_plan p, void *stream, cons
     if (st) return st;
     if (p->dtype == JLB_F64)
         return spmv::launch_variant<double>(as_stream(stream), p->base, p->m, p->nnz, p->rowptr,
-                                            p->colind, val, x, y, alpha, beta, p->variant);
+                                            p->colind, val, x, y, alpha, beta, p->variant, p->n,
+                                            p->lbw, p->ubw);
     return spmv::launch_variant<float>(as_stream(stream), p->base, p->m, p->nnz, p->rowptr,
-                                       p->colind, val, x, y, alpha, beta, p->variant);
+                                       p->colind, val, x, y, alpha, beta, p->variant, p->n, p->lbw,
+                                       p->ubw);
 }
 
 extern "C" JLB_API int jlb_spmv_plan_info(jlb_spmv_plan p, int64_t *max_row, double *mean_row,

@@ -236,3 +236,87 @@ def test_vector_variant_unaligned_values_fall_back():
     J.execute(J.SpMVOp, h, to_dev(x), y)
     J.device_status()
     assert np.array_equal(y.cpu().numpy(), O.spmv(rp, ci, val, x))
+
+
+def _banded_csr(m, lo_bw, hi_bw, seed, base=0, dtype=np.float64, drop=0.0):
+    """Rows whose columns are [r - lo_bw, r + hi_bw] clipped to the matrix,
+    a fraction `drop` of them left out."""
+    rng = np.random.default_rng(seed)
+    rows, cols = [], []
+    for r in range(m):
+        c = np.arange(max(0, r - lo_bw), min(m, r + hi_bw + 1))
+        if drop:
+            c = c[rng.random(c.shape[0]) >= drop]
+        rows.append(np.full(c.shape[0], r))
+        cols.append(c)
+    cols = np.concatenate(cols).astype(np.int32)
+    lens = np.array([len(r) for r in rows])
+    rp = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    val = rng.uniform(-1, 1, cols.shape[0]).astype(dtype)
+    return (rp + base).astype(np.int32), (cols + base).astype(np.int32), val
+
+
+@pytest.mark.parametrize("dtype", [np.float64, np.float32])
+@pytest.mark.parametrize("base", [0, 1])
+def test_banded_staged_x_variant(dtype, base):
+    """Variant 1 stages each 1024-row block's window of x in shared memory:
+    bit-exact with the oracle for rows of up to 32 entries (the same sums in
+    the same order as variant 0), beta != 0 included."""
+    m = 5000
+    rp, ci, val = _banded_csr(m, 9, 14, seed=80, base=base, dtype=dtype, drop=0.2)
+    rng = np.random.default_rng(81)
+    x = rng.uniform(-1, 1, m).astype(dtype)
+    y0 = rng.uniform(-1, 1, m).astype(dtype)
+    A = J.csr_tensor(to_dev(rp), to_dev(ci), to_dev(val), (m, m), origin=base)
+    h = J.prepare(J.B200Backend(), J.SpMVOp, A).set_variant(1)
+    assert h.info()["variant"] == 1
+    y = to_dev(np.zeros(m, dtype))
+    J.execute(J.SpMVOp, h, to_dev(x), y)
+    J.device_status()
+    assert np.array_equal(y.cpu().numpy(), O.spmv(rp - base, ci - base, val, x))
+    yb = to_dev(y0)
+    J.execute(J.SpMVOp, h, to_dev(x), yb, alpha=1.5, beta=-0.5)
+    J.device_status()
+    assert np.array_equal(yb.cpu().numpy(), O.spmv(rp - base, ci - base, val, x, y0, 1.5, -0.5))
+
+
+def test_banded_staged_x_long_rows_and_laplacian():
+    """Variant 1 on rows longer than 32 entries (the warp path, within
+    tolerance) and on the 5-point Laplacian (bit-exact)."""
+    m = 3000
+    rp, ci, val = _banded_csr(m, 30, 25, seed=82)
+    x = np.random.default_rng(83).uniform(-1, 1, m)
+    A = J.csr_tensor(to_dev(rp), to_dev(ci), to_dev(val), (m, m), origin=0)
+    h = J.prepare(J.B200Backend(), J.SpMVOp, A).set_variant(1)
+    y = torch.zeros(m, dtype=torch.float64, device=DEV)
+    J.execute(J.SpMVOp, h, to_dev(x), y)
+    J.device_status()
+    ref, bound = O.spmv_ref64(rp, ci, val, x)
+    assert_within(y.cpu().numpy(), ref, bound, 1e-12)
+    rp, ci, val, x = synth.config2(g=96)
+    n = 96 * 96
+    A = J.csr_tensor(to_dev(rp), to_dev(ci), to_dev(val), (n, n), origin=0)
+    h = J.prepare(J.B200Backend(), J.SpMVOp, A).set_variant(1)
+    y = torch.zeros(n, dtype=torch.float64, device=DEV)
+    J.execute(J.SpMVOp, h, to_dev(x), y)
+    J.device_status()
+    assert np.array_equal(y.cpu().numpy(), O.spmv(rp, ci, val, x))
+
+
+def test_banded_staged_x_falls_back_when_window_too_wide():
+    """A matrix whose bandwidth gives a window larger than shared memory (one
+    entry far from the diagonal) runs variant 0 under variant 1: bit-exact."""
+    m = 40000
+    rp, ci, val = _banded_csr(m, 2, 2, seed=84)
+    ci = ci.copy()
+    ci[rp[5]] = m - 1                  # row 5 reaches the last column
+    order = np.argsort(ci[rp[5]:rp[6]], kind="stable")
+    ci[rp[5]:rp[6]] = ci[rp[5]:rp[6]][order]
+    val[rp[5]:rp[6]] = val[rp[5]:rp[6]][order]
+    x = np.random.default_rng(85).uniform(-1, 1, m)
+    A = J.csr_tensor(to_dev(rp), to_dev(ci), to_dev(val), (m, m), origin=0)
+    h = J.prepare(J.B200Backend(), J.SpMVOp, A).set_variant(1)
+    y = torch.zeros(m, dtype=torch.float64, device=DEV)
+    J.execute(J.SpMVOp, h, to_dev(x), y)
+    J.device_status()
+    assert np.array_equal(y.cpu().numpy(), O.spmv(rp, ci, val, x))
