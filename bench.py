@@ -1120,9 +1120,9 @@ class CooToCsr(Single):
     """COO -> CSR of the cfg2 Laplacian (its 83.9 M fp64 entries given as
     row-ordered COO) through convert_format: count, host read of nnz, fill."""
 
-    key, kernel, dtype, profile, unit = ("coo2csr", "coo_keep", "f64 values, int32 indices",
+    key, kernel, dtype, profile, unit = ("coo2csr", "coo_keep_tiles", "f64 values, int32 indices",
                                          "coo2csr", "Gentries/s")
-    launches_per_step = 7          # keep, scan (3), row pointer fill and write, emit
+    launches_per_step = 8          # keep, scan of tile counts (3), of row counts (3), emit
 
     def host(self):
         rp, ci, val, _ = self.synth.config2(g=4096)

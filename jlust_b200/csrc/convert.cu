@@ -91,7 +91,15 @@ scan_tile_sums(int64_t n, const int32_t *__restrict__ counts, int64_t *__restric
     pdl_trigger();
     const int64_t t0 = (int64_t)blockIdx.x * kScanTile;
     int64_t v = 0;
-    if (t0 + kScanTile <= n) {
+    if (t0 + kScanTile <= n && (reinterpret_cast<uintptr_t>(counts) & 15) == 0) {
+        // four 16-byte loads a thread, striped
+        const int4 *c4 = reinterpret_cast<const int4 *>(counts + t0);
+#pragma unroll
+        for (int j = 0; j < kScanItems / 4; ++j) {
+            const int4 q = __ldg(c4 + j * kThreads + threadIdx.x);
+            v += (int64_t)q.x + q.y + q.z + q.w;
+        }
+    } else if (t0 + kScanTile <= n) {
 #pragma unroll
         for (int j = 0; j < kScanItems; ++j) v += ldg(counts + t0 + j * kThreads + threadIdx.x);
     } else {
@@ -175,6 +183,78 @@ scan_tiles_final(int64_t n, const int32_t *counts, int32_t *out, const int64_t *
     if (blockIdx.x == 0 && threadIdx.x == 0) out[0] = base;
 }
 
+// The final pass when `out` does not overlap `counts` and both are 16-byte
+// aligned: tile t writes out[t0 .. t0 + kScanTile) (the exclusive values of
+// its own counts; out[t0] is the tile's offset) with 16-byte stores, the
+// last tile also out[n].  Loads and stores are 16-byte vectors, striped.
+__global__ void __launch_bounds__(kThreads, 6)
+scan_tiles_final_aligned(int64_t n, const int32_t *__restrict__ counts, int32_t *__restrict__ out,
+                         const int64_t *__restrict__ sums, int base) {
+    __shared__ int64_t s_warp[kThreads / kWarp];
+    __shared__ int32_t s_tile[kScanTile + kScanTile / 32];
+    const int64_t t0 = (int64_t)blockIdx.x * kScanTile;
+    const bool full = t0 + kScanTile <= n;
+    if (full) {
+        const int4 *c4 = reinterpret_cast<const int4 *>(counts + t0);
+#pragma unroll
+        for (int j = 0; j < kScanItems / 4; ++j) {
+            const int k = 4 * (j * kThreads + threadIdx.x);
+            const int4 q = __ldg(c4 + j * kThreads + threadIdx.x);
+            s_tile[scan_pad(k)] = q.x;
+            s_tile[scan_pad(k + 1)] = q.y;
+            s_tile[scan_pad(k + 2)] = q.z;
+            s_tile[scan_pad(k + 3)] = q.w;
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < kScanItems; ++j) {
+            const int k = j * kThreads + threadIdx.x;
+            s_tile[scan_pad(k)] = t0 + k < n ? __ldg(counts + t0 + k) : 0;
+        }
+    }
+    pdl_wait();
+    const int64_t offset = sums[blockIdx.x] + base;
+    __syncthreads();
+    int64_t v = 0;
+#pragma unroll
+    for (int j = 0; j < kScanItems; ++j) v += s_tile[scan_pad(threadIdx.x * kScanItems + j)];
+    int64_t total;
+    int64_t run = block_exclusive_scan(v, s_warp, total) + offset;
+    bool over = false;
+#pragma unroll
+    for (int j = 0; j < kScanItems; ++j) {
+        const int q = scan_pad(threadIdx.x * kScanItems + j);
+        const int32_t c = s_tile[q];
+        over |= run > INT32_MAX;
+        s_tile[q] = (int32_t)run;   // exclusive: out[t0 + k]
+        run += c;
+    }
+    if (over) dev_error(DEV_ERR_OVERFLOW);
+    if (!full && threadIdx.x == kThreads - 1) {
+        if (run > INT32_MAX) dev_error(DEV_ERR_OVERFLOW);
+        out[n] = (int32_t)run;   // the last tile: the total
+    } else if (full && t0 + kScanTile == n && threadIdx.x == kThreads - 1) {
+        if (run > INT32_MAX) dev_error(DEV_ERR_OVERFLOW);
+        out[n] = (int32_t)run;
+    }
+    __syncthreads();
+    if (full) {
+        int4 *o4 = reinterpret_cast<int4 *>(out + t0);
+#pragma unroll
+        for (int j = 0; j < kScanItems / 4; ++j) {
+            const int k = 4 * (j * kThreads + threadIdx.x);
+            o4[j * kThreads + threadIdx.x] = make_int4(s_tile[scan_pad(k)], s_tile[scan_pad(k + 1)],
+                                                       s_tile[scan_pad(k + 2)], s_tile[scan_pad(k + 3)]);
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < kScanItems; ++j) {
+            const int k = j * kThreads + threadIdx.x;
+            if (t0 + k < n) out[t0 + k] = s_tile[scan_pad(k)];
+        }
+    }
+}
+
 __global__ void scan_write_base(int32_t *out, int base) { out[0] = base; }
 
 size_t scan_ws(int64_t n) { return (size_t)(ceil_div(n > 0 ? n : 1, kScanTile) * sizeof(int64_t)); }
@@ -205,7 +285,17 @@ int scan(cudaStream_t st, int64_t n, const int32_t *counts, int32_t *out, int ba
     JLB_CUDA(cudaLaunchKernelEx(&cfg, scan_sums_single, ntiles, sums));
     cfg.gridDim = dim3((unsigned)ntiles);
     cfg.blockDim = dim3(kThreads);
-    JLB_CUDA(cudaLaunchKernelEx(&cfg, scan_tiles_final, n, counts, out, (const int64_t *)sums, base));
+    // out[0 .. n] and counts[0 .. n) apart: aligned 16-byte stores of the
+    // exclusive values; otherwise (in place, out == counts - 1, or unaligned)
+    // each tile writes the inclusive values of its own counts
+    const char *cb = reinterpret_cast<const char *>(counts), *ob = reinterpret_cast<const char *>(out);
+    const bool apart = ob + (size_t)(n + 1) * 4 <= cb || cb + (size_t)n * 4 <= ob;
+    if (apart && aligned16(counts) && aligned16(out))
+        JLB_CUDA(cudaLaunchKernelEx(&cfg, scan_tiles_final_aligned, n, counts, out,
+                                    (const int64_t *)sums, base));
+    else
+        JLB_CUDA(cudaLaunchKernelEx(&cfg, scan_tiles_final, n, counts, out, (const int64_t *)sums,
+                                    base));
     JLB_LAUNCH_CHECK("exclusive_scan");
     return ok();
 }
@@ -643,6 +733,14 @@ __device__ __forceinline__ void mark_csr_count(const Src &s, int E0, int E1, int
     for (int g0 = (E0 & ~7) + warp * 8 * kWarp; g0 < E1; g0 += nwarps * 8 * kWarp) {
         const int g = g0 + 8 * lane;
         const bool interior = s.vec && g0 >= E0 && g0 + 8 * kWarp <= E1;   // warp-uniform
+        {
+            // this warp's next chunk into L2 while this one is worked on
+            const int64_t gn = (int64_t)g + nwarps * 8 * kWarp;
+            if (gn + 8 <= E1) {
+                asm volatile("prefetch.global.L2 [%0];" ::"l"(s.cols + gn));
+                asm volatile("prefetch.global.L2 [%0];" ::"l"(static_cast<const char *>(s.val) + gn * ES));
+            }
+        }
         if (interior) {
             const int4 p0 = __ldg(reinterpret_cast<const int4 *>(s.cols + g));
             const int4 p1 = __ldg(reinterpret_cast<const int4 *>(s.cols + g + 4));
@@ -1490,9 +1588,9 @@ emit_csr_rows(int64_t m, const int32_t *__restrict__ offs, const int32_t *__rest
 // explicit zeros are dropped (:316) and an entry whose coordinates equal
 // those of the nonzero entry before it is merged into it, keeping the first
 // value (the unique column level's run, :231-238).  So the CSR is a stable
-// compaction of the COO: keep[p] marks the entries that stay, an exclusive
-// scan of keep gives their slots, and the first kept entry of row r writes
-// rowptr for the rows since the previous kept entry's row.
+// compaction of the COO: keep[p] marks the entries that stay, their ranks
+// give their slots, and the first kept entry of row r writes rowptr for the
+// rows since the previous kept entry's row.
 
 // The last nonzero entry before p, or -1.  Every zero belongs to the run
 // before exactly one nonzero entry, so these walks add up to at most nnz.
@@ -1503,16 +1601,35 @@ __device__ __forceinline__ int64_t prev_nonzero(const void *__restrict__ val, in
     return q;
 }
 
-// The loads of an entry and of the entry before it are issued together (the
-// entry before is almost always the nonzero predecessor); only when that one
-// is an explicit zero does a thread walk further back.
+// ---------------------------------------- COO -> CSR by tiles of entries
+// The compaction works on tiles of kScanTile entries: the keep pass writes
+// one byte per entry, each tile's kept count and (count phase) each row's
+// kept count; the library scan turns the tile counts into tile offsets and
+// the row counts into the row pointer; the emit pass rebuilds each entry's
+// slot from its tile's keep bytes with a block scan.  No per-entry slot
+// array: each pass reads the COO arrays it needs once.
+
+// keep[p] (one byte): nonzero, inside the extents and (merge) not on the
+// coordinates of the nonzero entry before it; per tile the kept count; with
+// row_counts, each row's kept count (rows ascend, so a warp's 32 consecutive
+// entries fall in a few rows: one atomic per row a warp touches).  An entry's
+// loads and its predecessor's are issued together (the entry before is almost
+// always the nonzero predecessor); only past an explicit zero does a thread
+// walk back.
 template <int ES>
 __global__ void __launch_bounds__(kThreads)
-coo_keep(int64_t nnz, const int32_t *__restrict__ rows, const int32_t *__restrict__ cols,
-         const void *__restrict__ val, int base, int64_t m, int64_t n, bool merge,
-         int32_t *__restrict__ keep) {
-    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < nnz; p += stride) {
+coo_keep_tiles(int64_t nnz, const int32_t *__restrict__ rows, const int32_t *__restrict__ cols,
+               const void *__restrict__ val, int base, int64_t m, int64_t n, bool merge,
+               uint8_t *__restrict__ keep, int32_t *__restrict__ tcount,
+               int32_t *__restrict__ row_counts) {
+    __shared__ int64_t s_warp[kThreads / kWarp];
+    const int64_t t0 = (int64_t)blockIdx.x * kScanTile;
+    const int lane = threadIdx.x % kWarp;
+    int64_t cnt = 0;
+#pragma unroll 4
+    for (int i = 0; i < kScanItems; ++i) {
+        const int64_t p = t0 + (int64_t)i * kThreads + threadIdx.x;
+        if (p >= nnz) break;
         const bool has_prev = p > 0;
         const int32_t r = ldg(rows + p), c = ldg(cols + p);
         const int32_t r1 = has_prev ? ldg(rows + p - 1) : 0, c1 = has_prev ? ldg(cols + p - 1) : 0;
@@ -1546,67 +1663,73 @@ coo_keep(int64_t nnz, const int32_t *__restrict__ rows, const int32_t *__restric
                 }
             }
         }
-        keep[p] = k;
-    }
-}
-
-// rowptr[i] = total + base for every i: the rows past the last kept entry.
-__global__ void fill_rowptr(int64_t m, const int32_t *__restrict__ total, int base,
-                            int32_t *__restrict__ rowptr) {
-    const int32_t v = *total + base;
-    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i <= m; i += stride) rowptr[i] = v;
-}
-
-// The first kept entry of row r (slot s) writes rowptr[i] = s + base for the
-// rows i in (row of the nonzero entry before it, r].
-template <int ES>
-__global__ void __launch_bounds__(kThreads)
-coo_rowptr(int64_t nnz, const int32_t *__restrict__ rows, const void *__restrict__ val, int base,
-           int64_t m, const int32_t *__restrict__ keep, const int32_t *__restrict__ slot,
-           int32_t *__restrict__ rowptr) {
-    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < nnz; p += stride) {
-        const bool has_prev = p > 0;
-        const int kp = keep[p];
-        const int32_t r0 = ldg(rows + p), sp = slot[p];
-        const int32_t r1 = has_prev ? ldg(rows + p - 1) : 0;
-        const bool zero1 = !has_prev || is_zero<ES>(val, p - 1);
-        if (!kp) continue;
-        const int64_t r = (int64_t)r0 - base;
-        int64_t rp = -1;
-        if (!zero1) {
-            rp = (int64_t)r1 - base;
-        } else if (has_prev) {
-            const int64_t q = prev_nonzero<ES>(val, p - 1);
-            if (q >= 0) rp = (int64_t)ldg(rows + q) - base;
+        keep[p] = (uint8_t)k;
+        cnt += k;
+        if (row_counts) {
+            // lanes on one row: their kept count added once, by the lowest of
+            // the lanes running here together (a split warp only adds more
+            // atomics)
+            const unsigned same = __match_any_sync(__activemask(), k ? r : -1);
+            const unsigned kept = __ballot_sync(same, k) & same;
+            if (k && lane == __ffs(same) - 1) atomicAdd(&row_counts[r - base], __popc(kept));
         }
-        if (rp < -1) rp = -1;
-        for (int64_t i = rp + 1; i <= r && i < m; ++i) rowptr[i] = sp + base;
     }
+    int64_t tot;
+    block_exclusive_scan<kThreads>(cnt, s_warp, tot);
+    if (threadIdx.x == 0) tcount[blockIdx.x] = (int32_t)tot;
 }
 
+// Each entry's slot (its kept rank in storage order + the tile's first
+// slot), or -1 when it is not kept, into s_slot[scan_pad(k)] for entry
+// t0 + k: thread j ranks entries 16j .. 16j+15 (padded indices: no bank
+// conflicts).
+__device__ __forceinline__ void coo_tile_slots(int64_t nnz, int64_t t0, const uint8_t *__restrict__ keep,
+                                               int64_t first, int32_t *s_slot, int64_t *s_warp) {
+    for (int k = threadIdx.x; k < kScanTile; k += kThreads)
+        s_slot[scan_pad(k)] = t0 + k < nnz ? keep[t0 + k] : 0;
+    __syncthreads();
+    int64_t v = 0;
+#pragma unroll
+    for (int j = 0; j < kScanItems; ++j) v += s_slot[scan_pad(threadIdx.x * kScanItems + j)];
+    int64_t tot;
+    int64_t run = block_exclusive_scan<kThreads>(v, s_warp, tot) + first;
+#pragma unroll
+    for (int j = 0; j < kScanItems; ++j) {
+        const int kk = scan_pad(threadIdx.x * kScanItems + j);
+        const int32_t kp = s_slot[kk];
+        s_slot[kk] = kp ? (int32_t)run : -1;
+        run += kp;
+    }
+    __syncthreads();
+}
+
+// colind / values (and rows_out) of the kept entries at their slots.
 template <int ES>
 __global__ void __launch_bounds__(kThreads)
-coo_emit(int64_t nnz, const int32_t *__restrict__ rows, const int32_t *__restrict__ cols,
-         const void *__restrict__ val, const int32_t *__restrict__ keep,
-         const int32_t *__restrict__ slot, int64_t nnz_out, int32_t *__restrict__ rows_out,
-         int32_t *__restrict__ colind, void *__restrict__ out_val) {
-    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < nnz; p += stride) {
-        const int kp = keep[p];
-        const int64_t q = slot[p];
-        const int32_t c = ldg(cols + p);
-        if (!kp) continue;
-        if (q < 0 || q >= nnz_out) {
+coo_emit_tiles(int64_t nnz, const int32_t *__restrict__ rows, const int32_t *__restrict__ cols,
+               const void *__restrict__ val, const uint8_t *__restrict__ keep,
+               const int32_t *__restrict__ tfirst, int64_t nnz_out, int32_t *__restrict__ rows_out,
+               int32_t *__restrict__ colind, void *__restrict__ out_val) {
+    __shared__ int64_t s_warp[kThreads / kWarp];
+    __shared__ int32_t s_slot[kScanTile + kScanTile / 32];
+    const int64_t t0 = (int64_t)blockIdx.x * kScanTile;
+    coo_tile_slots(nnz, t0, keep, tfirst[blockIdx.x], s_slot, s_warp);
+#pragma unroll 4
+    for (int i = 0; i < kScanItems; ++i) {
+        const int k = i * kThreads + threadIdx.x;
+        const int64_t p = t0 + k;
+        const int64_t q = s_slot[scan_pad(k)];
+        if (p >= nnz || q < 0) continue;
+        if (q >= nnz_out) {
             dev_error(DEV_ERR_OVERFLOW);
             continue;
         }
         if (rows_out) rows_out[q] = ldg(rows + p);
-        colind[q] = c;
+        colind[q] = ldg(cols + p);
         copy_val<ES>(out_val, q, val, p);
     }
 }
+
 
 // coordinates[k] = i + base for k in [ptr[i], ptr[i+1]) - base: the outer
 // coordinate of every entry of a compressed level.  Each thread takes 16
@@ -2202,24 +2325,31 @@ extern "C" JLB_API int jlb_positions_to_coordinates(void *stream, int idx_base, 
 }
 
 // ------------------------------------------------------------- COO -> CSR
-// Workspace: [stamp | keep flags (nnz) | slots (nnz + 1) | scan scratch].  The
-// count phase stamps the flags and slots it leaves; a fill phase given the
-// same workspace for the same inputs uses them instead of recomputing.
+// Workspace: [stamp | keep bytes (nnz) | tile counts | tile first slots
+// (+ the total) | row counts (m) | scan scratch].  The count phase stamps the
+// keep bytes and tile slots it leaves; a fill phase given the same workspace
+// for the same inputs uses them instead of recomputing.
 namespace {
 struct CooCsrWs {
     uint64_t *stamp;
-    int32_t *keep, *slot;
+    uint8_t *keep;
+    int32_t *tcount, *tfirst, *rowcnt;
     char *scan;
+    int64_t ntiles;
     size_t scan_bytes, bytes;
 };
 
-CooCsrWs coo_csr_ws(void *ws, int64_t nnz) {
+CooCsrWs coo_csr_ws(void *ws, int64_t nnz, int64_t m) {
     CooCsrWs w{};
     Carve k{reinterpret_cast<char *>(ws)};
+    w.ntiles = ceil_div(nnz > 0 ? nnz : 1, conv::kScanTile);
     w.stamp = k.take<uint64_t>(1);
-    w.keep = k.take<int32_t>((size_t)(nnz > 0 ? nnz : 1));
-    w.slot = k.take<int32_t>((size_t)nnz + 1);
-    w.scan_bytes = conv::scan_ws(nnz > 0 ? nnz : 1);
+    w.keep = k.take<uint8_t>((size_t)(nnz > 0 ? nnz : 1));
+    w.tcount = k.take<int32_t>((size_t)w.ntiles);
+    w.tfirst = k.take<int32_t>((size_t)w.ntiles + 1);
+    w.rowcnt = k.take<int32_t>((size_t)(m > 0 ? m : 1));
+    const int64_t big = w.ntiles > m ? w.ntiles : m;
+    w.scan_bytes = conv::scan_ws(big > 0 ? big : 1);
     w.scan = k.take<char>(w.scan_bytes);
     w.bytes = k.off + 256;
     return w;
@@ -2232,24 +2362,27 @@ CooCsrWs coo_csr_ws(void *ws, int64_t nnz) {
         else conv::kernel<2><<<(grid), (threads), 0, (st)>>>(__VA_ARGS__);                \
     } while (0)
 
-// keep flags and their exclusive scan (slot[nnz] = entries kept); merge:
-// adjacent equal coordinates keep their first value (CSR targets), else only
-// zeros go (COO targets).
+// Keep bytes and tile first slots (tfirst[ntiles] = the kept total); with
+// row_counts (zeroed), each row's kept count too.  merge: adjacent equal
+// coordinates keep their first value (CSR targets), else only zeros go (COO
+// targets).
 int coo_csr_slots(cudaStream_t st, int dtype, int idx_base, int64_t m, int64_t n, int64_t nnz,
                   const int32_t *rows, const int32_t *cols, const void *val, const CooCsrWs &w,
-                  bool merge = true) {
+                  bool merge = true, int32_t *row_counts = nullptr) {
     if (nnz > 0) {
-        JLB_ES_LAUNCH(coo_keep, dtype_size(dtype), conv::grid_for(nnz), conv::kThreads, st, nnz,
-                      rows, cols, val, idx_base, m, n, merge, w.keep);
-        JLB_LAUNCH_CHECK("coo_keep");
+        JLB_ES_LAUNCH(coo_keep_tiles, dtype_size(dtype), (unsigned)w.ntiles, conv::kThreads, st, nnz,
+                      rows, cols, val, idx_base, m, n, merge, w.keep, w.tcount, row_counts);
+        JLB_LAUNCH_CHECK("coo_keep_tiles");
+        return conv::scan(st, w.ntiles, w.tcount, w.tfirst, 0, w.scan, w.scan_bytes);
     }
-    return conv::scan(st, nnz, w.keep, w.slot, 0, w.scan, w.scan_bytes);
+    JLB_CUDA(cudaMemsetAsync(w.tfirst, 0, (size_t)(w.ntiles + 1) * sizeof(int32_t), st));
+    return ok();
 }
 }  // namespace
 
 extern "C" JLB_API size_t jlb_coo_to_csr_workspace_size(int64_t m, int64_t n, int64_t nnz) {
     if (m < 0 || nnz < 0) return 0;
-    return coo_csr_ws(nullptr, nnz).bytes;
+    return coo_csr_ws(nullptr, nnz, m).bytes;
 }
 
 extern "C" JLB_API int jlb_coo_to_csr_count(void *stream, int dtype, int idx_base, int64_t m,
@@ -2262,29 +2395,27 @@ extern "C" JLB_API int jlb_coo_to_csr_count(void *stream, int dtype, int idx_bas
     if (m > INT32_MAX - 1) return fail(JLB_ERR_UNSUPPORTED_INDEX_TYPE, "rows exceed Int32");
     if (!rowptr || !nnz_out || (nnz > 0 && (!rows || !cols || !val)))
         return fail(JLB_ERR_INVALID_ARGUMENT, "null buffer");
-    const CooCsrWs w = coo_csr_ws(workspace, nnz);
+    const CooCsrWs w = coo_csr_ws(workspace, nnz, m);
     if (!workspace || workspace_bytes < w.bytes) return fail(JLB_ERR_WORKSPACE, "workspace too small");
     cudaStream_t st = as_stream(stream);
-    r = coo_csr_slots(st, dtype, idx_base, m, n, nnz, rows, cols, val, w);
+    if (m > 0) JLB_CUDA(cudaMemsetAsync(w.rowcnt, 0, (size_t)m * sizeof(int32_t), st));
+    r = coo_csr_slots(st, dtype, idx_base, m, n, nnz, rows, cols, val, w, true, w.rowcnt);
     if (r) return r;
-    conv::fill_rowptr<<<conv::grid_for(m + 1), conv::kThreads, 0, st>>>(m, w.slot + nnz, idx_base,
-                                                                        rowptr);
-    JLB_LAUNCH_CHECK("fill_rowptr");
-    if (nnz > 0) {
-        JLB_ES_LAUNCH(coo_rowptr, dtype_size(dtype), conv::grid_for(nnz), conv::kThreads, st, nnz,
-                      rows, val, idx_base, m, w.keep, w.slot, rowptr);
-        JLB_LAUNCH_CHECK("coo_rowptr");
-    }
+    // the row pointer: the exclusive scan of the rows' kept counts
+    r = conv::scan(st, m, w.rowcnt, rowptr, idx_base, w.scan, w.scan_bytes);
+    if (r) return r;
     // b1 = b2 = -2 marks a COO -> CSR workspace
     const uint64_t key = carry_key(m, n, nnz, -2, -2, idx_base, dtype, rows, cols, val);
     JLB_CUDA(cudaMemcpyAsync(w.stamp, &key, sizeof(key), cudaMemcpyHostToDevice, st));
     int32_t total = 0;
-    JLB_CUDA(cudaMemcpyAsync(&total, w.slot + nnz, sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+    JLB_CUDA(cudaMemcpyAsync(&total, w.tfirst + w.ntiles, sizeof(int32_t), cudaMemcpyDeviceToHost, st));
     JLB_CUDA(cudaStreamSynchronize(st));
     const int bits = take_dev_error_convert();
     if (bits < 0) return fail(JLB_ERR_CUDA, "reading the device error word failed");
     if (bits & DEV_ERR_BOUNDS)
         return fail(JLB_ERR_NONCANONICAL_STORAGE, "coordinate outside the matrix extents");
+    if (bits & DEV_ERR_OVERFLOW)
+        return fail(JLB_ERR_UNSUPPORTED_INDEX_TYPE, "kept entries overflow Int32 positions");
     if (bits & DEV_ERR_ORDER)
         return fail(JLB_ERR_NONCANONICAL_STORAGE,
                     "COO rows must not decrease (the COO format declares its rows ordered)");
@@ -2302,7 +2433,7 @@ extern "C" JLB_API int jlb_coo_to_csr_fill(void *stream, int dtype, int idx_base
     if ((nnz > 0 && (!rows || !cols || !val)) || (nnz_out > 0 && (!colind || !csr_val)))
         return fail(JLB_ERR_INVALID_ARGUMENT, "null buffer");
     if (nnz_out < 0 || nnz_out > nnz) return fail(JLB_ERR_INVALID_ARGUMENT, "bad nnz_out");
-    const CooCsrWs w = coo_csr_ws(workspace, nnz);
+    const CooCsrWs w = coo_csr_ws(workspace, nnz, m);
     if (!workspace || workspace_bytes < w.bytes) return fail(JLB_ERR_WORKSPACE, "workspace too small");
     if (nnz == 0) return ok();
     cudaStream_t st = as_stream(stream);
@@ -2313,9 +2444,9 @@ extern "C" JLB_API int jlb_coo_to_csr_fill(void *stream, int dtype, int idx_base
         r = coo_csr_slots(st, dtype, idx_base, m, n, nnz, rows, cols, val, w);
         if (r) return r;
     }
-    JLB_ES_LAUNCH(coo_emit, dtype_size(dtype), conv::grid_for(nnz), conv::kThreads, st, nnz, rows,
-                  cols, val, w.keep, w.slot, nnz_out, nullptr, colind, csr_val);
-    JLB_LAUNCH_CHECK("coo_emit");
+    JLB_ES_LAUNCH(coo_emit_tiles, dtype_size(dtype), (unsigned)w.ntiles, conv::kThreads, st, nnz,
+                  rows, cols, val, w.keep, w.tfirst, nnz_out, nullptr, colind, csr_val);
+    JLB_LAUNCH_CHECK("coo_emit_tiles");
     return ok();
 }
 
@@ -2326,7 +2457,7 @@ extern "C" JLB_API int jlb_coo_to_csr_fill(void *stream, int dtype, int idx_base
 // expanded, COO -> COO).  Workspace as for COO -> CSR; fill recomputes.
 extern "C" JLB_API size_t jlb_coo_drop_zeros_workspace_size(int64_t nnz) {
     if (nnz < 0) return 0;
-    return coo_csr_ws(nullptr, nnz).bytes;
+    return coo_csr_ws(nullptr, nnz, 0).bytes;
 }
 
 extern "C" JLB_API int jlb_coo_drop_zeros_count(void *stream, int dtype, int idx_base, int64_t m,
@@ -2338,18 +2469,20 @@ extern "C" JLB_API int jlb_coo_drop_zeros_count(void *stream, int dtype, int idx
     if (r) return r;
     if (!nnz_out || (nnz > 0 && (!rows || !cols || !val)))
         return fail(JLB_ERR_INVALID_ARGUMENT, "null buffer");
-    const CooCsrWs w = coo_csr_ws(workspace, nnz);
+    const CooCsrWs w = coo_csr_ws(workspace, nnz, 0);
     if (!workspace || workspace_bytes < w.bytes) return fail(JLB_ERR_WORKSPACE, "workspace too small");
     cudaStream_t st = as_stream(stream);
     r = coo_csr_slots(st, dtype, idx_base, m, n, nnz, rows, cols, val, w, false);
     if (r) return r;
     int32_t total = 0;
-    JLB_CUDA(cudaMemcpyAsync(&total, w.slot + nnz, sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+    JLB_CUDA(cudaMemcpyAsync(&total, w.tfirst + w.ntiles, sizeof(int32_t), cudaMemcpyDeviceToHost, st));
     JLB_CUDA(cudaStreamSynchronize(st));
     const int bits = take_dev_error_convert();
     if (bits < 0) return fail(JLB_ERR_CUDA, "reading the device error word failed");
     if (bits & DEV_ERR_BOUNDS)
         return fail(JLB_ERR_NONCANONICAL_STORAGE, "coordinate outside the matrix extents");
+    if (bits & DEV_ERR_OVERFLOW)
+        return fail(JLB_ERR_UNSUPPORTED_INDEX_TYPE, "kept entries overflow Int32 positions");
     *nnz_out = total;
     return ok();
 }
@@ -2366,14 +2499,14 @@ extern "C" JLB_API int jlb_coo_drop_zeros_fill(void *stream, int dtype, int idx_
         (nnz_out > 0 && (!rows_out || !cols_out || !val_out)))
         return fail(JLB_ERR_INVALID_ARGUMENT, "null buffer");
     if (nnz_out < 0 || nnz_out > nnz) return fail(JLB_ERR_INVALID_ARGUMENT, "bad nnz_out");
-    const CooCsrWs w = coo_csr_ws(workspace, nnz);
+    const CooCsrWs w = coo_csr_ws(workspace, nnz, 0);
     if (!workspace || workspace_bytes < w.bytes) return fail(JLB_ERR_WORKSPACE, "workspace too small");
     if (nnz == 0) return ok();
     cudaStream_t st = as_stream(stream);
     r = coo_csr_slots(st, dtype, idx_base, m, n, nnz, rows, cols, val, w, false);
     if (r) return r;
-    JLB_ES_LAUNCH(coo_emit, dtype_size(dtype), conv::grid_for(nnz), conv::kThreads, st, nnz, rows,
-                  cols, val, w.keep, w.slot, nnz_out, rows_out, cols_out, val_out);
-    JLB_LAUNCH_CHECK("coo_emit");
+    JLB_ES_LAUNCH(coo_emit_tiles, dtype_size(dtype), (unsigned)w.ntiles, conv::kThreads, st, nnz,
+                  rows, cols, val, w.keep, w.tfirst, nnz_out, rows_out, cols_out, val_out);
+    JLB_LAUNCH_CHECK("coo_emit_tiles");
     return ok();
 }

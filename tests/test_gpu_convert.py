@@ -270,3 +270,31 @@ def test_scan_total_past_int32_reported():
     out = J.exclusive_scan(to_dev(np.ones(10, np.int32)))
     J.device_status()
     assert out.cpu().tolist() == list(range(11))
+
+
+@pytest.mark.parametrize("n", [3 * 4096, 3 * 4096 + 5])
+@pytest.mark.parametrize("shift", [0, 1])
+def test_scan_aligned_and_unaligned_buffers(n, shift):
+    """Separate, 16-byte-aligned counts and output take the vector final pass
+    (tile t writes out[t0 ..] with 16-byte stores, the last tile out[n]);
+    buffers one element off a 16-byte boundary take the scalar pass; a whole
+    number of tiles and a ragged last tile."""
+    import ctypes as C
+
+    from jlust_b200 import _lib
+    from jlust_b200.backend import _stream
+    rng = np.random.default_rng(68 + n + shift)
+    c = rng.integers(0, 1000, size=n).astype(np.int32)
+    cbuf = torch.zeros(n + 4, dtype=torch.int32, device=DEV)
+    obuf = torch.full((n + 5,), -7, dtype=torch.int32, device=DEV)
+    counts, out = cbuf[shift:shift + n], obuf[shift:shift + n + 1]
+    counts.copy_(to_dev(c))
+    L = _lib.load()
+    wsb = L.jlb_scan_workspace_size(n)
+    ws = torch.empty(wsb, dtype=torch.uint8, device=DEV)
+    _lib.check(L.jlb_exclusive_scan_i32(_stream(DEV), n, C.c_void_p(counts.data_ptr()),
+                                        C.c_void_p(out.data_ptr()), 1, C.c_void_p(ws.data_ptr()),
+                                        wsb))
+    J.device_status()
+    assert np.array_equal(out.cpu().numpy(), O.exclusive_scan(c, base=1))
+    assert int(obuf[shift + n + 1:].eq(-7).all()) and (shift == 0 or int(obuf[0]) == -7)
