@@ -1611,11 +1611,13 @@ __device__ __forceinline__ int64_t prev_nonzero(const void *__restrict__ val, in
 
 // keep[p] (one byte): nonzero, inside the extents and (merge) not on the
 // coordinates of the nonzero entry before it; per tile the kept count; with
-// row_counts, each row's kept count (rows ascend, so a warp's 32 consecutive
-// entries fall in a few rows: one atomic per row a warp touches).  An entry's
-// loads and its predecessor's are issued together (the entry before is almost
-// always the nonzero predecessor); only past an explicit zero does a thread
-// walk back.
+// row_counts (zeroed), each row's kept count: rows ascend, so a warp's 32
+// consecutive entries fall in runs of equal rows; each run's first lane adds
+// the run's kept count with one atomic (runs from a shuffle and two ballots:
+// finding them with __match_any_sync took the kernel from 395 to 501 us on
+// the cfg2 Laplacian).  An entry's loads and its predecessor's are issued
+// together (the entry before is almost always the nonzero predecessor); only
+// past an explicit zero does a thread walk back.
 template <int ES>
 __global__ void __launch_bounds__(kThreads)
 coo_keep_tiles(int64_t nnz, const int32_t *__restrict__ rows, const int32_t *__restrict__ cols,
@@ -1666,12 +1668,20 @@ coo_keep_tiles(int64_t nnz, const int32_t *__restrict__ rows, const int32_t *__r
         keep[p] = (uint8_t)k;
         cnt += k;
         if (row_counts) {
-            // lanes on one row: their kept count added once, by the lowest of
-            // the lanes running here together (a split warp only adds more
-            // atomics)
-            const unsigned same = __match_any_sync(__activemask(), k ? r : -1);
-            const unsigned kept = __ballot_sync(same, k) & same;
-            if (k && lane == __ffs(same) - 1) atomicAdd(&row_counts[r - base], __popc(kept));
+            // a run starts where the row differs from the lane before's (or
+            // that lane is not here: a split warp only adds more atomics); it
+            // ends before the next run's first lane.  A run with a kept entry
+            // is on that entry's row, checked in bounds above.
+            const unsigned act = __activemask();
+            const int32_t rb = __shfl_up_sync(act, r, 1);
+            const bool head = lane == 0 || !((act >> (lane - 1)) & 1u) || rb != r;
+            const unsigned heads = __ballot_sync(act, head), kept = __ballot_sync(act, k);
+            if (head) {
+                const unsigned above = heads & (0xfffffffeu << lane);
+                const unsigned upto = above ? (above & (0u - above)) - 1u : 0xffffffffu;
+                const int kc = __popc(kept & upto & (0xffffffffu << lane));
+                if (kc) atomicAdd(&row_counts[r - base], kc);
+            }
         }
     }
     int64_t tot;
@@ -1703,7 +1713,10 @@ __device__ __forceinline__ void coo_tile_slots(int64_t nnz, int64_t t0, const ui
     __syncthreads();
 }
 
-// colind / values (and rows_out) of the kept entries at their slots.
+// colind / values (and rows_out) of the kept entries at their slots.  (A
+// version that loaded the thread's columns and values before the block scan
+// held 74 registers, three CTAs an SM, and took 598 us where this takes 455
+// on the cfg2 Laplacian.)
 template <int ES>
 __global__ void __launch_bounds__(kThreads)
 coo_emit_tiles(int64_t nnz, const int32_t *__restrict__ rows, const int32_t *__restrict__ cols,

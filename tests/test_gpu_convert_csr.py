@@ -91,6 +91,38 @@ def test_coo_to_csr_stable_compaction(dtype, base):
     assert U.origin.offset == base
 
 
+@pytest.mark.parametrize("dtype", [np.float64, np.float32, np.uint16])
+@pytest.mark.parametrize("offset", [0, 1])
+def test_coo_to_csr_vector_and_scalar_keep(dtype, offset):
+    """The keep pass takes four entries a thread when the COO arrays are
+    16-byte aligned and one entry otherwise (offset 1: views one element
+    in).  Dense rows and rows spread wider than a tile's 4096-row window,
+    zero runs across lanes, warps and a tile boundary with equal coordinates
+    on either side (merged across the zeros), and a ragged last tile."""
+    rng = np.random.default_rng(207 + offset)
+    m, n, k = 3_000_000, 50, 3 * 4096 + 1237
+    dense = np.sort(rng.integers(100, 100 + k // 8, k // 2))
+    rows = np.sort(np.concatenate([dense, rng.integers(0, m, k - k // 2)]))
+    cols = rng.integers(0, n, k)
+    val = _vals(rng, k, dtype, 0.05)
+    nz = np.uint16(0x3f80) if dtype == np.uint16 else dtype(1.5)
+    for a, b in ((4089, 4101), (4999, 5301), (127, 131), (8190, 8195)):
+        rows[a:b + 1] = rows[a]
+        cols[b] = cols[a]
+        val[a + 1:b] = 0
+        val[a] = val[b] = nz
+    rows = np.maximum.accumulate(rows)
+
+    def dev(x):
+        t = _dev_vals(np.concatenate([x[:1], x])) if offset else _dev_vals(x)
+        return t[offset:]
+    A = J.coo_tensor(dev((rows + 1).astype(np.int32)), dev((cols + 1).astype(np.int32)), dev(val),
+                     (m, n), origin=1)
+    U = J.convert_format(A, J.Formats.CSR)
+    J.device_status()
+    _same(U, O.coo_to_csr(m, n, rows + 1, cols + 1, val, 1))
+
+
 def test_coo_to_csr_rejects_decreasing_rows():
     A = _coo(4, 4, np.array([0, 2, 1]), np.array([0, 0, 0]), np.ones(3), 0)
     with pytest.raises(J.NonCanonicalStorage):
