@@ -1615,9 +1615,10 @@ __device__ __forceinline__ int64_t prev_nonzero(const void *__restrict__ val, in
 // consecutive entries fall in runs of equal rows; each run's first lane adds
 // the run's kept count with one atomic (runs from a shuffle and two ballots:
 // finding them with __match_any_sync took the kernel from 395 to 501 us on
-// the cfg2 Laplacian).  An entry's loads and its predecessor's are issued
-// together (the entry before is almost always the nonzero predecessor); only
-// past an explicit zero does a thread walk back.
+// the cfg2 Laplacian).  The entry before, almost always the nonzero
+// predecessor, is the lane before's entry and comes by shuffle (lane 0 loads
+// it: 395 -> about 385 us); only past an explicit zero does a thread walk
+// back.
 template <int ES>
 __global__ void __launch_bounds__(kThreads)
 coo_keep_tiles(int64_t nnz, const int32_t *__restrict__ rows, const int32_t *__restrict__ cols,
@@ -1633,10 +1634,17 @@ coo_keep_tiles(int64_t nnz, const int32_t *__restrict__ rows, const int32_t *__r
         const int64_t p = t0 + (int64_t)i * kThreads + threadIdx.x;
         if (p >= nnz) break;
         const bool has_prev = p > 0;
+        const unsigned act = __activemask();
         const int32_t r = ldg(rows + p), c = ldg(cols + p);
-        const int32_t r1 = has_prev ? ldg(rows + p - 1) : 0, c1 = has_prev ? ldg(cols + p - 1) : 0;
         const bool zero = is_zero<ES>(val, p);
-        const bool zero1 = !has_prev || is_zero<ES>(val, p - 1);
+        // entry p - 1 is the lane before's entry (lane 0 loads it)
+        int32_t r1 = __shfl_up_sync(act, r, 1), c1 = __shfl_up_sync(act, c, 1);
+        bool zero1 = __shfl_up_sync(act, (int)zero, 1) != 0;
+        if (lane == 0 || !((act >> (lane - 1)) & 1u)) {
+            r1 = has_prev ? ldg(rows + p - 1) : 0;
+            c1 = has_prev ? ldg(cols + p - 1) : 0;
+            zero1 = !has_prev || is_zero<ES>(val, p - 1);
+        }
         int k = 0;
         if (!zero) {
             if ((int64_t)r - base < 0 || (int64_t)r - base >= m || (int64_t)c - base < 0 ||
